@@ -1,0 +1,207 @@
+/*
+ * topos_b200.h -- C ABI of the B200 execution backend for topos compiled plans.
+ *
+ * topos (crate `topos`, repository shergin/poorgrad) compiles a recorded graph
+ * into a `Plan` (engine/plan.rs:97-283) and runs it node by node on the CPU
+ * (`Plan::forward`, engine/plan.rs:514-640).  Acceleration enters through its
+ * backend seam: a `Backend` variant with a `Manifest` (backend/manifest.rs:16-37)
+ * whose `status()` reports `BackendUnavailable` (backend/backend.rs:168-204),
+ * and per-task offers (`Elementary::gemm` / `map`, payload/elementary.rs:74-95)
+ * that answer "declined" (`None`) or a result.
+ *
+ * This library is a new implementer behind that seam.  A whole compiled plan
+ * (its node columns and the wanted/readable/required columns of `Plan::new`)
+ * is handed over once; the library lowers it into a device program (fused
+ * elementwise/broadcast/reduce kernels emitted per fusion group, row kernels,
+ * gather/scatter, tcgen05 GEMMs), lays every materialized value out in one
+ * liveness-planned device arena, and replays the program as a CUDA graph.
+ *
+ * Conventions (the reference's, kept):
+ *  - Every call returns TB_OK (0) or an error code; the thread-local message of
+ *    the last failure is `tb_last_error()`.
+ *  - TB_DECLINED means "this backend does not serve the request"; the caller
+ *    computes on its own path, exactly like a backend offer answering `None`.
+ *  - A runtime failure poisons the library (backend/cuda/kernels/mod.rs:94-105):
+ *    `tb_status` then answers TB_POISONED and every later call declines.
+ *  - The caller owns host buffers; the library owns device memory and handles.
+ *  - There is no CPU fallback inside the library: a missing device answers
+ *    TB_PLATFORM_UNSUPPORTED from `tb_status` and an error from every call.
+ */
+#ifndef TOPOS_B200_H
+#define TOPOS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes; 1..4 mirror `BackendUnavailable` (backend/backend.rs:168-204) */
+enum {
+  TB_OK = 0,
+  TB_NOT_COMPILED = 1,          /* BackendUnavailable::NotCompiled */
+  TB_PLATFORM_UNSUPPORTED = 2,  /* BackendUnavailable::PlatformUnsupported */
+  TB_INITIALIZATION = 3,        /* BackendUnavailable::Initialization(msg) */
+  TB_POISONED = 4,              /* BackendUnavailable::Poisoned(msg) */
+  TB_DECLINED = 5,              /* the offer answers `None` */
+  TB_INVALID = 6,               /* a malformed request (the reference panics) */
+  TB_RUNTIME = 7                /* a CUDA / NCCL failure during a call */
+};
+
+/* ---- opcodes: `Function` variant order (function/function.rs:26-59) */
+enum {
+  TB_OP_LEAF = 0, TB_OP_PARAMETER, TB_OP_INPUT, TB_OP_ADD, TB_OP_SUB, TB_OP_MUL,
+  TB_OP_DIV, TB_OP_NEG, TB_OP_TANH, TB_OP_EXP, TB_OP_LN, TB_OP_MATMUL,
+  TB_OP_TRANSPOSE, TB_OP_SUM, TB_OP_SUM_ALONG, TB_OP_BROADCAST,
+  TB_OP_BROADCAST_ALONG, TB_OP_RESHAPE, TB_OP_PERMUTE, TB_OP_NARROW, TB_OP_PAD,
+  TB_OP_UNFOLD, TB_OP_FOLD, TB_OP_GATHER, TB_OP_SCATTER, TB_OP_LOG_SOFTMAX,
+  TB_OP_LOG_SUM_EXP, TB_OP_SQRT, TB_OP_POWF, TB_OP_MAXIMUM, TB_OP_RELU,
+  TB_OP_STEP, TB_OP_COUNT
+};
+
+/* ---- payload kinds: the storage representations (payload/storage.rs:36-51) */
+enum { TB_PAYLOAD_NONE = 0, TB_PAYLOAD_DENSE = 1, TB_PAYLOAD_CONSTANT = 2, TB_PAYLOAD_SELECTION = 3 };
+
+/* ---- numerics posture (backend/numerics.rs:25-43) */
+enum { TB_NUMERICS_FAST = 0, TB_NUMERICS_EXACT = 1 };
+
+#define TB_MAX_RANK 8
+
+/* One recorded node: a row of the tape's structure columns
+ * (graph/structure.rs:23-61) plus the plan's per-node columns. */
+typedef struct tb_node {
+  int32_t op;                   /* TB_OP_* */
+  int32_t rank;                 /* rank of the node's shape */
+  int64_t shape[TB_MAX_RANK];   /* the recorded shape */
+  int32_t operands[2];          /* operand node indices, -1 when absent */
+  int64_t attrs[TB_MAX_RANK];   /* axis/start/len/full_extent/size/step/dilation/extent/rows,
+                                   or the permute order; see each op's record site */
+  int32_t slot;                 /* Parameter / Input slot, else -1 */
+  int32_t payload;              /* TB_PAYLOAD_* of a Leaf, or of an Input's fed kind */
+  float constant;               /* CONSTANT value; SELECTION `one` */
+  int32_t vocab;                /* SELECTION vocabulary (= shape[1]) */
+  const float* dense;           /* DENSE leaf elements, row-major, host memory */
+  const int32_t* indices;       /* SELECTION leaf indices (shape[0] entries), host memory */
+  uint8_t wanted;               /* Plan::new closure (engine/plan.rs:154-172) */
+  uint8_t readable;             /* a root or observed value */
+  uint8_t required;             /* read by a derivative rule of a training plan (201-225) */
+  uint8_t reserved;
+} tb_node;
+
+/* A compiled request over a network (`Network::compile`, engine/plan.rs:655-663). */
+typedef struct tb_plan_desc {
+  int64_t node_count;
+  const tb_node* nodes;
+  int32_t backward;             /* Request::backward (engine/request.rs:70) */
+  int32_t numerics;             /* TB_NUMERICS_* (engine/request.rs:84) */
+} tb_plan_desc;
+
+/* One fed input (`Plan::forward` feeds, engine/plan.rs:534-564). */
+typedef struct tb_feed {
+  int32_t slot;                 /* input slot */
+  int32_t on_device;            /* 1: pointers are device memory; 0: host memory */
+  const float* dense;           /* DENSE input: volume elements */
+  const int32_t* indices;       /* SELECTION input: shape[0] indices */
+} tb_feed;
+
+typedef struct tb_plan tb_plan;
+typedef struct tb_params tb_params;
+typedef struct tb_optimizer tb_optimizer;
+typedef struct tb_comm tb_comm;
+
+typedef struct tb_plan_stats {
+  int64_t kernels;              /* launches in one run of the device program */
+  int64_t arena_bytes;          /* liveness-planned arena size */
+  int64_t unplanned_bytes;      /* sum of all buffer sizes without reuse */
+  int64_t fused_nodes;          /* wanted nodes that were never materialized */
+  int32_t bit_identical;        /* 1 when every kernel reproduces the interpreter bitwise */
+  int32_t gemms;                /* GEMM launches per run */
+} tb_plan_stats;
+
+/* ---- backend status (`Manifest::status`, backend/manifest.rs:16-37) */
+/* Replaces: the cuda backend's lazy `context()` + POISON check
+ * (backend/cuda/kernels/mod.rs:36-58). Forces lazy set-up; returns TB_* code. */
+int tb_status(char* message, size_t capacity);
+/* Thread-local message of the last failed call on this thread. */
+const char* tb_last_error(void);
+
+/* ---- compiled plans */
+/* Replaces: the node loop of `Plan::forward` (engine/plan.rs:566-622) for one
+ * compiled request.  Lowers the plan to a device program.  Answers TB_DECLINED
+ * for an EXACT-posture plan that holds a kernel that is not bit-identical
+ * (`Fidelity::meets`, backend/coverage.rs:26-32). */
+int tb_plan_compile(const tb_plan_desc* desc, tb_plan** plan);
+void tb_plan_destroy(tb_plan* plan);
+int tb_plan_stats_get(const tb_plan* plan, tb_plan_stats* stats);
+/* Human-readable kernel list of the device program (cf. `Plan::describe`,
+ * engine/plan.rs:408-490); returns the needed length. */
+int64_t tb_plan_describe(const tb_plan* plan, char* buffer, size_t capacity);
+
+/* ---- device-resident `Parameters` (graph/parameters.rs:27) */
+/* Creates zeroed device storage for every parameter slot of the plan's network. */
+int tb_params_create(const tb_plan* plan, tb_params** params);
+void tb_params_destroy(tb_params* params);
+int tb_params_upload(tb_params* params, int32_t slot, const float* host, int64_t count);
+int tb_params_download(const tb_params* params, int32_t slot, float* host, int64_t count);
+
+/* ---- running (`Plan::forward` -> `Run`, engine/plan.rs:514-640; `Run::of`, run.rs:139) */
+/* Enqueues one run: feeds are copied into the plan's input buffers, then the
+ * device program (and an attached gradient exchange and optimizer step) is
+ * launched as one CUDA graph.  Asynchronous with respect to the host. */
+int tb_plan_run(tb_plan* plan, tb_params* params, int32_t feed_count, const tb_feed* feeds);
+/* Waits for the plan's stream. */
+int tb_plan_synchronize(tb_plan* plan);
+/* Copies a readable value (row-major, volume elements) to host memory (waits). */
+int tb_plan_read(tb_plan* plan, int64_t node, float* host, int64_t count);
+/* Device address of a readable value's contiguous buffer (valid until the next run). */
+int tb_plan_device_pointer(tb_plan* plan, int64_t node, const float** device);
+/* The CUDA stream (cudaStream_t) the plan runs on. */
+void* tb_plan_stream(tb_plan* plan);
+
+/* ---- optimizer step (graph/parameters.rs:90-146; neural/optimizer.rs:40-51; neural/adam.rs:19-171) */
+enum { TB_OPTIMIZER_SGD = 0, TB_OPTIMIZER_ADAM = 1, TB_OPTIMIZER_ADAMW = 2 };
+typedef struct tb_optimizer_desc {
+  int32_t kind;                 /* TB_OPTIMIZER_* */
+  float learning_rate;
+  float beta1, beta2, epsilon;  /* Adam / AdamW (adam.rs:33-45) */
+  float decay;                  /* AdamW (adam.rs:118-126), applied to rank >= 2 (adam.rs:167-169) */
+  float gradient_scale;         /* multiplies each gradient first (1/shards, mlp_parallel.rs:170-171); 1 = off */
+} tb_optimizer_desc;
+/* Binds gradient nodes of a plan (readable values) to parameter slots. */
+int tb_optimizer_create(tb_plan* plan, tb_params* params, const tb_optimizer_desc* desc,
+                        int32_t count, const int32_t* slots, const int64_t* gradient_nodes,
+                        tb_optimizer** optimizer);
+void tb_optimizer_destroy(tb_optimizer* optimizer);
+int tb_optimizer_set_learning_rate(tb_optimizer* optimizer, float learning_rate);
+/* Runs the step inside every later `tb_plan_run` of its plan (one graph launch per step). */
+int tb_plan_attach_optimizer(tb_plan* plan, tb_optimizer* optimizer);
+/* Downloads Adam moments of a slot (first, second); count elements each. */
+int tb_optimizer_state(const tb_optimizer* optimizer, int32_t slot, float* first, float* second, int64_t count);
+
+/* ---- data parallel gradient exchange (new: the reference has no communication backend;
+ *      replaces the host `tree_sum` of examples/makemore/mlp_parallel.rs:59-71) */
+int tb_comm_unique_id(uint8_t id[128]);
+int tb_comm_init(int32_t rank, int32_t world, const uint8_t id[128], tb_comm** comm);
+void tb_comm_destroy(tb_comm* comm);
+/* Sum-allreduces the plan's gradient outputs bound by its optimizer, bucket by
+ * bucket as the program finishes them, before the optimizer step. */
+int tb_plan_attach_comm(tb_plan* plan, tb_comm* comm, int64_t bucket_bytes);
+int tb_comm_allreduce(tb_comm* comm, float* device, int64_t count, void* stream);
+
+/* ---- per-task faces (`Elementary::gemm` / `map`, payload/elementary.rs:74-95) */
+/* Replaces: `executed_f32` of the cuda backend (backend/cuda/kernels/gemm.rs:54-163).
+ * out[m, n] = a[m, k] . b[k, n] with element (i, j) of a at a[i*a_strides[0] + j*a_strides[1]]
+ * (`GemmTask`, payload/gemm.rs:40-125); host buffers.  TB_DECLINED below the size
+ * threshold or for unsupported strides. */
+int tb_gemm_f32(const float* a, int64_t a_len, const int64_t a_strides[2],
+                const float* b, int64_t b_len, const int64_t b_strides[2],
+                int64_t m, int64_t k, int64_t n, float* out);
+/* Replaces: `MapTask` offers (payload/elementary.rs:89-95): op is TB_OP_EXP,
+ * TB_OP_LN, TB_OP_SQRT or TB_OP_TANH; host buffers. */
+int tb_map_f32(int32_t op, const float* in, int64_t count, float* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TOPOS_B200_H */

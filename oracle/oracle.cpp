@@ -1,0 +1,497 @@
+// oracle.cpp -- CPU restatement of the topos interpreter's arithmetic.
+//
+// TEST INFRASTRUCTURE ONLY.  This file is the parity oracle for the B200
+// backend: tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg load
+// it as the checker or as the timed reference-CPU path.  The product
+// (poorgrad_b200/, libtopos_b200.so) never links, loads or calls it.
+//
+// It restates, for f32 payloads, what topos computes when a compiled plan runs
+// on its default build (no backend features):
+//   * the plan/interpreter node loop (engine/plan.rs:566-622, engine/run.rs:417-526),
+//   * each Function's forward (function/*.rs `forward`),
+//   * the Tensor arithmetic those forwards call (payload/tensor.rs):
+//     elementwise map/zip in logical row-major order (365-510),
+//     serial left-fold reductions seeded with the first element (1055-1124),
+//     the slice-path GEMM seeded with the first product term, inner steps in
+//     ascending order (payload/gemm.rs:140-211),
+//     gather / scatter-add from zero in source order (1554-1618),
+//     pad / unfold / fold (1292-1463),
+//   * scalar semantics of payload/elementary.rs:116-143 (libm expf/logf/tanhf/
+//     powf, sqrtf, `f32::max` for maximum, `x >= t` for step).
+// Compiled with -O2 -ffp-contract=off and without fast-math: no contraction,
+// no reassociation, exactly as the Rust source is evaluated.
+//
+// Values are independent of storage representation (payload/tests/
+// tensor_tests.rs:1209-1240), so every value is held densely except constants
+// (one scalar) and selections (indices), which gather/scatter need.
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../include/topos_b200.h"
+
+namespace {
+
+struct Val {
+  int kind = TB_PAYLOAD_DENSE;  // DENSE, CONSTANT or SELECTION
+  std::vector<int64_t> shape;
+  std::vector<float> data;      // DENSE
+  float c = 0.0f;               // CONSTANT value / SELECTION one
+  std::vector<int32_t> idx;     // SELECTION
+  int64_t vocab = 0;
+
+  int64_t volume() const {
+    int64_t v = 1;
+    for (auto e : shape) v *= e;
+    return v;
+  }
+  float get(int64_t i) const {
+    switch (kind) {
+      case TB_PAYLOAD_CONSTANT: return c;
+      case TB_PAYLOAD_SELECTION: return (i % vocab) == idx[i / vocab] ? c : 0.0f;
+      default: return data[i];
+    }
+  }
+};
+
+// `f32::max` (elementary.rs:137-139): the non-NaN argument when one is NaN;
+// otherwise the larger, the first argument on ties.
+inline float fmax_ref(float a, float b) {
+  if (std::isnan(a)) return b;
+  if (std::isnan(b)) return a;
+  return (b > a) ? b : a;
+}
+
+Val dense(std::vector<int64_t> shape) {
+  Val v;
+  v.kind = TB_PAYLOAD_DENSE;
+  v.shape = std::move(shape);
+  v.data.assign(v.volume(), 0.0f);
+  return v;
+}
+
+Val constant(std::vector<int64_t> shape, float c) {
+  Val v;
+  v.kind = TB_PAYLOAD_CONSTANT;
+  v.shape = std::move(shape);
+  v.c = c;
+  return v;
+}
+
+std::vector<int64_t> node_shape(const tb_node& n) {
+  return std::vector<int64_t>(n.shape, n.shape + n.rank);
+}
+
+template <class F>
+Val map1(const Val& a, F f) {
+  if (a.kind == TB_PAYLOAD_CONSTANT) return constant(a.shape, f(a.c));
+  Val out = dense(a.shape);
+  for (int64_t i = 0; i < out.volume(); ++i) out.data[i] = f(a.get(i));
+  return out;
+}
+
+template <class F>
+Val zip(const Val& a, const Val& b, F f) {
+  if (a.shape != b.shape) throw std::runtime_error("tensors have different shapes");
+  if (a.kind == TB_PAYLOAD_CONSTANT && b.kind == TB_PAYLOAD_CONSTANT)
+    return constant(a.shape, f(a.c, b.c));
+  Val out = dense(a.shape);
+  for (int64_t i = 0; i < out.volume(); ++i) out.data[i] = f(a.get(i), b.get(i));
+  return out;
+}
+
+void split3(const std::vector<int64_t>& shape, int axis, int64_t& outer, int64_t& extent,
+            int64_t& inner) {
+  outer = 1;
+  inner = 1;
+  for (int i = 0; i < axis; ++i) outer *= shape[i];
+  extent = shape[axis];
+  for (size_t i = axis + 1; i < shape.size(); ++i) inner *= shape[i];
+}
+
+std::vector<int64_t> without(const std::vector<int64_t>& s, int axis) {
+  std::vector<int64_t> r;
+  for (int i = 0; i < (int)s.size(); ++i)
+    if (i != axis) r.push_back(s[i]);
+  return r;
+}
+
+// payload/tensor.rs:1073-1093
+Val sum_along(const Val& a, int axis) {
+  int64_t outer, extent, inner;
+  split3(a.shape, axis, outer, extent, inner);
+  Val out = dense(without(a.shape, axis));
+  for (int64_t o = 0; o < outer; ++o)
+    for (int64_t in = 0; in < inner; ++in) {
+      float total = a.get((o * extent + 0) * inner + in);
+      for (int64_t s = 1; s < extent; ++s) total = total + a.get((o * extent + s) * inner + in);
+      out.data[o * inner + in] = total;
+    }
+  return out;
+}
+
+// payload/tensor.rs:1104-1124
+Val max_along(const Val& a, int axis) {
+  int64_t outer, extent, inner;
+  split3(a.shape, axis, outer, extent, inner);
+  Val out = dense(without(a.shape, axis));
+  for (int64_t o = 0; o < outer; ++o)
+    for (int64_t in = 0; in < inner; ++in) {
+      float largest = a.get((o * extent + 0) * inner + in);
+      for (int64_t s = 1; s < extent; ++s)
+        largest = fmax_ref(largest, a.get((o * extent + s) * inner + in));
+      out.data[o * inner + in] = largest;
+    }
+  return out;
+}
+
+// payload/tensor.rs:1147-1171 (a view; materialized here)
+Val broadcast_along(const Val& a, int axis, const std::vector<int64_t>& ref) {
+  if (a.kind == TB_PAYLOAD_CONSTANT) return constant(ref, a.c);
+  int64_t outer, extent, inner;
+  split3(ref, axis, outer, extent, inner);
+  Val out = dense(ref);
+  for (int64_t o = 0; o < outer; ++o)
+    for (int64_t s = 0; s < extent; ++s)
+      for (int64_t in = 0; in < inner; ++in)
+        out.data[(o * extent + s) * inner + in] = a.get(o * inner + in);
+  return out;
+}
+
+// row-major strides of a shape
+std::vector<int64_t> strides_of(const std::vector<int64_t>& s) {
+  std::vector<int64_t> st(s.size(), 1);
+  for (int i = (int)s.size() - 2; i >= 0; --i) st[i] = st[i + 1] * s[i + 1];
+  return st;
+}
+
+// Materializes a strided reading of `a`: output element at multi-index `m`
+// reads a.get(offset + sum m[i]*strides[i]).
+Val strided(const Val& a, const std::vector<int64_t>& shape, int64_t offset,
+            const std::vector<int64_t>& strides) {
+  Val out = dense(shape);
+  int64_t vol = out.volume();
+  int rank = (int)shape.size();
+  std::vector<int64_t> m(rank, 0);
+  for (int64_t i = 0; i < vol; ++i) {
+    int64_t src = offset;
+    for (int d = 0; d < rank; ++d) src += m[d] * strides[d];
+    out.data[i] = a.get(src);
+    for (int d = rank - 1; d >= 0; --d) {
+      if (++m[d] < shape[d]) break;
+      m[d] = 0;
+    }
+  }
+  return out;
+}
+
+// payload/tensor.rs:921-1027 and payload/gemm.rs:140-211
+Val matmul(const Val& a, const Val& b) {
+  int rank = (int)a.shape.size();
+  int split = rank - 2;
+  int64_t rows = a.shape[split], inner = a.shape[split + 1], cols = b.shape[split + 1];
+  int64_t batches = 1;
+  std::vector<int64_t> shape;
+  for (int i = 0; i < split; ++i) {
+    batches *= a.shape[i];
+    shape.push_back(a.shape[i]);
+  }
+  shape.push_back(rows);
+  shape.push_back(cols);
+  Val out = dense(shape);
+  // dense copies make the inner loops plain slices
+  std::vector<float> A(a.volume()), B(b.volume());
+  for (int64_t i = 0; i < a.volume(); ++i) A[i] = a.get(i);
+  for (int64_t i = 0; i < b.volume(); ++i) B[i] = b.get(i);
+  for (int64_t bt = 0; bt < batches; ++bt) {
+    const float* Ab = A.data() + bt * rows * inner;
+    const float* Bb = B.data() + bt * inner * cols;
+    float* Cb = out.data.data() + bt * rows * cols;
+    for (int64_t r = 0; r < rows; ++r) {
+      float* acc = Cb + r * cols;
+      const float first = Ab[r * inner];
+      for (int64_t c = 0; c < cols; ++c) acc[c] = first * Bb[c];
+      for (int64_t s = 1; s < inner; ++s) {
+        const float av = Ab[r * inner + s];
+        const float* brow = Bb + s * cols;
+        for (int64_t c = 0; c < cols; ++c) acc[c] = acc[c] + av * brow[c];
+      }
+    }
+  }
+  return out;
+}
+
+struct Oracle {
+  const tb_plan_desc* desc;
+  std::vector<Val> values;
+};
+
+Val source_payload(const tb_node& n, const float* dense_ptr, const int32_t* idx_ptr) {
+  Val v;
+  v.shape = node_shape(n);
+  if (n.payload == TB_PAYLOAD_CONSTANT) {
+    v.kind = TB_PAYLOAD_CONSTANT;
+    v.c = n.constant;
+  } else if (n.payload == TB_PAYLOAD_SELECTION) {
+    v.kind = TB_PAYLOAD_SELECTION;
+    v.c = n.constant;
+    v.vocab = n.shape[1];
+    if (!idx_ptr) throw std::runtime_error("selection without indices");
+    v.idx.assign(idx_ptr, idx_ptr + n.shape[0]);
+  } else {
+    v.kind = TB_PAYLOAD_DENSE;
+    if (!dense_ptr) throw std::runtime_error("dense source without elements");
+    v.data.assign(dense_ptr, dense_ptr + v.volume());
+  }
+  return v;
+}
+
+Val forward(const tb_node& n, const Val* x, const Val* y) {
+  const int64_t* at = n.attrs;
+  std::vector<int64_t> shape = node_shape(n);
+  switch (n.op) {
+    case TB_OP_ADD: return zip(*x, *y, [](float l, float r) { return l + r; });
+    case TB_OP_SUB: return zip(*x, *y, [](float l, float r) { return l - r; });
+    case TB_OP_MUL: return zip(*x, *y, [](float l, float r) { return l * r; });
+    case TB_OP_DIV: return zip(*x, *y, [](float l, float r) { return l / r; });
+    case TB_OP_NEG: return map1(*x, [](float v) { return -v; });
+    case TB_OP_TANH: return map1(*x, [](float v) { return tanhf(v); });
+    case TB_OP_EXP: return map1(*x, [](float v) { return expf(v); });
+    case TB_OP_LN: return map1(*x, [](float v) { return logf(v); });
+    case TB_OP_SQRT: return map1(*x, [](float v) { return sqrtf(v); });
+    case TB_OP_POWF: return zip(*x, *y, [](float l, float r) { return powf(l, r); });
+    case TB_OP_MAXIMUM: return zip(*x, *y, [](float l, float r) { return fmax_ref(l, r); });
+    case TB_OP_RELU: return map1(*x, [](float v) { return fmax_ref(v, 0.0f); });
+    case TB_OP_STEP:
+      return zip(*x, *y, [](float l, float r) { return l >= r ? 1.0f : 0.0f; });
+    case TB_OP_MATMUL: return matmul(*x, *y);
+    case TB_OP_TRANSPOSE: {
+      if (x->shape.size() < 2) {
+        Val v = *x;
+        v.shape = shape;
+        return v;
+      }
+      if (x->kind == TB_PAYLOAD_CONSTANT) return constant(shape, x->c);
+      return strided(*x, shape, 0, {1, x->shape[1]});
+    }
+    case TB_OP_SUM: {  // payload/tensor.rs:1055-1063
+      float total = x->get(0);
+      for (int64_t i = 1; i < x->volume(); ++i) total = total + x->get(i);
+      return constant({}, total);
+    }
+    case TB_OP_SUM_ALONG: return sum_along(*x, (int)at[0]);
+    case TB_OP_BROADCAST: return constant(shape, x->get(0));
+    case TB_OP_BROADCAST_ALONG: return broadcast_along(*x, (int)at[0], shape);
+    case TB_OP_RESHAPE: {
+      Val v = *x;
+      v.shape = shape;
+      if (v.kind == TB_PAYLOAD_SELECTION) {  // a reshaped selection is dense
+        Val d = dense(shape);
+        for (int64_t i = 0; i < d.volume(); ++i) d.data[i] = x->get(i);
+        return d;
+      }
+      return v;
+    }
+    case TB_OP_PERMUTE: {
+      if (x->kind == TB_PAYLOAD_CONSTANT) return constant(shape, x->c);
+      std::vector<int64_t> src = strides_of(x->shape), st(shape.size());
+      for (size_t j = 0; j < shape.size(); ++j) st[j] = src[at[j]];
+      return strided(*x, shape, 0, st);
+    }
+    case TB_OP_NARROW: {
+      if (x->kind == TB_PAYLOAD_CONSTANT) return constant(shape, x->c);
+      std::vector<int64_t> st = strides_of(x->shape);
+      return strided(*x, shape, at[1] * st[at[0]], st);
+    }
+    case TB_OP_UNFOLD: {  // layout.unfold: (count, size) pair at axis
+      if (x->kind == TB_PAYLOAD_CONSTANT) return constant(shape, x->c);
+      int axis = (int)at[0];
+      std::vector<int64_t> src = strides_of(x->shape), st;
+      for (int i = 0; i < (int)x->shape.size(); ++i) {
+        if (i == axis) {
+          st.push_back(src[i] * at[2]);
+          st.push_back(src[i] * at[3]);
+        } else {
+          st.push_back(src[i]);
+        }
+      }
+      return strided(*x, shape, 0, st);
+    }
+    case TB_OP_PAD: {  // payload/tensor.rs:1292-1330
+      int axis = (int)at[0];
+      int64_t start = at[1], full = at[2];
+      int64_t outer, len, inner;
+      split3(x->shape, axis, outer, len, inner);
+      Val out = dense(shape);
+      int64_t w = 0;
+      for (int64_t o = 0; o < outer; ++o)
+        for (int64_t p = 0; p < full; ++p)
+          for (int64_t in = 0; in < inner; ++in)
+            out.data[w++] = (p >= start && p < start + len)
+                                ? x->get((o * len + (p - start)) * inner + in)
+                                : 0.0f;
+      return out;
+    }
+    case TB_OP_FOLD: {  // payload/tensor.rs:1392-1463
+      int axis = (int)at[0];
+      int64_t size = at[1], step = at[2], dilation = at[3], extent = at[4];
+      int64_t count = x->shape[axis];
+      int64_t outer = 1, inner = 1;
+      for (int i = 0; i < axis; ++i) outer *= x->shape[i];
+      for (size_t i = axis + 2; i < x->shape.size(); ++i) inner *= x->shape[i];
+      Val out = dense(shape);
+      int64_t w = 0;
+      for (int64_t o = 0; o < outer; ++o)
+        for (int64_t p = 0; p < extent; ++p)
+          for (int64_t in = 0; in < inner; ++in) {
+            float total = 0.0f;
+            for (int64_t k = 0; k < size; ++k) {
+              int64_t reach = k * dilation;
+              if (reach > p) break;
+              int64_t rest = p - reach;
+              if (rest % step != 0) continue;
+              int64_t window = rest / step;
+              if (window >= count) continue;
+              total = total + x->get(((o * count + window) * size + k) * inner + in);
+            }
+            out.data[w++] = total;
+          }
+      return out;
+    }
+    case TB_OP_GATHER: {  // payload/tensor.rs:1554-1576
+      if (y->kind != TB_PAYLOAD_SELECTION) throw std::runtime_error("gather needs a selection");
+      int64_t row = 1;
+      for (size_t i = 1; i < x->shape.size(); ++i) row *= x->shape[i];
+      Val out = dense(shape);
+      for (size_t s = 0; s < y->idx.size(); ++s)
+        for (int64_t o = 0; o < row; ++o) out.data[s * row + o] = x->get(y->idx[s] * row + o);
+      return out;
+    }
+    case TB_OP_SCATTER: {  // payload/tensor.rs:1582-1618
+      if (y->kind != TB_PAYLOAD_SELECTION) throw std::runtime_error("scatter needs a selection");
+      int64_t row = 1;
+      for (size_t i = 1; i < x->shape.size(); ++i) row *= x->shape[i];
+      Val out = dense(shape);  // zeros
+      for (size_t s = 0; s < y->idx.size(); ++s)
+        for (int64_t o = 0; o < row; ++o) {
+          int64_t p = (int64_t)y->idx[s] * row + o;
+          out.data[p] = out.data[p] + x->get(s * row + o);
+        }
+      return out;
+    }
+    case TB_OP_LOG_SOFTMAX: {  // function/log_softmax.rs:51-65
+      int axis = (int)at[0];
+      Val peak = broadcast_along(max_along(*x, axis), axis, x->shape);
+      Val shifted = zip(*x, peak, [](float l, float r) { return l - r; });
+      Val e = map1(shifted, [](float v) { return expf(v); });
+      Val normalizer = map1(sum_along(e, axis), [](float v) { return logf(v); });
+      Val nb = broadcast_along(normalizer, axis, shifted.shape);
+      return zip(shifted, nb, [](float l, float r) { return l - r; });
+    }
+    case TB_OP_LOG_SUM_EXP: {  // function/log_sum_exp.rs:53-63
+      int axis = (int)at[0];
+      Val peak = max_along(*x, axis);
+      Val shifted = zip(*x, broadcast_along(peak, axis, x->shape),
+                        [](float l, float r) { return l - r; });
+      Val e = map1(shifted, [](float v) { return expf(v); });
+      Val lse = map1(sum_along(e, axis), [](float v) { return logf(v); });
+      return zip(peak, lse, [](float l, float r) { return l + r; });
+    }
+    default: throw std::runtime_error("oracle: unsupported op " + std::to_string(n.op));
+  }
+}
+
+thread_local std::string g_error;
+
+}  // namespace
+
+extern "C" {
+
+const char* oracle_last_error(void) { return g_error.c_str(); }
+
+// Runs a compiled plan on the CPU (`Plan::forward`, engine/plan.rs:514-640).
+// params[slot] are host f32 arrays; feeds override Input payloads; the values of
+// `read_nodes` are written row-major into `outputs[i]`.
+int oracle_run(const tb_plan_desc* desc, const float* const* params, int32_t param_count,
+               int32_t feed_count, const tb_feed* feeds, int32_t read_count,
+               const int64_t* read_nodes, float* const* outputs) {
+  try {
+    const int64_t n = desc->node_count;
+    std::vector<Val> values(n);
+    std::vector<const tb_feed*> feed_of;
+    for (int32_t f = 0; f < feed_count; ++f) {
+      if ((int32_t)feed_of.size() <= feeds[f].slot) feed_of.resize(feeds[f].slot + 1, nullptr);
+      feed_of[feeds[f].slot] = &feeds[f];
+    }
+    // release bookkeeping of forward-only plans is irrelevant to values; the
+    // oracle keeps everything so any readable value can be read back.
+    for (int64_t i = 0; i < n; ++i) {
+      const tb_node& node = desc->nodes[i];
+      if (!node.wanted) continue;
+      switch (node.op) {
+        case TB_OP_LEAF: values[i] = source_payload(node, node.dense, node.indices); break;
+        case TB_OP_PARAMETER:
+          if (node.slot >= param_count) throw std::runtime_error("missing parameter slot");
+          values[i] = source_payload(node, params[node.slot], nullptr);
+          values[i].kind = TB_PAYLOAD_DENSE;
+          break;
+        case TB_OP_INPUT: {
+          const tb_feed* f =
+              node.slot < (int32_t)feed_of.size() ? feed_of[node.slot] : nullptr;
+          tb_node copy = node;
+          if (copy.payload == TB_PAYLOAD_NONE) copy.payload = TB_PAYLOAD_DENSE;
+          values[i] = source_payload(copy, f ? f->dense : node.dense,
+                                     f ? f->indices : node.indices);
+          break;
+        }
+        default: {
+          const Val* x = node.operands[0] >= 0 ? &values[node.operands[0]] : nullptr;
+          const Val* y = node.operands[1] >= 0 ? &values[node.operands[1]] : nullptr;
+          values[i] = forward(node, x, y);
+        }
+      }
+    }
+    for (int32_t r = 0; r < read_count; ++r) {
+      const Val& v = values[read_nodes[r]];
+      for (int64_t i = 0; i < v.volume(); ++i) outputs[r][i] = v.get(i);
+    }
+    return 0;
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return 1;
+  }
+}
+
+// The interpreter's serial-order GEMM alone (payload/gemm.rs:140-211) over
+// dense row-major operands: the CPU baseline of the GEMM configs.
+void oracle_gemm(const float* a, const float* b, float* c, int64_t m, int64_t k, int64_t n) {
+  for (int64_t r = 0; r < m; ++r) {
+    float* acc = c + r * n;
+    const float first = a[r * k];
+    for (int64_t j = 0; j < n; ++j) acc[j] = first * b[j];
+    for (int64_t s = 1; s < k; ++s) {
+      const float av = a[r * k + s];
+      const float* brow = b + s * n;
+      for (int64_t j = 0; j < n; ++j) acc[j] = acc[j] + av * brow[j];
+    }
+  }
+}
+
+// libm scalar maps of payload/elementary.rs:116-143, for ulp measurements.
+void oracle_map(int32_t op, const float* in, int64_t count, float* out) {
+  for (int64_t i = 0; i < count; ++i) {
+    float v = in[i];
+    switch (op) {
+      case TB_OP_EXP: out[i] = expf(v); break;
+      case TB_OP_LN: out[i] = logf(v); break;
+      case TB_OP_SQRT: out[i] = sqrtf(v); break;
+      case TB_OP_TANH: out[i] = tanhf(v); break;
+      default: out[i] = v;
+    }
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,130 @@
+// faces.cu -- the per-task offers of the backend seam (`Elementary::gemm` and
+// `Elementary::map`, payload/elementary.rs:74-95) for callers that are not
+// running a whole compiled plan.  Same contract as the reference cuda backend
+// (backend/cuda/kernels/gemm.rs:54-163, mod.rs:69-89): host slices in, an owned
+// row-major result out, "declined" for tasks below the size threshold.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+#include "../../include/topos_b200.h"
+#include "kernels.h"
+
+namespace {
+
+// Tasks with 2mnk below this many flops stay on the caller's path
+// (the reference's cuda backend threshold, backend/cuda/kernels/mod.rs:34).
+constexpr int64_t kMinFlops = int64_t(1) << 24;
+
+__device__ __forceinline__ float tf32_rna(float x) {
+  unsigned r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// Strided [rows, depth] operand -> K-major hi/lo [rows, kp].
+__global__ void k_prep_strided(const float* __restrict__ x, int64_t s_row, int64_t s_depth,
+                               int64_t rows, int64_t depth, int64_t kp, float* __restrict__ hi,
+                               float* __restrict__ lo) {
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < rows * kp;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = t / kp, k = t % kp;
+    const float v = k < depth ? x[r * s_row + k * s_depth] : 0.0f;
+    const float h = tf32_rna(v);
+    hi[t] = h;
+    lo[t] = __fsub_rn(v, h);
+  }
+}
+
+__global__ void k_map(int op, const float* __restrict__ in, float* __restrict__ out, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = in[i];
+    float r = v;
+    switch (op) {
+      case TB_OP_EXP: r = expf(v); break;
+      case TB_OP_LN: r = logf(v); break;
+      case TB_OP_SQRT: r = __fsqrt_rn(v); break;
+      case TB_OP_TANH: r = tanhf(v); break;
+    }
+    out[i] = r;
+  }
+}
+
+int64_t span_of(int64_t rows, int64_t cols, const int64_t s[2]) {
+  return (rows - 1) * s[0] + (cols - 1) * s[1] + 1;
+}
+
+}  // namespace
+
+extern "C" int tb_gemm_f32(const float* a, int64_t a_len, const int64_t a_strides[2],
+                           const float* b, int64_t b_len, const int64_t b_strides[2], int64_t m,
+                           int64_t k, int64_t n, float* out) {
+  char msg[8];
+  int s = tb_status(msg, sizeof msg);
+  if (s != TB_OK) return s;
+  if (m <= 1 || n <= 1 || 2 * m * n * k < kMinFlops) return TB_DECLINED;
+  if (a_strides[0] < 0 || a_strides[1] < 0 || b_strides[0] < 0 || b_strides[1] < 0)
+    return TB_DECLINED;
+  if (span_of(m, k, a_strides) > a_len || span_of(k, n, b_strides) > b_len) return TB_INVALID;
+  const int64_t kp = (k + 31) / 32 * 32;
+  float *da = nullptr, *db = nullptr, *dc = nullptr, *ws = nullptr;
+  const int64_t al = span_of(m, k, a_strides), bl = span_of(k, n, b_strides);
+  cudaStream_t st = nullptr;
+  int rc = TB_OK;
+  do {
+    if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) { rc = TB_RUNTIME; break; }
+    if (cudaMalloc(&da, al * 4) || cudaMalloc(&db, bl * 4) || cudaMalloc(&dc, m * n * 4) ||
+        cudaMalloc(&ws, (2 * m * kp + 2 * n * kp) * 4)) { rc = TB_RUNTIME; break; }
+    cudaMemcpyAsync(da, a, al * 4, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(db, b, bl * 4, cudaMemcpyHostToDevice, st);
+    float* ahi = ws;
+    float* alo = ahi + m * kp;
+    float* bhi = alo + m * kp;
+    float* blo = bhi + n * kp;
+    int grid = 148 * 4;
+    k_prep_strided<<<grid, 256, 0, st>>>(da, a_strides[0], a_strides[1], m, k, kp, ahi, alo);
+    // B^T as [n, k]: row j of B^T walks column j of B
+    k_prep_strided<<<grid, 256, 0, st>>>(db, b_strides[1], b_strides[0], n, k, kp, bhi, blo);
+    tb::launch_gemm(ahi, alo, bhi, blo, dc, 1, m, n, kp, st);
+    cudaMemcpyAsync(out, dc, m * n * 4, cudaMemcpyDeviceToHost, st);
+    if (cudaStreamSynchronize(st) != cudaSuccess) rc = TB_RUNTIME;
+  } while (false);
+  if (da) cudaFree(da);
+  if (db) cudaFree(db);
+  if (dc) cudaFree(dc);
+  if (ws) cudaFree(ws);
+  if (st) cudaStreamDestroy(st);
+  return rc;
+}
+
+extern "C" int tb_map_f32(int32_t op, const float* in, int64_t count, float* out) {
+  char msg[8];
+  int s = tb_status(msg, sizeof msg);
+  if (s != TB_OK) return s;
+  if (op != TB_OP_EXP && op != TB_OP_LN && op != TB_OP_SQRT && op != TB_OP_TANH)
+    return TB_DECLINED;
+  if (count < (1 << 17)) return TB_DECLINED;
+  float *d = nullptr;
+  if (cudaMalloc(&d, count * 8) != cudaSuccess) return TB_RUNTIME;
+  cudaMemcpy(d, in, count * 4, cudaMemcpyHostToDevice);
+  k_map<<<148 * 8, 256>>>(op, d, d + count, count);
+  cudaMemcpy(out, d + count, count * 4, cudaMemcpyDeviceToHost);
+  cudaError_t e = cudaGetLastError();
+  cudaFree(d);
+  return e == cudaSuccess ? TB_OK : TB_RUNTIME;
+}
+
+// ---- internal hooks for tests (not part of the public ABI)
+extern "C" void tbx_set_gemm_engine(int engine) { tb::set_gemm_engine(engine); }
+extern "C" int tbx_gemm_prepared(const float* a_hi, const float* a_lo, const float* b_hi,
+                                 const float* b_lo, float* c, int64_t batch, int64_t m, int64_t n,
+                                 int64_t kp, int engine) {
+  cudaStream_t st = 0;
+  if (engine == 1)
+    tb::launch_gemm_simt(a_hi, a_lo, b_hi, b_lo, c, batch, m, n, kp, st);
+  else if (!tb::launch_gemm_tcgen05(a_hi, a_lo, b_hi, b_lo, c, batch, m, n, kp, st))
+    return TB_DECLINED;
+  return cudaDeviceSynchronize() == cudaSuccess ? TB_OK : TB_RUNTIME;
+}

@@ -1,0 +1,313 @@
+// kernels.cu -- hand-written kernels that are not emitted per plan:
+// the stable selection sort behind deterministic scatter-add, the partial-sum
+// finalizer of fused column/full reductions, the SIMT GEMM path and the
+// multi-tensor optimizer steps.
+#include <cstdio>
+
+#include <algorithm>
+
+#include "kernels.h"
+
+namespace tb {
+namespace {
+
+constexpr int TILE = 1024;  // selection entries per warp tile
+
+__global__ void k_sort_init(const int* __restrict__ idx, int* __restrict__ keys,
+                            int* __restrict__ vals, int64_t count) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    keys[i] = idx[i];
+    vals[i] = (int)i;
+  }
+}
+
+// One warp per tile: digit histogram of the tile.
+__global__ void k_radix_count(const int* __restrict__ keys, int* __restrict__ counts,
+                              int64_t count, int shift, int64_t tiles) {
+  __shared__ int hist[256];
+  const int64_t tile = blockIdx.x;
+  for (int d = threadIdx.x; d < 256; d += 32) hist[d] = 0;
+  __syncwarp();
+  const int64_t begin = tile * TILE;
+  const int64_t end = (begin + TILE < count ? begin + TILE : count);
+  for (int64_t i = begin + threadIdx.x; i < end; i += 32)
+    atomicAdd(&hist[(keys[i] >> shift) & 255], 1);
+  __syncwarp();
+  for (int d = threadIdx.x; d < 256; d += 32) counts[(int64_t)d * tiles + tile] = hist[d];
+}
+
+// Exclusive scan of n ints by one block of 1024 threads.
+__global__ void k_scan(int* __restrict__ data, int64_t n) {
+  __shared__ int sums[1024];
+  const int t = threadIdx.x;
+  const int64_t per = (n + 1023) / 1024;
+  const int64_t begin = t * per;
+  const int64_t end = (begin + per < n ? begin + per : n);
+  int local = 0;
+  for (int64_t i = begin; i < end; ++i) local += data[i];
+  sums[t] = local;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {
+    int v = t >= off ? sums[t - off] : 0;
+    __syncthreads();
+    sums[t] += v;
+    __syncthreads();
+  }
+  int run = sums[t] - local;
+  for (int64_t i = begin; i < end; ++i) {
+    int v = data[i];
+    data[i] = run;
+    run += v;
+  }
+}
+
+// One warp per tile: stable scatter by digit.  Items are taken 32 at a time in
+// source order; lanes with equal digits are ranked by lane.
+__global__ void k_radix_scatter(const int* __restrict__ keys, const int* __restrict__ vals,
+                                int* __restrict__ keys_out, int* __restrict__ vals_out,
+                                const int* __restrict__ offsets, int64_t count, int shift,
+                                int64_t tiles) {
+  __shared__ int running[256];
+  const int64_t tile = blockIdx.x;
+  const int lane = threadIdx.x;
+  for (int d = lane; d < 256; d += 32) running[d] = offsets[(int64_t)d * tiles + tile];
+  __syncwarp();
+  const int64_t begin = tile * TILE;
+  const int64_t end = (begin + TILE < count ? begin + TILE : count);
+  for (int64_t base = begin; base < end; base += 32) {
+    const int64_t i = base + lane;
+    const bool valid = i < end;
+    const unsigned active = __ballot_sync(0xffffffffu, valid);
+    int key = 0, val = 0, digit = 256 + lane;  // invalid lanes get unique digits
+    if (valid) {
+      key = keys[i];
+      val = vals[i];
+      digit = (key >> shift) & 255;
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, digit) & active;
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    int pos = 0;
+    if (valid) pos = running[digit] + rank;
+    __syncwarp();
+    if (valid) {
+      keys_out[pos] = key;
+      vals_out[pos] = val;
+      const int leader = 31 - __clz(peers);
+      if (lane == leader) running[digit] += __popc(peers);
+    }
+    __syncwarp();
+  }
+}
+
+__global__ void k_segments(const int* __restrict__ keys, int* __restrict__ rstart,
+                           int* __restrict__ rend, int64_t count) {
+  for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < count;
+       p += (int64_t)gridDim.x * blockDim.x) {
+    const int k = keys[p];
+    if (p == 0 || keys[p - 1] != k) rstart[k] = (int)p;
+    if (p == count - 1 || keys[p + 1] != k) rend[k] = (int)(p + 1);
+  }
+}
+
+__global__ void k_final_sum(const float* __restrict__ part, float* __restrict__ out,
+                            int64_t blocks, int64_t width) {
+  for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < width;
+       j += (int64_t)gridDim.x * blockDim.x) {
+    float acc = part[j];
+    for (int64_t b = 1; b < blocks; ++b) acc = __fadd_rn(acc, part[b * width + j]);
+    out[j] = acc;
+  }
+}
+
+// SIMT GEMM over K-major prepared operands: 64x64 tiles, 4x4 per thread.
+// The operands are reassembled as hi + lo (exactly the original f32 values).
+__global__ void __launch_bounds__(256) k_gemm_simt(const float* __restrict__ ahi,
+                                                   const float* __restrict__ alo,
+                                                   const float* __restrict__ bhi,
+                                                   const float* __restrict__ blo,
+                                                   float* __restrict__ c, int64_t m, int64_t n,
+                                                   int64_t kp) {
+  __shared__ float As[16][68];
+  __shared__ float Bs[16][68];
+  const int64_t b = blockIdx.z;
+  const int64_t m0 = (int64_t)blockIdx.y * 64, n0 = (int64_t)blockIdx.x * 64;
+  const float* Ah = ahi + b * m * kp;
+  const float* Al = alo + b * m * kp;
+  const float* Bh = bhi + b * n * kp;
+  const float* Bl = blo + b * n * kp;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  float acc[4][4] = {};
+  const int lr = threadIdx.x >> 2;       // 0..63 row within tile
+  const int lk = (threadIdx.x & 3) * 4;  // 0,4,8,12
+  for (int64_t k0 = 0; k0 < kp; k0 += 16) {
+    {
+      const int64_t r = m0 + lr;
+      float4 h = make_float4(0, 0, 0, 0), l = h;
+      if (r < m) {
+        h = *(const float4*)(Ah + r * kp + k0 + lk);
+        l = *(const float4*)(Al + r * kp + k0 + lk);
+      }
+      As[lk + 0][lr] = h.x + l.x;
+      As[lk + 1][lr] = h.y + l.y;
+      As[lk + 2][lr] = h.z + l.z;
+      As[lk + 3][lr] = h.w + l.w;
+    }
+    {
+      const int64_t r = n0 + lr;
+      float4 h = make_float4(0, 0, 0, 0), l = h;
+      if (r < n) {
+        h = *(const float4*)(Bh + r * kp + k0 + lk);
+        l = *(const float4*)(Bl + r * kp + k0 + lk);
+      }
+      Bs[lk + 0][lr] = h.x + l.x;
+      Bs[lk + 1][lr] = h.y + l.y;
+      Bs[lk + 2][lr] = h.z + l.z;
+      Bs[lk + 3][lr] = h.w + l.w;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float av[4], bv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) av[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) bv[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+  float* C = c + b * m * n;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t r = m0 + ty * 4 + i;
+    if (r >= m) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t col = n0 + tx * 4 + j;
+      if (col < n) C[r * n + col] = acc[i][j];
+    }
+  }
+}
+
+__global__ void k_adam_scalars(float* s, float beta1, float beta2) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    s[0] = __fmul_rn(s[0], beta1);
+    s[1] = __fmul_rn(s[1], beta2);
+    s[2] = __fsub_rn(1.0f, s[0]);
+    s[3] = __fsub_rn(1.0f, s[1]);
+  }
+}
+
+// Multi-tensor optimizer step; op order follows neural/optimizer.rs:40-51 (SGD)
+// and neural/adam.rs:62-85, 137-157 (Adam, AdamW).
+__global__ void k_optimizer(const OptEntry* __restrict__ entries, int count, int64_t total,
+                            const float* __restrict__ s, const float* __restrict__ lr_ptr,
+                            int kind, float beta1, float beta2, float share1, float share2,
+                            float eps, float decay, float gscale) {
+  const float lr = *lr_ptr;
+  const float c1 = kind ? s[2] : 0.0f, c2 = kind ? s[3] : 0.0f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int lo = 0, hi = count - 1;
+    while (lo < hi) {
+      int mid = (lo + hi + 1) >> 1;
+      if (entries[mid].start <= i) lo = mid; else hi = mid - 1;
+    }
+    const OptEntry& e = entries[lo];
+    const int64_t j = i - e.start;
+    float g = e.g[j];
+    if (gscale != 1.0f) g = __fmul_rn(g, gscale);
+    const float p = e.p[j];
+    if (kind == 0) {
+      e.p[j] = __fsub_rn(p, __fmul_rn(g, lr));
+      continue;
+    }
+    const float first = __fadd_rn(__fmul_rn(e.m[j], beta1), __fmul_rn(g, share1));
+    const float second = __fadd_rn(__fmul_rn(e.v[j], beta2), __fmul_rn(__fmul_rn(g, g), share2));
+    e.m[j] = first;
+    e.v[j] = second;
+    const float cf = __fdiv_rn(first, c1);
+    const float cs = __fdiv_rn(second, c2);
+    const float d = __fdiv_rn(cf, __fadd_rn(__fsqrt_rn(cs), eps));
+    const float stepped = __fsub_rn(p, __fmul_rn(d, lr));
+    if (kind == 2 && e.decay) {
+      e.p[j] = __fsub_rn(stepped, __fmul_rn(__fmul_rn(p, decay), lr));
+    } else {
+      e.p[j] = stepped;
+    }
+  }
+}
+
+int g_engine = 0;
+
+}  // namespace
+
+void set_gemm_engine(int engine) { g_engine = engine; }
+int gemm_engine() { return g_engine; }
+
+void launch_selection_sort(const int* indices, int* keys, int* vals, int* tmp_keys,
+                           int* tmp_vals, int* counts, int* rstart, int* rend, int64_t count,
+                           int64_t rows, int passes, int64_t tiles, cudaStream_t stream) {
+  int grid = (int)std::min<int64_t>((count + 255) / 256, 148 * 8);
+  k_sort_init<<<grid, 256, 0, stream>>>(indices, keys, vals, count);
+  int* src_k = keys;
+  int* src_v = vals;
+  int* dst_k = tmp_keys;
+  int* dst_v = tmp_vals;
+  for (int p = 0; p < passes; ++p) {
+    const int shift = 8 * p;
+    k_radix_count<<<(unsigned)tiles, 32, 0, stream>>>(src_k, counts, count, shift, tiles);
+    k_scan<<<1, 1024, 0, stream>>>(counts, 256 * tiles);
+    k_radix_scatter<<<(unsigned)tiles, 32, 0, stream>>>(src_k, src_v, dst_k, dst_v, counts,
+                                                        count, shift, tiles);
+    std::swap(src_k, dst_k);
+    std::swap(src_v, dst_v);
+  }
+  if (src_k != keys) {
+    cudaMemcpyAsync(keys, src_k, count * 4, cudaMemcpyDeviceToDevice, stream);
+    cudaMemcpyAsync(vals, src_v, count * 4, cudaMemcpyDeviceToDevice, stream);
+  }
+  cudaMemsetAsync(rstart, 0, rows * 4, stream);
+  cudaMemsetAsync(rend, 0, rows * 4, stream);
+  k_segments<<<grid, 256, 0, stream>>>(keys, rstart, rend, count);
+}
+
+void launch_final_sum(const float* part, float* out, int64_t blocks, int64_t width,
+                      cudaStream_t stream) {
+  int grid = (int)std::max<int64_t>(1, std::min<int64_t>((width + 255) / 256, 148 * 4));
+  k_final_sum<<<grid, 256, 0, stream>>>(part, out, blocks, width);
+}
+
+void launch_gemm_simt(const float* a_hi, const float* a_lo, const float* b_hi,
+                      const float* b_lo, float* c, int64_t batch, int64_t m, int64_t n,
+                      int64_t kp, cudaStream_t stream) {
+  dim3 grid((unsigned)((n + 63) / 64), (unsigned)((m + 63) / 64), (unsigned)batch);
+  k_gemm_simt<<<grid, 256, 0, stream>>>(a_hi, a_lo, b_hi, b_lo, c, m, n, kp);
+}
+
+void launch_gemm(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
+                 float* c, int64_t batch, int64_t m, int64_t n, int64_t kp,
+                 cudaStream_t stream) {
+  if (g_engine != 1 &&
+      launch_gemm_tcgen05(a_hi, a_lo, b_hi, b_lo, c, batch, m, n, kp, stream))
+    return;
+  launch_gemm_simt(a_hi, a_lo, b_hi, b_lo, c, batch, m, n, kp, stream);
+}
+
+void launch_adam_scalars(float* s, float beta1, float beta2, cudaStream_t stream) {
+  k_adam_scalars<<<1, 32, 0, stream>>>(s, beta1, beta2);
+}
+
+void launch_optimizer(const OptEntry* entries, int count, int64_t total, const float* scalars,
+                      const float* lr, int kind, float beta1, float beta2, float share1,
+                      float share2, float eps, float decay, float gscale, cudaStream_t stream) {
+  int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 148 * 8));
+  k_optimizer<<<grid, 256, 0, stream>>>(entries, count, total, scalars, lr, kind, beta1, beta2,
+                                       share1, share2, eps, decay, gscale);
+}
+
+}  // namespace tb

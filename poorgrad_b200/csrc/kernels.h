@@ -1,0 +1,53 @@
+// kernels.h -- host launchers of the hand-written (non-emitted) kernels.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace tb {
+
+// Stable sort of selection indices by target row, then per-row segments
+// [rstart[r], rend[r]) of source positions in ascending source order.
+void launch_selection_sort(const int* indices, int* keys, int* vals, int* tmp_keys,
+                           int* tmp_vals, int* counts, int* rstart, int* rend, int64_t count,
+                           int64_t rows, int passes, int64_t tiles, cudaStream_t stream);
+
+// out[j] = part[0][j] + part[1][j] + ... (ascending block order).
+void launch_final_sum(const float* part, float* out, int64_t blocks, int64_t width,
+                      cudaStream_t stream);
+
+// C[b] = (Ahi+Alo)[b] . (Bhi+Blo)[b]^T over K-major prepared operands;
+// the tcgen05 path when available, else a SIMT path.
+void launch_gemm(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
+                 float* c, int64_t batch, int64_t m, int64_t n, int64_t kp,
+                 cudaStream_t stream);
+// The SIMT path alone (tests compare the two).
+void launch_gemm_simt(const float* a_hi, const float* a_lo, const float* b_hi,
+                      const float* b_lo, float* c, int64_t batch, int64_t m, int64_t n,
+                      int64_t kp, cudaStream_t stream);
+// The tcgen05 path alone; returns false when the shape is not served.
+bool launch_gemm_tcgen05(const float* a_hi, const float* a_lo, const float* b_hi,
+                         const float* b_lo, float* c, int64_t batch, int64_t m, int64_t n,
+                         int64_t kp, cudaStream_t stream);
+// Selects the GEMM engine: 0 = automatic, 1 = SIMT only, 2 = tcgen05 only.
+void set_gemm_engine(int engine);
+int gemm_engine();
+
+struct OptEntry {
+  float* p;
+  const float* g;
+  float* m;
+  float* v;
+  int64_t count;
+  int64_t start;
+  int32_t decay;
+  int32_t pad;
+};
+
+// Per-step optimizer scalars: s[0]=beta1^t, s[1]=beta2^t, s[2]=1-beta1^t, s[3]=1-beta2^t.
+void launch_adam_scalars(float* s, float beta1, float beta2, cudaStream_t stream);
+// One multi-tensor step over all entries (kind: 0 SGD, 1 Adam, 2 AdamW).
+void launch_optimizer(const OptEntry* entries, int count, int64_t total, const float* scalars,
+                      const float* lr, int kind, float beta1, float beta2, float share1,
+                      float share2, float eps, float decay, float gscale, cudaStream_t stream);
+
+}  // namespace tb

@@ -1,0 +1,1850 @@
+// lower.cpp -- plan columns -> device program (value kinds, fusion groups,
+// emitted kernel sources, buffer liveness and the arena layout).
+//
+// The node semantics restated here are those of topos's Function rules and
+// Tensor arithmetic (function/*.rs `forward`, payload/tensor.rs); the device
+// arithmetic uses IEEE round-to-nearest intrinsics without contraction so that
+// every elementwise group without a transcendental reproduces the interpreter
+// bit for bit.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <sstream>
+#include <stdexcept>
+#include <unordered_map>
+
+#include "engine.h"
+
+namespace tb {
+namespace {
+
+[[noreturn]] void fail(const std::string& m) { throw std::runtime_error(m); }
+
+bool is_elementwise(int op) {
+  switch (op) {
+    case TB_OP_ADD: case TB_OP_SUB: case TB_OP_MUL: case TB_OP_DIV: case TB_OP_NEG:
+    case TB_OP_TANH: case TB_OP_EXP: case TB_OP_LN: case TB_OP_SQRT: case TB_OP_POWF:
+    case TB_OP_MAXIMUM: case TB_OP_RELU: case TB_OP_STEP:
+      return true;
+    default:
+      return false;
+  }
+}
+
+bool is_view(int op) {
+  switch (op) {
+    case TB_OP_TRANSPOSE: case TB_OP_BROADCAST: case TB_OP_BROADCAST_ALONG:
+    case TB_OP_RESHAPE: case TB_OP_PERMUTE: case TB_OP_NARROW: case TB_OP_UNFOLD:
+      return true;
+    default:
+      return false;
+  }
+}
+
+bool is_transcendental(int op) {
+  return op == TB_OP_TANH || op == TB_OP_EXP || op == TB_OP_LN || op == TB_OP_POWF;
+}
+
+// `f32::max` (payload/elementary.rs:137-139); ties keep the first argument.
+float fmax_ref(float a, float b) {
+  if (std::isnan(a)) return b;
+  if (std::isnan(b)) return a;
+  return (b > a) ? b : a;
+}
+
+// Host evaluation of one elementwise op on constants: the same IEEE f32
+// operations (this file is compiled without contraction) and the host libm.
+float fold_scalar(int op, float a, float b) {
+  switch (op) {
+    case TB_OP_ADD: return a + b;
+    case TB_OP_SUB: return a - b;
+    case TB_OP_MUL: return a * b;
+    case TB_OP_DIV: return a / b;
+    case TB_OP_NEG: return -a;
+    case TB_OP_TANH: return tanhf(a);
+    case TB_OP_EXP: return expf(a);
+    case TB_OP_LN: return logf(a);
+    case TB_OP_SQRT: return sqrtf(a);
+    case TB_OP_POWF: return powf(a, b);
+    case TB_OP_MAXIMUM: return fmax_ref(a, b);
+    case TB_OP_RELU: return fmax_ref(a, 0.0f);
+    case TB_OP_STEP: return a >= b ? 1.0f : 0.0f;
+  }
+  fail("fold_scalar: not elementwise");
+}
+
+Layout contiguous(const Node& n) {
+  Layout l;
+  l.rank = n.rank;
+  int64_t s = 1;
+  for (int i = n.rank - 1; i >= 0; --i) {
+    l.shape[i] = n.shape[i];
+    l.stride[i] = s;
+    s *= n.shape[i];
+  }
+  return l;
+}
+
+// View-compatible strides for a reshape (the chunk-matching rule used by
+// strided tensor libraries); false when the reshape needs a copy.
+bool reshape_strides(const Layout& in, const Node& out, Layout& res) {
+  res = Layout();
+  res.rank = out.rank;
+  res.offset = in.offset;
+  for (int i = 0; i < out.rank; ++i) res.shape[i] = out.shape[i];
+  if (in.rank == 0) {
+    for (int i = 0; i < out.rank; ++i) res.stride[i] = 0;
+    return true;
+  }
+  int view_d = out.rank - 1;
+  int64_t chunk_base_stride = in.stride[in.rank - 1];
+  int64_t tensor_numel = 1, view_numel = 1;
+  for (int tensor_d = in.rank - 1; tensor_d >= 0; --tensor_d) {
+    tensor_numel *= in.shape[tensor_d];
+    if (tensor_d == 0 || (in.shape[tensor_d - 1] != 1 &&
+                          in.stride[tensor_d - 1] != tensor_numel * chunk_base_stride)) {
+      while (view_d >= 0 && (view_numel < tensor_numel || out.shape[view_d] == 1)) {
+        res.stride[view_d] = view_numel * chunk_base_stride;
+        view_numel *= out.shape[view_d];
+        --view_d;
+      }
+      if (view_numel != tensor_numel) return false;
+      if (tensor_d > 0) {
+        chunk_base_stride = in.stride[tensor_d - 1];
+        tensor_numel = 1;
+        view_numel = 1;
+      }
+    }
+  }
+  return view_d == -1;
+}
+
+// The layout of view node `n` over its operand's layout `in`.
+bool view_layout(const Node& n, const Node& operand, const Layout& in, Layout& out) {
+  const int64_t* at = n.attrs;
+  out = in;
+  switch (n.op) {
+    case TB_OP_TRANSPOSE:
+      if (in.rank == 2) {
+        std::swap(out.shape[0], out.shape[1]);
+        std::swap(out.stride[0], out.stride[1]);
+      }
+      return true;
+    case TB_OP_PERMUTE:
+      for (int j = 0; j < n.rank; ++j) {
+        out.shape[j] = in.shape[at[j]];
+        out.stride[j] = in.stride[at[j]];
+      }
+      return true;
+    case TB_OP_NARROW:
+      out.offset = in.offset + at[1] * in.stride[at[0]];
+      out.shape[at[0]] = at[2];
+      return true;
+    case TB_OP_BROADCAST_ALONG: {
+      int axis = (int)at[0];
+      out.rank = n.rank;
+      for (int j = 0, s = 0; j < n.rank; ++j) {
+        if (j == axis) {
+          out.shape[j] = n.shape[j];
+          out.stride[j] = 0;
+        } else {
+          out.shape[j] = in.shape[s];
+          out.stride[j] = in.stride[s];
+          ++s;
+        }
+      }
+      return true;
+    }
+    case TB_OP_BROADCAST: {
+      out.rank = n.rank;
+      for (int j = 0; j < n.rank; ++j) {
+        out.shape[j] = n.shape[j];
+        out.stride[j] = 0;
+      }
+      return true;
+    }
+    case TB_OP_RESHAPE:
+      return reshape_strides(in, n, out);
+    case TB_OP_UNFOLD: {
+      int axis = (int)at[0];
+      out.rank = n.rank;
+      for (int j = 0, s = 0; j < n.rank; ++j) {
+        if (j == axis) {
+          out.shape[j] = n.shape[j];
+          out.stride[j] = in.stride[s] * at[2];
+        } else if (j == axis + 1) {
+          out.shape[j] = n.shape[j];
+          out.stride[j] = in.stride[s] * at[3];
+          ++s;
+        } else {
+          out.shape[j] = in.shape[s];
+          out.stride[j] = in.stride[s];
+          ++s;
+        }
+      }
+      (void)operand;
+      return true;
+    }
+  }
+  return false;
+}
+
+// ------------------------------------------------------------ index strings
+bool numeric(const std::string& s, int64_t& v) {
+  if (s.empty()) return false;
+  char* end = nullptr;
+  long long x = strtoll(s.c_str(), &end, 10);
+  if (*end) return false;
+  v = x;
+  return true;
+}
+std::string lit(int64_t v) {
+  std::string s = std::to_string(v);
+  if (v > 2147483647LL || v < -2147483647LL) s += "LL";
+  return s;
+}
+std::string s_add(const std::string& a, const std::string& b) {
+  int64_t x, y;
+  bool na = numeric(a, x), nb = numeric(b, y);
+  if (na && nb) return lit(x + y);
+  if (na && x == 0) return b;
+  if (nb && y == 0) return a;
+  return "(" + a + "+" + b + ")";
+}
+std::string s_mul(const std::string& a, int64_t k) {
+  int64_t x;
+  if (k == 0) return "0";
+  if (k == 1) return a;
+  if (numeric(a, x)) return lit(x * k);
+  return "(" + a + "*" + lit(k) + ")";
+}
+std::string s_div(const std::string& a, int64_t k) {
+  int64_t x;
+  if (k == 1) return a;
+  if (numeric(a, x)) return lit(x / k);
+  return "(" + a + "/" + lit(k) + ")";
+}
+std::string s_mod(const std::string& a, int64_t k) {
+  int64_t x;
+  if (k == 1) return "0";
+  if (numeric(a, x)) return lit(x % k);
+  return "(" + a + "%" + lit(k) + ")";
+}
+std::string flit(float f) {
+  uint32_t bits;
+  memcpy(&bits, &f, 4);
+  char buf[40];
+  snprintf(buf, sizeof buf, "__int_as_float(0x%08x)", bits);
+  return buf;
+}
+
+struct Idx {
+  std::vector<std::string> c;
+  int lane = -1;          // c.back() == lbase + lane
+  std::string lbase;
+};
+
+}  // namespace
+
+// ============================================================== lowering
+class Lowerer {
+ public:
+  Program& P;
+  explicit Lowerer(Program& p) : P(p) {}
+
+  int add_node(const Node& n) {
+    P.nodes.push_back(n);
+    P.info.emplace_back();
+    return (int)P.nodes.size() - 1;
+  }
+
+  int resolve(int n) const {
+    while (n >= 0 && P.info[n].alias >= 0) n = P.info[n].alias;
+    return n;
+  }
+
+  int new_buffer(Storage s, int64_t bytes, int node, int slot = -1) {
+    Buffer b;
+    b.storage = s;
+    b.bytes = bytes;
+    b.node = node;
+    b.slot = slot;
+    P.buffers.push_back(b);
+    return (int)P.buffers.size() - 1;
+  }
+
+  // ---- pass 1: load columns, expand LogSumExp / LogSoftmax into primitives
+  void load(const tb_plan_desc* d) {
+    const int64_t count = d->node_count;
+    P.nodes.reserve(count * 2);
+    for (int64_t i = 0; i < count; ++i) {
+      const tb_node& s = d->nodes[i];
+      Node n;
+      n.op = s.op;
+      n.rank = s.rank;
+      if (s.rank < 0 || s.rank > TB_MAX_RANK) fail("node rank out of range");
+      for (int k = 0; k < s.rank; ++k) n.shape[k] = s.shape[k];
+      for (int k = 0; k < TB_MAX_RANK; ++k) n.attrs[k] = s.attrs[k];
+      n.operands[0] = s.operands[0];
+      n.operands[1] = s.operands[1];
+      n.slot = s.slot;
+      n.payload = s.payload;
+      n.constant = s.constant;
+      n.vocab = s.vocab;
+      n.dense = s.dense;
+      n.indices = s.indices;
+      n.wanted = s.wanted;
+      n.readable = s.readable;
+      for (int k = 0; k < 2; ++k)
+        if (n.operands[k] >= i) fail("operand links must point backwards");
+      P.nodes.push_back(n);
+      P.info.emplace_back();
+      if (n.op == TB_OP_PARAMETER) {
+        P.parameter_slots = std::max(P.parameter_slots, n.slot + 1);
+        if ((int)P.parameter_shapes.size() <= n.slot) P.parameter_shapes.resize(n.slot + 1);
+        P.parameter_shapes[n.slot] = n.dims();
+      }
+      if (n.op == TB_OP_INPUT) P.input_slots = std::max(P.input_slots, n.slot + 1);
+    }
+    P.input_buffer.assign(P.input_slots, -1);
+    P.input_node.assign(P.input_slots, -1);
+    for (int64_t i = 0; i < count; ++i) {
+      Node& n = P.nodes[i];
+      for (int k = 0; k < 2; ++k)
+        if (n.operands[k] >= 0) n.operands[k] = resolve(n.operands[k]);
+      if (n.op == TB_OP_INPUT) P.input_node[n.slot] = (int)i;
+      if (!n.wanted) continue;
+      if (n.op == TB_OP_LOG_SUM_EXP || n.op == TB_OP_LOG_SOFTMAX) {
+        expand_log_domain((int)i);
+      } else {
+        P.order.push_back((int)i);
+      }
+    }
+  }
+
+  // function/log_sum_exp.rs:53-63 and function/log_softmax.rs:51-65 as
+  // primitive nodes: peak, shifted, exp, row sum, ln, and the combination.
+  void expand_log_domain(int i) {
+    Node src = P.nodes[i];
+    int x = src.operands[0];
+    int axis = (int)src.attrs[0];
+    const Node xn = P.nodes[x];
+    auto mk = [&](int op, int a, int b, const Node& shape_of, bool drop_axis) {
+      Node n;
+      n.op = op;
+      n.operands[0] = a;
+      n.operands[1] = b;
+      n.wanted = true;
+      n.attrs[0] = axis;
+      n.rank = 0;
+      for (int k = 0; k < shape_of.rank; ++k)
+        if (!(drop_axis && k == axis)) n.shape[n.rank++] = shape_of.shape[k];
+      int id = add_node(n);
+      P.order.push_back(id);
+      return id;
+    };
+    int peak = mk(TB_OP_MAX_ALONG, x, -1, xn, true);
+    int peak_b = mk(TB_OP_BROADCAST_ALONG, peak, x, xn, false);
+    int shifted = mk(TB_OP_SUB, x, peak_b, xn, false);
+    int e = mk(TB_OP_EXP, shifted, -1, xn, false);
+    int total = mk(TB_OP_SUM_ALONG, e, -1, xn, true);
+    int normalizer = mk(TB_OP_LN, total, -1, P.nodes[total], false);
+    int out;
+    if (src.op == TB_OP_LOG_SUM_EXP) {
+      out = mk(TB_OP_ADD, peak, normalizer, P.nodes[peak], false);
+    } else {
+      int nb = mk(TB_OP_BROADCAST_ALONG, normalizer, shifted, xn, false);
+      out = mk(TB_OP_SUB, shifted, nb, xn, false);
+    }
+    P.nodes[out].readable = src.readable;
+    P.info[i].alias = out;
+  }
+
+  // ---- pass 2: consumer counts
+  void count_consumers() {
+    for (int n : P.order) {
+      const Node& nd = P.nodes[n];
+      if (nd.op == TB_OP_LEAF || nd.op == TB_OP_PARAMETER || nd.op == TB_OP_INPUT) continue;
+      int a = nd.operands[0], b = nd.operands[1];
+      if (nd.op == TB_OP_BROADCAST || nd.op == TB_OP_BROADCAST_ALONG) b = -1;
+      if (a >= 0) P.info[a].consumers++;
+      if (b >= 0 && b != a) P.info[b].consumers++;
+    }
+  }
+
+  bool source_layout(int n) const {
+    const Node& nd = P.nodes[n];
+    return nd.op == TB_OP_LEAF || nd.op == TB_OP_PARAMETER || nd.op == TB_OP_INPUT;
+  }
+
+  void materialize(int n) {
+    Info& f = P.info[n];
+    f.materialized = true;
+    if (f.kind == Kind::None) f.kind = Kind::Expr;
+    f.buf = new_buffer(Storage::Arena, P.nodes[n].volume() * 4, n);
+    f.lay = contiguous(P.nodes[n]);
+    f.owner = n;
+    f.heavy.clear();
+    f.ops = 0;
+  }
+
+  // ---- pass 3: kinds, constant folding, view folding, materialization
+  void classify() {
+    for (int n : P.order) {
+      Node& nd = P.nodes[n];
+      Info& f = P.info[n];
+      const int a = nd.operands[0], b = nd.operands[1];
+      switch (nd.op) {
+        case TB_OP_LEAF:
+          if (nd.payload == TB_PAYLOAD_CONSTANT) {
+            f.kind = Kind::Const;
+            f.c = nd.constant;
+          } else if (nd.payload == TB_PAYLOAD_SELECTION) {
+            f.kind = Kind::Sel;
+            f.one = nd.constant;
+            f.buf = new_buffer(Storage::LeafIndices, nd.shape[0] * 4, n);
+          } else if (nd.payload == TB_PAYLOAD_DENSE) {
+            f.kind = Kind::Layout;
+            f.buf = new_buffer(Storage::Leaf, nd.volume() * 4, n);
+            f.lay = contiguous(nd);
+            f.owner = n;
+          } else {
+            fail("leaf without payload");
+          }
+          break;
+        case TB_OP_PARAMETER:
+          f.kind = Kind::Layout;
+          f.buf = new_buffer(Storage::Parameter, nd.volume() * 4, n, nd.slot);
+          f.lay = contiguous(nd);
+          f.owner = n;
+          break;
+        case TB_OP_INPUT:
+          if (nd.payload == TB_PAYLOAD_SELECTION) {
+            f.kind = Kind::Sel;
+            f.one = nd.constant;
+            f.buf = new_buffer(Storage::InputIndices, nd.shape[0] * 4, n, nd.slot);
+          } else {
+            f.kind = Kind::Layout;
+            f.buf = new_buffer(Storage::Input, nd.volume() * 4, n, nd.slot);
+            f.lay = contiguous(nd);
+            f.owner = n;
+          }
+          P.input_buffer[nd.slot] = f.buf;
+          break;
+        default:
+          classify_computed(n, a, b);
+      }
+      if (nd.readable && !f.materialized && f.kind != Kind::Sel) materialize(n);
+    }
+  }
+
+  void classify_computed(int n, int a, int b) {
+    Node& nd = P.nodes[n];
+    Info& f = P.info[n];
+    const Info* fa = a >= 0 ? &P.info[a] : nullptr;
+    const Info* fb = b >= 0 ? &P.info[b] : nullptr;
+    if (is_elementwise(nd.op)) {
+      bool binary = nd.op == TB_OP_ADD || nd.op == TB_OP_SUB || nd.op == TB_OP_MUL ||
+                    nd.op == TB_OP_DIV || nd.op == TB_OP_POWF || nd.op == TB_OP_MAXIMUM ||
+                    nd.op == TB_OP_STEP;
+      if (fa->kind == Kind::Const && (!binary || fb->kind == Kind::Const)) {
+        f.kind = Kind::Const;
+        f.c = fold_scalar(nd.op, fa->c, binary ? fb->c : 0.0f);
+        return;
+      }
+      expression(n);
+      return;
+    }
+    if (is_view(nd.op)) {
+      if (fa->kind == Kind::Const) {
+        f.kind = Kind::Const;
+        f.c = fa->c;
+        return;
+      }
+      if (fa->kind == Kind::Layout || fa->materialized) {
+        Layout l;
+        if (view_layout(nd, P.nodes[a], fa->lay, l)) {
+          f.kind = Kind::Layout;
+          f.lay = l;
+          f.buf = fa->buf;
+          f.owner = fa->owner;
+          return;
+        }
+      }
+      expression(n);
+      return;
+    }
+    switch (nd.op) {
+      case TB_OP_PAD:
+        expression(n);
+        return;
+      case TB_OP_GATHER:
+        if (fb->kind != Kind::Sel) fail("gather needs a selection operand");
+        if (fa->kind == Kind::Const) {
+          f.kind = Kind::Const;
+          f.c = fa->c;
+          return;
+        }
+        expression(n);
+        return;
+      case TB_OP_SUM:
+      case TB_OP_SUM_ALONG:
+      case TB_OP_MAX_ALONG:
+        if (fa->kind == Kind::Const) {
+          // a serial left fold of identical values (payload/tensor.rs:1055-1124)
+          int64_t extent = nd.op == TB_OP_SUM ? P.nodes[a].volume()
+                                              : P.nodes[a].shape[nd.attrs[0]];
+          float acc = fa->c;
+          for (int64_t s = 1; s < extent; ++s)
+            acc = nd.op == TB_OP_MAX_ALONG ? fmax_ref(acc, fa->c) : acc + fa->c;
+          f.kind = Kind::Const;
+          f.c = acc;
+          return;
+        }
+        f.kind = Kind::Expr;
+        materialize(n);
+        return;
+      case TB_OP_MATMUL:
+      case TB_OP_SCATTER:
+      case TB_OP_FOLD:
+        if (nd.op == TB_OP_SCATTER && fb->kind != Kind::Sel) fail("scatter needs a selection operand");
+        f.kind = Kind::Expr;
+        materialize(n);
+        return;
+      default:
+        fail("unsupported op " + std::to_string(nd.op));
+    }
+  }
+
+  // A computed elementwise or index-mapping value: recomputed by each consumer
+  // unless it is shared and reads several large buffers, or grows too large.
+  void expression(int n) {
+    Node& nd = P.nodes[n];
+    Info& f = P.info[n];
+    f.kind = Kind::Expr;
+    f.ops = 1;
+    std::vector<int> heavy;
+    const int64_t vol = nd.volume();
+    for (int k = 0; k < 2; ++k) {
+      int o = nd.operands[k];
+      if (o < 0) continue;
+      if (nd.op == TB_OP_GATHER && k == 1) continue;
+      if ((nd.op == TB_OP_BROADCAST || nd.op == TB_OP_BROADCAST_ALONG) && k == 1) continue;
+      const Info& fo = P.info[o];
+      if (fo.materialized || fo.kind == Kind::Layout) {
+        if (P.buffers[fo.buf].bytes / 4 * 4 >= vol) heavy.push_back(fo.buf);
+      } else if (fo.kind == Kind::Expr) {
+        f.ops += fo.ops;
+        heavy.insert(heavy.end(), fo.heavy.begin(), fo.heavy.end());
+      }
+    }
+    std::sort(heavy.begin(), heavy.end());
+    heavy.erase(std::unique(heavy.begin(), heavy.end()), heavy.end());
+    if (heavy.size() > 4) heavy.resize(4);
+    f.heavy = heavy;
+    if ((f.consumers >= 2 && heavy.size() >= 2) || f.ops > 40) materialize(n);
+  }
+
+  // ---- pass 4: fusion groups
+  enum Ctx { ID = 0, ROWB = 1, OTHER = 2 };
+  struct Group {
+    std::vector<int64_t> space;
+    std::vector<Member> members;
+    std::map<int, int> index;  // node -> member position
+    std::set<int> after;       // open groups that must be emitted first
+    bool open = true;
+  };
+  std::vector<Group> groups;
+  std::map<std::vector<int64_t>, int> open_group;
+  std::vector<int> group_of;  // node -> group id
+
+  void walk(int n, int ctx, std::set<std::pair<int, int>>& seen,
+            std::vector<std::pair<int, int>>& out, bool is_root) {
+    if (!seen.insert({n, ctx}).second) return;
+    const Info& f = P.info[n];
+    if (!is_root) {
+      if (f.materialized) {
+        out.push_back({n, ctx});
+        return;
+      }
+      if (f.kind == Kind::Const || f.kind == Kind::Sel) return;
+      if (f.kind == Kind::Layout && source_layout(n)) return;
+    }
+    const Node& nd = P.nodes[n];
+    if (source_layout(n)) return;
+    if (is_elementwise(nd.op)) {
+      for (int k = 0; k < 2; ++k)
+        if (nd.operands[k] >= 0) walk(nd.operands[k], ctx, seen, out, false);
+      return;
+    }
+    if (nd.op == TB_OP_BROADCAST_ALONG) {
+      int c = (ctx == ID && nd.attrs[0] == nd.rank - 1) ? ROWB : OTHER;
+      walk(nd.operands[0], c, seen, out, false);
+      return;
+    }
+    if (nd.op == TB_OP_SUM || nd.op == TB_OP_SUM_ALONG || nd.op == TB_OP_MAX_ALONG) {
+      walk(nd.operands[0], ID, seen, out, false);  // the reduction's input space
+      return;
+    }
+    if (nd.op == TB_OP_GATHER) {
+      walk(nd.operands[0], OTHER, seen, out, false);
+      return;
+    }
+    for (int k = 0; k < 2; ++k) {
+      if (nd.operands[k] < 0) continue;
+      if ((nd.op == TB_OP_BROADCAST || nd.op == TB_OP_BROADCAST_ALONG) && k == 1) continue;
+      walk(nd.operands[k], OTHER, seen, out, false);
+    }
+  }
+
+  std::vector<std::pair<int, int>> refs(int n) {
+    std::set<std::pair<int, int>> seen;
+    std::vector<std::pair<int, int>> out;
+    walk(n, ID, seen, out, true);
+    return out;
+  }
+
+  // whether open group `b` must run after open group `a` (transitively)
+  bool runs_after(int b, int a) {
+    std::vector<int> stack{b};
+    std::set<int> seen;
+    while (!stack.empty()) {
+      int x = stack.back();
+      stack.pop_back();
+      if (x == a) return true;
+      if (!seen.insert(x).second) continue;
+      for (int y : groups[x].after)
+        if (groups[y].open) stack.push_back(y);
+    }
+    return false;
+  }
+
+  void flush(int g) {
+    Group& G0 = groups[g];
+    if (!G0.open) return;
+    G0.open = false;
+    std::set<int> deps = G0.after;
+    for (int d : deps) flush(d);
+    Group& G = groups[g];
+    open_group.erase(G.space);
+    Kernel k;
+    bool reductions = false;
+    for (auto& m : G.members)
+      if (m.type != MemberType::EW) reductions = true;
+    k.type = reductions ? KType::ROW : KType::EW;
+    k.members = G.members;
+    k.space = G.space;
+    P.kernels.push_back(k);
+  }
+
+  void flush_refs(const std::vector<std::pair<int, int>>& r) {
+    for (auto& [node, ctx] : r) {
+      int g = group_of[node];
+      if (g >= 0 && groups[g].open) flush(g);
+    }
+  }
+
+  int row_vec(const std::vector<int64_t>& space) const {
+    if (space.empty()) return 1;
+    return space.back() % 4 == 0 ? 4 : 1;
+  }
+
+  // threads per row and chunks per thread of a row-space kernel
+  void row_shape(const std::vector<int64_t>& space, int64_t& T, int64_t& KC, int& vec) const {
+    int64_t L = space.empty() ? 1 : space.back();
+    vec = row_vec(space);
+    int64_t chunks = (L + vec - 1) / vec;
+    T = 32;
+    while (T * 2 <= chunks && T < 256) T *= 2;
+    KC = (chunks + T - 1) / T;
+  }
+
+  void group_member(int n, MemberType type, const std::vector<int64_t>& space) {
+    auto r = refs(n);
+    // Members of open groups read in a way the group cannot serve are flushed.
+    auto it = open_group.find(space);
+    int g = it == open_group.end() ? -1 : it->second;
+    int phase = 0;
+    bool conflict = false;
+    std::set<int> before;
+    for (auto& [node, ctx] : r) {
+      int og = group_of[node];
+      if (og < 0 || !groups[og].open) continue;
+      if (og != g) {
+        before.insert(og);
+        continue;
+      }
+      const Member& m = groups[g].members[groups[g].index[node]];
+      if (ctx == ID && m.type == MemberType::EW) {
+        phase = std::max(phase, m.phase);
+      } else if (ctx == ROWB && (m.type == MemberType::ROW_SUM || m.type == MemberType::ROW_MAX)) {
+        phase = std::max(phase, m.phase + 1);
+      } else {
+        conflict = true;
+      }
+    }
+    if (g >= 0 && (conflict || groups[g].members.size() >= 48 || phase > 6)) {
+      flush(g);
+      g = -1;
+      phase = 0;
+    }
+    // groups this member reads must run first; if one of them already has to
+    // run after this member's group, that group is closed and a new one opens
+    for (int og : before) {
+      if (g >= 0 && groups[og].open && runs_after(og, g)) {
+        flush(og);
+        g = -1;
+        phase = 0;
+      }
+    }
+    if (g < 0) {
+      Group G;
+      G.space = space;
+      groups.push_back(G);
+      g = (int)groups.size() - 1;
+      open_group[space] = g;
+    }
+    for (int og : before)
+      if (groups[og].open && og != g) groups[g].after.insert(og);
+    Member m{n, type, phase};
+    groups[g].index[n] = (int)groups[g].members.size();
+    groups[g].members.push_back(m);
+    group_of[n] = g;
+  }
+
+  void own_kernel(int n, KType type) {
+    auto r = refs(n);
+    flush_refs(r);
+    Kernel k;
+    k.type = type;
+    k.node = n;
+    k.members.push_back(Member{n, MemberType::EW, 0});
+    P.kernels.push_back(k);
+  }
+
+  void group_all() {
+    group_of.assign(P.nodes.size(), -1);
+    for (int n : P.order) {
+      const Node& nd = P.nodes[n];
+      const Info& f = P.info[n];
+      if (!f.materialized || f.owner != n) continue;
+      if (source_layout(n) && !nd.readable) continue;
+      switch (nd.op) {
+        case TB_OP_MATMUL: {
+          auto r = refs(n);
+          flush_refs(r);
+          matmul_kernels(n);
+          break;
+        }
+        case TB_OP_SCATTER: {
+          auto r = refs(n);
+          flush_refs(r);
+          int sel = nd.operands[1];
+          if (!P.sort_of.count(sel)) {
+            Kernel s;
+            s.type = KType::SORT;
+            s.sel = sel;
+            P.kernels.push_back(s);
+            P.sort_of[sel] = (int)P.kernels.size() - 1;
+          }
+          own_kernel(n, KType::SCATTER);
+          break;
+        }
+        case TB_OP_FOLD:
+          own_kernel(n, KType::FOLD);
+          break;
+        case TB_OP_SUM:
+        case TB_OP_SUM_ALONG:
+        case TB_OP_MAX_ALONG: {
+          const Node& x = P.nodes[nd.operands[0]];
+          std::vector<int64_t> space = x.dims();
+          bool max = nd.op == TB_OP_MAX_ALONG;
+          if (nd.op == TB_OP_SUM) {
+            if (x.rank == 0) {
+              group_member(n, MemberType::EW, nd.dims());
+            } else {
+              group_member(n, MemberType::ALL_SUM, space);
+            }
+            break;
+          }
+          int axis = (int)nd.attrs[0];
+          if (axis == x.rank - 1) {
+            group_member(n, max ? MemberType::ROW_MAX : MemberType::ROW_SUM, space);
+            break;
+          }
+          if (!max && x.rank == 2 && axis == 0) {
+            int64_t T, KC;
+            int vec;
+            row_shape(space, T, KC, vec);
+            if (KC * vec <= 32 && space[1] <= 8192) {
+              group_member(n, MemberType::COL_SUM, space);
+              break;
+            }
+          }
+          own_kernel(n, KType::REDUCE);
+          break;
+        }
+        default:
+          group_member(n, MemberType::EW, nd.dims());
+      }
+    }
+    for (size_t g = 0; g < groups.size(); ++g) flush((int)g);
+  }
+
+  void matmul_kernels(int n) {
+    const Node& nd = P.nodes[n];
+    const Node& A = P.nodes[nd.operands[0]];
+    const Node& B = P.nodes[nd.operands[1]];
+    int split = A.rank - 2;
+    int64_t batch = 1;
+    for (int i = 0; i < split; ++i) batch *= A.shape[i];
+    int64_t M = A.shape[split], K = A.shape[split + 1], N = B.shape[split + 1];
+    int64_t Kp = (K + 31) / 32 * 32;
+    Kernel pa, pb, g;
+    pa.type = pb.type = KType::PREP;
+    pa.node = pb.node = n;
+    pa.batch = pb.batch = g.batch = batch;
+    pa.m = g.m = M;
+    pb.m = N;
+    pa.k = pb.k = g.k = K;
+    pa.kp = pb.kp = g.kp = Kp;
+    g.n = N;
+    int ahi = new_buffer(Storage::Arena, batch * M * Kp * 4, -1);
+    int alo = new_buffer(Storage::Arena, batch * M * Kp * 4, -1);
+    int bhi = new_buffer(Storage::Arena, batch * N * Kp * 4, -1);
+    int blo = new_buffer(Storage::Arena, batch * N * Kp * 4, -1);
+    pa.a_hi = ahi;
+    pa.a_lo = alo;
+    pa.sel = 0;  // operand position
+    pb.a_hi = bhi;
+    pb.a_lo = blo;
+    pb.sel = 1;
+    g.type = KType::GEMM;
+    g.node = n;
+    g.a_hi = ahi;
+    g.a_lo = alo;
+    g.b_hi = bhi;
+    g.b_lo = blo;
+    g.out = P.info[n].buf;
+    g.exact = false;
+    P.kernels.push_back(pa);
+    P.kernels.push_back(pb);
+    P.kernels.push_back(g);
+    P.gemms++;
+  }
+
+  void run(const tb_plan_desc* d) {
+    load(d);
+    count_consumers();
+    classify();
+    group_all();
+  }
+};
+
+// ============================================================== codegen
+class Emitter {
+ public:
+  Program& P;
+  Kernel& K;
+  int kid;
+  std::ostringstream body;
+  std::vector<std::unordered_map<std::string, std::string>> memo;
+  std::map<int, int> param_of;   // buffer -> parameter position
+  std::map<int, int> member_of;  // node -> member index (current kernel)
+  int phase = 0;
+  int tmp = 0;
+  int indent = 2;
+  bool exact = true;
+  bool wide = false;             // 64-bit indices
+  int vec = 1;
+
+  Emitter(Program& p, Kernel& k, int id) : P(p), K(k), kid(id) {
+    memo.emplace_back();
+    for (size_t i = 0; i < K.members.size(); ++i) member_of[K.members[i].node] = (int)i;
+  }
+
+  std::string pad() const { return std::string(indent, ' '); }
+  void line(const std::string& s) { body << pad() << s << "\n"; }
+  std::string var(const char* p = "v") { return std::string(p) + std::to_string(tmp++); }
+
+  int param(int buf) {
+    auto it = param_of.find(buf);
+    if (it != param_of.end()) return it->second;
+    int k = (int)K.params.size();
+    K.params.push_back(buf);
+    param_of[buf] = k;
+    return k;
+  }
+  std::string fptr(int buf) { return "((float*)prm.p[" + std::to_string(param(buf)) + "])"; }
+  std::string iptr(int buf) { return "((const int*)prm.p[" + std::to_string(param(buf)) + "])"; }
+
+  const std::string* find(const std::string& key) const {
+    for (auto it = memo.rbegin(); it != memo.rend(); ++it) {
+      auto f = it->find(key);
+      if (f != it->end()) return &f->second;
+    }
+    return nullptr;
+  }
+  void push() { memo.emplace_back(); }
+  void pop() { memo.pop_back(); }
+
+  static std::string key(int n, const Idx& idx) {
+    std::string k = std::to_string(n) + "@";
+    for (auto& c : idx.c) k += c + ",";
+    return k;
+  }
+
+  std::string load(int buf, const Layout& lay, const Idx& idx) {
+    if ((int)idx.c.size() != lay.rank) fail("index rank mismatch in load");
+    bool aligned = lay.offset % 4 == 0;
+    for (int d = 0; d + 1 < lay.rank; ++d)
+      if (lay.stride[d] % 4 != 0) aligned = false;
+    if (idx.lane >= 0 && vec == 4 && lay.rank > 0 && lay.stride[lay.rank - 1] == 1 && aligned) {
+      std::string off = lit(lay.offset);
+      for (int d = 0; d < lay.rank; ++d) {
+        const std::string& c = d == lay.rank - 1 ? idx.lbase : idx.c[d];
+        off = s_add(off, s_mul(c, lay.stride[d]));
+      }
+      std::string k = "vec|" + std::to_string(buf) + "|" + off;
+      const std::string* hit = find(k);
+      std::string v;
+      if (hit) {
+        v = *hit;
+      } else {
+        v = var("q");
+        line("const float4 " + v + " = *(const float4*)(" + fptr(buf) + " + " + off + ");");
+        memo.back()[k] = v;
+      }
+      static const char* comp[4] = {".x", ".y", ".z", ".w"};
+      return v + comp[idx.lane];
+    }
+    std::string off = lit(lay.offset);
+    for (int d = 0; d < lay.rank; ++d) off = s_add(off, s_mul(idx.c[d], lay.stride[d]));
+    std::string k = "ld|" + std::to_string(buf) + "|" + off;
+    const std::string* hit = find(k);
+    if (hit) return *hit;
+    std::string v = var();
+    line("const float " + v + " = " + fptr(buf) + "[" + off + "];");
+    memo.back()[k] = v;
+    return v;
+  }
+
+  // The value of node n at idx, as seen by a consumer.
+  std::string ref(int n, const Idx& idx) {
+    const Info& f = P.info[n];
+    if (f.kind == Kind::Const && !f.materialized) return flit(f.c);
+    std::string k = key(n, idx);
+    if (const std::string* hit = find(k)) return *hit;
+    auto mit = member_of.find(n);
+    if (mit != member_of.end()) {
+      const Member& m = K.members[mit->second];
+      if ((m.type == MemberType::ROW_SUM || m.type == MemberType::ROW_MAX) && m.phase < phase)
+        return "rv" + std::to_string(mit->second);
+    }
+    if (f.kind == Kind::Sel && !f.materialized) {
+      std::string v = var();
+      line("const float " + v + " = (" + iptr(f.buf) + "[" + idx.c[0] + "] == (int)(" + idx.c[1] +
+           ")) ? " + flit(f.one) + " : 0.0f;");
+      memo.back()[k] = v;
+      return v;
+    }
+    if (f.materialized || f.kind == Kind::Layout) {
+      std::string v = load(f.buf, f.lay, idx);
+      return v;
+    }
+    std::string v = def(n, idx);
+    memo.back()[k] = v;
+    return v;
+  }
+
+  Idx keep_lane(const Idx& from, std::vector<std::string> c) {
+    Idx r;
+    r.c = std::move(c);
+    if (from.lane >= 0 && !r.c.empty() && !from.c.empty() && r.c.back() == from.c.back()) {
+      r.lane = from.lane;
+      r.lbase = from.lbase;
+    }
+    return r;
+  }
+
+  // The defining computation of node n at idx.
+  std::string def(int n, const Idx& idx) {
+    const Node& nd = P.nodes[n];
+    const int64_t* at = nd.attrs;
+    const int a = nd.operands[0], b = nd.operands[1];
+    if (P.info[n].kind == Kind::Const) return flit(P.info[n].c);
+    if (nd.op == TB_OP_LEAF || nd.op == TB_OP_PARAMETER || nd.op == TB_OP_INPUT) {
+      const Info& f = P.info[n];
+      if (f.kind == Kind::Sel) {
+        std::string v = var();
+        line("const float " + v + " = (" + iptr(f.buf) + "[" + idx.c[0] + "] == (int)(" +
+             idx.c[1] + ")) ? " + flit(f.one) + " : 0.0f;");
+        return v;
+      }
+      // readable source: its original layout over its own storage
+      Layout l = contiguous(nd);
+      int src = -1;
+      for (size_t i = 0; i < P.buffers.size(); ++i)
+        if (P.buffers[i].node == n && P.buffers[i].storage != Storage::Arena) src = (int)i;
+      return load(src, l, idx);
+    }
+    if (is_elementwise(nd.op)) {
+      std::string x = ref(a, idx);
+      std::string y = b >= 0 ? ref(b, idx) : "";
+      std::string e;
+      switch (nd.op) {
+        case TB_OP_ADD: e = "__fadd_rn(" + x + ", " + y + ")"; break;
+        case TB_OP_SUB: e = "__fsub_rn(" + x + ", " + y + ")"; break;
+        case TB_OP_MUL: e = "__fmul_rn(" + x + ", " + y + ")"; break;
+        case TB_OP_DIV: e = "__fdiv_rn(" + x + ", " + y + ")"; break;
+        case TB_OP_NEG: e = "(-" + x + ")"; break;
+        case TB_OP_TANH: e = "tanhf(" + x + ")"; break;
+        case TB_OP_EXP: e = "expf(" + x + ")"; break;
+        case TB_OP_LN: e = "logf(" + x + ")"; break;
+        case TB_OP_SQRT: e = "__fsqrt_rn(" + x + ")"; break;
+        case TB_OP_POWF: e = "powf(" + x + ", " + y + ")"; break;
+        case TB_OP_MAXIMUM: e = "tb_max(" + x + ", " + y + ")"; break;
+        case TB_OP_RELU: e = "tb_max(" + x + ", 0.0f)"; break;
+        case TB_OP_STEP: e = "((" + x + " >= " + y + ") ? 1.0f : 0.0f)"; break;
+      }
+      if (is_transcendental(nd.op)) exact = false;
+      std::string v = var();
+      line("const float " + v + " = " + e + ";");
+      return v;
+    }
+    const Node& on = P.nodes[a >= 0 ? a : n];
+    std::vector<std::string> c;
+    switch (nd.op) {
+      case TB_OP_TRANSPOSE:
+        c = idx.c;
+        if (nd.rank == 2) std::swap(c[0], c[1]);
+        return ref(a, keep_lane(idx, c));
+      case TB_OP_PERMUTE:
+        c.assign(nd.rank, "0");
+        for (int j = 0; j < nd.rank; ++j) c[at[j]] = idx.c[j];
+        return ref(a, keep_lane(idx, c));
+      case TB_OP_NARROW:
+        c = idx.c;
+        c[at[0]] = s_add(c[at[0]], lit(at[1]));
+        return ref(a, keep_lane(idx, c));
+      case TB_OP_BROADCAST_ALONG:
+        for (int j = 0; j < nd.rank; ++j)
+          if (j != at[0]) c.push_back(idx.c[j]);
+        return ref(a, keep_lane(idx, c));
+      case TB_OP_BROADCAST:
+        c.assign(on.rank, "0");
+        return ref(a, keep_lane(idx, c));
+      case TB_OP_RESHAPE: {
+        std::string lin = "0";
+        int64_t s = 1;
+        for (int j = nd.rank - 1; j >= 0; --j) {
+          lin = s_add(s_mul(idx.c[j], s), lin);
+          s *= nd.shape[j];
+        }
+        // align trailing equal extents directly
+        c.assign(on.rank, "");
+        int64_t st = 1;
+        for (int j = on.rank - 1; j >= 0; --j) {
+          std::string q = s_div(lin, st);
+          c[j] = j == 0 ? q : s_mod(q, on.shape[j]);
+          st *= on.shape[j];
+        }
+        // equal trailing extents: the last index passes through unchanged
+        if (on.rank > 0 && nd.rank > 0 && on.shape[on.rank - 1] == nd.shape[nd.rank - 1])
+          c[on.rank - 1] = idx.c[nd.rank - 1];
+        return ref(a, keep_lane(idx, c));
+      }
+      case TB_OP_UNFOLD: {
+        int axis = (int)at[0];
+        for (int j = 0; j < nd.rank; ++j) {
+          if (j == axis) {
+            c.push_back(s_add(s_mul(idx.c[j], at[2]), s_mul(idx.c[j + 1], at[3])));
+          } else if (j == axis + 1) {
+            continue;
+          } else {
+            c.push_back(idx.c[j]);
+          }
+        }
+        return ref(a, keep_lane(idx, c));
+      }
+      case TB_OP_PAD: {
+        int axis = (int)at[0];
+        int64_t start = at[1], len = on.shape[axis];
+        std::string v = var();
+        line("float " + v + " = 0.0f;");
+        line("if (" + idx.c[axis] + " >= " + lit(start) + " && " + idx.c[axis] + " < " +
+             lit(start + len) + ") {");
+        indent += 2;
+        push();
+        c = idx.c;
+        c[axis] = s_add(c[axis], lit(-start));
+        std::string x = ref(a, keep_lane(idx, c));
+        line(v + " = " + x + ";");
+        pop();
+        indent -= 2;
+        line("}");
+        return v;
+      }
+      case TB_OP_SUM:
+        if (on.rank == 0) return ref(a, idx);  // the sum of one element is itself
+        break;
+      case TB_OP_GATHER: {
+        const Info& s = P.info[b];
+        std::string r = var("r");
+        line("const I " + r + " = (I)" + iptr(s.buf) + "[" + idx.c[0] + "];");
+        c = idx.c;
+        c[0] = r;
+        return ref(a, keep_lane(idx, c));
+      }
+    }
+    fail("codegen: node " + std::to_string(n) + " op " + std::to_string(nd.op) +
+         " must be materialized");
+  }
+
+  // unravel a linear index string into shape components
+  std::vector<std::string> unravel(const std::string& lin, const std::vector<int64_t>& shape,
+                                   const std::string& prefix) {
+    std::vector<std::string> c(shape.size());
+    std::string rest = lin;
+    for (int j = (int)shape.size() - 1; j >= 0; --j) {
+      std::string name = prefix + std::to_string(j);
+      if (j == 0) {
+        line("const I " + name + " = " + rest + ";");
+      } else {
+        line("const I " + name + " = " + s_mod(rest, shape[j]) + ";");
+        std::string r2 = var("u");
+        line("const I " + r2 + " = " + s_div(rest, shape[j]) + ";");
+        rest = r2;
+      }
+      c[j] = name;
+    }
+    return c;
+  }
+};
+
+namespace {
+
+std::string prelude() {
+  return R"(
+#define TB_INF __int_as_float(0x7f800000)
+__device__ __forceinline__ float tb_max(float a, float b) {
+  if (isnan(a)) return b;
+  if (isnan(b)) return a;
+  return (b > a) ? b : a;
+}
+__device__ __forceinline__ float tb_tf32(float x) {
+  unsigned r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+)";
+}
+
+int64_t volume_of(const std::vector<int64_t>& s) {
+  int64_t v = 1;
+  for (auto e : s) v *= e;
+  return v;
+}
+
+bool needs_wide(const Program& P, const Kernel& K) {
+  int64_t big = volume_of(K.space);
+  for (int b : K.params) big = std::max(big, P.buffers[b].bytes / 4);
+  if (K.node >= 0) big = std::max(big, P.nodes[K.node].volume());
+  big = std::max(big, K.batch * std::max(K.m, K.n) * std::max<int64_t>(K.kp, 1));
+  return big >= (1LL << 31) - 1;
+}
+
+const int SMS = 148;
+
+}  // namespace
+
+// ---- flat elementwise group
+static void emit_ew(Program& P, Kernel& K, Emitter& E) {
+  const std::vector<int64_t>& S = K.space;
+  int64_t total = volume_of(S);
+  E.vec = (!S.empty() && S.back() % 4 == 0) ? 4 : 1;
+  int64_t units = total / E.vec;
+  K.block = 256;
+  K.grid = std::max<int64_t>(1, std::min<int64_t>((units + 255) / 256, SMS * 8));
+  E.line("for (I t = (I)blockIdx.x * 256 + threadIdx.x; t < " + lit(units) +
+         "; t += (I)gridDim.x * 256) {");
+  E.indent += 2;
+  E.line("const I lin = t * " + std::to_string(E.vec) + ";");
+  std::vector<std::string> base = E.unravel("lin", S, "i");
+  std::vector<std::vector<std::string>> vals(K.members.size());
+  for (int v = 0; v < E.vec; ++v) {
+    Idx idx;
+    idx.c = base;
+    if (!S.empty() && E.vec > 1) {
+      idx.c.back() = s_add(base.back(), std::to_string(v));
+      idx.lane = v;
+      idx.lbase = base.back();
+    }
+    for (size_t m = 0; m < K.members.size(); ++m) {
+      int n = K.members[m].node;
+      std::string x = E.def(n, idx);
+      E.memo.back()[Emitter::key(n, idx)] = x;
+      vals[m].push_back(x);
+    }
+  }
+  for (size_t m = 0; m < K.members.size(); ++m) {
+    int buf = P.info[K.members[m].node].buf;
+    if (E.vec == 4) {
+      E.line("*(float4*)(" + E.fptr(buf) + " + lin) = make_float4(" + vals[m][0] + ", " +
+             vals[m][1] + ", " + vals[m][2] + ", " + vals[m][3] + ");");
+    } else {
+      E.line(E.fptr(buf) + "[lin] = " + vals[m][0] + ";");
+    }
+  }
+  E.indent -= 2;
+  E.line("}");
+}
+
+// ---- row-space group: phases of elementwise work separated by row reductions
+static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
+                     std::vector<Kernel>& finals) {
+  const std::vector<int64_t>& S = K.space;
+  int64_t L = S.back();
+  int64_t R = volume_of(S) / L;
+  int64_t T, KC;
+  int vec;
+  Lw.row_shape(S, T, KC, vec);
+  E.vec = vec;
+  int64_t teams = 256 / T;
+  bool has_col = false, has_all = false;
+  int maxphase = 0;
+  for (auto& m : K.members) {
+    if (m.type == MemberType::COL_SUM) has_col = true;
+    if (m.type == MemberType::ALL_SUM) has_all = true;
+    maxphase = std::max(maxphase, m.phase);
+  }
+  K.block = 256;
+  int64_t cap = has_col ? SMS * 2 : SMS * 4;
+  K.grid = std::max<int64_t>(1, std::min<int64_t>((R + teams - 1) / teams, cap));
+  if (has_col || has_all) E.exact = false;
+  E.line("__shared__ float sred[8];");
+  if (has_col) E.line("__shared__ float scol[" + lit(L) + "];");
+  E.line("const int tid = threadIdx.x, team = tid / " + std::to_string(T) + ", tl = tid % " +
+         std::to_string(T) + ";");
+  (void)teams;
+  for (size_t m = 0; m < K.members.size(); ++m) {
+    if (K.members[m].type == MemberType::COL_SUM)
+      E.line("float ca" + std::to_string(m) + "[" + std::to_string(KC * vec) + "] = {0};");
+    if (K.members[m].type == MemberType::ALL_SUM) E.line("float fa" + std::to_string(m) + " = 0.0f;");
+  }
+  E.line("for (I base = (I)blockIdx.x * " + std::to_string(teams) + "; base < " + lit(R) +
+         "; base += (I)gridDim.x * " + std::to_string(teams) + ") {");
+  E.indent += 2;
+  E.line("const I row = base + team;");
+  E.line("const bool act = row < " + lit(R) + ";");
+  std::vector<int64_t> lead(S.begin(), S.end() - 1);
+  std::vector<std::string> rc = lead.empty() ? std::vector<std::string>{}
+                                             : E.unravel("row", lead, "i");
+  for (int ph = 0; ph <= maxphase; ++ph) {
+    E.phase = ph;
+    E.line("// phase " + std::to_string(ph));
+    for (size_t m = 0; m < K.members.size(); ++m) {
+      const Member& mm = K.members[m];
+      if (mm.phase != ph) continue;
+      if (mm.type == MemberType::ROW_SUM) E.line("float ra" + std::to_string(m) + " = 0.0f;");
+      if (mm.type == MemberType::ROW_MAX)
+        E.line("float ra" + std::to_string(m) + " = __int_as_float(0x7fc00000);");
+    }
+    bool unroll = has_col;
+    E.line(unroll ? "#pragma unroll" : "#pragma unroll 1");
+    E.line("for (int kc = 0; kc < " + std::to_string(KC) + "; ++kc) {");
+    E.indent += 2;
+    E.line("const I j0 = ((I)kc * " + std::to_string(T) + " + tl) * " + std::to_string(vec) + ";");
+    E.line("if (act && j0 < " + lit(L) + ") {");
+    E.indent += 2;
+    E.push();
+    std::vector<std::vector<std::string>> vals(K.members.size());
+    for (int v = 0; v < vec; ++v) {
+      Idx idx;
+      idx.c = rc;
+      idx.c.push_back(vec > 1 ? s_add("j0", std::to_string(v)) : "j0");
+      if (vec > 1) {
+        idx.lane = v;
+        idx.lbase = "j0";
+      }
+      for (size_t m = 0; m < K.members.size(); ++m) {
+        const Member& mm = K.members[m];
+        if (mm.phase != ph) continue;
+        int n = mm.node;
+        std::string x;
+        if (mm.type == MemberType::EW) {
+          x = E.def(n, idx);
+          E.memo.back()[Emitter::key(n, idx)] = x;
+        } else {
+          x = E.ref(P.nodes[n].operands[0], idx);
+        }
+        vals[m].push_back(x);
+        std::string ms = std::to_string(m);
+        switch (mm.type) {
+          case MemberType::ROW_SUM: E.line("ra" + ms + " = __fadd_rn(ra" + ms + ", " + x + ");"); break;
+          case MemberType::ROW_MAX: E.line("ra" + ms + " = tb_max(ra" + ms + ", " + x + ");"); break;
+          case MemberType::COL_SUM:
+            E.line("ca" + ms + "[kc * " + std::to_string(vec) + " + " + std::to_string(v) +
+                   "] = __fadd_rn(ca" + ms + "[kc * " + std::to_string(vec) + " + " +
+                   std::to_string(v) + "], " + x + ");");
+            break;
+          case MemberType::ALL_SUM: E.line("fa" + ms + " = __fadd_rn(fa" + ms + ", " + x + ");"); break;
+          default: break;
+        }
+      }
+    }
+    for (size_t m = 0; m < K.members.size(); ++m) {
+      const Member& mm = K.members[m];
+      if (mm.phase != ph || mm.type != MemberType::EW) continue;
+      int buf = P.info[mm.node].buf;
+      if (vec == 4) {
+        E.line("*(float4*)(" + E.fptr(buf) + " + row * " + lit(L) + " + j0) = make_float4(" +
+               vals[m][0] + ", " + vals[m][1] + ", " + vals[m][2] + ", " + vals[m][3] + ");");
+      } else {
+        E.line(E.fptr(buf) + "[row * " + lit(L) + " + j0] = " + vals[m][0] + ";");
+      }
+    }
+    E.pop();
+    E.indent -= 2;
+    E.line("}");
+    E.indent -= 2;
+    E.line("}");
+    // team reductions of this phase
+    for (size_t m = 0; m < K.members.size(); ++m) {
+      const Member& mm = K.members[m];
+      if (mm.phase != ph || (mm.type != MemberType::ROW_SUM && mm.type != MemberType::ROW_MAX))
+        continue;
+      E.exact = false;
+      std::string ms = std::to_string(m);
+      std::string op = mm.type == MemberType::ROW_SUM ? "__fadd_rn" : "tb_max";
+      E.line("float rv" + ms + " = ra" + ms + ";");
+      int64_t width = std::min<int64_t>(T, 32);
+      for (int64_t o = width / 2; o > 0; o /= 2)
+        E.line("rv" + ms + " = " + op + "(rv" + ms + ", __shfl_xor_sync(0xffffffffu, rv" + ms +
+               ", " + std::to_string(o) + "));");
+      if (T > 32) {
+        E.line("if ((tid & 31) == 0) sred[tid >> 5] = rv" + ms + ";");
+        E.line("__syncthreads();");
+        int64_t w = T / 32;
+        E.line("{ const int w0 = team * " + std::to_string(w) + "; rv" + ms + " = sred[w0];");
+        for (int64_t q = 1; q < w; ++q)
+          E.line("  rv" + ms + " = " + op + "(rv" + ms + ", sred[w0 + " + std::to_string(q) + "]);");
+        E.line("}");
+        E.line("__syncthreads();");
+      }
+      E.line("if (act && tl == 0) " + E.fptr(P.info[mm.node].buf) + "[row] = rv" + ms + ";");
+    }
+  }
+  E.indent -= 2;
+  E.line("}");
+  // column and full sums: per-block partials, combined by a FINAL kernel
+  for (size_t m = 0; m < K.members.size(); ++m) {
+    const Member& mm = K.members[m];
+    std::string ms = std::to_string(m);
+    if (mm.type == MemberType::COL_SUM) {
+      int part = Lw.new_buffer(Storage::Arena, K.grid * L * 4, -1);
+      E.line("{");
+      E.line("  for (int tm = 0; tm < " + std::to_string(teams) + "; ++tm) {");
+      E.line("    if (team == tm) {");
+      E.line("#pragma unroll");
+      E.line("      for (int kc = 0; kc < " + std::to_string(KC) + "; ++kc) {");
+      for (int v = 0; v < vec; ++v) {
+        E.line("        { const I j = ((I)kc * " + std::to_string(T) + " + tl) * " +
+               std::to_string(vec) + " + " + std::to_string(v) + "; if (j < " + lit(L) +
+               ") scol[j] = tm == 0 ? ca" + ms + "[kc * " + std::to_string(vec) + " + " +
+               std::to_string(v) + "] : __fadd_rn(scol[j], ca" + ms + "[kc * " +
+               std::to_string(vec) + " + " + std::to_string(v) + "]); }");
+      }
+      E.line("      }");
+      E.line("    }");
+      E.line("    __syncthreads();");
+      E.line("  }");
+      E.line("  for (I j = tid; j < " + lit(L) + "; j += 256) " + E.fptr(part) +
+             "[(I)blockIdx.x * " + lit(L) + " + j] = scol[j];");
+      E.line("  __syncthreads();");
+      E.line("}");
+      Kernel f;
+      f.type = KType::FINAL;
+      f.partial = part;
+      f.final_out = P.info[mm.node].buf;
+      f.final_blocks = K.grid;
+      f.final_width = L;
+      f.exact = false;
+      finals.push_back(f);
+    }
+    if (mm.type == MemberType::ALL_SUM) {
+      int part = Lw.new_buffer(Storage::Arena, K.grid * 4, -1);
+      E.line("{");
+      E.line("  float s = fa" + ms + ";");
+      for (int o = 16; o > 0; o /= 2)
+        E.line("  s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, " + std::to_string(o) + "));");
+      E.line("  if ((tid & 31) == 0) sred[tid >> 5] = s;");
+      E.line("  __syncthreads();");
+      E.line("  if (tid == 0) { float t = sred[0]; for (int w = 1; w < 8; ++w) t = __fadd_rn(t, sred[w]); " +
+             E.fptr(part) + "[blockIdx.x] = t; }");
+      E.line("  __syncthreads();");
+      E.line("}");
+      Kernel f;
+      f.type = KType::FINAL;
+      f.partial = part;
+      f.final_out = P.info[mm.node].buf;
+      f.final_blocks = K.grid;
+      f.final_width = 1;
+      f.exact = false;
+      finals.push_back(f);
+    }
+  }
+}
+
+// ---- generic serial reduction: one thread per output, ascending order
+static void emit_reduce(Program& P, Kernel& K, Emitter& E) {
+  int n = K.node;
+  const Node& nd = P.nodes[n];
+  const Node& x = P.nodes[nd.operands[0]];
+  int axis = (int)nd.attrs[0];
+  bool max = nd.op == TB_OP_MAX_ALONG;
+  int64_t outs = nd.volume();
+  K.grid = std::max<int64_t>(1, std::min<int64_t>((outs + 255) / 256, SMS * 8));
+  E.line("for (I t = (I)blockIdx.x * 256 + threadIdx.x; t < " + lit(outs) +
+         "; t += (I)gridDim.x * 256) {");
+  E.indent += 2;
+  std::vector<std::string> oc = E.unravel("t", nd.dims(), "o");
+  std::vector<std::string> c;
+  for (int j = 0, s = 0; j < x.rank; ++j) c.push_back(j == axis ? "0" : oc[s++]);
+  Idx first;
+  first.c = c;
+  E.push();
+  std::string x0 = E.ref(nd.operands[0], first);
+  E.line("float acc = " + x0 + ";");
+  E.pop();
+  E.line("for (I s = 1; s < " + lit(x.shape[axis]) + "; ++s) {");
+  E.indent += 2;
+  E.push();
+  Idx at;
+  at.c = c;
+  at.c[axis] = "s";
+  std::string xv = E.ref(nd.operands[0], at);
+  E.line(std::string("acc = ") + (max ? "tb_max" : "__fadd_rn") + "(acc, " + xv + ");");
+  E.pop();
+  E.indent -= 2;
+  E.line("}");
+  E.line(E.fptr(P.info[n].buf) + "[t] = acc;");
+  E.indent -= 2;
+  E.line("}");
+}
+
+// ---- scatter-add over the stably sorted selection (payload/tensor.rs:1582-1618)
+static void emit_scatter(Program& P, Kernel& K, Emitter& E, const Kernel& sort) {
+  int n = K.node;
+  const Node& nd = P.nodes[n];
+  int64_t rows = nd.shape[0];
+  int64_t width = nd.volume() / rows;
+  std::vector<int64_t> rest(nd.shape + 1, nd.shape + nd.rank);
+  K.grid = std::max<int64_t>(1, std::min<int64_t>((rows * width + 255) / 256, SMS * 8));
+  E.line("for (I t = (I)blockIdx.x * 256 + threadIdx.x; t < " + lit(rows * width) +
+         "; t += (I)gridDim.x * 256) {");
+  E.indent += 2;
+  E.line("const I row = t / " + lit(width) + ";");
+  E.line("const I o = t % " + lit(width) + ";");
+  std::vector<std::string> oc = rest.empty() ? std::vector<std::string>{} : E.unravel("o", rest, "c");
+  E.line("float acc = 0.0f;");
+  E.line("const int q1 = " + E.iptr(sort.rend) + "[row];");
+  E.line("for (int q = " + E.iptr(sort.rstart) + "[row]; q < q1; ++q) {");
+  E.indent += 2;
+  E.line("const I s = (I)" + E.iptr(sort.vals) + "[q];");
+  E.push();
+  Idx at;
+  at.c.push_back("s");
+  for (auto& c : oc) at.c.push_back(c);
+  std::string g = E.ref(nd.operands[0], at);
+  E.line("acc = __fadd_rn(acc, " + g + ");");
+  E.pop();
+  E.indent -= 2;
+  E.line("}");
+  E.line(E.fptr(P.info[n].buf) + "[t] = acc;");
+  E.indent -= 2;
+  E.line("}");
+}
+
+// ---- fold (payload/tensor.rs:1392-1463)
+static void emit_fold(Program& P, Kernel& K, Emitter& E) {
+  int n = K.node;
+  const Node& nd = P.nodes[n];
+  const Node& x = P.nodes[nd.operands[0]];
+  int axis = (int)nd.attrs[0];
+  int64_t size = nd.attrs[1], step = nd.attrs[2], dil = nd.attrs[3];
+  int64_t count = x.shape[axis];
+  int64_t outs = nd.volume();
+  K.grid = std::max<int64_t>(1, std::min<int64_t>((outs + 255) / 256, SMS * 8));
+  E.line("for (I t = (I)blockIdx.x * 256 + threadIdx.x; t < " + lit(outs) +
+         "; t += (I)gridDim.x * 256) {");
+  E.indent += 2;
+  std::vector<std::string> oc = E.unravel("t", nd.dims(), "o");
+  E.line("float acc = 0.0f;");
+  E.line("for (I k = 0; k < " + lit(size) + "; ++k) {");
+  E.indent += 2;
+  E.line("const I reach = k * " + lit(dil) + ";");
+  E.line("if (reach > " + oc[axis] + ") break;");
+  E.line("const I rest = " + oc[axis] + " - reach;");
+  E.line("if (rest % " + lit(step) + " != 0) continue;");
+  E.line("const I w = rest / " + lit(step) + ";");
+  E.line("if (w >= " + lit(count) + ") continue;");
+  E.push();
+  Idx at;
+  for (int j = 0; j < nd.rank; ++j) {
+    if (j == axis) {
+      at.c.push_back("w");
+      at.c.push_back("k");
+    } else {
+      at.c.push_back(oc[j]);
+    }
+  }
+  std::string v = E.ref(nd.operands[0], at);
+  E.line("acc = __fadd_rn(acc, " + v + ");");
+  E.pop();
+  E.indent -= 2;
+  E.line("}");
+  E.line(E.fptr(P.info[n].buf) + "[t] = acc;");
+  E.indent -= 2;
+  E.line("}");
+}
+
+// ---- GEMM operand preparation: tf32 hi/lo split into K-major [batch, R, Kp]
+static void emit_prep(Program& P, Kernel& K, Emitter& E) {
+  const Node& mm = P.nodes[K.node];
+  int x = mm.operands[K.sel];
+  const Node& xn = P.nodes[x];
+  int split = xn.rank - 2;
+  std::vector<int64_t> bshape(xn.shape, xn.shape + split);
+  int64_t R = K.m, Kd = K.k, Kp = K.kp;
+  bool is_b = K.sel == 1;
+  // transpose through shared memory when the operand is contiguous along R
+  bool tile = false;
+  const Info& f = P.info[x];
+  if (f.materialized || f.kind == Kind::Layout) {
+    int64_t sk = f.lay.stride[is_b ? split : split + 1];
+    int64_t sr = f.lay.stride[is_b ? split + 1 : split];
+    tile = sk != 1 && sr == 1;
+  }
+  auto operand_idx = [&](const std::vector<std::string>& bc, const std::string& r,
+                         const std::string& k) {
+    Idx idx;
+    idx.c = bc;
+    if (is_b) {
+      idx.c.push_back(k);
+      idx.c.push_back(r);
+    } else {
+      idx.c.push_back(r);
+      idx.c.push_back(k);
+    }
+    return idx;
+  };
+  std::string hi = E.fptr(K.a_hi), lo = E.fptr(K.a_lo);
+  if (!tile) {
+    int64_t quads = K.batch * R * (Kp / 4);
+    K.grid = std::max<int64_t>(1, std::min<int64_t>((quads + 255) / 256, SMS * 8));
+    E.vec = (!is_b && Kd % 4 == 0) ? 4 : 1;
+    E.line("for (I t = (I)blockIdx.x * 256 + threadIdx.x; t < " + lit(quads) +
+           "; t += (I)gridDim.x * 256) {");
+    E.indent += 2;
+    E.line("const I kq = t % " + lit(Kp / 4) + ";");
+    E.line("const I rest = t / " + lit(Kp / 4) + ";");
+    E.line("const I r = rest % " + lit(R) + ";");
+    E.line("const I b = rest / " + lit(R) + ";");
+    E.line("const I k0 = kq * 4;");
+    std::vector<std::string> bc = bshape.empty() ? std::vector<std::string>{}
+                                                 : E.unravel("b", bshape, "bb");
+    E.line("float x0 = 0.0f, x1 = 0.0f, x2 = 0.0f, x3 = 0.0f;");
+    if (Kd % 4 == 0) {
+      E.line("if (k0 < " + lit(Kd) + ") {");
+      E.indent += 2;
+      E.push();
+      for (int v = 0; v < 4; ++v) {
+        Idx idx = operand_idx(bc, "r", s_add("k0", std::to_string(v)));
+        if (E.vec == 4) {
+          idx.lane = v;
+          idx.lbase = "k0";
+        }
+        std::string xv = E.ref(x, idx);
+        E.line("x" + std::to_string(v) + " = " + xv + ";");
+      }
+      E.pop();
+      E.indent -= 2;
+      E.line("}");
+    } else {
+      for (int v = 0; v < 4; ++v) {
+        E.line("if (k0 + " + std::to_string(v) + " < " + lit(Kd) + ") {");
+        E.indent += 2;
+        E.push();
+        Idx idx = operand_idx(bc, "r", s_add("k0", std::to_string(v)));
+        std::string xv = E.ref(x, idx);
+        E.line("x" + std::to_string(v) + " = " + xv + ";");
+        E.pop();
+        E.indent -= 2;
+        E.line("}");
+      }
+    }
+    E.line("const float h0 = tb_tf32(x0), h1 = tb_tf32(x1), h2 = tb_tf32(x2), h3 = tb_tf32(x3);");
+    E.line("const I o = (b * " + lit(R) + " + r) * " + lit(Kp) + " + k0;");
+    E.line("*(float4*)(" + hi + " + o) = make_float4(h0, h1, h2, h3);");
+    E.line("*(float4*)(" + lo + " + o) = make_float4(__fsub_rn(x0, h0), __fsub_rn(x1, h1), "
+           "__fsub_rn(x2, h2), __fsub_rn(x3, h3));");
+    E.indent -= 2;
+    E.line("}");
+    return;
+  }
+  int64_t rt = (R + 31) / 32, kt = Kp / 32;
+  int64_t tiles = K.batch * rt * kt;
+  K.grid = std::max<int64_t>(1, std::min<int64_t>(tiles, SMS * 16));
+  E.vec = 1;
+  E.line("__shared__ float sm[32][33];");
+  E.line("const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;");
+  E.line("for (I t = blockIdx.x; t < " + lit(tiles) + "; t += gridDim.x) {");
+  E.indent += 2;
+  E.line("const I kt = t % " + lit(kt) + ";");
+  E.line("const I rest = t / " + lit(kt) + ";");
+  E.line("const I r0 = (rest % " + lit(rt) + ") * 32;");
+  E.line("const I b = rest / " + lit(rt) + ";");
+  E.line("const I k0 = kt * 32;");
+  std::vector<std::string> bc = bshape.empty() ? std::vector<std::string>{}
+                                               : E.unravel("b", bshape, "bb");
+  E.line("#pragma unroll");
+  E.line("for (int q = 0; q < 4; ++q) {");
+  E.indent += 2;
+  E.line("const I r = r0 + tx, k = k0 + ty + 8 * q;");
+  E.line("float xv = 0.0f;");
+  E.line("if (r < " + lit(R) + " && k < " + lit(Kd) + ") {");
+  E.indent += 2;
+  E.push();
+  Idx idx = operand_idx(bc, "r", "k");
+  std::string xv = E.ref(x, idx);
+  E.line("xv = " + xv + ";");
+  E.pop();
+  E.indent -= 2;
+  E.line("}");
+  E.line("sm[ty + 8 * q][tx] = xv;");
+  E.indent -= 2;
+  E.line("}");
+  E.line("__syncthreads();");
+  E.line("#pragma unroll");
+  E.line("for (int q = 0; q < 4; ++q) {");
+  E.line("  const I r = r0 + ty + 8 * q;");
+  E.line("  const float xv = sm[tx][ty + 8 * q];");
+  E.line("  const float h = tb_tf32(xv);");
+  E.line("  if (r < " + lit(R) + ") { const I o = (b * " + lit(R) + " + r) * " + lit(Kp) +
+         " + k0 + tx; " + hi + "[o] = h; " + lo + "[o] = __fsub_rn(xv, h); }");
+  E.line("}");
+  E.line("__syncthreads();");
+  E.indent -= 2;
+  E.line("}");
+}
+
+// ---- buffer liveness and the arena layout
+static void plan_arena(Program& P) {
+  const int never = -1;
+  for (auto& b : P.buffers) {
+    b.first = never;
+    b.last = never;
+  }
+  for (size_t k = 0; k < P.kernels.size(); ++k) {
+    const Kernel& K = P.kernels[k];
+    auto touch = [&](int buf) {
+      if (buf < 0) return;
+      Buffer& b = P.buffers[buf];
+      if (b.first == never) b.first = (int)k;
+      b.first = std::min(b.first, (int)k);
+      b.last = std::max(b.last, (int)k);
+    };
+    for (int b : K.reads) touch(b);
+    for (int b : K.writes) touch(b);
+  }
+  const int end = (int)P.kernels.size();
+  std::vector<int> ids;
+  for (size_t i = 0; i < P.buffers.size(); ++i) {
+    Buffer& b = P.buffers[i];
+    if (b.storage != Storage::Arena) continue;
+    if (b.node >= 0 && P.nodes[b.node].readable) b.keep = true;
+    if (b.first == never) continue;
+    if (b.keep) b.last = end;
+    ids.push_back((int)i);
+  }
+  // Readable values (the plan's results, gradients among them) live past the
+  // program: they are packed first, contiguously in the order they are
+  // written, so gradient exchange can move them in few large ranges.
+  std::vector<int> kept, rest;
+  for (int id : ids) (P.buffers[id].keep ? kept : rest).push_back(id);
+  std::sort(kept.begin(), kept.end(), [&](int x, int y) {
+    if (P.buffers[x].first != P.buffers[y].first) return P.buffers[x].first < P.buffers[y].first;
+    return x < y;
+  });
+  int64_t base = 0;
+  P.unplanned_bytes = 0;
+  for (int id : kept) {
+    Buffer& b = P.buffers[id];
+    b.offset = base;
+    base += (b.bytes + 255) / 256 * 256;
+  }
+  P.unplanned_bytes = base;
+  ids = rest;
+  std::sort(ids.begin(), ids.end(), [&](int x, int y) {
+    if (P.buffers[x].bytes != P.buffers[y].bytes) return P.buffers[x].bytes > P.buffers[y].bytes;
+    return x < y;
+  });
+  std::vector<int> placed;
+  int64_t top = base;
+  for (int id : ids) {
+    Buffer& b = P.buffers[id];
+    int64_t size = (b.bytes + 255) / 256 * 256;
+    P.unplanned_bytes += size;
+    std::vector<std::pair<int64_t, int64_t>> busy;
+    for (int o : placed) {
+      const Buffer& q = P.buffers[o];
+      if (q.first <= b.last && b.first <= q.last)
+        busy.push_back({q.offset, q.offset + (q.bytes + 255) / 256 * 256});
+    }
+    std::sort(busy.begin(), busy.end());
+    int64_t at = base;
+    for (auto& [s, e] : busy) {
+      if (at + size <= s) break;
+      at = std::max(at, e);
+    }
+    b.offset = at;
+    top = std::max(top, at + size);
+    placed.push_back(id);
+  }
+  P.arena_bytes = top;
+}
+
+std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
+  if (!desc || desc->node_count <= 0 || !desc->nodes) fail("empty plan");
+  auto prog = std::make_unique<Program>();
+  Program& P = *prog;
+  Lowerer Lw(P);
+  Lw.run(desc);
+
+  // codegen; FINAL kernels are inserted right after their row kernel
+  std::vector<Kernel> kernels;
+  kernels.swap(P.kernels);
+  std::map<std::string, std::string> dedupe;  // body -> function name
+  std::ostringstream all;
+  all << prelude();
+  std::map<int, int> sort_index;  // old SORT kernel index -> new index
+  for (size_t i = 0; i < kernels.size(); ++i) {
+    Kernel K = kernels[i];
+    std::vector<Kernel> finals;
+    if (K.type == KType::GEMM) {
+      K.reads = {K.a_hi, K.a_lo, K.b_hi, K.b_lo};
+      K.writes = {K.out};
+      K.exact = false;
+      K.describe = "gemm3xtf32 batch=" + std::to_string(K.batch) + " m=" + std::to_string(K.m) +
+                   " n=" + std::to_string(K.n) + " k=" + std::to_string(K.k);
+      P.kernels.push_back(K);
+      continue;
+    }
+    if (K.type == KType::SORT) {
+      const Node& s = P.nodes[K.sel];
+      K.count = s.shape[0];
+      K.rows = s.shape[1];
+      int bits = 0;
+      while ((1LL << bits) < K.rows) ++bits;
+      K.passes = std::max(1, (bits + 7) / 8);
+      K.tiles = (K.count + 1023) / 1024;
+      K.keys = Lw.new_buffer(Storage::Arena, K.count * 4, -1);
+      K.vals = Lw.new_buffer(Storage::Arena, K.count * 4, -1);
+      K.tmp_keys = Lw.new_buffer(Storage::Arena, K.count * 4, -1);
+      K.tmp_vals = Lw.new_buffer(Storage::Arena, K.count * 4, -1);
+      K.counts = Lw.new_buffer(Storage::Arena, 256 * K.tiles * 4, -1);
+      K.rstart = Lw.new_buffer(Storage::Arena, K.rows * 4, -1);
+      K.rend = Lw.new_buffer(Storage::Arena, K.rows * 4, -1);
+      K.out = P.info[K.sel].buf;  // the index buffer
+      K.reads = {K.out};
+      K.writes = {K.keys, K.vals, K.tmp_keys, K.tmp_vals, K.counts, K.rstart, K.rend};
+      K.describe = "sort selection node " + std::to_string(K.sel) + " count=" +
+                   std::to_string(K.count) + " rows=" + std::to_string(K.rows);
+      sort_index[(int)i] = (int)P.kernels.size();
+      P.kernels.push_back(K);
+      continue;
+    }
+    Emitter E(P, K, (int)P.kernels.size());
+    switch (K.type) {
+      case KType::EW: emit_ew(P, K, E); break;
+      case KType::ROW: emit_row(P, K, E, Lw, finals); break;
+      case KType::REDUCE: emit_reduce(P, K, E); break;
+      case KType::SCATTER: {
+        int sk = sort_index.at(P.sort_of.at(P.nodes[K.node].operands[1]));
+        K.sel = sk;
+        emit_scatter(P, K, E, P.kernels[sk]);
+        break;
+      }
+      case KType::FOLD: emit_fold(P, K, E); break;
+      case KType::PREP: emit_prep(P, K, E); break;
+      default: fail("codegen: unexpected kernel type");
+    }
+    K.exact = E.exact;
+    E.wide = needs_wide(P, K);
+    std::ostringstream fn;
+    fn << "struct PRM_NAME { void* p[" << std::max<size_t>(1, K.params.size()) << "]; };\n";
+    fn << "extern \"C\" __global__ void __launch_bounds__(256) NAME(const PRM_NAME prm) {\n";
+    fn << "  typedef " << (E.wide ? "long long" : "int") << " I;\n";
+    fn << E.body.str() << "}\n";
+    std::string text = fn.str();
+    auto it = dedupe.find(text);
+    if (it == dedupe.end()) {
+      std::string name = "tbk" + std::to_string(dedupe.size());
+      std::string src = text;
+      for (size_t p; (p = src.find("PRM_NAME")) != std::string::npos;)
+        src.replace(p, 8, "P_" + name);
+      for (size_t p; (p = src.find("NAME(")) != std::string::npos;) src.replace(p, 4, name);
+      all << src << "\n";
+      it = dedupe.emplace(text, name).first;
+    }
+    K.name = it->second;
+    K.source.clear();
+    for (int b : K.params) {
+      const Buffer& bf = P.buffers[b];
+      bool written = false;
+      for (auto& m : K.members)
+        if (P.info[m.node].buf == b && P.info[m.node].owner == m.node) written = true;
+      if (b == K.a_hi || b == K.a_lo) written = true;
+      if (bf.storage == Storage::Arena && bf.node < 0 && K.type == KType::ROW) written = true;
+      (written ? K.writes : K.reads).push_back(b);
+    }
+    if (K.type == KType::SCATTER) {
+      const Kernel& s = P.kernels[K.sel];
+      K.reads.push_back(s.vals);
+      K.reads.push_back(s.rstart);
+      K.reads.push_back(s.rend);
+    }
+    std::ostringstream d;
+    static const char* names[] = {"ew", "row", "reduce", "prep", "gemm", "sort", "scatter", "fold", "final"};
+    d << names[(int)K.type] << " " << K.name << " grid=" << K.grid;
+    if (!K.space.empty()) {
+      d << " space=[";
+      for (size_t j = 0; j < K.space.size(); ++j) d << (j ? "," : "") << K.space[j];
+      d << "]";
+    }
+    d << " members=";
+    for (auto& m : K.members) d << m.node << (m.phase ? "p" + std::to_string(m.phase) : "") << " ";
+    d << (K.exact ? "exact" : "tolerance");
+    K.describe = d.str();
+    P.kernels.push_back(K);
+    for (auto& f : finals) {
+      f.reads = {f.partial};
+      f.writes = {f.final_out};
+      f.describe = "final partials=" + std::to_string(f.final_blocks) + "x" +
+                   std::to_string(f.final_width);
+      P.kernels.push_back(f);
+    }
+  }
+  P.source = all.str();
+  P.exact = true;
+  for (auto& k : P.kernels) P.exact = P.exact && k.exact;
+  P.fused_nodes = 0;
+  for (int n : P.order)
+    if (P.info[n].kind == Kind::Expr && !P.info[n].materialized) P.fused_nodes++;
+  plan_arena(P);
+  return prog;
+}
+
+}  // namespace tb

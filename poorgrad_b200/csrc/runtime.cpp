@@ -1,0 +1,864 @@
+// runtime.cpp -- the C ABI of include/topos_b200.h: lazy device set-up and
+// poisoning, NVRTC compilation of the emitted kernels, device buffers (one
+// liveness-planned arena per plan), the CUDA-graph replay of a plan, device
+// parameters, optimizer steps and the NCCL gradient exchange.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
+#include <nvrtc.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <functional>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <sstream>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "engine.h"
+#include "kernels.h"
+
+namespace {
+
+thread_local std::string g_error;
+std::mutex g_mutex;
+int g_state = -1;  // -1 unknown, else TB_* status
+std::string g_status_message;
+
+struct Failure : std::runtime_error {
+  int code;
+  Failure(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+[[noreturn]] void runtime_fail(const std::string& m) { throw Failure(TB_RUNTIME, m); }
+
+void check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) runtime_fail(std::string(what) + ": " + cudaGetErrorString(e));
+}
+// Driver entry points, resolved through the runtime so that the library does
+// not link libcuda (it loads on machines without a driver and reports
+// PlatformUnsupported there).
+struct Driver {
+  CUresult (*GetErrorString)(CUresult, const char**) = nullptr;
+  CUresult (*ModuleLoadData)(CUmodule*, const void*) = nullptr;
+  CUresult (*ModuleGetFunction)(CUfunction*, CUmodule, const char*) = nullptr;
+  CUresult (*LaunchKernel)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned,
+                           unsigned, CUstream, void**, void**) = nullptr;
+  CUresult (*FuncSetAttribute)(CUfunction, CUfunction_attribute, int) = nullptr;
+};
+Driver g_driver;
+
+bool load_driver() {
+  auto get = [](const char* name, void** fn) {
+    cudaDriverEntryPointQueryResult q;
+    return cudaGetDriverEntryPoint(name, fn, cudaEnableDefault, &q) == cudaSuccess &&
+           q == cudaDriverEntryPointSuccess && *fn;
+  };
+  return get("cuGetErrorString", (void**)&g_driver.GetErrorString) &&
+         get("cuModuleLoadData", (void**)&g_driver.ModuleLoadData) &&
+         get("cuModuleGetFunction", (void**)&g_driver.ModuleGetFunction) &&
+         get("cuLaunchKernel", (void**)&g_driver.LaunchKernel) &&
+         get("cuFuncSetAttribute", (void**)&g_driver.FuncSetAttribute);
+}
+
+void check(CUresult e, const char* what) {
+  if (e != CUDA_SUCCESS) {
+    const char* s = nullptr;
+    if (g_driver.GetErrorString) g_driver.GetErrorString(e, &s);
+    runtime_fail(std::string(what) + ": " + (s ? s : std::to_string((int)e)));
+  }
+}
+
+// Lazy set-up, once per process (backend/cuda/kernels/mod.rs:36-58): a device
+// must exist; everything else is per plan.
+int ensure_ready() {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (g_state >= 0) return g_state;
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count == 0) {
+    g_state = TB_PLATFORM_UNSUPPORTED;
+    g_status_message = e != cudaSuccess ? cudaGetErrorString(e) : "no CUDA device";
+    return g_state;
+  }
+  if (cudaFree(nullptr) != cudaSuccess || !load_driver()) {
+    g_state = TB_INITIALIZATION;
+    g_status_message = "CUDA context or driver entry points unavailable";
+    return g_state;
+  }
+  g_state = TB_OK;
+  return g_state;
+}
+
+void poison(const std::string& why) {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (g_state == TB_OK) {
+    g_state = TB_POISONED;
+    g_status_message = why;
+  }
+}
+
+template <class F>
+int guarded(F&& body, bool needs_device = true) {
+  try {
+    if (needs_device) {
+      int s = ensure_ready();
+      if (s != TB_OK) {
+        g_error = "backend unavailable: " + g_status_message;
+        return s;
+      }
+    }
+    return body();
+  } catch (const Failure& f) {
+    g_error = f.what();
+    if (f.code == TB_RUNTIME) poison(f.what());
+    return f.code;
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return TB_INVALID;
+  }
+}
+
+// ---- NVRTC: one program per distinct source text, cached for the process
+struct CompiledModule {
+  CUmodule module = nullptr;
+  int device = -1;
+};
+std::map<std::pair<std::string, int>, CompiledModule> g_modules;
+std::mutex g_module_mutex;
+
+CUmodule compile_module(const std::string& source, int device) {
+  std::lock_guard<std::mutex> lock(g_module_mutex);
+  auto key = std::make_pair(source, device);
+  auto it = g_modules.find(key);
+  if (it != g_modules.end()) return it->second.module;
+  nvrtcProgram prog;
+  if (nvrtcCreateProgram(&prog, source.c_str(), "topos_b200_fused.cu", 0, nullptr, nullptr) !=
+      NVRTC_SUCCESS)
+    runtime_fail("nvrtcCreateProgram failed");
+  const char* opts[] = {"-arch=sm_100a", "--fmad=false", "-prec-div=true", "-prec-sqrt=true",
+                        "-ftz=false", "-std=c++17", "-default-device", "-lineinfo"};
+  nvrtcResult r = nvrtcCompileProgram(prog, sizeof(opts) / sizeof(opts[0]), opts);
+  if (r != NVRTC_SUCCESS) {
+    size_t n = 0;
+    nvrtcGetProgramLogSize(prog, &n);
+    std::string log(n, '\0');
+    nvrtcGetProgramLog(prog, &log[0]);
+    nvrtcDestroyProgram(&prog);
+    throw Failure(TB_INVALID, "NVRTC compile failed:\n" + log.substr(0, 4000));
+  }
+  size_t size = 0;
+  nvrtcGetCUBINSize(prog, &size);
+  std::string cubin(size, '\0');
+  nvrtcGetCUBIN(prog, &cubin[0]);
+  nvrtcDestroyProgram(&prog);
+  CUmodule mod;
+  check(g_driver.ModuleLoadData(&mod, cubin.data()), "cuModuleLoadData");
+  g_modules[key] = CompiledModule{mod, device};
+  return mod;
+}
+
+// ---- NCCL, loaded at run time (the process may already hold torch's copy)
+struct Nccl {
+  void* handle = nullptr;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  ncclResult_t (*GroupStart)() = nullptr;
+  ncclResult_t (*GroupEnd)() = nullptr;
+  const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+Nccl* nccl() {
+  static Nccl n;
+  static bool tried = false;
+  if (tried) return n.handle ? &n : nullptr;
+  tried = true;
+  const char* names[] = {"libnccl.so.2", "libnccl.so"};
+  for (const char* name : names) {
+    n.handle = dlopen(name, RTLD_NOW | RTLD_GLOBAL | RTLD_NOLOAD);
+    if (!n.handle) n.handle = dlopen(name, RTLD_NOW | RTLD_GLOBAL);
+    if (n.handle) break;
+  }
+  if (!n.handle) return nullptr;
+  n.GetUniqueId = (decltype(n.GetUniqueId))dlsym(n.handle, "ncclGetUniqueId");
+  n.CommInitRank = (decltype(n.CommInitRank))dlsym(n.handle, "ncclCommInitRank");
+  n.CommDestroy = (decltype(n.CommDestroy))dlsym(n.handle, "ncclCommDestroy");
+  n.AllReduce = (decltype(n.AllReduce))dlsym(n.handle, "ncclAllReduce");
+  n.GroupStart = (decltype(n.GroupStart))dlsym(n.handle, "ncclGroupStart");
+  n.GroupEnd = (decltype(n.GroupEnd))dlsym(n.handle, "ncclGroupEnd");
+  n.GetErrorString = (decltype(n.GetErrorString))dlsym(n.handle, "ncclGetErrorString");
+  if (!n.GetUniqueId || !n.CommInitRank || !n.AllReduce) {
+    n.handle = nullptr;
+    return nullptr;
+  }
+  return &n;
+}
+void check_nccl(ncclResult_t r, const char* what) {
+  if (r != ncclSuccess) {
+    Nccl* n = nccl();
+    runtime_fail(std::string(what) + ": " +
+                 (n && n->GetErrorString ? n->GetErrorString(r) : std::to_string(r)));
+  }
+}
+
+}  // namespace
+
+struct tb_params {
+  int device = 0;
+  void* base = nullptr;
+  std::vector<float*> slot;
+  std::vector<int64_t> count;
+  ~tb_params() {
+    if (base) cudaFree(base);
+  }
+};
+
+struct tb_comm {
+  ncclComm_t comm = nullptr;
+  int rank = 0, world = 1;
+  ~tb_comm() {
+    if (comm && nccl() && nccl()->CommDestroy) nccl()->CommDestroy(comm);
+  }
+};
+
+struct tb_optimizer {
+  tb_plan* plan = nullptr;
+  tb_params* params = nullptr;
+  tb_optimizer_desc desc{};
+  std::vector<int32_t> slots;
+  std::vector<int> grad_buffers;       // plan buffer ids
+  std::vector<tb::OptEntry> host_entries;
+  tb::OptEntry* entries = nullptr;     // device table
+  float* state = nullptr;              // moments (Adam): first then second per slot
+  float* scalars = nullptr;            // beta powers and corrections, learning rate
+  int64_t total = 0;
+  std::vector<int64_t> state_offset;   // per entry
+  ~tb_optimizer() {
+    if (entries) cudaFree(entries);
+    if (state) cudaFree(state);
+    if (scalars) cudaFree(scalars);
+  }
+};
+
+struct tb_plan {
+  std::unique_ptr<tb::Program> prog;
+  int device = 0;
+  cudaStream_t stream = nullptr, comm_stream = nullptr;
+  char* arena = nullptr;
+  std::vector<void*> own;              // input/leaf allocations
+  std::vector<void*> buffer_ptr;       // resolved device pointer per buffer id
+  CUmodule module = nullptr;
+  std::vector<CUfunction> fn;          // per kernel (emitted kernels)
+  std::vector<std::vector<void*>> kparams;
+  tb_params* bound = nullptr;
+  cudaGraphExec_t graph = nullptr;
+  bool graph_dirty = true;
+  tb_optimizer* optimizer = nullptr;
+  tb_comm* comm = nullptr;
+  int64_t bucket_bytes = 0;
+  std::vector<cudaEvent_t> events;
+  int64_t launches = 0;
+  ~tb_plan() {
+    if (graph) cudaGraphExecDestroy(graph);
+    for (auto e : events) cudaEventDestroy(e);
+    if (arena) cudaFree(arena);
+    for (void* p : own) cudaFree(p);
+    if (stream) cudaStreamDestroy(stream);
+    if (comm_stream) cudaStreamDestroy(comm_stream);
+  }
+};
+
+namespace {
+
+int resolve_node(const tb::Program& P, int64_t node) {
+  if (node < 0 || node >= (int64_t)P.nodes.size()) throw Failure(TB_INVALID, "node out of range");
+  int n = (int)node;
+  while (P.info[n].alias >= 0) n = P.info[n].alias;
+  return n;
+}
+
+int readable_buffer(const tb::Program& P, int64_t node) {
+  int n = resolve_node(P, node);
+  const tb::Info& f = P.info[n];
+  if (!P.nodes[n].readable || !f.materialized || f.owner != n)
+    throw Failure(TB_INVALID, "node " + std::to_string(node) + " is not a readable value of the plan");
+  return f.buf;
+}
+
+void bind_params(tb_plan* plan, tb_params* params) {
+  tb::Program& P = *plan->prog;
+  if (plan->bound == params) return;
+  for (size_t b = 0; b < P.buffers.size(); ++b) {
+    const tb::Buffer& buf = P.buffers[b];
+    if (buf.storage != tb::Storage::Parameter) continue;
+    if (!params || buf.slot >= (int)params->slot.size())
+      throw Failure(TB_INVALID, "parameters do not cover the plan's parameter slots");
+    if (params->count[buf.slot] * 4 != buf.bytes)
+      throw Failure(TB_INVALID, "parameter slot size disagrees with the plan");
+    plan->buffer_ptr[b] = params->slot[buf.slot];
+  }
+  plan->kparams.assign(P.kernels.size(), {});
+  for (size_t k = 0; k < P.kernels.size(); ++k) {
+    const tb::Kernel& K = P.kernels[k];
+    for (int b : K.params) plan->kparams[k].push_back(plan->buffer_ptr[b]);
+  }
+  plan->bound = params;
+  plan->graph_dirty = true;
+}
+
+float* fp(tb_plan* plan, int b) { return (float*)plan->buffer_ptr[b]; }
+int* ip(tb_plan* plan, int b) { return (int*)plan->buffer_ptr[b]; }
+
+// gradient ranges of the attached optimizer, issued after their last writer
+struct Bucket {
+  int after_kernel;
+  char* begin;
+  int64_t bytes;
+};
+
+std::vector<Bucket> gradient_buckets(tb_plan* plan) {
+  std::vector<Bucket> out;
+  if (!plan->optimizer || !plan->comm) return out;
+  tb::Program& P = *plan->prog;
+  struct Span {
+    char* begin;
+    int64_t bytes;
+    int writer;
+  };
+  std::vector<Span> spans;
+  for (int b : plan->optimizer->grad_buffers) {
+    const tb::Buffer& buf = P.buffers[b];
+    int writer = -1;
+    for (size_t k = 0; k < P.kernels.size(); ++k)
+      for (int w : P.kernels[k].writes)
+        if (w == b) writer = std::max(writer, (int)k);
+    spans.push_back({(char*)plan->buffer_ptr[b], buf.bytes, writer});
+  }
+  std::sort(spans.begin(), spans.end(), [](const Span& a, const Span& b) { return a.begin < b.begin; });
+  // merge neighbours (the arena packs readable values contiguously in write order)
+  std::vector<Span> merged;
+  for (auto& s : spans) {
+    if (!merged.empty()) {
+      Span& m = merged.back();
+      int64_t gap = s.begin - (m.begin + m.bytes);
+      if (gap >= 0 && gap < 256 && m.bytes < plan->bucket_bytes) {
+        m.bytes = s.begin + s.bytes - m.begin;
+        m.writer = std::max(m.writer, s.writer);
+        continue;
+      }
+    }
+    merged.push_back(s);
+  }
+  for (auto& m : merged) out.push_back({m.writer, m.begin, m.bytes});
+  return out;
+}
+
+void enqueue_program(tb_plan* plan, cudaStream_t stream) {
+  tb::Program& P = *plan->prog;
+  std::vector<Bucket> buckets = gradient_buckets(plan);
+  int64_t launches = 0;
+  size_t next_event = 0;
+  auto event = [&]() {
+    if (next_event == plan->events.size()) {
+      cudaEvent_t e;
+      check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+      plan->events.push_back(e);
+    }
+    return plan->events[next_event++];
+  };
+  bool comm_used = false;
+  for (size_t k = 0; k < P.kernels.size(); ++k) {
+    const tb::Kernel& K = P.kernels[k];
+    switch (K.type) {
+      case tb::KType::GEMM:
+        tb::launch_gemm(fp(plan, K.a_hi), fp(plan, K.a_lo), fp(plan, K.b_hi), fp(plan, K.b_lo),
+                        fp(plan, K.out), K.batch, K.m, K.n, K.kp, stream);
+        launches += 1;
+        break;
+      case tb::KType::SORT:
+        tb::launch_selection_sort(ip(plan, K.out), ip(plan, K.keys), ip(plan, K.vals),
+                                  ip(plan, K.tmp_keys), ip(plan, K.tmp_vals), ip(plan, K.counts),
+                                  ip(plan, K.rstart), ip(plan, K.rend), K.count, K.rows,
+                                  (int)K.passes, K.tiles, stream);
+        launches += 2 + 3 * K.passes;
+        break;
+      case tb::KType::FINAL:
+        tb::launch_final_sum(fp(plan, K.partial), fp(plan, K.final_out), K.final_blocks,
+                             K.final_width, stream);
+        launches += 1;
+        break;
+      default: {
+        void* args[] = {plan->kparams[k].data()};
+        check(g_driver.LaunchKernel(plan->fn[k], (unsigned)K.grid, 1, 1, (unsigned)K.block, 1, 1,
+                             (unsigned)K.smem, stream, args, nullptr),
+              "cuLaunchKernel");
+        launches += 1;
+      }
+    }
+    check(cudaGetLastError(), "kernel launch");
+    for (const Bucket& b : buckets) {
+      if (b.after_kernel != (int)k) continue;
+      cudaEvent_t e = event();
+      check(cudaEventRecord(e, stream), "cudaEventRecord");
+      check(cudaStreamWaitEvent(plan->comm_stream, e, 0), "cudaStreamWaitEvent");
+      check_nccl(nccl()->AllReduce(b.begin, b.begin, b.bytes / 4, ncclFloat32, ncclSum,
+                                   plan->comm->comm, plan->comm_stream),
+                 "ncclAllReduce");
+      comm_used = true;
+    }
+  }
+  if (comm_used) {
+    cudaEvent_t e = event();
+    check(cudaEventRecord(e, plan->comm_stream), "cudaEventRecord");
+    check(cudaStreamWaitEvent(stream, e, 0), "cudaStreamWaitEvent");
+  }
+  if (plan->optimizer) {
+    tb_optimizer* o = plan->optimizer;
+    if (o->desc.kind != TB_OPTIMIZER_SGD) {
+      tb::launch_adam_scalars(o->scalars, o->desc.beta1, o->desc.beta2, stream);
+      launches += 1;
+    }
+    float share1 = 1.0f - o->desc.beta1;
+    float share2 = 1.0f - o->desc.beta2;
+    tb::launch_optimizer(o->entries, (int)o->host_entries.size(), o->total, o->scalars,
+                         o->scalars + 4, o->desc.kind, o->desc.beta1, o->desc.beta2, share1,
+                         share2, o->desc.epsilon, o->desc.decay, o->desc.gradient_scale, stream);
+    launches += 1;
+    check(cudaGetLastError(), "optimizer launch");
+  }
+  plan->launches = launches;
+}
+
+void instantiate(tb_plan* plan) {
+  tb::Program& P = *plan->prog;
+  check(cudaGetDevice(&plan->device), "cudaGetDevice");
+  check(cudaFree(nullptr), "context init");
+  check(cudaStreamCreateWithFlags(&plan->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  check(cudaStreamCreateWithFlags(&plan->comm_stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  plan->buffer_ptr.assign(P.buffers.size(), nullptr);
+  if (P.arena_bytes > 0) check(cudaMalloc((void**)&plan->arena, P.arena_bytes), "cudaMalloc(arena)");
+  for (size_t b = 0; b < P.buffers.size(); ++b) {
+    tb::Buffer& buf = P.buffers[b];
+    const tb::Node* node = buf.node >= 0 ? &P.nodes[buf.node] : nullptr;
+    switch (buf.storage) {
+      case tb::Storage::Arena:
+        if (buf.first >= 0) plan->buffer_ptr[b] = plan->arena + buf.offset;
+        break;
+      case tb::Storage::Parameter:
+        break;
+      case tb::Storage::Input:
+      case tb::Storage::InputIndices:
+      case tb::Storage::Leaf:
+      case tb::Storage::LeafIndices: {
+        void* p = nullptr;
+        check(cudaMalloc(&p, std::max<int64_t>(buf.bytes, 16)), "cudaMalloc(source)");
+        plan->own.push_back(p);
+        plan->buffer_ptr[b] = p;
+        const void* init = nullptr;
+        if (buf.storage == tb::Storage::Leaf || buf.storage == tb::Storage::Input)
+          init = node->dense;
+        else
+          init = node->indices;
+        if (init) check(cudaMemcpy(p, init, buf.bytes, cudaMemcpyHostToDevice), "upload source");
+        else check(cudaMemset(p, 0, buf.bytes), "cudaMemset(source)");
+        if ((buf.storage == tb::Storage::Leaf || buf.storage == tb::Storage::LeafIndices) && !init)
+          throw Failure(TB_INVALID, "leaf without payload");
+        break;
+      }
+    }
+  }
+  plan->module = compile_module(P.source, plan->device);
+  plan->fn.assign(P.kernels.size(), nullptr);
+  for (size_t k = 0; k < P.kernels.size(); ++k) {
+    const tb::Kernel& K = P.kernels[k];
+    if (K.name.empty()) continue;
+    check(g_driver.ModuleGetFunction(&plan->fn[k], plan->module, K.name.c_str()), "cuModuleGetFunction");
+  }
+}
+
+void run_plan(tb_plan* plan) {
+  if (plan->graph_dirty) {
+    if (plan->graph) {
+      cudaGraphExecDestroy(plan->graph);
+      plan->graph = nullptr;
+    }
+    cudaGraph_t g;
+    check(cudaStreamBeginCapture(plan->stream, cudaStreamCaptureModeThreadLocal), "BeginCapture");
+    try {
+      enqueue_program(plan, plan->stream);
+    } catch (...) {
+      cudaStreamEndCapture(plan->stream, &g);
+      throw;
+    }
+    check(cudaStreamEndCapture(plan->stream, &g), "EndCapture");
+    check(cudaGraphInstantiate(&plan->graph, g, 0), "cudaGraphInstantiate");
+    cudaGraphDestroy(g);
+    plan->graph_dirty = false;
+  }
+  check(cudaGraphLaunch(plan->graph, plan->stream), "cudaGraphLaunch");
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* tb_last_error(void) { return g_error.c_str(); }
+
+int tb_status(char* message, size_t capacity) {
+  int s = ensure_ready();
+  std::string m;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    s = g_state;
+    m = g_status_message;
+  }
+  if (message && capacity) {
+    snprintf(message, capacity, "%s", m.c_str());
+  }
+  return s;
+}
+
+int tb_plan_compile(const tb_plan_desc* desc, tb_plan** out) {
+  return guarded([&]() {
+    auto prog = tb::lower(desc);
+    if (desc->numerics == TB_NUMERICS_EXACT && !prog->exact) {
+      g_error = "the plan holds kernels that are not bit-identical to the interpreter";
+      return (int)TB_DECLINED;
+    }
+    std::unique_ptr<tb_plan> plan(new tb_plan());
+    plan->prog = std::move(prog);
+    instantiate(plan.get());
+    *out = plan.release();
+    return (int)TB_OK;
+  });
+}
+
+void tb_plan_destroy(tb_plan* plan) {
+  if (!plan) return;
+  if (plan->stream) cudaStreamSynchronize(plan->stream);
+  delete plan;
+}
+
+int tb_plan_stats_get(const tb_plan* plan, tb_plan_stats* s) {
+  return guarded([&]() {
+    const tb::Program& P = *plan->prog;
+    s->kernels = plan->launches ? plan->launches : (int64_t)P.kernels.size();
+    s->arena_bytes = P.arena_bytes;
+    s->unplanned_bytes = P.unplanned_bytes;
+    s->fused_nodes = P.fused_nodes;
+    s->bit_identical = P.exact ? 1 : 0;
+    s->gemms = P.gemms;
+    return (int)TB_OK;
+  }, false);
+}
+
+int64_t tb_plan_describe(const tb_plan* plan, char* buffer, size_t capacity) {
+  std::ostringstream o;
+  const tb::Program& P = *plan->prog;
+  for (size_t k = 0; k < P.kernels.size(); ++k) o << k << ": " << P.kernels[k].describe << "\n";
+  o << "arena " << P.arena_bytes << " bytes (" << P.unplanned_bytes << " without reuse)\n";
+  std::string s = o.str();
+  if (buffer && capacity) snprintf(buffer, capacity, "%s", s.c_str());
+  return (int64_t)s.size() + 1;
+}
+
+int tb_params_create(const tb_plan* plan, tb_params** out) {
+  return guarded([&]() {
+    const tb::Program& P = *plan->prog;
+    std::unique_ptr<tb_params> p(new tb_params());
+    check(cudaGetDevice(&p->device), "cudaGetDevice");
+    int slots = P.parameter_slots;
+    std::vector<int64_t> offset(slots);
+    int64_t total = 0;
+    p->count.assign(slots, 0);
+    for (int s = 0; s < slots; ++s) {
+      int64_t c = 1;
+      for (auto e : P.parameter_shapes[s]) c *= e;
+      p->count[s] = c;
+      offset[s] = total;
+      total += (c + 63) / 64 * 64;
+    }
+    check(cudaMalloc(&p->base, std::max<int64_t>(total * 4, 256)), "cudaMalloc(parameters)");
+    check(cudaMemset(p->base, 0, std::max<int64_t>(total * 4, 256)), "cudaMemset(parameters)");
+    for (int s = 0; s < slots; ++s) p->slot.push_back((float*)p->base + offset[s]);
+    *out = p.release();
+    return (int)TB_OK;
+  });
+}
+
+void tb_params_destroy(tb_params* params) { delete params; }
+
+int tb_params_upload(tb_params* params, int32_t slot, const float* host, int64_t count) {
+  return guarded([&]() {
+    if (slot < 0 || slot >= (int)params->slot.size() || count != params->count[slot])
+      throw Failure(TB_INVALID, "parameter slot or size mismatch");
+    check(cudaMemcpy(params->slot[slot], host, count * 4, cudaMemcpyHostToDevice), "upload");
+    return (int)TB_OK;
+  });
+}
+
+int tb_params_download(const tb_params* params, int32_t slot, float* host, int64_t count) {
+  return guarded([&]() {
+    if (slot < 0 || slot >= (int)params->slot.size() || count != params->count[slot])
+      throw Failure(TB_INVALID, "parameter slot or size mismatch");
+    check(cudaDeviceSynchronize(), "sync");
+    check(cudaMemcpy(host, params->slot[slot], count * 4, cudaMemcpyDeviceToHost), "download");
+    return (int)TB_OK;
+  });
+}
+
+int tb_plan_run(tb_plan* plan, tb_params* params, int32_t feed_count, const tb_feed* feeds) {
+  return guarded([&]() {
+    tb::Program& P = *plan->prog;
+    bind_params(plan, params);
+    for (int32_t f = 0; f < feed_count; ++f) {
+      const tb_feed& feed = feeds[f];
+      if (feed.slot < 0 || feed.slot >= P.input_slots)
+        throw Failure(TB_INVALID, "fed slot is not an input of the plan");
+      int b = P.input_buffer[feed.slot];
+      if (b < 0) continue;  // an input the plan does not read
+      const tb::Buffer& buf = P.buffers[b];
+      const void* src = buf.storage == tb::Storage::InputIndices ? (const void*)feed.indices
+                                                                 : (const void*)feed.dense;
+      if (!src) throw Failure(TB_INVALID, "feed of the wrong payload kind");
+      check(cudaMemcpyAsync(plan->buffer_ptr[b], src, buf.bytes,
+                            feed.on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                            plan->stream),
+            "feed copy");
+    }
+    run_plan(plan);
+    return (int)TB_OK;
+  });
+}
+
+int tb_plan_synchronize(tb_plan* plan) {
+  return guarded([&]() {
+    check(cudaStreamSynchronize(plan->stream), "cudaStreamSynchronize");
+    return (int)TB_OK;
+  });
+}
+
+int tb_plan_read(tb_plan* plan, int64_t node, float* host, int64_t count) {
+  return guarded([&]() {
+    int b = readable_buffer(*plan->prog, node);
+    if (count * 4 != plan->prog->buffers[b].bytes) throw Failure(TB_INVALID, "read size mismatch");
+    check(cudaMemcpyAsync(host, plan->buffer_ptr[b], count * 4, cudaMemcpyDeviceToHost,
+                          plan->stream),
+          "read");
+    check(cudaStreamSynchronize(plan->stream), "cudaStreamSynchronize");
+    return (int)TB_OK;
+  });
+}
+
+int tb_plan_device_pointer(tb_plan* plan, int64_t node, const float** device) {
+  return guarded([&]() {
+    int b = readable_buffer(*plan->prog, node);
+    *device = (const float*)plan->buffer_ptr[b];
+    return (int)TB_OK;
+  });
+}
+
+void* tb_plan_stream(tb_plan* plan) { return plan ? (void*)plan->stream : nullptr; }
+
+int tb_optimizer_create(tb_plan* plan, tb_params* params, const tb_optimizer_desc* desc,
+                        int32_t count, const int32_t* slots, const int64_t* gradient_nodes,
+                        tb_optimizer** out) {
+  return guarded([&]() {
+    if (desc->kind < 0 || desc->kind > 2) throw Failure(TB_INVALID, "unknown optimizer kind");
+    bind_params(plan, params);
+    std::unique_ptr<tb_optimizer> o(new tb_optimizer());
+    o->plan = plan;
+    o->params = params;
+    o->desc = *desc;
+    int64_t total = 0;
+    for (int32_t i = 0; i < count; ++i) {
+      int slot = slots[i];
+      if (slot < 0 || slot >= (int)params->slot.size()) throw Failure(TB_INVALID, "bad slot");
+      int b = readable_buffer(*plan->prog, gradient_nodes[i]);
+      if (plan->prog->buffers[b].bytes != params->count[slot] * 4)
+        throw Failure(TB_INVALID, "gradient and parameter sizes differ");
+      tb::OptEntry e{};
+      e.p = params->slot[slot];
+      e.g = (const float*)plan->buffer_ptr[b];
+      e.count = params->count[slot];
+      e.start = total;
+      e.decay = plan->prog->parameter_shapes[slot].size() >= 2 ? 1 : 0;
+      o->slots.push_back(slot);
+      o->grad_buffers.push_back(b);
+      o->host_entries.push_back(e);
+      total += e.count;
+    }
+    o->total = total;
+    check(cudaMalloc((void**)&o->scalars, 8 * 4), "cudaMalloc(scalars)");
+    float init[8] = {1.0f, 1.0f, 0.0f, 0.0f, desc->learning_rate, 0, 0, 0};
+    check(cudaMemcpy(o->scalars, init, sizeof init, cudaMemcpyHostToDevice), "upload scalars");
+    if (desc->kind != TB_OPTIMIZER_SGD && total > 0) {
+      check(cudaMalloc((void**)&o->state, total * 2 * 4), "cudaMalloc(moments)");
+      check(cudaMemset(o->state, 0, total * 2 * 4), "cudaMemset(moments)");
+      for (auto& e : o->host_entries) {
+        e.m = o->state + e.start;
+        e.v = o->state + total + e.start;
+      }
+    }
+    if (!o->host_entries.empty()) {
+      check(cudaMalloc((void**)&o->entries, o->host_entries.size() * sizeof(tb::OptEntry)),
+            "cudaMalloc(entries)");
+      check(cudaMemcpy(o->entries, o->host_entries.data(),
+                       o->host_entries.size() * sizeof(tb::OptEntry), cudaMemcpyHostToDevice),
+            "upload entries");
+    }
+    *out = o.release();
+    return (int)TB_OK;
+  });
+}
+
+void tb_optimizer_destroy(tb_optimizer* o) {
+  if (!o) return;
+  if (o->plan && o->plan->optimizer == o) {
+    o->plan->optimizer = nullptr;
+    o->plan->graph_dirty = true;
+  }
+  cudaDeviceSynchronize();
+  delete o;
+}
+
+int tb_optimizer_set_learning_rate(tb_optimizer* o, float lr) {
+  return guarded([&]() {
+    o->desc.learning_rate = lr;
+    check(cudaMemcpyAsync(o->scalars + 4, &o->desc.learning_rate, 4, cudaMemcpyHostToDevice,
+                          o->plan->stream),
+          "upload learning rate");
+    check(cudaStreamSynchronize(o->plan->stream), "sync");
+    return (int)TB_OK;
+  });
+}
+
+int tb_plan_attach_optimizer(tb_plan* plan, tb_optimizer* o) {
+  return guarded([&]() {
+    if (o && o->plan != plan) throw Failure(TB_INVALID, "optimizer belongs to another plan");
+    plan->optimizer = o;
+    plan->graph_dirty = true;
+    return (int)TB_OK;
+  });
+}
+
+int tb_optimizer_state(const tb_optimizer* o, int32_t slot, float* first, float* second,
+                       int64_t count) {
+  return guarded([&]() {
+    if (!o->state) throw Failure(TB_INVALID, "optimizer has no moments");
+    for (size_t i = 0; i < o->slots.size(); ++i) {
+      if (o->slots[i] != slot) continue;
+      const tb::OptEntry& e = o->host_entries[i];
+      if (e.count != count) throw Failure(TB_INVALID, "size mismatch");
+      check(cudaDeviceSynchronize(), "sync");
+      check(cudaMemcpy(first, e.m, count * 4, cudaMemcpyDeviceToHost), "download");
+      check(cudaMemcpy(second, e.v, count * 4, cudaMemcpyDeviceToHost), "download");
+      return (int)TB_OK;
+    }
+    throw Failure(TB_INVALID, "slot not bound to the optimizer");
+  });
+}
+
+int tb_comm_unique_id(uint8_t id[128]) {
+  return guarded([&]() {
+    Nccl* n = nccl();
+    if (!n) throw Failure(TB_INITIALIZATION, "NCCL is not loadable");
+    ncclUniqueId u;
+    check_nccl(n->GetUniqueId(&u), "ncclGetUniqueId");
+    memcpy(id, u.internal, 128);
+    return (int)TB_OK;
+  });
+}
+
+int tb_comm_init(int32_t rank, int32_t world, const uint8_t id[128], tb_comm** out) {
+  return guarded([&]() {
+    Nccl* n = nccl();
+    if (!n) throw Failure(TB_INITIALIZATION, "NCCL is not loadable");
+    std::unique_ptr<tb_comm> c(new tb_comm());
+    ncclUniqueId u;
+    memcpy(u.internal, id, 128);
+    check_nccl(n->CommInitRank(&c->comm, world, u, rank), "ncclCommInitRank");
+    c->rank = rank;
+    c->world = world;
+    *out = c.release();
+    return (int)TB_OK;
+  });
+}
+
+void tb_comm_destroy(tb_comm* comm) { delete comm; }
+
+int tb_plan_attach_comm(tb_plan* plan, tb_comm* comm, int64_t bucket_bytes) {
+  return guarded([&]() {
+    plan->comm = comm;
+    plan->bucket_bytes = bucket_bytes > 0 ? bucket_bytes : (int64_t)32 << 20;
+    plan->graph_dirty = true;
+    return (int)TB_OK;
+  });
+}
+
+int tb_comm_allreduce(tb_comm* comm, float* device, int64_t count, void* stream) {
+  return guarded([&]() {
+    check_nccl(nccl()->AllReduce(device, device, count, ncclFloat32, ncclSum, comm->comm,
+                                 (cudaStream_t)stream),
+               "ncclAllReduce");
+    return (int)TB_OK;
+  });
+}
+
+// ---- internal hooks for CPU-side tests (not part of the public ABI): lowering
+// and NVRTC compilation need no device.
+int64_t tbx_lower_describe(const tb_plan_desc* desc, char* buffer, size_t capacity, int with_source) {
+  try {
+    auto prog = tb::lower(desc);
+    std::ostringstream o;
+    for (size_t k = 0; k < prog->kernels.size(); ++k) o << k << ": " << prog->kernels[k].describe << "\n";
+    o << "arena " << prog->arena_bytes << " bytes (" << prog->unplanned_bytes << " without reuse)\n";
+    o << "exact " << (prog->exact ? 1 : 0) << " fused " << prog->fused_nodes << "\n";
+    if (with_source) o << prog->source;
+    std::string s = o.str();
+    if (buffer && capacity) snprintf(buffer, capacity, "%s", s.c_str());
+    return (int64_t)s.size() + 1;
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return -1;
+  }
+}
+
+int tbx_nvrtc_check(const tb_plan_desc* desc) {
+  try {
+    auto prog = tb::lower(desc);
+    nvrtcProgram p;
+    if (nvrtcCreateProgram(&p, prog->source.c_str(), "check.cu", 0, nullptr, nullptr) != NVRTC_SUCCESS)
+      return TB_RUNTIME;
+    const char* opts[] = {"-arch=sm_100a", "--fmad=false", "-prec-div=true", "-prec-sqrt=true",
+                          "-ftz=false", "-std=c++17", "-default-device"};
+    nvrtcResult r = nvrtcCompileProgram(p, 7, opts);
+    if (r != NVRTC_SUCCESS) {
+      size_t n = 0;
+      nvrtcGetProgramLogSize(p, &n);
+      std::string log(n, '\0');
+      nvrtcGetProgramLog(p, &log[0]);
+      g_error = log.substr(0, 4000);
+    }
+    nvrtcDestroyProgram(&p);
+    return r == NVRTC_SUCCESS ? TB_OK : TB_INVALID;
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return TB_INVALID;
+  }
+}
+
+// ---- per-task faces
+int tb_gemm_f32(const float* a, int64_t a_len, const int64_t a_strides[2], const float* b,
+                int64_t b_len, const int64_t b_strides[2], int64_t m, int64_t k, int64_t n,
+                float* out);
+int tb_map_f32(int32_t op, const float* in, int64_t count, float* out);
+
+}  // extern "C"

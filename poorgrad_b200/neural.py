@@ -1,0 +1,149 @@
+"""Neural compositions recorded on a :class:`~poorgrad_b200.graph.Tape`: the
+subset of topos `neural/` the training configs use.  Each records exactly the
+formula of its reference, so the plan columns match what topos would compile.
+
+- :class:`Linear` -- `neural/linear.rs:94-105`: ``x.matmul(W) + b.broadcast_along(0, .)``
+- :class:`LayerNorm` -- `neural/layer_norm.rs:100-132`
+- :func:`gelu` -- the tanh form of `examples/gpt2/model.rs:81-97`
+- :func:`cross_entropy` -- `neural/loss.rs:44-63`
+- initializers -- `neural/init.rs:50-216` (splitmix64 streams)
+"""
+from __future__ import annotations
+
+import math
+from typing import List
+
+import numpy as np
+
+from .graph import Dense, Tape, Value, counted, filled
+
+GOLDEN = np.uint64(0x9E3779B97F4A7C15)
+MIX1 = np.uint64(0xBF58476D1CE4E5B9)
+MIX2 = np.uint64(0x94D049BB133111EB)
+
+
+class Stream:
+    """A splitmix64 state advanced once per draw (`init.rs:50-61`)."""
+
+    def __init__(self, seed: int):
+        self.state = np.uint64(seed)
+
+    def raw(self, n: int) -> np.ndarray:
+        with np.errstate(over="ignore"):
+            steps = np.arange(1, n + 1, dtype=np.uint64)
+            states = self.state + steps * GOLDEN
+            self.state = self.state + np.uint64(n) * GOLDEN
+            z = states
+            z = (z ^ (z >> np.uint64(30))) * MIX1
+            z = (z ^ (z >> np.uint64(27))) * MIX2
+            return z ^ (z >> np.uint64(31))
+
+    def unit(self, n: int) -> np.ndarray:
+        """`unit`: the top 53 bits over 2^53, in f64."""
+        return (self.raw(n) >> np.uint64(11)).astype(np.float64) / float(1 << 53)
+
+    def standard_normal(self, n: int) -> np.ndarray:
+        """Box-Muller with two draws per value (`init.rs:67-71`)."""
+        u = self.unit(2 * n).reshape(n, 2)
+        radius = np.sqrt(-2.0 * np.log(1.0 - u[:, 0]))
+        angle = 2.0 * math.pi * u[:, 1]
+        return radius * np.cos(angle)
+
+
+def uniform(seed: int, scale: float):
+    """`init::uniform`: ``(2u - 1) * scale``, cast to f32 once."""
+    stream = Stream(seed)
+
+    def draw(shape, override=None) -> np.ndarray:
+        n = int(np.prod(shape)) if len(shape) else 1
+        s = scale if override is None else override
+        return ((stream.unit(n) * 2.0 - 1.0) * s).astype(np.float32).reshape(shape)
+    return draw
+
+
+def normal(seed: int, deviation: float):
+    """`init::normal`: ``standard_normal * deviation``."""
+    stream = Stream(seed)
+
+    def draw(shape) -> np.ndarray:
+        n = int(np.prod(shape)) if len(shape) else 1
+        return (stream.standard_normal(n) * deviation).astype(np.float32).reshape(shape)
+    return draw
+
+
+def unit_uniform(seed: int):
+    """``U[0, 1)`` from the same stream (`unit`)."""
+    stream = Stream(seed)
+
+    def draw(shape) -> np.ndarray:
+        n = int(np.prod(shape)) if len(shape) else 1
+        return stream.unit(n).astype(np.float32).reshape(shape)
+    return draw
+
+
+def integers(seed: int, high: int, n: int) -> np.ndarray:
+    """Uniform integers ``0..high`` from one stream: ``floor(unit * high)``."""
+    u = Stream(seed).unit(n)
+    return np.minimum((u * high).astype(np.int64), high - 1)
+
+
+class Linear:
+    def __init__(self, tape: Tape, weights: np.ndarray, bias: np.ndarray):
+        assert weights.ndim == 2 and bias.ndim == 1 and weights.shape[1] == bias.shape[0]
+        self.weights = tape.parameter(Dense(weights.shape, weights))
+        self.bias = tape.parameter(Dense(bias.shape, bias))
+
+    def parameters(self) -> List[Value]:
+        return [self.weights, self.bias]
+
+    def express(self, x: Value) -> Value:
+        product = x.matmul(self.weights)
+        return product + self.bias.broadcast_along(0, product)
+
+
+class LayerNorm:
+    def __init__(self, tape: Tape, features: int, epsilon: float = 1e-5):
+        self.scale = tape.parameter(Dense((features,), np.ones(features, np.float32)))
+        self.shift = tape.parameter(Dense((features,), np.zeros(features, np.float32)))
+        self.epsilon = tape.leaf(filled((), epsilon))
+
+    def parameters(self) -> List[Value]:
+        return [self.scale, self.shift]
+
+    def express(self, x: Value) -> Value:
+        assert len(x.shape) == 2
+        mean = x.mean_along(1)
+        centered = x - mean.broadcast_along(1, x)
+        variance = (centered * centered).mean_along(1)
+        deviation = (variance + self.epsilon.broadcast_like(variance)).sqrt()
+        normalized = centered / deviation.broadcast_along(1, x)
+        return normalized * self.scale.broadcast_along(0, x) + self.shift.broadcast_along(0, x)
+
+
+class Gelu:
+    """``0.5 x (1 + tanh(0.7978846 (x + 0.044715 x^3)))`` with scalar leaves."""
+
+    def __init__(self, tape: Tape):
+        self.half = tape.leaf(filled((), 0.5))
+        self.one = tape.leaf(filled((), 1.0))
+        self.root = tape.leaf(filled((), 0.7978846))
+        self.coefficient = tape.leaf(filled((), 0.044715))
+
+    def express(self, x: Value) -> Value:
+        cubic = x * x * x * self.coefficient.broadcast_like(x)
+        inner = ((x + cubic) * self.root.broadcast_like(x)).tanh()
+        return x * (inner + self.one.broadcast_like(inner)) * self.half.broadcast_like(x)
+
+
+def cross_entropy(logits: Value, targets: Value) -> Value:
+    """`neural/loss.rs:44-63`: ``(Σ(Σ_1 t · lse(logits)) - Σ(t·logits)) / Σ t``."""
+    assert len(logits.shape) == 2 and targets.shape == logits.shape
+    normalizers = (targets.sum_along(1) * logits.logsumexp(1)).sum()
+    alignment = (targets * logits).sum()
+    return (normalizers - alignment) / targets.sum()
+
+
+def sgd_reference(params, grads, lr):
+    """Host f32 restatement of `Sgd::step` for checks: ``p - g·lr``."""
+    lr = np.float32(lr)
+    return [(p - g * lr).astype(np.float32) for p, g in zip(params, grads)]

@@ -1,0 +1,311 @@
+"""Parity of the B200 device program with the CPU oracle, through the C ABI.
+
+Bars (stated per assertion):
+  * bit-exact for elementwise groups without transcendentals, views, gather,
+    scatter-add and pad/concat;
+  * transcendental groups (tanh/exp/ln/pow via CUDA's libm against glibc):
+    relative error <= 4e-6 (a few ulp);
+  * tree reductions: |dev - ref| <= 1e-6 * sum|terms| + tiny;
+  * GEMM (3xTF32): |dev - ref| <= 8 eps sqrt(k) (1 + |ref|)
+    (backend/cuda/tests/cuda_tests.rs:141-150).
+"""
+import math
+
+import numpy as np
+import pytest
+
+import oracle
+from poorgrad_b200 import backend, configs, neural
+from poorgrad_b200.graph import Dense, Tape, concat, filled, selection, tensor
+from poorgrad_b200.plan import Request
+
+pytestmark = pytest.mark.gpu
+EPS = np.finfo(np.float32).eps
+
+
+def both(tape, roots, feeds=None, params=None):
+    net = tape.into_network()
+    cols = net.compile(Request(roots))
+    p = net.parameters() if params is None else params
+    ref = oracle.run(cols, p, feeds)
+    plan = backend.DevicePlan(cols)
+    dp = backend.DeviceParameters(plan, p)
+    plan.forward(dp, feeds, sync=True)
+    dev = {i: plan.of(i) for i in ref}
+    return ref, dev, plan
+
+
+def rnd(shape, seed, lo=-1.0, hi=1.0):
+    rng = np.random.default_rng(seed)
+    return rng.uniform(lo, hi, size=shape).astype(np.float32)
+
+
+def assert_exact(a, b):
+    assert a.shape == b.shape
+    assert np.array_equal(a, b, equal_nan=True), f"max diff {np.nanmax(np.abs(a - b))}"
+
+
+def assert_rel(dev, ref, rtol=4e-6, atol=1e-7):
+    np.testing.assert_allclose(dev, ref, rtol=rtol, atol=atol)
+
+
+def assert_gemm(dev, ref, k):
+    tol = 8 * EPS * math.sqrt(k) * (1 + np.abs(ref))
+    err = np.abs(dev - ref)
+    assert np.all(err <= tol), f"worst ratio {np.max(err / tol)}"
+
+
+# ------------------------------------------------------------ elementwise
+@pytest.mark.parametrize("shape", [(7,), (3, 5), (64, 64), (33, 130), (2, 3, 8)])
+def test_arithmetic_group_is_bit_exact(device, shape):
+    t = Tape()
+    x = t.parameter(tensor(shape, rnd(shape, 1)))
+    y = t.parameter(tensor(shape, rnd(shape, 2, 0.5, 2.0)))
+    z = ((x * y - x / y) + (-x)).maximum(y * x) + x.relu() * x.step(y)
+    s = z.sqrt() if False else z
+    loss = (s * s).sum()
+    gx, gy = t.differentiate(loss, [x, y])
+    ref, dev, plan = both(t, [s, gx, gy])
+    assert_exact(dev[s.index], ref[s.index])
+    assert_exact(dev[gx.index], ref[gx.index])
+    assert_exact(dev[gy.index], ref[gy.index])
+
+
+@pytest.mark.parametrize("op", ["tanh", "exp", "ln", "sqrt"])
+def test_transcendental_maps(device, op):
+    shape = (129, 67)
+    t = Tape()
+    lo = 0.1 if op in ("ln", "sqrt") else -4.0
+    x = t.parameter(tensor(shape, rnd(shape, 3, lo, 4.0)))
+    y = getattr(x, op)()
+    loss = y.sum()
+    (g,) = t.differentiate(loss, [x])
+    ref, dev, _ = both(t, [y, g])
+    if op == "sqrt":
+        assert_exact(dev[y.index], ref[y.index])
+    else:
+        assert_rel(dev[y.index], ref[y.index])
+    assert_rel(dev[g.index], ref[g.index], rtol=1e-5)
+
+
+def test_powf_forward_and_gradients(device):
+    shape = (31, 17)
+    t = Tape()
+    b = t.parameter(tensor(shape, rnd(shape, 4, 0.5, 2.0)))
+    e = t.parameter(tensor(shape, rnd(shape, 5, -2.0, 2.0)))
+    y = b.powf(e)
+    gb, ge = t.differentiate(y.sum(), [b, e])
+    ref, dev, _ = both(t, [y, gb, ge])
+    for n in (y, gb, ge):
+        assert_rel(dev[n.index], ref[n.index], rtol=2e-5)
+
+
+# ------------------------------------------------------------ views and indexing
+def test_views_pad_concat_are_bit_exact(device):
+    t = Tape()
+    x = t.parameter(tensor((4, 6), rnd((4, 6), 6)))
+    y = t.parameter(tensor((6, 4), rnd((6, 4), 7)))
+    a = x.transpose() * y
+    b = x.narrow(1, 2, 3).pad(1, 1, 5)
+    c = concat([x.narrow(1, 0, 2), y.transpose().narrow(1, 1, 3)], 1)
+    d = x.reshape((2, 12)).permute((1, 0)).reshape((6, 4)) + y
+    e = x.unfold(1, 3, 2, 1)
+    loss = a.sum() + b.sum() + c.sum() + d.sum() + (e * e).sum()
+    gx, gy = t.differentiate(loss, [x, y])
+    ref, dev, _ = both(t, [a, b, c, d, e, gx, gy])
+    for n in (a, b, c, d, e, gx, gy):
+        if n in (gx, gy):
+            assert_rel(dev[n.index], ref[n.index], rtol=1e-6, atol=1e-6)
+        else:
+            assert_exact(dev[n.index], ref[n.index])
+
+
+def test_gather_and_scatter_known_rows(device):
+    # payload/tests/tensor_tests.rs:995-1016 on the device
+    t = Tape()
+    table = t.parameter(tensor([3, 2], [1, 2, 3, 4, 5, 6]))
+    sel = t.input(selection([0, 2, 0], 3))
+    gathered = table.gather(sel)
+    ones = t.leaf(filled([3, 2], 1.0))
+    scattered = ones.scatter(sel, 3)
+    ref, dev, _ = both(t, [gathered, scattered])
+    assert dev[gathered.index].reshape(-1).tolist() == [1, 2, 5, 6, 1, 2]
+    assert dev[scattered.index].reshape(-1).tolist() == [2, 2, 0, 0, 1, 1]
+
+
+@pytest.mark.parametrize("count,vocab,width", [(1000, 27, 64), (4097, 300, 5), (20000, 3, 7)])
+def test_scatter_add_is_serial_order_exact(device, count, vocab, width):
+    rng = np.random.default_rng(count)
+    idx = rng.integers(0, vocab, count)
+    g = rng.standard_normal((count, width)).astype(np.float32)
+    t = Tape()
+    gp = t.parameter(tensor(g.shape, g))
+    sel = t.input(selection(idx, vocab))
+    out = gp.scatter(sel, vocab)
+    ref, dev, _ = both(t, [out])
+    assert_exact(dev[out.index], ref[out.index])
+
+
+# ------------------------------------------------------------ reductions and row ops
+@pytest.mark.parametrize("shape", [(5, 7), (64, 8192), (300, 27), (2, 3, 129)])
+def test_reductions(device, shape):
+    t = Tape()
+    x = t.parameter(tensor(shape, rnd(shape, 8)))
+    r = len(shape)
+    rows = x.sum_along(r - 1)
+    cols = x.sum_along(0)
+    total = x.sum()
+    lse = x.logsumexp(r - 1)
+    ls = x.log_softmax(r - 1)
+    ref, dev, _ = both(t, [rows, cols, total, lse, ls])
+    mag = np.abs(ref[ls.index]).max() + 1
+    for n in (rows, cols, total):
+        np.testing.assert_allclose(dev[n.index], ref[n.index], rtol=1e-5,
+                                   atol=1e-6 * shape[-1] * 2)
+    assert_rel(dev[lse.index], ref[lse.index], rtol=1e-5, atol=1e-6)
+    assert_rel(dev[ls.index], ref[ls.index], rtol=1e-5, atol=1e-6 * mag)
+
+
+def test_layer_norm_forward_and_gradients(device):
+    t = Tape()
+    x = t.parameter(tensor((40, 96), rnd((40, 96), 9, -3, 3)))
+    ln = neural.LayerNorm(t, 96)
+    y = ln.express(x)
+    w = t.leaf(tensor((40, 96), rnd((40, 96), 10)))
+    loss = (y * w).sum()
+    grads = t.differentiate(loss, [x] + ln.parameters())
+    ref, dev, _ = both(t, [y] + grads)
+    for n in [y] + grads:
+        np.testing.assert_allclose(dev[n.index], ref[n.index], rtol=2e-4, atol=2e-5)
+
+
+# ------------------------------------------------------------ GEMM
+GRID = [(2, 3, 4), (5, 7, 3), (17, 33, 9), (64, 64, 64), (2, 64, 128), (129, 65, 257)]
+
+
+@pytest.mark.parametrize("m,k,n", GRID)
+@pytest.mark.parametrize("form", ["contiguous", "transposed", "narrowed"])
+def test_gemm_shape_grid(device, m, k, n, form):
+    # backend/cuda/tests/cuda_tests.rs:54-201: shape grid x stride forms
+    t = Tape()
+    if form == "contiguous":
+        a = t.parameter(tensor((m, k), rnd((m, k), m)))
+        b = t.parameter(tensor((k, n), rnd((k, n), n)))
+        A, B = a, b
+    elif form == "transposed":
+        a = t.parameter(tensor((k, m), rnd((k, m), m)))
+        b = t.parameter(tensor((n, k), rnd((n, k), n)))
+        A, B = a.transpose(), b.transpose()
+    else:
+        a = t.parameter(tensor((m, k + 3), rnd((m, k + 3), m)))
+        b = t.parameter(tensor((k, n + 2), rnd((k, n + 2), n)))
+        A, B = a.narrow(1, 2, k), b.narrow(1, 1, n)
+    c = A.matmul(B)
+    ref, dev, _ = both(t, [c])
+    assert_gemm(dev[c.index], ref[c.index], k)
+
+
+def test_batched_gemm_and_gradients(device):
+    t = Tape()
+    a = t.parameter(tensor((3, 2, 20, 12), rnd((3, 2, 20, 12), 11)))
+    b = t.parameter(tensor((3, 2, 12, 9), rnd((3, 2, 12, 9), 12)))
+    c = a.matmul(b)
+    ga, gb = t.differentiate((c * c).sum(), [a, b])
+    ref, dev, _ = both(t, [c, ga, gb])
+    assert_gemm(dev[c.index], ref[c.index], 12)
+    np.testing.assert_allclose(dev[ga.index], ref[ga.index], rtol=1e-5, atol=1e-4)
+    np.testing.assert_allclose(dev[gb.index], ref[gb.index], rtol=1e-5, atol=1e-4)
+
+
+def test_repeated_runs_are_bitwise_identical(device):
+    # backend/cuda/tests/cuda_tests.rs:241-257
+    w = configs.fused(rows=96, cols=256)
+    plan = backend.DevicePlan(w.columns)
+    dp = backend.DeviceParameters(plan, w.network.parameters())
+    outs = []
+    for _ in range(3):
+        plan.forward(dp, sync=True)
+        outs.append([plan.of(g).copy() for g in w.grads])
+    for o in outs[1:]:
+        for x, y in zip(outs[0], o):
+            assert x.tobytes() == y.tobytes()
+
+
+# ------------------------------------------------------------ configs at test sizes
+def _config_parity(w, feeds, rtol, atol):
+    params = w.network.parameters()
+    ref = oracle.run(w.columns, params, feeds)
+    plan = backend.DevicePlan(w.columns)
+    dp = backend.DeviceParameters(plan, params)
+    plan.forward(dp, feeds, sync=True)
+    for i, r in ref.items():
+        d = plan.of(i)
+        scale = np.abs(r).max() + 1e-30
+        np.testing.assert_allclose(d, r, rtol=rtol, atol=atol * scale)
+    return plan, dp
+
+
+def test_c2_fused_microbench_small(device):
+    w = configs.fused(rows=64, cols=520)
+    _config_parity(w, {}, rtol=2e-5, atol=1e-5)
+
+
+def test_c1_mlp_step_matches_oracle(device):
+    w = configs.mlp(batch=128)
+    feeds = w.feeds(0)
+    _config_parity(w, feeds, rtol=1e-4, atol=2e-5)
+
+
+def test_c4_char_mlp_small(device):
+    w = configs.char_mlp(batch=256)
+    _config_parity(w, w.feeds(0), rtol=1e-3, atol=1e-4)
+
+
+def test_c5_gpt2_tiny(device):
+    w = configs.gpt2(batch=2, seq=16, layers=2, d=32, heads=4, vocab=50, mlp=64)
+    _config_parity(w, w.feeds(0), rtol=1e-3, atol=1e-4)
+
+
+def test_sgd_step_matches_the_reference_rule(device):
+    w = configs.mlp(batch=128)
+    feeds = w.feeds(0)
+    params = w.network.parameters()
+    ref = oracle.run(w.columns, params, feeds)
+    plan = backend.DevicePlan(w.columns)
+    dp = backend.DeviceParameters(plan, params)
+    # first run without the optimizer to read this step's gradients
+    plan.forward(dp, feeds, sync=True)
+    grads = [plan.of(g) for g in w.grads]
+    opt = backend.Optimizer(plan, dp, backend.SGD, zip(w.params, w.grads), 0.1)
+    plan.forward(dp, feeds, sync=True)
+    for p, g, sym in zip(params, grads, w.params):
+        slot = w.columns.nodes[sym.index].slot
+        expect = (p.reshape(g.shape) - g * np.float32(0.1)).astype(np.float32)
+        assert_exact(dp.download(slot).reshape(g.shape), expect)
+
+
+def test_adam_and_adamw_steps_match_the_reference_rule(device):
+    w = configs.char_mlp(batch=128)
+    feeds = w.feeds(0)
+    params = w.network.parameters()
+    for kind in (backend.ADAM, backend.ADAMW):
+        plan = backend.DevicePlan(w.columns)
+        dp = backend.DeviceParameters(plan, params)
+        plan.forward(dp, feeds, sync=True)
+        grads = [plan.of(g) for g in w.grads]
+        opt = backend.Optimizer(plan, dp, kind, zip(w.params, w.grads), 1e-3, 0.9, 0.999, 1e-8,
+                                decay=0.1)
+        plan.forward(dp, feeds, sync=True)
+        b1, b2, eps, lr, dec = (np.float32(v) for v in (0.9, 0.999, 1e-8, 1e-3, 0.1))
+        one = np.float32(1)
+        for p, g, sym in zip(params, grads, w.params):
+            slot = w.columns.nodes[sym.index].slot
+            p = p.reshape(g.shape)
+            m = np.float32(0) * b1 + g * (one - b1)
+            v = np.float32(0) * b2 + (g * g) * (one - b2)
+            c1, c2 = one - b1, one - b2
+            d = (m / c1) / (np.sqrt(v / c2) + eps)
+            stepped = p - d * lr
+            if kind == backend.ADAMW and g.ndim >= 2:
+                stepped = stepped - (p * dec) * lr
+            assert_exact(dp.download(slot).reshape(g.shape), stepped.astype(np.float32))

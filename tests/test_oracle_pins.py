@@ -1,0 +1,186 @@
+"""Pins the CPU oracle (and the host graph/plan mirror) against the known
+answers of the reference's own tests.  The reference is Rust and cannot be
+built here, so these assertions -- restated from its test files, cited per
+test -- are what anchor the oracle's parity."""
+import math
+import struct
+
+import numpy as np
+import pytest
+
+import oracle
+from poorgrad_b200 import neural
+from poorgrad_b200.graph import Tape, filled, selection, tensor
+from poorgrad_b200.plan import Request
+
+
+def run(tape, roots, feeds=None):
+    net = tape.into_network()
+    cols = net.compile(Request(roots))
+    return oracle.run(cols, net.parameters(), feeds)
+
+
+def test_sigmoid_composition_value_and_gradient(built):
+    # engine/tests/run_tests.rs:343-355: sigmoid(0) = 0.5, its derivative 0.25
+    t = Tape()
+    x = t.parameter(tensor([], [0.0]))
+    one = t.leaf(filled([], 1.0))
+    s = one / (one + (-x).exp())
+    (g,) = t.differentiate(s, [x])
+    out = run(t, [s, g])
+    assert out[s.index] == 0.5 and out[g.index] == 0.25
+
+
+def test_gather_and_scatter_known_rows(built):
+    # payload/tests/tensor_tests.rs:995-1016
+    t = Tape()
+    table = t.leaf(tensor([3, 2], [1, 2, 3, 4, 5, 6]))
+    sel = t.leaf(selection([0, 2, 0], 3))
+    gathered = table.gather(sel)
+    ones = t.leaf(filled([3, 2], 1.0))
+    scattered = ones.scatter(sel, 3)
+    out = run(t, [gathered, scattered])
+    assert out[gathered.index].reshape(-1).tolist() == [1, 2, 5, 6, 1, 2]
+    assert out[scattered.index].reshape(-1).tolist() == [2, 2, 0, 0, 1, 1]
+
+
+def test_matmul_transpose_sum_broadcast(built):
+    # payload/tests/tensor_tests.rs:232-250
+    t = Tape()
+    m = t.leaf(tensor([2, 2], [1, 2, 3, 4]))
+    c = t.leaf(tensor([2, 1], [5, 6]))
+    product = m.matmul(c)
+    tr = m.transpose()
+    total = m.sum()
+    spread = total.broadcast_like(c)
+    out = run(t, [product, tr, total, spread])
+    assert out[product.index].reshape(-1).tolist() == [17, 39]
+    assert out[tr.index].reshape(-1).tolist() == [1, 3, 2, 4]
+    assert out[total.index] == 10
+    assert out[spread.index].reshape(-1).tolist() == [10, 10]
+
+
+def test_matmul_gradients_through_transposed_operands(built):
+    # payload/tests/tensor_tests.rs:269-288
+    t = Tape()
+    a = t.parameter(tensor([2, 2], [1, 2, 3, 4]))
+    b = t.parameter(tensor([2, 1], [5, 6]))
+    loss = a.matmul(b).sum()
+    ga, gb = t.differentiate(loss, [a, b])
+    out = run(t, [loss, ga, gb])
+    assert out[loss.index] == 56
+    assert out[ga.index].reshape(-1).tolist() == [5, 6, 5, 6]
+    assert out[gb.index].reshape(-1).tolist() == [4, 6]
+
+
+def test_negative_zero_terms_keep_their_sign(built):
+    # payload/tests/gemm_tests.rs:130-139
+    t = Tape()
+    left = t.leaf(tensor([1, 2], [-0.0, 0.0]))
+    right = t.leaf(tensor([2, 1], [0.0, -0.0]))
+    p = left.matmul(right)
+    out = run(t, [p])
+    assert math.copysign(1.0, float(out[p.index].reshape(-1)[0])) == -1.0
+
+
+def test_product_matches_a_naive_in_order_loop_bitwise(built):
+    # engine/tests/plan_tests.rs:542-591: 32x32x32 f32 product, serial k
+    rng = np.random.default_rng(0)
+    a = rng.standard_normal((32, 32)).astype(np.float32)
+    b = rng.standard_normal((32, 32)).astype(np.float32)
+    t = Tape()
+    p = t.leaf(tensor(a.shape, a)).matmul(t.leaf(tensor(b.shape, b)))
+    out = run(t, [p])[p.index]
+    ref = a[:, 0:1] * b[0:1, :]
+    for k in range(1, 32):
+        ref = ref + a[:, k:k + 1] * b[k:k + 1, :]
+    assert out.tobytes() == ref.astype(np.float32).tobytes()
+
+
+def test_log_softmax_rows_and_gradient(built):
+    # payload/tests/tensor_tests.rs:1119-1152 (f64 there; f32 tolerance here)
+    t = Tape()
+    logits = t.leaf(tensor([2, 2], [0, 0, 1, 3]))
+    lp = logits.log_softmax(1)
+    out = run(t, [lp])[lp.index]
+    assert np.allclose(np.exp(out).sum(axis=1), 1.0, atol=1e-6)
+    t = Tape()
+    x = t.parameter(tensor([1, 2], [0.0, math.log(3.0)]))
+    loss = x.log_softmax(1).sum()
+    (g,) = t.differentiate(loss, [x])
+    out = run(t, [g])[g.index].reshape(-1)
+    assert np.allclose(out, [0.5, -0.5], atol=1e-6)
+
+
+def test_relu_masks_gradients_by_sign(built):
+    # payload/tests/tensor_tests.rs:1162-1178
+    t = Tape()
+    x = t.parameter(tensor([4], [-2.0, -0.5, 0.0, 3.0]))
+    a = x.relu()
+    loss = a.sum()
+    (g,) = t.differentiate(loss, [x])
+    out = run(t, [a, g])
+    assert out[a.index].tolist() == [0, 0, 0, 3]
+    assert out[g.index].tolist() == [0, 0, 1, 1]
+
+
+def test_cross_entropy_gradient_is_probabilities_minus_targets(built):
+    # neural/tests/loss_tests.rs:39-56
+    t = Tape()
+    logits = t.parameter(tensor([2, 2], [0.0, math.log(3.0), 0.0, 0.0]))
+    targets = t.input(selection([0, 1], 2))
+    loss = neural.cross_entropy(logits, targets)
+    (g,) = t.differentiate(loss, [logits])
+    out = run(t, [g])[g.index].reshape(-1)
+    assert np.allclose(out, [-0.375, 0.375, 0.25, -0.25], atol=1e-6)
+
+
+def test_cross_entropy_of_uniform_logits_is_log_classes(built):
+    # neural/tests/loss_tests.rs:6-19
+    t = Tape()
+    logits = t.leaf(filled([2, 3], 0.0))
+    targets = t.input(selection([0, 2], 3))
+    loss = neural.cross_entropy(logits, targets)
+    out = run(t, [loss])[loss.index]
+    assert abs(float(out) - math.log(3.0)) < 1e-6
+
+
+def test_extreme_finite_logits_keep_the_f32_loss_finite(built):
+    # neural/tests/loss_tests.rs:124-133
+    t = Tape()
+    logits = t.leaf(tensor([1, 2], [-3.0e38, 3.0e38]))
+    targets = t.input(selection([1], 2))
+    loss = neural.cross_entropy(logits, targets)
+    assert run(t, [loss])[loss.index] == 0.0
+
+
+def _bits32(x):
+    return [struct.unpack("<I", struct.pack("<f", float(v)))[0] for v in np.asarray(x).reshape(-1)]
+
+
+def _f32_of(bits64):
+    return [struct.unpack("<I", struct.pack("<f", struct.unpack("<d", struct.pack("<Q", b))[0]))[0]
+            for b in bits64]
+
+
+def test_seeded_streams_are_pinned(built):
+    # neural/tests/init_tests.rs:81-134: the f32 path is the f64 stream
+    # rounded once per element
+    uni = [0xbfcc341e1ba6cdf8, 0xbfeeecf0ca02f0e8, 0x3fe9a610202eac4a, 0x3fc53aeb70673e28]
+    nor = [0x3fffa194ec47d228, 0xc00dd3fde5949e97, 0x3f800ea29c8645d7, 0xbff0efc91ba890b4]
+    assert _bits32(neural.uniform(7, 1.0)((4,))) == _f32_of(uni)
+    assert _bits32(neural.normal(7, 2.0)((4,))) == _f32_of(nor)
+
+
+def test_plan_columns_release_like_the_reference(built):
+    # engine/tests/plan_tests.rs:133-150 (liveness diamond): a value with two
+    # consumers is released by the later one; roots are never released
+    t = Tape()
+    x = t.parameter(tensor([2], [1.0, 2.0]))
+    a = x.exp()
+    b = a * a
+    c = a + b
+    net = t.into_network()
+    cols = net.compile(Request([c]))
+    assert a.index in cols.releases[c.index]
+    assert all(c.index not in r for r in cols.releases)
