@@ -147,8 +147,8 @@ class Feeds:
                     data = np.ascontiguousarray(payload, dtype=np.float32).reshape(-1)
                     self._keep.append(data)
                     rec.dense = fptr(data)
-            elif isinstance(payload, tuple) and payload[0] == "device":
-                rec.on_device = 1
+            elif isinstance(payload, tuple) and payload[0] in ("device", "host"):
+                rec.on_device = 1 if payload[0] == "device" else 0
                 if payload[2] == "indices":
                     rec.indices = C.cast(C.c_void_p(payload[1]), C.POINTER(C.c_int32))
                 else:

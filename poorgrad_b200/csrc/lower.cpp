@@ -949,6 +949,14 @@ class Emitter {
       memo.back()[k] = v;
       return v;
     }
+    if (f.kind == Kind::Layout && !f.materialized && f.owner >= 0 && f.owner != n &&
+        member_of.count(f.owner)) {
+      // a view of a value this kernel computes: follow the view to the value
+      // (registers or this thread's own stores), never the half-written buffer
+      std::string v = def(n, idx);
+      memo.back()[k] = v;
+      return v;
+    }
     if (f.materialized || f.kind == Kind::Layout) {
       std::string v = load(f.buf, f.lay, idx);
       return v;

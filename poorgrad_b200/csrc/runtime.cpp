@@ -360,6 +360,40 @@ std::vector<Bucket> gradient_buckets(tb_plan* plan) {
   return out;
 }
 
+int64_t launch_kernel(tb_plan* plan, size_t k, cudaStream_t stream) {
+  tb::Program& P = *plan->prog;
+  const tb::Kernel& K = P.kernels[k];
+  int64_t launches = 0;
+  switch (K.type) {
+    case tb::KType::GEMM:
+      tb::launch_gemm(fp(plan, K.a_hi), fp(plan, K.a_lo), fp(plan, K.b_hi), fp(plan, K.b_lo),
+                      fp(plan, K.out), K.batch, K.m, K.n, K.kp, stream);
+      launches += 1;
+      break;
+    case tb::KType::SORT:
+      tb::launch_selection_sort(ip(plan, K.out), ip(plan, K.keys), ip(plan, K.vals),
+                                ip(plan, K.tmp_keys), ip(plan, K.tmp_vals), ip(plan, K.counts),
+                                ip(plan, K.rstart), ip(plan, K.rend), K.count, K.rows,
+                                (int)K.passes, K.tiles, stream);
+      launches += 2 + 3 * K.passes;
+      break;
+    case tb::KType::FINAL:
+      tb::launch_final_sum(fp(plan, K.partial), fp(plan, K.final_out), K.final_blocks,
+                           K.final_width, stream);
+      launches += 1;
+      break;
+    default: {
+      void* args[] = {plan->kparams[k].data()};
+      check(g_driver.LaunchKernel(plan->fn[k], (unsigned)K.grid, 1, 1, (unsigned)K.block, 1, 1,
+                                  (unsigned)K.smem, stream, args, nullptr),
+            "cuLaunchKernel");
+      launches += 1;
+    }
+  }
+  check(cudaGetLastError(), "kernel launch");
+  return launches;
+}
+
 void enqueue_program(tb_plan* plan, cudaStream_t stream) {
   tb::Program& P = *plan->prog;
   std::vector<Bucket> buckets = gradient_buckets(plan);
@@ -375,34 +409,7 @@ void enqueue_program(tb_plan* plan, cudaStream_t stream) {
   };
   bool comm_used = false;
   for (size_t k = 0; k < P.kernels.size(); ++k) {
-    const tb::Kernel& K = P.kernels[k];
-    switch (K.type) {
-      case tb::KType::GEMM:
-        tb::launch_gemm(fp(plan, K.a_hi), fp(plan, K.a_lo), fp(plan, K.b_hi), fp(plan, K.b_lo),
-                        fp(plan, K.out), K.batch, K.m, K.n, K.kp, stream);
-        launches += 1;
-        break;
-      case tb::KType::SORT:
-        tb::launch_selection_sort(ip(plan, K.out), ip(plan, K.keys), ip(plan, K.vals),
-                                  ip(plan, K.tmp_keys), ip(plan, K.tmp_vals), ip(plan, K.counts),
-                                  ip(plan, K.rstart), ip(plan, K.rend), K.count, K.rows,
-                                  (int)K.passes, K.tiles, stream);
-        launches += 2 + 3 * K.passes;
-        break;
-      case tb::KType::FINAL:
-        tb::launch_final_sum(fp(plan, K.partial), fp(plan, K.final_out), K.final_blocks,
-                             K.final_width, stream);
-        launches += 1;
-        break;
-      default: {
-        void* args[] = {plan->kparams[k].data()};
-        check(g_driver.LaunchKernel(plan->fn[k], (unsigned)K.grid, 1, 1, (unsigned)K.block, 1, 1,
-                             (unsigned)K.smem, stream, args, nullptr),
-              "cuLaunchKernel");
-        launches += 1;
-      }
-    }
-    check(cudaGetLastError(), "kernel launch");
+    launches += launch_kernel(plan, k, stream);
     for (const Bucket& b : buckets) {
       if (b.after_kernel != (int)k) continue;
       cudaEvent_t e = event();
@@ -853,6 +860,53 @@ int tbx_nvrtc_check(const tb_plan_desc* desc) {
     g_error = e.what();
     return TB_INVALID;
   }
+}
+
+// Times each kernel of a bound plan on its own (after one warm launch):
+// ms[k] = average of `reps` launches.  Returns the kernel count.
+int64_t tbx_profile_kernels(tb_plan* plan, int reps, float* ms, int64_t capacity) {
+  int rc = guarded([&]() {
+    if (!plan->bound) throw Failure(TB_INVALID, "run the plan once before profiling");
+    tb::Program& P = *plan->prog;
+    cudaEvent_t a, b;
+    check(cudaEventCreate(&a), "cudaEventCreate");
+    check(cudaEventCreate(&b), "cudaEventCreate");
+    for (size_t k = 0; k < P.kernels.size() && (int64_t)k < capacity; ++k) {
+      launch_kernel(plan, k, plan->stream);
+      check(cudaEventRecord(a, plan->stream), "record");
+      for (int r = 0; r < reps; ++r) launch_kernel(plan, k, plan->stream);
+      check(cudaEventRecord(b, plan->stream), "record");
+      check(cudaEventSynchronize(b), "sync");
+      float t = 0;
+      cudaEventElapsedTime(&t, a, b);
+      ms[k] = t / reps;
+    }
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    return (int)TB_OK;
+  });
+  return rc == TB_OK ? (int64_t)plan->prog->kernels.size() : -1;
+}
+
+// Per-kernel facts for roofline accounting: type, gemm dims, bytes of the
+// buffers it reads and writes.
+int tbx_kernel_facts(tb_plan* plan, int64_t k, int64_t* facts) {
+  return guarded([&]() {
+    tb::Program& P = *plan->prog;
+    const tb::Kernel& K = P.kernels.at(k);
+    int64_t rd = 0, wr = 0;
+    for (int b : K.reads) rd += P.buffers[b].bytes;
+    for (int b : K.writes) wr += P.buffers[b].bytes;
+    facts[0] = (int64_t)K.type;
+    facts[1] = K.batch;
+    facts[2] = K.m;
+    facts[3] = K.n;
+    facts[4] = K.k;
+    facts[5] = rd;
+    facts[6] = wr;
+    facts[7] = K.grid;
+    return (int)TB_OK;
+  }, false);
 }
 
 // ---- per-task faces
