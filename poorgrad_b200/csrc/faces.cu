@@ -87,7 +87,7 @@ extern "C" int tb_gemm_f32(const float* a, int64_t a_len, const int64_t a_stride
     k_prep_strided<<<grid, 256, 0, st>>>(da, a_strides[0], a_strides[1], m, k, kp, ahi, alo);
     // B^T as [n, k]: row j of B^T walks column j of B
     k_prep_strided<<<grid, 256, 0, st>>>(db, b_strides[1], b_strides[0], n, k, kp, bhi, blo);
-    tb::launch_gemm(ahi, alo, bhi, blo, dc, 1, m, n, kp, st);
+    tb::launch_gemm(ahi, alo, bhi, blo, dc, nullptr, 1, 1, m, n, kp, st);
     cudaMemcpyAsync(out, dc, m * n * 4, cudaMemcpyDeviceToHost, st);
     if (cudaStreamSynchronize(st) != cudaSuccess) rc = TB_RUNTIME;
   } while (false);
@@ -119,12 +119,17 @@ extern "C" int tb_map_f32(int32_t op, const float* in, int64_t count, float* out
 // ---- internal hooks for tests (not part of the public ABI)
 extern "C" void tbx_set_gemm_engine(int engine) { tb::set_gemm_engine(engine); }
 extern "C" int tbx_gemm_prepared(const float* a_hi, const float* a_lo, const float* b_hi,
-                                 const float* b_lo, float* c, int64_t batch, int64_t m, int64_t n,
-                                 int64_t kp, int engine) {
+                                 const float* b_lo, float* c, float* partial, int splits,
+                                 int64_t batch, int64_t m, int64_t n, int64_t kp, int engine) {
   cudaStream_t st = 0;
   if (engine == 1)
     tb::launch_gemm_simt(a_hi, a_lo, b_hi, b_lo, c, batch, m, n, kp, st);
-  else if (!tb::launch_gemm_tcgen05(a_hi, a_lo, b_hi, b_lo, c, batch, m, n, kp, st))
+  else if (!tb::launch_gemm_tcgen05_split(a_hi, a_lo, b_hi, b_lo, c, partial, splits, batch, m,
+                                          n, kp, st))
     return TB_DECLINED;
   return cudaDeviceSynchronize() == cudaSuccess ? TB_OK : TB_RUNTIME;
+}
+extern "C" int tbx_gemm_error(void) { return tb::gemm_error(); }
+extern "C" int tbx_gemm_splits(int64_t batch, int64_t m, int64_t n, int64_t kp) {
+  return tb::gemm_splits(batch, m, n, kp);
 }

@@ -1,9 +1,392 @@
-// gemm_sm100.cu -- tcgen05/TMEM 3xTF32 GEMM (placeholder until the sm_100a path lands).
+// gemm_sm100.cu -- 3xTF32 GEMM on the 5th-generation tensor cores (tcgen05).
+//
+// C[b] = A[b] . B[b]^T over operands prepared K-major as tf32 pairs
+// (hi = rna_tf32(x), lo = x - hi): C = Ahi.Bhi + Ahi.Blo + Alo.Bhi, the f32
+// accumulator held in tensor memory (TMEM).  One CTA computes a 128 x BN tile:
+//   warp 0      TMA producer: four tiles per k-block (A hi/lo, B hi/lo), 128B
+//               swizzle, into a STAGES-deep ring guarded by mbarriers;
+//   warp 1      MMA issuer: one elected thread issues tcgen05.mma kind::tf32
+//               (M=128, N=BN, K=8), three products per k-step, and commits each
+//               stage back to the producer;
+//   warps 2..5  epilogue: every CHUNK k-blocks the tensor-memory partial is
+//               read (tcgen05.ld, each warp its TMEM lane quarter) and added in
+//               IEEE f32 to register accumulators, then row-major f32 stores;
+//               warp 2 owns the TMEM allocation.
+// The tensor cores accumulate with truncating adders, so an accumulation chain
+// of k terms drifts like k ulps; draining the accumulator every CHUNK k-blocks
+// (two TMEM buffers, the MMA warp filling one while the epilogue drains the
+// other) bounds the chain and keeps the result as accurate as a serial f32 sum.
+// Split-K writes ordered partials that a second kernel sums in split order.
+// No TMA multicast is used anywhere (operands may live on any GPU's arena).
+// Every mbarrier wait is bounded by the global timer: on expiry the kernel
+// records an error code, stops issuing work and releases its TMEM.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+
 #include "kernels.h"
 
 namespace tb {
-bool launch_gemm_tcgen05(const float*, const float*, const float*, const float*, float*,
-                         int64_t, int64_t, int64_t, int64_t, cudaStream_t) {
-  return false;
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 128;
+constexpr int BK = 32;               // f32 elements per k-block (128 bytes: one swizzle row)
+constexpr int STAGES = 3;
+constexpr int CHUNK = 4;             // k-blocks per tensor-memory accumulation chain
+constexpr int TILE_A = BM * BK * 4;  // bytes of one A tile (hi or lo)
+constexpr int TILE_B = BN * BK * 4;
+constexpr int STAGE_BYTES = 2 * TILE_A + 2 * TILE_B;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr int THREADS = 192;
+constexpr unsigned long long WAIT_NS = 4000000000ull;  // 4 s per wait
+
+__device__ int g_gemm_error = 0;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
 }
+__device__ __forceinline__ unsigned long long now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false (and the error flag set) when the deadline passes.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+  if (mbar_try(bar, parity)) return true;
+  const unsigned long long start = now_ns();
+  while (!mbar_try(bar, parity)) {
+    if (now_ns() - start > WAIT_NS) {
+      atomicExch(&g_gemm_error, code);
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"((uint64_t)map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+// K-major operand tile with 128-byte swizzle: 8-row atoms 1024 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;            // leading byte offset (unused for swizzled K-major): 16 B
+  d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset: 1024 B between 8-row atoms
+  d |= (uint64_t)1 << 46;            // descriptor version for tcgen05
+  d |= (uint64_t)2 << 61;            // 128-byte swizzle
+  return d;
+}
+// kind::tf32 instruction descriptor: f32 accumulator, tf32 A and B, both K-major.
+__host__ __device__ constexpr uint32_t instr_desc(int m, int n) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(m >> 4) << 24);
+}
+__device__ __forceinline__ void umma_tf32(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(addr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    k_gemm_tcgen05(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
+                   const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
+                   float* __restrict__ out, int m, int n, int k_blocks, int split_blocks,
+                   int splits, long long split_stride) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = (uint64_t*)(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;   // [2]: chunk partial ready in TMEM buffer b
+  uint64_t* acc_empty = acc_full + 2;    // [2]: TMEM buffer b drained by the epilogue
+  uint32_t* tmem_slot = (uint32_t*)(acc_empty + 2);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+  const int split = blockIdx.z % splits, batch = blockIdx.z / splits;
+  const int kb0 = split * split_blocks;
+  const int kb1 = min(k_blocks, kb0 + split_blocks);
+  const int nkb = kb1 - kb0;
+  const int chunks = (nkb + CHUNK - 1) / CHUNK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(2 * BN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % STAGES;
+        const uint32_t round = i / STAGES;
+        if (!mbar_wait(&empty[s], (round & 1) ^ 1, 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        if (*abort_flag) break;
+        uint8_t* base = smem + s * STAGE_BYTES;
+        mbar_expect_tx(&full[s], STAGE_BYTES);
+        const int kx = (kb0 + i) * BK;
+        tma_load_3d(base, &ta_hi, kx, m0, batch, &full[s]);
+        tma_load_3d(base + TILE_A, &ta_lo, kx, m0, batch, &full[s]);
+        tma_load_3d(base + 2 * TILE_A, &tb_hi, kx, n0, batch, &full[s]);
+        tma_load_3d(base + 2 * TILE_A + TILE_B, &tb_lo, kx, n0, batch, &full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = instr_desc(BM, BN);
+      for (int c = 0; c < chunks && !*abort_flag; ++c) {
+        const int b = c & 1;
+        if (!mbar_wait(&acc_empty[b], ((c >> 1) & 1) ^ 1, 4)) {
+          *abort_flag = 1;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t acc = tmem + b * BN;
+        const int i_end = min(nkb, (c + 1) * CHUNK);
+        for (int i = c * CHUNK; i < i_end; ++i) {
+          const int s = i % STAGES;
+          const uint32_t round = i / STAGES;
+          if (!mbar_wait(&full[s], round & 1, 2)) {
+            *abort_flag = 1;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t a_hi = base, a_lo = base + TILE_A;
+          const uint32_t b_hi = base + 2 * TILE_A, b_lo = b_hi + TILE_B;
+#pragma unroll
+          for (int kk = 0; kk < BK / 8; ++kk) {
+            const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle row
+            const uint32_t first = (i > c * CHUNK || kk > 0) ? 1u : 0u;
+            umma_tf32(acc, smem_desc(a_lo + off), smem_desc(b_hi + off), idesc, first);
+            umma_tf32(acc, smem_desc(a_hi + off), smem_desc(b_lo + off), idesc, 1u);
+            umma_tf32(acc, smem_desc(a_hi + off), smem_desc(b_hi + off), idesc, 1u);
+          }
+          umma_commit(&empty[s]);
+        }
+        umma_commit(&acc_full[b]);
+      }
+    }
+  } else {
+    // epilogue: warps 2..5 drain TMEM lane quarters (warp % 4) chunk by chunk
+    const int q = warp & 3;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    float total[BN];
+#pragma unroll
+    for (int j = 0; j < BN; ++j) total[j] = 0.0f;
+    bool ok = true;
+    for (int c = 0; c < chunks; ++c) {
+      const int b = c & 1;
+      if (ok && !mbar_wait(&acc_full[b], (c >> 1) & 1, 3)) ok = false;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+      for (int g = 0; g < BN / 16; ++g) {
+        uint32_t r[16];
+        tmem_ld16(tmem + lane_base + b * BN + g * 16, r);
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          total[g * 16 + j] = c == 0 ? __uint_as_float(r[j])
+                                     : __fadd_rn(total[g * 16 + j], __uint_as_float(r[j]));
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&acc_empty[b]))
+                   : "memory");
+      if (!ok) break;
+    }
+    const int row = m0 + q * 32 + lane;
+    float* dst = out + (long long)split * split_stride + (long long)batch * m * n;
+    if (ok && !*abort_flag && row < m) {
+      const bool vec = (n % 4) == 0;
+      float* p = dst + (long long)row * n + n0;
+#pragma unroll
+      for (int g = 0; g < BN / 16; ++g) {
+        const int col = n0 + g * 16;
+        if (vec && col + 16 <= n) {
+#pragma unroll
+          for (int j = 0; j < 16; j += 4)
+            *(float4*)(p + g * 16 + j) = make_float4(total[g * 16 + j], total[g * 16 + j + 1],
+                                                     total[g * 16 + j + 2], total[g * 16 + j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (col + j < n) p[g * 16 + j] = total[g * 16 + j];
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 2) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
+  }
+}
+
+__global__ void k_split_sum(const float* __restrict__ partial, float* __restrict__ out,
+                            long long count, int splits) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < count;
+       i += (long long)gridDim.x * blockDim.x) {
+    float acc = partial[i];
+    for (int s = 1; s < splits; ++s) acc = __fadd_rn(acc, partial[(long long)s * count + i]);
+    out[i] = acc;
+  }
+}
+
+typedef CUresult (*EncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+  static EncodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiled)p;
+  });
+  return fn;
+}
+
+bool make_map(CUtensorMap* map, const float* base, int64_t kp, int64_t rows, int64_t batch,
+              int box_rows) {
+  EncodeTiled enc = encoder();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)kp, (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(kp * 4), (cuuint64_t)(rows * kp * 4)};
+  cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)base, dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+int gemm_splits(int64_t batch, int64_t m, int64_t n, int64_t kp) {
+  const int64_t tiles = batch * ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
+  const int64_t kb = kp / BK;
+  if (tiles >= 120 || kb < 16) return 1;
+  int64_t s = (148 + tiles - 1) / tiles;
+  s = std::min<int64_t>(s, kb / 8);
+  s = std::max<int64_t>(s, 1);
+  // every split must own at least one k-block
+  const int64_t per = (kb + s - 1) / s;
+  return (int)((kb + per - 1) / per);
+}
+
+bool launch_gemm_tcgen05_split(const float* a_hi, const float* a_lo, const float* b_hi,
+                               const float* b_lo, float* c, float* partial, int splits,
+                               int64_t batch, int64_t m, int64_t n, int64_t kp,
+                               cudaStream_t stream) {
+  if (kp % BK != 0 || m >= (1LL << 31) || n >= (1LL << 31) || batch > 65535) return false;
+  if (((uintptr_t)a_hi | (uintptr_t)a_lo | (uintptr_t)b_hi | (uintptr_t)b_lo) & 15) return false;
+  CUtensorMap ma, mal, mb, mbl;
+  if (!make_map(&ma, a_hi, kp, m, batch, BM) || !make_map(&mal, a_lo, kp, m, batch, BM) ||
+      !make_map(&mb, b_hi, kp, n, batch, BN) || !make_map(&mbl, b_lo, kp, n, batch, BN))
+    return false;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(k_gemm_tcgen05, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             SMEM_BYTES) != cudaSuccess)
+      return false;
+    configured = true;
+  }
+  const int kb = (int)(kp / BK);
+  if (splits < 1 || !partial) splits = 1;
+  const int per = (kb + splits - 1) / splits;
+  float* target = splits > 1 ? partial : c;
+  dim3 grid((unsigned)((n + BN - 1) / BN), (unsigned)((m + BM - 1) / BM),
+            (unsigned)(batch * splits));
+  k_gemm_tcgen05<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mal, mb, mbl, target, (int)m, (int)n,
+                                                        kb, per, splits,
+                                                        (long long)(batch * m * n));
+  if (splits > 1) {
+    const long long count = batch * m * n;
+    int blocks = (int)std::min<long long>((count + 255) / 256, 148 * 8);
+    k_split_sum<<<blocks, 256, 0, stream>>>(partial, c, count, splits);
+  }
+  return cudaPeekAtLastError() == cudaSuccess;
+}
+
+bool launch_gemm_tcgen05(const float* a_hi, const float* a_lo, const float* b_hi,
+                         const float* b_lo, float* c, int64_t batch, int64_t m, int64_t n,
+                         int64_t kp, cudaStream_t stream) {
+  return launch_gemm_tcgen05_split(a_hi, a_lo, b_hi, b_lo, c, nullptr, 1, batch, m, n, kp, stream);
+}
+
+int gemm_error() {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_gemm_error, sizeof(int));
+  return v;
+}
+
 }  // namespace tb

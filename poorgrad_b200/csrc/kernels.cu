@@ -3,6 +3,7 @@
 // finalizer of fused column/full reductions, the SIMT GEMM path and the
 // multi-tensor optimizer steps.
 #include <cstdio>
+#include <cstdlib>
 
 #include <algorithm>
 
@@ -242,7 +243,11 @@ __global__ void k_optimizer(const OptEntry* __restrict__ entries, int count, int
   }
 }
 
-int g_engine = 0;
+int engine_from_env() {
+  const char* e = getenv("TB_GEMM_ENGINE");
+  return e ? atoi(e) : 0;
+}
+int g_engine = engine_from_env();
 
 }  // namespace
 
@@ -290,10 +295,10 @@ void launch_gemm_simt(const float* a_hi, const float* a_lo, const float* b_hi,
 }
 
 void launch_gemm(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
-                 float* c, int64_t batch, int64_t m, int64_t n, int64_t kp,
-                 cudaStream_t stream) {
-  if (g_engine != 1 &&
-      launch_gemm_tcgen05(a_hi, a_lo, b_hi, b_lo, c, batch, m, n, kp, stream))
+                 float* c, float* partial, int splits, int64_t batch, int64_t m, int64_t n,
+                 int64_t kp, cudaStream_t stream) {
+  if (g_engine != 1 && launch_gemm_tcgen05_split(a_hi, a_lo, b_hi, b_lo, c, partial, splits,
+                                                 batch, m, n, kp, stream))
     return;
   launch_gemm_simt(a_hi, a_lo, b_hi, b_lo, c, batch, m, n, kp, stream);
 }

@@ -16,18 +16,26 @@ void launch_final_sum(const float* part, float* out, int64_t blocks, int64_t wid
                       cudaStream_t stream);
 
 // C[b] = (Ahi+Alo)[b] . (Bhi+Blo)[b]^T over K-major prepared operands;
-// the tcgen05 path when available, else a SIMT path.
+// the tcgen05 path (split-K into `partial` when splits > 1), else a SIMT path.
 void launch_gemm(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
-                 float* c, int64_t batch, int64_t m, int64_t n, int64_t kp,
-                 cudaStream_t stream);
+                 float* c, float* partial, int splits, int64_t batch, int64_t m, int64_t n,
+                 int64_t kp, cudaStream_t stream);
 // The SIMT path alone (tests compare the two).
 void launch_gemm_simt(const float* a_hi, const float* a_lo, const float* b_hi,
                       const float* b_lo, float* c, int64_t batch, int64_t m, int64_t n,
                       int64_t kp, cudaStream_t stream);
-// The tcgen05 path alone; returns false when the shape is not served.
+// The tcgen05 path; returns false when the shape or alignment is not served.
 bool launch_gemm_tcgen05(const float* a_hi, const float* a_lo, const float* b_hi,
                          const float* b_lo, float* c, int64_t batch, int64_t m, int64_t n,
                          int64_t kp, cudaStream_t stream);
+bool launch_gemm_tcgen05_split(const float* a_hi, const float* a_lo, const float* b_hi,
+                               const float* b_lo, float* c, float* partial, int splits,
+                               int64_t batch, int64_t m, int64_t n, int64_t kp,
+                               cudaStream_t stream);
+// Split-K factor the tcgen05 path uses for a shape (1 = no split).
+int gemm_splits(int64_t batch, int64_t m, int64_t n, int64_t kp);
+// Error code recorded by a tcgen05 GEMM whose bounded wait expired (0 = none).
+int gemm_error();
 // Selects the GEMM engine: 0 = automatic, 1 = SIMT only, 2 = tcgen05 only.
 void set_gemm_engine(int engine);
 int gemm_engine();

@@ -15,6 +15,7 @@
 #include <unordered_map>
 
 #include "engine.h"
+#include "kernels.h"
 
 namespace tb {
 namespace {
@@ -828,6 +829,8 @@ class Lowerer {
     g.b_lo = blo;
     g.out = P.info[n].buf;
     g.exact = false;
+    g.passes = gemm_splits(batch, M, N, Kp);  // split-K factor
+    if (g.passes > 1) g.partial = new_buffer(Storage::Arena, g.passes * batch * M * N * 4, -1);
     P.kernels.push_back(pa);
     P.kernels.push_back(pb);
     P.kernels.push_back(g);
@@ -1744,9 +1747,11 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
     if (K.type == KType::GEMM) {
       K.reads = {K.a_hi, K.a_lo, K.b_hi, K.b_lo};
       K.writes = {K.out};
+      if (K.partial >= 0) K.writes.push_back(K.partial);
       K.exact = false;
       K.describe = "gemm3xtf32 batch=" + std::to_string(K.batch) + " m=" + std::to_string(K.m) +
-                   " n=" + std::to_string(K.n) + " k=" + std::to_string(K.k);
+                   " n=" + std::to_string(K.n) + " k=" + std::to_string(K.k) +
+                   " splits=" + std::to_string(K.passes);
       P.kernels.push_back(K);
       continue;
     }

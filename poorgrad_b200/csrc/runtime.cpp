@@ -367,7 +367,8 @@ int64_t launch_kernel(tb_plan* plan, size_t k, cudaStream_t stream) {
   switch (K.type) {
     case tb::KType::GEMM:
       tb::launch_gemm(fp(plan, K.a_hi), fp(plan, K.a_lo), fp(plan, K.b_hi), fp(plan, K.b_lo),
-                      fp(plan, K.out), K.batch, K.m, K.n, K.kp, stream);
+                      fp(plan, K.out), K.partial >= 0 ? fp(plan, K.partial) : nullptr,
+                      (int)K.passes, K.batch, K.m, K.n, K.kp, stream);
       launches += 1;
       break;
     case tb::KType::SORT:

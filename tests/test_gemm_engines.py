@@ -1,0 +1,51 @@
+"""The tcgen05 3xTF32 GEMM against an f64 reference and against the SIMT
+engine, on prepared K-major tf32 hi/lo operands, including ragged tiles,
+batches and split-K.  Bar: |dev - ref| <= 8 eps sqrt(k) (1 + |ref|)
+(backend/cuda/tests/cuda_tests.rs:141-150)."""
+import ctypes as C
+import math
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+EPS = float(np.finfo(np.float32).eps)
+
+
+def _prep(torch, x, kp):
+    # hi = rna_tf32(x) via the 13-bit rounding of the f32 pattern, lo = x - hi
+    b, r, k = x.shape
+    pad = torch.zeros((b, r, kp), dtype=torch.float32, device=x.device)
+    pad[:, :, :k] = x
+    bits = pad.view(torch.int32)
+    hi = ((bits + 0x1000) & ~0x1FFF).view(torch.float32)
+    hi = torch.where(torch.isfinite(pad), hi, pad)
+    return hi.contiguous(), (pad - hi).contiguous()
+
+
+@pytest.mark.parametrize("batch,m,n,k,splits", [
+    (1, 128, 128, 32, 1), (1, 256, 384, 96, 1), (2, 130, 70, 40, 1), (1, 1, 5, 7, 1),
+    (3, 200, 136, 300, 1), (1, 512, 512, 4096, 4), (1, 128, 256, 1024, 3)])
+def test_tcgen05_matches_f64(device, batch, m, n, k, splits):
+    import torch
+    from poorgrad_b200.abi import load_library
+    lib = load_library()
+    lib.tbx_gemm_prepared.restype = C.c_int
+    lib.tbx_gemm_prepared.argtypes = [C.c_void_p] * 6 + [C.c_int] + [C.c_int64] * 4 + [C.c_int]
+    g = torch.Generator(device="cuda").manual_seed(batch * m + n + k)
+    a = torch.rand((batch, m, k), device="cuda", generator=g) * 2 - 1
+    bt = torch.rand((batch, n, k), device="cuda", generator=g) * 2 - 1
+    kp = (k + 31) // 32 * 32
+    ahi, alo = _prep(torch, a, kp)
+    bhi, blo = _prep(torch, bt, kp)
+    ref = torch.bmm(a.double(), bt.double().transpose(1, 2))
+    tol = 8 * EPS * math.sqrt(k) * (1 + ref.abs())
+    for engine in (2, 1):
+        c = torch.full((batch, m, n), float("nan"), device="cuda")
+        part = torch.empty((max(splits, 1), batch, m, n), device="cuda")
+        rc = lib.tbx_gemm_prepared(ahi.data_ptr(), alo.data_ptr(), bhi.data_ptr(), blo.data_ptr(),
+                                   c.data_ptr(), part.data_ptr(), splits, batch, m, n, kp, engine)
+        assert rc == 0, f"engine {engine} rc {rc}"
+        assert lib.tbx_gemm_error() == 0
+        err = (c.double() - ref).abs()
+        assert torch.all(err <= tol), f"engine {engine}: worst {(err / tol).max().item()}"
