@@ -104,7 +104,7 @@ def gemm(m: int = 4096, k: int = 4096, n: int = 4096, seed: int = 3) -> Workload
     params = [A, B]
     grads = tape.differentiate(loss, params)
     network = tape.into_network()
-    columns = network.compile(Request([C] + grads))
+    columns = network.compile(Request([loss, C] + grads))
     return Workload(f"gemm{m}x{k}x{n}", tape, network, columns, loss, params, grads, {"dC": dC},
                     lambda step: {}, 1, {}, flops=float(3 * 2 * m * n * k), extra={"C": C})
 
