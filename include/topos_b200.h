@@ -201,6 +201,20 @@ int tb_gemm_f32(const float* a, int64_t a_len, const int64_t a_strides[2],
  * TB_OP_LN, TB_OP_SQRT or TB_OP_TANH; host buffers. */
 int tb_map_f32(int32_t op, const float* in, int64_t count, float* out);
 
+/* ---- allocation-free GEMM (no counterpart in the reference: topos's cuda backend always
+ *      allocates device buffers from its pool for each product).
+ * For callers that cannot let the library call cudaMalloc -- a host framework whose own pool
+ * owns and accounts for every device allocation, or code that must not allocate after start-up.
+ * out[m, n] = a[m, k] . b[k, n], all DEVICE pointers, strides in elements as in tb_gemm_f32;
+ * enqueued on `stream` (a cudaStream_t; 0 = the legacy default stream), asynchronous.
+ * The only scratch is a fixed 16 MiB device array inside the library: requests needing more
+ * than 2*(m+n)*roundup(k,32) <= 4,194,304 floats answer TB_INVALID (tb_last_error says so).
+ * The first call on each device resolves the array's address with that device current.
+ * Calls that overlap on the GPU share the array and race; the caller serializes them. */
+int tb_gemm_f32_noalloc(const float* a, const int64_t a_strides[2], const float* b,
+                        const int64_t b_strides[2], int64_t m, int64_t k, int64_t n, float* out,
+                        void* stream);
+
 #ifdef __cplusplus
 }
 #endif

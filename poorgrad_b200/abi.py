@@ -209,6 +209,9 @@ def load_library() -> C.CDLL:
                                   C.c_int64, C.c_int64, C.c_int64, C.POINTER(C.c_float)]),
         "tb_map_f32": (C.c_int, [C.c_int32, C.POINTER(C.c_float), C.c_int64,
                                  C.POINTER(C.c_float)]),
+        "tb_gemm_f32_noalloc": (C.c_int, [C.c_void_p, C.POINTER(C.c_int64), C.c_void_p,
+                                          C.POINTER(C.c_int64), C.c_int64, C.c_int64, C.c_int64,
+                                          C.c_void_p, C.c_void_p]),
     }
     for name, (restype, argtypes) in sigs.items():
         fn = getattr(lib, name)

@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdio>
+#include <mutex>
 #include <string>
 
 #include "../../include/topos_b200.h"
@@ -132,4 +134,86 @@ extern "C" int tbx_gemm_prepared(const float* a_hi, const float* a_lo, const flo
 extern "C" int tbx_gemm_error(void) { return tb::gemm_error(); }
 extern "C" int tbx_gemm_splits(int64_t batch, int64_t m, int64_t n, int64_t kp) {
   return tb::gemm_splits(batch, m, n, kp);
+}
+
+// ---- allocation-free GEMM
+//
+// Some callers cannot let this library call cudaMalloc: a host framework that
+// owns every device allocation through its own pool (and accounts for it), or
+// code that must never allocate after start-up.  tb_gemm_f32_noalloc serves
+// them: the caller passes device inputs and output, and the only scratch --
+// the tf32 hi/lo split of both operands -- lives in the fixed array below.
+// The array is a file-scope device variable: every GPU that loads the library
+// holds its 16 MiB until the process exits.  All calls on a device share it,
+// so calls that overlap on the GPU (different streams, or different host
+// threads) race on it; callers serialize them.  Each call rewrites every
+// scratch element it reads (padding included), so nothing needs clearing.
+namespace {
+constexpr int64_t kNoAllocScratchFloats = int64_t(4) << 20;  // 16 MiB of f32
+__device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+
+std::mutex g_noalloc_mutex;
+float* g_noalloc_ptr[256] = {};  // per device: the array's device address
+
+// Host code cannot use the array's name as a device address: resolve it once
+// per device, with that device current.
+float* noalloc_scratch(int device) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (device < 0 || device >= 256) return nullptr;
+  if (!g_noalloc_ptr[device]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) return nullptr;
+    g_noalloc_ptr[device] = (float*)p;
+  }
+  return g_noalloc_ptr[device];
+}
+}  // namespace
+
+extern "C" int tb_gemm_f32_noalloc(const float* a, const int64_t a_strides[2], const float* b,
+                                   const int64_t b_strides[2], int64_t m, int64_t k, int64_t n,
+                                   float* out, void* stream) {
+  // readiness without the library's lazy set-up (which initializes the context
+  // through a cudaFree(nullptr) call this entry point must not make)
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+    tb::set_last_error("tb_gemm_f32_noalloc: no CUDA device");
+    return TB_PLATFORM_UNSUPPORTED;
+  }
+  if (tb::poisoned()) {
+    tb::set_last_error("tb_gemm_f32_noalloc: the backend is poisoned");
+    return TB_POISONED;
+  }
+  if (m < 1 || n < 1 || k < 1 || a_strides[0] < 0 || a_strides[1] < 0 || b_strides[0] < 0 ||
+      b_strides[1] < 0) {
+    tb::set_last_error("tb_gemm_f32_noalloc: invalid shape or strides");
+    return TB_INVALID;
+  }
+  const int64_t kp = (k + 31) / 32 * 32;
+  const int64_t need = 2 * (m + n) * kp;
+  if (need > kNoAllocScratchFloats) {
+    char text[200];
+    snprintf(text, sizeof text,
+             "tb_gemm_f32_noalloc: needs %lld floats of scratch (2*(m+n)*roundup(k,32)); the "
+             "fixed scratch holds %lld (16 MiB)",
+             (long long)need, (long long)kNoAllocScratchFloats);
+    tb::set_last_error(text);
+    return TB_INVALID;
+  }
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return TB_RUNTIME;
+  float* ws = noalloc_scratch(device);
+  if (!ws) {
+    tb::set_last_error("tb_gemm_f32_noalloc: cudaGetSymbolAddress failed");
+    return TB_RUNTIME;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  float* ahi = ws;
+  float* alo = ahi + m * kp;
+  float* bhi = alo + m * kp;
+  float* blo = bhi + n * kp;
+  const int grid = 148 * 4;
+  k_prep_strided<<<grid, 256, 0, st>>>(a, a_strides[0], a_strides[1], m, k, kp, ahi, alo);
+  k_prep_strided<<<grid, 256, 0, st>>>(b, b_strides[1], b_strides[0], n, k, kp, bhi, blo);
+  tb::launch_gemm(ahi, alo, bhi, blo, out, nullptr, 1, 1, m, n, kp, st);
+  return cudaPeekAtLastError() == cudaSuccess ? TB_OK : TB_RUNTIME;
 }

@@ -36,6 +36,10 @@ bool launch_gemm_tcgen05_split(const float* a_hi, const float* a_lo, const float
 int gemm_splits(int64_t batch, int64_t m, int64_t n, int64_t kp);
 // Error code recorded by a tcgen05 GEMM whose bounded wait expired (0 = none).
 int gemm_error();
+// Sets the thread-local message returned by tb_last_error().
+void set_last_error(const char* message);
+// Whether an earlier runtime failure poisoned the library.
+bool poisoned();
 // Selects the GEMM engine: 0 = automatic, 1 = SIMT only, 2 = tcgen05 only.
 void set_gemm_engine(int engine);
 int gemm_engine();

@@ -210,6 +210,14 @@ void check_nccl(ncclResult_t r, const char* what) {
 
 }  // namespace
 
+namespace tb {
+void set_last_error(const char* message) { g_error = message; }
+bool poisoned() {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  return g_state == TB_POISONED;
+}
+}  // namespace tb
+
 struct tb_params {
   int device = 0;
   void* base = nullptr;
