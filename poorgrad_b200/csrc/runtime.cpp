@@ -837,6 +837,16 @@ int64_t tbx_lower_describe(const tb_plan_desc* desc, char* buffer, size_t capaci
     for (size_t k = 0; k < prog->kernels.size(); ++k) o << k << ": " << prog->kernels[k].describe << "\n";
     o << "arena " << prog->arena_bytes << " bytes (" << prog->unplanned_bytes << " without reuse)\n";
     o << "exact " << (prog->exact ? 1 : 0) << " fused " << prog->fused_nodes << "\n";
+    for (size_t b = 0; b < prog->buffers.size(); ++b) {
+      const tb::Buffer& buf = prog->buffers[b];
+      if (!buf.keep) continue;
+      int writer = -1;
+      for (size_t k = 0; k < prog->kernels.size(); ++k)
+        for (int w : prog->kernels[k].writes)
+          if (w == (int)b) writer = (int)k;
+      o << "keep buffer " << b << " node " << buf.node << " offset " << buf.offset << " bytes "
+        << buf.bytes << " writer " << writer << "\n";
+    }
     if (with_source) o << prog->source;
     std::string s = o.str();
     if (buffer && capacity) snprintf(buffer, capacity, "%s", s.c_str());

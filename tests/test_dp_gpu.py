@@ -42,8 +42,8 @@ def _rank(rank, world, port, out):
               w.inputs["targets"]: Selection(t[sl], 27)}
     plan = backend.DevicePlan(w.columns)
     dp = backend.DeviceParameters(plan, w.network.parameters())
-    backend.Optimizer(plan, dp, backend.SGD, zip(w.params, w.grads), 0.1,
-                      gradient_scale=1.0 / world)
+    opt = backend.Optimizer(plan, dp, backend.SGD, zip(w.params, w.grads), 0.1,
+                            gradient_scale=1.0 / world)  # kept alive: it detaches when freed
     uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
     if rank == 0:
         uid.copy_(torch.tensor(list(backend.Comm.unique_id()), dtype=torch.uint8))
@@ -54,7 +54,7 @@ def _rank(rank, world, port, out):
     slots = [w.columns.nodes[p.index].slot for p in w.params]
     out[rank] = [dp.download(s) for s in slots]
     dist.barrier()
-    del comm
+    del opt, comm
     dist.destroy_process_group()
 
 
