@@ -16,6 +16,7 @@
 // of k terms drifts like k ulps; draining the accumulator every CHUNK k-blocks
 // (two TMEM buffers, the MMA warp filling one while the epilogue drains the
 // other) bounds the chain and keeps the result as accurate as a serial f32 sum.
+// The kernel is persistent (one CTA per SM walking the tiles).
 // Split-K writes ordered partials that a second kernel sums in split order.
 // No TMA multicast is used anywhere (operands may live on any GPU's arena).
 // Every mbarrier wait is bounded by the global timer: on expiry the kernel
@@ -25,6 +26,7 @@
 
 #include <cstdint>
 #include <cstdio>
+#include <algorithm>
 #include <mutex>
 
 #include "kernels.h"
@@ -130,11 +132,29 @@ __device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t* r) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Work item w of tiles_n x tiles_m x (batch * splits): n fastest.
+struct Work {
+  int n0, m0, split, batch;
+};
+__device__ __forceinline__ Work decode(int w, int tiles_n, int tiles_m, int splits) {
+  Work r;
+  r.n0 = (w % tiles_n) * BN;
+  w /= tiles_n;
+  r.m0 = (w % tiles_m) * BM;
+  w /= tiles_m;
+  r.split = w % splits;
+  r.batch = w / splits;
+  return r;
+}
+
+// Persistent: each CTA walks work items blockIdx.x, +gridDim.x, ...; the
+// stage ring and the two accumulator buffers carry their phases across tiles,
+// so the epilogue of one tile overlaps the main loop of the next.
 __global__ void __launch_bounds__(THREADS, 1)
     k_gemm_tcgen05(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
                    const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
                    float* __restrict__ out, int m, int n, int k_blocks, int split_blocks,
-                   int splits, long long split_stride) {
+                   int splits, long long split_stride, int tiles_n, int tiles_m, int work_items) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* full = (uint64_t*)(smem + STAGES * STAGE_BYTES);
@@ -145,12 +165,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
-  const int split = blockIdx.z % splits, batch = blockIdx.z / splits;
-  const int kb0 = split * split_blocks;
-  const int kb1 = min(k_blocks, kb0 + split_blocks);
-  const int nkb = kb1 - kb0;
-  const int chunks = (nkb + CHUNK - 1) / CHUNK;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -178,102 +192,126 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % STAGES;
-        const uint32_t round = i / STAGES;
-        if (!mbar_wait(&empty[s], (round & 1) ^ 1, 1)) {
-          *abort_flag = 1;
-          break;
+      uint32_t g = 0;  // k-blocks issued by this CTA so far
+      for (int w = blockIdx.x; w < work_items && !*abort_flag; w += gridDim.x) {
+        const Work t = decode(w, tiles_n, tiles_m, splits);
+        const int kb0 = t.split * split_blocks;
+        const int nkb = min(k_blocks, kb0 + split_blocks) - kb0;
+        for (int i = 0; i < nkb; ++i, ++g) {
+          const int s = g % STAGES;
+          const uint32_t round = g / STAGES;
+          if (!mbar_wait(&empty[s], (round & 1) ^ 1, 1)) {
+            *abort_flag = 1;
+            break;
+          }
+          if (*abort_flag) break;
+          uint8_t* base = smem + s * STAGE_BYTES;
+          mbar_expect_tx(&full[s], STAGE_BYTES);
+          const int kx = (kb0 + i) * BK;
+          tma_load_3d(base, &ta_hi, kx, t.m0, t.batch, &full[s]);
+          tma_load_3d(base + TILE_A, &ta_lo, kx, t.m0, t.batch, &full[s]);
+          tma_load_3d(base + 2 * TILE_A, &tb_hi, kx, t.n0, t.batch, &full[s]);
+          tma_load_3d(base + 2 * TILE_A + TILE_B, &tb_lo, kx, t.n0, t.batch, &full[s]);
         }
-        if (*abort_flag) break;
-        uint8_t* base = smem + s * STAGE_BYTES;
-        mbar_expect_tx(&full[s], STAGE_BYTES);
-        const int kx = (kb0 + i) * BK;
-        tma_load_3d(base, &ta_hi, kx, m0, batch, &full[s]);
-        tma_load_3d(base + TILE_A, &ta_lo, kx, m0, batch, &full[s]);
-        tma_load_3d(base + 2 * TILE_A, &tb_hi, kx, n0, batch, &full[s]);
-        tma_load_3d(base + 2 * TILE_A + TILE_B, &tb_lo, kx, n0, batch, &full[s]);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = instr_desc(BM, BN);
-      for (int c = 0; c < chunks && !*abort_flag; ++c) {
-        const int b = c & 1;
-        if (!mbar_wait(&acc_empty[b], ((c >> 1) & 1) ^ 1, 4)) {
-          *abort_flag = 1;
-          break;
-        }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t acc = tmem + b * BN;
-        const int i_end = min(nkb, (c + 1) * CHUNK);
-        for (int i = c * CHUNK; i < i_end; ++i) {
-          const int s = i % STAGES;
-          const uint32_t round = i / STAGES;
-          if (!mbar_wait(&full[s], round & 1, 2)) {
+      uint32_t g = 0, gc = 0;  // k-blocks and chunks consumed by this CTA so far
+      for (int w = blockIdx.x; w < work_items && !*abort_flag; w += gridDim.x) {
+        const Work t = decode(w, tiles_n, tiles_m, splits);
+        const int kb0 = t.split * split_blocks;
+        const int nkb = min(k_blocks, kb0 + split_blocks) - kb0;
+        const int chunks = (nkb + CHUNK - 1) / CHUNK;
+        for (int c = 0; c < chunks && !*abort_flag; ++c, ++gc) {
+          const int b = gc & 1;
+          if (!mbar_wait(&acc_empty[b], ((gc >> 1) & 1) ^ 1, 4)) {
             *abort_flag = 1;
             break;
           }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
-          const uint32_t a_hi = base, a_lo = base + TILE_A;
-          const uint32_t b_hi = base + 2 * TILE_A, b_lo = b_hi + TILE_B;
+          const uint32_t acc = tmem + b * BN;
+          const int i_end = min(nkb, (c + 1) * CHUNK);
+          for (int i = c * CHUNK; i < i_end; ++i, ++g) {
+            const int s = g % STAGES;
+            const uint32_t round = g / STAGES;
+            if (!mbar_wait(&full[s], round & 1, 2)) {
+              *abort_flag = 1;
+              break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+            const uint32_t a_hi = base, a_lo = base + TILE_A;
+            const uint32_t b_hi = base + 2 * TILE_A, b_lo = b_hi + TILE_B;
 #pragma unroll
-          for (int kk = 0; kk < BK / 8; ++kk) {
-            const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle row
-            const uint32_t first = (i > c * CHUNK || kk > 0) ? 1u : 0u;
-            umma_tf32(acc, smem_desc(a_lo + off), smem_desc(b_hi + off), idesc, first);
-            umma_tf32(acc, smem_desc(a_hi + off), smem_desc(b_lo + off), idesc, 1u);
-            umma_tf32(acc, smem_desc(a_hi + off), smem_desc(b_hi + off), idesc, 1u);
+            for (int kk = 0; kk < BK / 8; ++kk) {
+              const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle row
+              const uint32_t first = (i > c * CHUNK || kk > 0) ? 1u : 0u;
+              umma_tf32(acc, smem_desc(a_lo + off), smem_desc(b_hi + off), idesc, first);
+              umma_tf32(acc, smem_desc(a_hi + off), smem_desc(b_lo + off), idesc, 1u);
+              umma_tf32(acc, smem_desc(a_hi + off), smem_desc(b_hi + off), idesc, 1u);
+            }
+            umma_commit(&empty[s]);
           }
-          umma_commit(&empty[s]);
+          umma_commit(&acc_full[b]);
         }
-        umma_commit(&acc_full[b]);
       }
     }
   } else {
     // epilogue: warps 2..5 drain TMEM lane quarters (warp % 4) chunk by chunk
     const int q = warp & 3;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    float total[BN];
-#pragma unroll
-    for (int j = 0; j < BN; ++j) total[j] = 0.0f;
+    uint32_t gc = 0;
     bool ok = true;
-    for (int c = 0; c < chunks; ++c) {
-      const int b = c & 1;
-      if (ok && !mbar_wait(&acc_full[b], (c >> 1) & 1, 3)) ok = false;
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    for (int w = blockIdx.x; w < work_items && ok; w += gridDim.x) {
+      const Work t = decode(w, tiles_n, tiles_m, splits);
+      const int kb0 = t.split * split_blocks;
+      const int nkb = min(k_blocks, kb0 + split_blocks) - kb0;
+      const int chunks = (nkb + CHUNK - 1) / CHUNK;
+      float total[BN];
 #pragma unroll
-      for (int g = 0; g < BN / 16; ++g) {
-        uint32_t r[16];
-        tmem_ld16(tmem + lane_base + b * BN + g * 16, r);
+      for (int j = 0; j < BN; ++j) total[j] = 0.0f;
+      for (int c = 0; c < chunks; ++c, ++gc) {
+        const int b = gc & 1;
+        if (!mbar_wait(&acc_full[b], (gc >> 1) & 1, 3)) {
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-          total[g * 16 + j] = c == 0 ? __uint_as_float(r[j])
-                                     : __fadd_rn(total[g * 16 + j], __uint_as_float(r[j]));
-      }
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&acc_empty[b]))
-                   : "memory");
-      if (!ok) break;
-    }
-    const int row = m0 + q * 32 + lane;
-    float* dst = out + (long long)split * split_stride + (long long)batch * m * n;
-    if (ok && !*abort_flag && row < m) {
-      const bool vec = (n % 4) == 0;
-      float* p = dst + (long long)row * n + n0;
-#pragma unroll
-      for (int g = 0; g < BN / 16; ++g) {
-        const int col = n0 + g * 16;
-        if (vec && col + 16 <= n) {
-#pragma unroll
-          for (int j = 0; j < 16; j += 4)
-            *(float4*)(p + g * 16 + j) = make_float4(total[g * 16 + j], total[g * 16 + j + 1],
-                                                     total[g * 16 + j + 2], total[g * 16 + j + 3]);
-        } else {
+        for (int gq = 0; gq < BN / 16; ++gq) {
+          uint32_t r[16];
+          tmem_ld16(tmem + lane_base + b * BN + gq * 16, r);
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            if (col + j < n) p[g * 16 + j] = total[g * 16 + j];
+            total[gq * 16 + j] = c == 0 ? __uint_as_float(r[j])
+                                        : __fadd_rn(total[gq * 16 + j], __uint_as_float(r[j]));
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&acc_empty[b]))
+                     : "memory");
+      }
+      if (!ok || *abort_flag) break;
+      const int row = t.m0 + q * 32 + lane;
+      if (row < m) {
+        float* dst = out + (long long)t.split * split_stride + (long long)t.batch * m * n;
+        const bool vec = (n % 4) == 0;
+        float* p = dst + (long long)row * n + t.n0;
+#pragma unroll
+        for (int gq = 0; gq < BN / 16; ++gq) {
+          const int col = t.n0 + gq * 16;
+          if (vec && col + 16 <= n) {
+#pragma unroll
+            for (int j = 0; j < 16; j += 4)
+              *(float4*)(p + gq * 16 + j) =
+                  make_float4(total[gq * 16 + j], total[gq * 16 + j + 1], total[gq * 16 + j + 2],
+                              total[gq * 16 + j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (col + j < n) p[gq * 16 + j] = total[gq * 16 + j];
+          }
         }
       }
     }
@@ -364,11 +402,21 @@ bool launch_gemm_tcgen05_split(const float* a_hi, const float* a_lo, const float
   if (splits < 1 || !partial) splits = 1;
   const int per = (kb + splits - 1) / splits;
   float* target = splits > 1 ? partial : c;
-  dim3 grid((unsigned)((n + BN - 1) / BN), (unsigned)((m + BM - 1) / BM),
-            (unsigned)(batch * splits));
+  const int tiles_n = (int)((n + BN - 1) / BN), tiles_m = (int)((m + BM - 1) / BM);
+  const long long items = (long long)tiles_n * tiles_m * batch * splits;
+  if (items >= (1LL << 31)) return false;
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  const int grid = (int)std::min<long long>(items, sms);
   k_gemm_tcgen05<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mal, mb, mbl, target, (int)m, (int)n,
                                                         kb, per, splits,
-                                                        (long long)(batch * m * n));
+                                                        (long long)(batch * m * n), tiles_n,
+                                                        tiles_m, (int)items);
   if (splits > 1) {
     const long long count = batch * m * n;
     int blocks = (int)std::min<long long>((count + 255) / 256, 148 * 8);

@@ -23,19 +23,22 @@ __global__ void k_sort_init(const int* __restrict__ idx, int* __restrict__ keys,
   }
 }
 
-// One warp per tile: digit histogram of the tile.
-__global__ void k_radix_count(const int* __restrict__ keys, int* __restrict__ counts,
-                              int64_t count, int shift, int64_t tiles) {
+// One block of TILE threads per tile, one item per thread: digit histogram,
+// aggregated per warp before the shared-memory atomics.
+__global__ void __launch_bounds__(TILE) k_radix_count(const int* __restrict__ keys,
+                                                      int* __restrict__ counts, int64_t count,
+                                                      int shift, int64_t tiles) {
   __shared__ int hist[256];
   const int64_t tile = blockIdx.x;
-  for (int d = threadIdx.x; d < 256; d += 32) hist[d] = 0;
-  __syncwarp();
-  const int64_t begin = tile * TILE;
-  const int64_t end = (begin + TILE < count ? begin + TILE : count);
-  for (int64_t i = begin + threadIdx.x; i < end; i += 32)
-    atomicAdd(&hist[(keys[i] >> shift) & 255], 1);
-  __syncwarp();
-  for (int d = threadIdx.x; d < 256; d += 32) counts[(int64_t)d * tiles + tile] = hist[d];
+  if (threadIdx.x < 256) hist[threadIdx.x] = 0;
+  __syncthreads();
+  const int64_t i = tile * TILE + threadIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int digit = i < count ? (keys[i] >> shift) & 255 : 256 + lane;
+  const unsigned peers = __match_any_sync(0xffffffffu, digit);
+  if (digit < 256 && lane == 31 - __clz(peers)) atomicAdd(&hist[digit], __popc(peers));
+  __syncthreads();
+  if (threadIdx.x < 256) counts[(int64_t)threadIdx.x * tiles + tile] = hist[threadIdx.x];
 }
 
 // Exclusive scan of n ints by one block of 1024 threads.
@@ -63,41 +66,45 @@ __global__ void k_scan(int* __restrict__ data, int64_t n) {
   }
 }
 
-// One warp per tile: stable scatter by digit.  Items are taken 32 at a time in
-// source order; lanes with equal digits are ranked by lane.
-__global__ void k_radix_scatter(const int* __restrict__ keys, const int* __restrict__ vals,
-                                int* __restrict__ keys_out, int* __restrict__ vals_out,
-                                const int* __restrict__ offsets, int64_t count, int shift,
-                                int64_t tiles) {
-  __shared__ int running[256];
+// One block of TILE threads per tile: a stable scatter by digit.  Within a
+// warp, equal digits are ranked by lane; across warps, by a per-digit prefix
+// over the warps in order -- so items keep their source order.
+__global__ void __launch_bounds__(TILE) k_radix_scatter(const int* __restrict__ keys,
+                                                        const int* __restrict__ vals,
+                                                        int* __restrict__ keys_out,
+                                                        int* __restrict__ vals_out,
+                                                        const int* __restrict__ offsets,
+                                                        int64_t count, int shift, int64_t tiles) {
+  __shared__ int warp_count[TILE / 32][256];
   const int64_t tile = blockIdx.x;
-  const int lane = threadIdx.x;
-  for (int d = lane; d < 256; d += 32) running[d] = offsets[(int64_t)d * tiles + tile];
-  __syncwarp();
-  const int64_t begin = tile * TILE;
-  const int64_t end = (begin + TILE < count ? begin + TILE : count);
-  for (int64_t base = begin; base < end; base += 32) {
-    const int64_t i = base + lane;
-    const bool valid = i < end;
-    const unsigned active = __ballot_sync(0xffffffffu, valid);
-    int key = 0, val = 0, digit = 256 + lane;  // invalid lanes get unique digits
-    if (valid) {
-      key = keys[i];
-      val = vals[i];
-      digit = (key >> shift) & 255;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int x = threadIdx.x; x < (TILE / 32) * 256; x += TILE) (&warp_count[0][0])[x] = 0;
+  __syncthreads();
+  const int64_t i = tile * TILE + threadIdx.x;
+  const bool valid = i < count;
+  int key = 0, val = 0, digit = 256 + lane;
+  if (valid) {
+    key = keys[i];
+    val = vals[i];
+    digit = (key >> shift) & 255;
+  }
+  const unsigned peers = __match_any_sync(0xffffffffu, digit);
+  const int rank = __popc(peers & ((1u << lane) - 1u));
+  if (valid && lane == 31 - __clz(peers)) warp_count[warp][digit] = __popc(peers);
+  __syncthreads();
+  if (threadIdx.x < 256) {
+    int run = offsets[(int64_t)threadIdx.x * tiles + tile];
+    for (int w = 0; w < TILE / 32; ++w) {
+      const int c = warp_count[w][threadIdx.x];
+      warp_count[w][threadIdx.x] = run;
+      run += c;
     }
-    const unsigned peers = __match_any_sync(0xffffffffu, digit) & active;
-    const int rank = __popc(peers & ((1u << lane) - 1u));
-    int pos = 0;
-    if (valid) pos = running[digit] + rank;
-    __syncwarp();
-    if (valid) {
-      keys_out[pos] = key;
-      vals_out[pos] = val;
-      const int leader = 31 - __clz(peers);
-      if (lane == leader) running[digit] += __popc(peers);
-    }
-    __syncwarp();
+  }
+  __syncthreads();
+  if (valid) {
+    const int pos = warp_count[warp][digit] + rank;
+    keys_out[pos] = key;
+    vals_out[pos] = val;
   }
 }
 
@@ -111,13 +118,30 @@ __global__ void k_segments(const int* __restrict__ keys, int* __restrict__ rstar
   }
 }
 
-__global__ void k_final_sum(const float* __restrict__ part, float* __restrict__ out,
-                            int64_t blocks, int64_t width) {
-  for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < width;
-       j += (int64_t)gridDim.x * blockDim.x) {
-    float acc = part[j];
-    for (int64_t b = 1; b < blocks; ++b) acc = __fadd_rn(acc, part[b * width + j]);
-    out[j] = acc;
+// 32 columns per block: lane = column, the 8 warps take every 8th partial row;
+// the 8 per-warp sums are then combined in warp order (a fixed, deterministic
+// association).
+__global__ void __launch_bounds__(256) k_final_sum(const float* __restrict__ part,
+                                                   float* __restrict__ out, int64_t blocks,
+                                                   int64_t width) {
+  __shared__ float acc_s[8][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t j = (int64_t)blockIdx.x * 32 + lane;
+  float acc = 0.0f;
+  bool any = false;
+  if (j < width) {
+    for (int64_t b = warp; b < blocks; b += 8) {
+      const float v = part[b * width + j];
+      acc = any ? __fadd_rn(acc, v) : v;
+      any = true;
+    }
+  }
+  acc_s[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && j < width) {
+    float t = acc_s[0][lane];
+    for (int w = 1; w < 8 && w < blocks; ++w) t = __fadd_rn(t, acc_s[w][lane]);
+    out[j] = t;
   }
 }
 
@@ -265,9 +289,9 @@ void launch_selection_sort(const int* indices, int* keys, int* vals, int* tmp_ke
   int* dst_v = tmp_vals;
   for (int p = 0; p < passes; ++p) {
     const int shift = 8 * p;
-    k_radix_count<<<(unsigned)tiles, 32, 0, stream>>>(src_k, counts, count, shift, tiles);
+    k_radix_count<<<(unsigned)tiles, TILE, 0, stream>>>(src_k, counts, count, shift, tiles);
     k_scan<<<1, 1024, 0, stream>>>(counts, 256 * tiles);
-    k_radix_scatter<<<(unsigned)tiles, 32, 0, stream>>>(src_k, src_v, dst_k, dst_v, counts,
+    k_radix_scatter<<<(unsigned)tiles, TILE, 0, stream>>>(src_k, src_v, dst_k, dst_v, counts,
                                                         count, shift, tiles);
     std::swap(src_k, dst_k);
     std::swap(src_v, dst_v);
@@ -283,8 +307,7 @@ void launch_selection_sort(const int* indices, int* keys, int* vals, int* tmp_ke
 
 void launch_final_sum(const float* part, float* out, int64_t blocks, int64_t width,
                       cudaStream_t stream) {
-  int grid = (int)std::max<int64_t>(1, std::min<int64_t>((width + 255) / 256, 148 * 4));
-  k_final_sum<<<grid, 256, 0, stream>>>(part, out, blocks, width);
+  k_final_sum<<<(unsigned)((width + 31) / 32), 256, 0, stream>>>(part, out, blocks, width);
 }
 
 void launch_gemm_simt(const float* a_hi, const float* a_lo, const float* b_hi,

@@ -1263,7 +1263,7 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
         E.line("float ra" + std::to_string(m) + " = __int_as_float(0x7fc00000);");
     }
     bool unroll = has_col;
-    E.line(unroll ? "#pragma unroll" : "#pragma unroll 1");
+    E.line(unroll ? "#pragma unroll" : "#pragma unroll 4");
     E.line("for (int kc = 0; kc < " + std::to_string(KC) + "; ++kc) {");
     E.indent += 2;
     E.line("const I j0 = ((I)kc * " + std::to_string(T) + " + tl) * " + std::to_string(vec) + ";");
@@ -1461,7 +1461,53 @@ static void emit_scatter(Program& P, Kernel& K, Emitter& E, const Kernel& sort) 
   std::vector<std::string> oc = rest.empty() ? std::vector<std::string>{} : E.unravel("o", rest, "c");
   E.line("float acc = 0.0f;");
   E.line("const int q1 = " + E.iptr(sort.rend) + "[row];");
-  E.line("for (int q = " + E.iptr(sort.rstart) + "[row]; q < q1; ++q) {");
+  E.line("int q = " + E.iptr(sort.rstart) + "[row];");
+  if (width % 32 == 0) {
+    // a warp covers 32 columns of one row: its lanes load 32 source indices at
+    // once, broadcast them by shuffle, issue the 32 loads, then add in
+    // ascending source order
+    E.line("for (; q < q1; q += 32) {");
+    E.indent += 2;
+    E.line("const int cnt = q1 - q < 32 ? q1 - q : 32;");
+    E.line("const int sv = (q + (int)(threadIdx.x & 31) < q1) ? " + E.iptr(sort.vals) +
+           "[q + (threadIdx.x & 31)] : 0;");
+    std::vector<std::string> terms;
+    for (int j = 0; j < 32; ++j) {
+      std::string sj = "s" + std::to_string(j);
+      E.line("const I " + sj + " = (I)__shfl_sync(0xffffffffu, sv, " + std::to_string(j) + ");");
+      E.push();
+      Idx at;
+      at.c.push_back(sj);
+      for (auto& c : oc) at.c.push_back(c);
+      terms.push_back(E.ref(nd.operands[0], at));
+      E.pop();
+    }
+    for (int j = 0; j < 32; ++j)
+      E.line("if (" + std::to_string(j) + " < cnt) acc = __fadd_rn(acc, " + terms[j] + ");");
+    E.indent -= 2;
+    E.line("}");
+  }
+  // eight sources per step: their loads are issued together, then added in
+  // ascending source order (the reference's serial order is kept exactly)
+  E.line("for (; q + 8 <= q1; q += 8) {");
+  E.indent += 2;
+  std::vector<std::string> terms;
+  for (int j = 0; j < 8; ++j) {
+    std::string sj = "s" + std::to_string(j);
+    E.line("const I " + sj + " = (I)" + E.iptr(sort.vals) + "[q + " + std::to_string(j) + "];");
+  }
+  for (int j = 0; j < 8; ++j) {
+    E.push();
+    Idx at;
+    at.c.push_back("s" + std::to_string(j));
+    for (auto& c : oc) at.c.push_back(c);
+    terms.push_back(E.ref(nd.operands[0], at));
+    E.pop();
+  }
+  for (auto& g : terms) E.line("acc = __fadd_rn(acc, " + g + ");");
+  E.indent -= 2;
+  E.line("}");
+  E.line("for (; q < q1; ++q) {");
   E.indent += 2;
   E.line("const I s = (I)" + E.iptr(sort.vals) + "[q];");
   E.push();
