@@ -41,29 +41,43 @@ __global__ void __launch_bounds__(TILE) k_radix_count(const int* __restrict__ ke
   if (threadIdx.x < 256) counts[(int64_t)threadIdx.x * tiles + tile] = hist[threadIdx.x];
 }
 
-// Exclusive scan of n ints by one block of 1024 threads.
-__global__ void k_scan(int* __restrict__ data, int64_t n) {
-  __shared__ int sums[1024];
-  const int t = threadIdx.x;
-  const int64_t per = (n + 1023) / 1024;
-  const int64_t begin = t * per;
-  const int64_t end = (begin + per < n ? begin + per : n);
-  int local = 0;
-  for (int64_t i = begin; i < end; ++i) local += data[i];
-  sums[t] = local;
-  __syncthreads();
-  for (int off = 1; off < 1024; off <<= 1) {
-    int v = t >= off ? sums[t - off] : 0;
-    __syncthreads();
-    sums[t] += v;
-    __syncthreads();
+// Exclusive scan of the digit-major counts [256][tiles] in one block: thread d
+// scans digit d's row (loads issued 8 at a time), the digit totals are scanned
+// across the block, and each row is shifted by its digit's base.
+__global__ void __launch_bounds__(256) k_scan_digits(int* __restrict__ counts, int64_t tiles) {
+  __shared__ int totals[256];
+  const int d = threadIdx.x;
+  int* row = counts + (int64_t)d * tiles;
+  int run = 0;
+  int64_t t = 0;
+  for (; t + 8 <= tiles; t += 8) {
+    int v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = row[t + j];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      row[t + j] = run;
+      run += v[j];
+    }
   }
-  int run = sums[t] - local;
-  for (int64_t i = begin; i < end; ++i) {
-    int v = data[i];
-    data[i] = run;
+  for (; t < tiles; ++t) {
+    const int v = row[t];
+    row[t] = run;
     run += v;
   }
+  totals[d] = run;
+  __syncthreads();
+  if (d == 0) {
+    int acc = 0;
+    for (int x = 0; x < 256; ++x) {
+      const int v = totals[x];
+      totals[x] = acc;
+      acc += v;
+    }
+  }
+  __syncthreads();
+  const int base = totals[d];
+  for (t = 0; t < tiles; ++t) row[t] += base;
 }
 
 // One block of TILE threads per tile: a stable scatter by digit.  Within a
@@ -282,26 +296,24 @@ void launch_selection_sort(const int* indices, int* keys, int* vals, int* tmp_ke
                            int* tmp_vals, int* counts, int* rstart, int* rend, int64_t count,
                            int64_t rows, int passes, int64_t tiles, cudaStream_t stream) {
   int grid = (int)std::min<int64_t>((count + 255) / 256, 148 * 8);
-  k_sort_init<<<grid, 256, 0, stream>>>(indices, keys, vals, count);
-  int* src_k = keys;
-  int* src_v = vals;
-  int* dst_k = tmp_keys;
-  int* dst_v = tmp_vals;
+  // start in the buffer pair that makes the last pass land in (keys, vals)
+  const bool odd = passes % 2 == 1;
+  int* src_k = odd ? tmp_keys : keys;
+  int* src_v = odd ? tmp_vals : vals;
+  int* dst_k = odd ? keys : tmp_keys;
+  int* dst_v = odd ? vals : tmp_vals;
+  k_sort_init<<<grid, 256, 0, stream>>>(indices, src_k, src_v, count);
   for (int p = 0; p < passes; ++p) {
     const int shift = 8 * p;
     k_radix_count<<<(unsigned)tiles, TILE, 0, stream>>>(src_k, counts, count, shift, tiles);
-    k_scan<<<1, 1024, 0, stream>>>(counts, 256 * tiles);
+    k_scan_digits<<<1, 256, 0, stream>>>(counts, tiles);
     k_radix_scatter<<<(unsigned)tiles, TILE, 0, stream>>>(src_k, src_v, dst_k, dst_v, counts,
                                                         count, shift, tiles);
     std::swap(src_k, dst_k);
     std::swap(src_v, dst_v);
   }
-  if (src_k != keys) {
-    cudaMemcpyAsync(keys, src_k, count * 4, cudaMemcpyDeviceToDevice, stream);
-    cudaMemcpyAsync(vals, src_v, count * 4, cudaMemcpyDeviceToDevice, stream);
-  }
   cudaMemsetAsync(rstart, 0, rows * 4, stream);
-  cudaMemsetAsync(rend, 0, rows * 4, stream);
+  cudaMemsetAsync(rend, 0, rows * 4, stream);  // rows without sources: empty segments
   k_segments<<<grid, 256, 0, stream>>>(keys, rstart, rend, count);
 }
 

@@ -1463,18 +1463,26 @@ static void emit_scatter(Program& P, Kernel& K, Emitter& E, const Kernel& sort) 
   E.line("const int q1 = " + E.iptr(sort.rend) + "[row];");
   E.line("int q = " + E.iptr(sort.rstart) + "[row];");
   if (width % 32 == 0) {
-    // a warp covers 32 columns of one row: its lanes load 32 source indices at
-    // once, broadcast them by shuffle, issue the 32 loads, then add in
-    // ascending source order
-    E.line("for (; q < q1; q += 32) {");
+    // a warp covers 32 columns of one row: its lanes load 64 source indices
+    // at once (the next 64 are prefetched while these are used), broadcast
+    // them by shuffle, issue the 64 loads, then add in ascending source order
+    const std::string lane = "(int)(threadIdx.x & 31)";
+    auto idx_load = [&](const std::string& off) {
+      return "(q + " + off + " + " + lane + " < q1) ? " + E.iptr(sort.vals) + "[q + " + off +
+             " + " + lane + "] : 0";
+    };
+    E.line("int sa = " + idx_load("0") + ";");
+    E.line("int sb = " + idx_load("32") + ";");
+    E.line("for (; q < q1; q += 64) {");
     E.indent += 2;
-    E.line("const int cnt = q1 - q < 32 ? q1 - q : 32;");
-    E.line("const int sv = (q + (int)(threadIdx.x & 31) < q1) ? " + E.iptr(sort.vals) +
-           "[q + (threadIdx.x & 31)] : 0;");
+    E.line("const int cnt = q1 - q < 64 ? q1 - q : 64;");
+    E.line("const int na = " + idx_load("64") + ";");
+    E.line("const int nb = " + idx_load("96") + ";");
     std::vector<std::string> terms;
-    for (int j = 0; j < 32; ++j) {
+    for (int j = 0; j < 64; ++j) {
       std::string sj = "s" + std::to_string(j);
-      E.line("const I " + sj + " = (I)__shfl_sync(0xffffffffu, sv, " + std::to_string(j) + ");");
+      E.line("const I " + sj + " = (I)__shfl_sync(0xffffffffu, " + (j < 32 ? "sa" : "sb") + ", " +
+             std::to_string(j & 31) + ");");
       E.push();
       Idx at;
       at.c.push_back(sj);
@@ -1482,8 +1490,10 @@ static void emit_scatter(Program& P, Kernel& K, Emitter& E, const Kernel& sort) 
       terms.push_back(E.ref(nd.operands[0], at));
       E.pop();
     }
-    for (int j = 0; j < 32; ++j)
+    for (int j = 0; j < 64; ++j)
       E.line("if (" + std::to_string(j) + " < cnt) acc = __fadd_rn(acc, " + terms[j] + ");");
+    E.line("sa = na;");
+    E.line("sb = nb;");
     E.indent -= 2;
     E.line("}");
   }
@@ -1567,6 +1577,63 @@ static void emit_fold(Program& P, Kernel& K, Emitter& E) {
   E.line("}");
 }
 
+// The logical axis of node n along which consecutive elements sit next to
+// each other in the memory the expression ultimately reads (the axis a
+// coalesced reader should walk).
+static int fast_axis(const Program& P, int n, int depth = 0) {
+  const Node& nd = P.nodes[n];
+  const Info& f = P.info[n];
+  const int last = nd.rank - 1;
+  if (nd.rank <= 1 || depth > 64) return last;
+  if (f.materialized || f.kind == Kind::Layout) {
+    for (int d = nd.rank - 1; d >= 0; --d)
+      if (f.lay.stride[d] == 1 && f.lay.shape[d] > 1) return d;
+    return last;
+  }
+  const int a = nd.operands[0];
+  const int64_t* at = nd.attrs;
+  if (is_elementwise(nd.op)) {
+    // follow the operand that reads a full-size buffer rather than a broadcast
+    for (int k = 0; k < 2; ++k) {
+      int o = nd.operands[k];
+      if (o < 0) continue;
+      const Info& fo = P.info[o];
+      if (fo.kind == Kind::Const || fo.kind == Kind::Sel) continue;
+      if ((fo.materialized || fo.kind == Kind::Layout)) {
+        bool broadcast = false;
+        for (int d = 0; d < fo.lay.rank; ++d)
+          if (fo.lay.stride[d] == 0 && fo.lay.shape[d] > 1) broadcast = true;
+        if (broadcast) continue;
+      }
+      return fast_axis(P, o, depth + 1);
+    }
+    return last;
+  }
+  switch (nd.op) {
+    case TB_OP_TRANSPOSE: return fast_axis(P, a, depth + 1) == 0 ? 1 : 0;
+    case TB_OP_PERMUTE: {
+      int fa = fast_axis(P, a, depth + 1);
+      for (int j = 0; j < nd.rank; ++j)
+        if (at[j] == fa) return j;
+      return last;
+    }
+    case TB_OP_NARROW:
+    case TB_OP_PAD:
+      return fast_axis(P, a, depth + 1);
+    case TB_OP_BROADCAST_ALONG: {
+      int fa = fast_axis(P, a, depth + 1);
+      return fa >= at[0] ? fa + 1 : fa;
+    }
+    case TB_OP_RESHAPE:
+    case TB_OP_GATHER: {
+      const Node& on = P.nodes[a];
+      (void)on;  // row-major results of a reshape or a row gather run along the last axis
+      return last;
+    }
+  }
+  return last;
+}
+
 // ---- GEMM operand preparation: tf32 hi/lo split into K-major [batch, R, Kp]
 static void emit_prep(Program& P, Kernel& K, Emitter& E) {
   const Node& mm = P.nodes[K.node];
@@ -1577,13 +1644,8 @@ static void emit_prep(Program& P, Kernel& K, Emitter& E) {
   int64_t R = K.m, Kd = K.k, Kp = K.kp;
   bool is_b = K.sel == 1;
   // transpose through shared memory when the operand is contiguous along R
-  bool tile = false;
-  const Info& f = P.info[x];
-  if (f.materialized || f.kind == Kind::Layout) {
-    int64_t sk = f.lay.stride[is_b ? split : split + 1];
-    int64_t sr = f.lay.stride[is_b ? split + 1 : split];
-    tile = sk != 1 && sr == 1;
-  }
+  const int fa = fast_axis(P, x);
+  const bool tile = fa == (is_b ? split + 1 : split);
   auto operand_idx = [&](const std::vector<std::string>& bc, const std::string& r,
                          const std::string& k) {
     Idx idx;
