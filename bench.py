@@ -204,7 +204,7 @@ def cpu_baseline(name):
     return {"value": n / dt, "unit": unit, "cores": 1, "kind": "port", "sample": sample}
 
 
-KTYPES = ["ew", "row", "reduce", "prep", "gemm", "sort", "scatter", "fold", "final"]
+KTYPES = ["ew", "row", "reduce", "prep", "gemm", "sort", "scatter", "fold", "final", "segsum"]
 
 
 def kernel_profile(plan, reps=20):
@@ -253,6 +253,8 @@ def main():
     ap.add_argument("--impl", default="b200")
     ap.add_argument("--config", default=DEFAULT_CONFIG)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-kernel-profile", action="store_true",
+                    help="skip the per-kernel timing pass (for runs under a profiler)")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args, args.config)
@@ -360,7 +362,7 @@ def main():
     e2e_value = samples / (ms_e2e / args.steps * 1e-3)
 
     stats = plan.stats()
-    rows = kernel_profile(plan) if rank == 0 else []
+    rows = kernel_profile(plan) if rank == 0 and not args.no_kernel_profile else []
     roof = roofline(rows) if rows else None
     if rank == 0:
         cpu = None if args.no_cpu else cpu_baseline(args.config)

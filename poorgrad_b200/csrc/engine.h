@@ -92,7 +92,8 @@ enum class KType {
   SORT,       // stable index sort of a selection (scatter)
   SCATTER,    // serial-order scatter-add
   FOLD,       // window fold
-  FINAL       // sum of per-block partials
+  FINAL,      // sum of per-block partials
+  SEGSUM      // serial segment sums of a target-ordered scatter source
 };
 
 struct Kernel {

@@ -38,34 +38,19 @@ __global__ void __launch_bounds__(TILE) k_radix_count(const int* __restrict__ ke
   const unsigned peers = __match_any_sync(0xffffffffu, digit);
   if (digit < 256 && lane == 31 - __clz(peers)) atomicAdd(&hist[digit], __popc(peers));
   __syncthreads();
-  if (threadIdx.x < 256) counts[(int64_t)threadIdx.x * tiles + tile] = hist[threadIdx.x];
+  if (threadIdx.x < 256) {
+    counts[tile * 256 + threadIdx.x] = hist[threadIdx.x];
+    if (hist[threadIdx.x]) atomicAdd(&counts[tiles * 256 + threadIdx.x], hist[threadIdx.x]);
+  }
 }
 
-// Exclusive scan of the digit-major counts [256][tiles] in one block: thread d
-// scans digit d's row (loads issued 8 at a time), the digit totals are scanned
-// across the block, and each row is shifted by its digit's base.
+// Offsets from the tile-major counts [tiles][256] and the digit totals
+// counts[tiles][...] (accumulated by the count kernel): thread d walks the
+// tiles with coalesced loads, starting from the exclusive scan of the totals.
 __global__ void __launch_bounds__(256) k_scan_digits(int* __restrict__ counts, int64_t tiles) {
   __shared__ int totals[256];
   const int d = threadIdx.x;
-  int* row = counts + (int64_t)d * tiles;
-  int run = 0;
-  int64_t t = 0;
-  for (; t + 8 <= tiles; t += 8) {
-    int v[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = row[t + j];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      row[t + j] = run;
-      run += v[j];
-    }
-  }
-  for (; t < tiles; ++t) {
-    const int v = row[t];
-    row[t] = run;
-    run += v;
-  }
-  totals[d] = run;
+  totals[d] = counts[tiles * 256 + d];
   __syncthreads();
   if (d == 0) {
     int acc = 0;
@@ -76,8 +61,23 @@ __global__ void __launch_bounds__(256) k_scan_digits(int* __restrict__ counts, i
     }
   }
   __syncthreads();
-  const int base = totals[d];
-  for (t = 0; t < tiles; ++t) row[t] += base;
+  int run = totals[d];
+  int64_t t = 0;
+  for (; t + 8 <= tiles; t += 8) {
+    int v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = counts[(t + j) * 256 + d];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      counts[(t + j) * 256 + d] = run;
+      run += v[j];
+    }
+  }
+  for (; t < tiles; ++t) {
+    const int v = counts[t * 256 + d];
+    counts[t * 256 + d] = run;
+    run += v;
+  }
 }
 
 // One block of TILE threads per tile: a stable scatter by digit.  Within a
@@ -107,7 +107,7 @@ __global__ void __launch_bounds__(TILE) k_radix_scatter(const int* __restrict__ 
   if (valid && lane == 31 - __clz(peers)) warp_count[warp][digit] = __popc(peers);
   __syncthreads();
   if (threadIdx.x < 256) {
-    int run = offsets[(int64_t)threadIdx.x * tiles + tile];
+    int run = offsets[tile * 256 + threadIdx.x];
     for (int w = 0; w < TILE / 32; ++w) {
       const int c = warp_count[w][threadIdx.x];
       warp_count[w][threadIdx.x] = run;
@@ -144,7 +144,18 @@ __global__ void __launch_bounds__(256) k_final_sum(const float* __restrict__ par
   float acc = 0.0f;
   bool any = false;
   if (j < width) {
-    for (int64_t b = warp; b < blocks; b += 8) {
+    int64_t b = warp;
+    for (; b + 56 < blocks; b += 64) {  // eight rows per step: loads first, adds in order
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = part[(b + 8 * u) * width + j];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        acc = any ? __fadd_rn(acc, v[u]) : v[u];
+        any = true;
+      }
+    }
+    for (; b < blocks; b += 8) {
       const float v = part[b * width + j];
       acc = any ? __fadd_rn(acc, v) : v;
       any = true;
@@ -156,6 +167,37 @@ __global__ void __launch_bounds__(256) k_final_sum(const float* __restrict__ par
     float t = acc_s[0][lane];
     for (int w = 1; w < 8 && w < blocks; ++w) t = __fadd_rn(t, acc_s[w][lane]);
     out[j] = t;
+  }
+}
+
+// One thread per output; the segment's rows are contiguous, loaded 64 at a
+// time (many bytes in flight for long segments) and added in ascending order
+// from zero.
+__global__ void k_segment_sum(const float* __restrict__ perm, const int* __restrict__ rstart,
+                              const int* __restrict__ rend, float* __restrict__ out,
+                              int64_t rows, int64_t width) {
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < rows * width;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = t / width, c = t % width;
+    const int64_t q1 = rend[row];
+    int64_t q = rstart[row];
+    float acc = 0.0f;
+    for (; q + 64 <= q1; q += 64) {
+      float v[64];
+#pragma unroll
+      for (int j = 0; j < 64; ++j) v[j] = perm[(q + j) * width + c];
+#pragma unroll
+      for (int j = 0; j < 64; ++j) acc = __fadd_rn(acc, v[j]);
+    }
+    for (; q + 8 <= q1; q += 8) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = perm[(q + j) * width + c];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, v[j]);
+    }
+    for (; q < q1; ++q) acc = __fadd_rn(acc, perm[q * width + c]);
+    out[t] = acc;
   }
 }
 
@@ -305,6 +347,7 @@ void launch_selection_sort(const int* indices, int* keys, int* vals, int* tmp_ke
   k_sort_init<<<grid, 256, 0, stream>>>(indices, src_k, src_v, count);
   for (int p = 0; p < passes; ++p) {
     const int shift = 8 * p;
+    cudaMemsetAsync(counts + tiles * 256, 0, 256 * 4, stream);  // digit totals
     k_radix_count<<<(unsigned)tiles, TILE, 0, stream>>>(src_k, counts, count, shift, tiles);
     k_scan_digits<<<1, 256, 0, stream>>>(counts, tiles);
     k_radix_scatter<<<(unsigned)tiles, TILE, 0, stream>>>(src_k, src_v, dst_k, dst_v, counts,
@@ -315,6 +358,12 @@ void launch_selection_sort(const int* indices, int* keys, int* vals, int* tmp_ke
   cudaMemsetAsync(rstart, 0, rows * 4, stream);
   cudaMemsetAsync(rend, 0, rows * 4, stream);  // rows without sources: empty segments
   k_segments<<<grid, 256, 0, stream>>>(keys, rstart, rend, count);
+}
+
+void launch_segment_sum(const float* perm, const int* rstart, const int* rend, float* out,
+                        int64_t rows, int64_t width, cudaStream_t stream) {
+  int grid = (int)std::max<int64_t>(1, std::min<int64_t>((rows * width + 255) / 256, 148 * 8));
+  k_segment_sum<<<grid, 256, 0, stream>>>(perm, rstart, rend, out, rows, width);
 }
 
 void launch_final_sum(const float* part, float* out, int64_t blocks, int64_t width,

@@ -15,6 +15,10 @@ void launch_selection_sort(const int* indices, int* keys, int* vals, int* tmp_ke
 void launch_final_sum(const float* part, float* out, int64_t blocks, int64_t width,
                       cudaStream_t stream);
 
+// out[r, c] = 0 + perm[rstart[r], c] + ... + perm[rend[r]-1, c] (ascending rows).
+void launch_segment_sum(const float* perm, const int* rstart, const int* rend, float* out,
+                        int64_t rows, int64_t width, cudaStream_t stream);
+
 // C[b] = (Ahi+Alo)[b] . (Bhi+Blo)[b]^T over K-major prepared operands;
 // the tcgen05 path (split-K into `partial` when splits > 1), else a SIMT path.
 void launch_gemm(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,

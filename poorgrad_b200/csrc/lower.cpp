@@ -657,7 +657,10 @@ class Lowerer {
     vec = row_vec(space);
     int64_t chunks = (L + vec - 1) / vec;
     T = 32;
-    while (T * 2 <= chunks && T < 256) T *= 2;
+    // rows of up to 16 chunks per lane: one warp per row (shuffle-only
+    // reductions, many rows in flight); longer rows: up to 256 threads
+    if (chunks > 32 * 16)
+      while (T * 2 <= chunks && T < 256) T *= 2;
     KC = (chunks + T - 1) / T;
   }
 
@@ -1231,7 +1234,8 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
     maxphase = std::max(maxphase, m.phase);
   }
   K.block = 256;
-  int64_t cap = has_col ? SMS * 2 : SMS * 4;
+  // per-block column partials cost blocks * L floats: fewer blocks for wide rows
+  int64_t cap = (has_col && L >= 4096) ? SMS * 2 : SMS * 4;
   K.grid = std::max<int64_t>(1, std::min<int64_t>((R + teams - 1) / teams, cap));
   if (has_col || has_all) E.exact = false;
   E.line("__shared__ float sred[8];");
@@ -1446,90 +1450,31 @@ static void emit_reduce(Program& P, Kernel& K, Emitter& E) {
 }
 
 // ---- scatter-add over the stably sorted selection (payload/tensor.rs:1582-1618)
+// This kernel writes the scatter source rows in target order (perm[q] =
+// g[vals[q]]), a fully parallel copy; a SEGSUM kernel then sums each target's
+// contiguous rows from zero in ascending source order -- the reference's
+// serial order, so the result is bit-identical.
 static void emit_scatter(Program& P, Kernel& K, Emitter& E, const Kernel& sort) {
   int n = K.node;
   const Node& nd = P.nodes[n];
-  int64_t rows = nd.shape[0];
-  int64_t width = nd.volume() / rows;
+  const Node& g = P.nodes[nd.operands[0]];
+  int64_t count = g.shape[0];
+  int64_t width = nd.volume() / nd.shape[0];
   std::vector<int64_t> rest(nd.shape + 1, nd.shape + nd.rank);
-  K.grid = std::max<int64_t>(1, std::min<int64_t>((rows * width + 255) / 256, SMS * 8));
-  E.line("for (I t = (I)blockIdx.x * 256 + threadIdx.x; t < " + lit(rows * width) +
+  int64_t total = count * width;
+  K.grid = std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, SMS * 8));
+  E.line("for (I t = (I)blockIdx.x * 256 + threadIdx.x; t < " + lit(total) +
          "; t += (I)gridDim.x * 256) {");
   E.indent += 2;
-  E.line("const I row = t / " + lit(width) + ";");
+  E.line("const I q = t / " + lit(width) + ";");
   E.line("const I o = t % " + lit(width) + ";");
   std::vector<std::string> oc = rest.empty() ? std::vector<std::string>{} : E.unravel("o", rest, "c");
-  E.line("float acc = 0.0f;");
-  E.line("const int q1 = " + E.iptr(sort.rend) + "[row];");
-  E.line("int q = " + E.iptr(sort.rstart) + "[row];");
-  if (width % 32 == 0) {
-    // a warp covers 32 columns of one row: its lanes load 64 source indices
-    // at once (the next 64 are prefetched while these are used), broadcast
-    // them by shuffle, issue the 64 loads, then add in ascending source order
-    const std::string lane = "(int)(threadIdx.x & 31)";
-    auto idx_load = [&](const std::string& off) {
-      return "(q + " + off + " + " + lane + " < q1) ? " + E.iptr(sort.vals) + "[q + " + off +
-             " + " + lane + "] : 0";
-    };
-    E.line("int sa = " + idx_load("0") + ";");
-    E.line("int sb = " + idx_load("32") + ";");
-    E.line("for (; q < q1; q += 64) {");
-    E.indent += 2;
-    E.line("const int cnt = q1 - q < 64 ? q1 - q : 64;");
-    E.line("const int na = " + idx_load("64") + ";");
-    E.line("const int nb = " + idx_load("96") + ";");
-    std::vector<std::string> terms;
-    for (int j = 0; j < 64; ++j) {
-      std::string sj = "s" + std::to_string(j);
-      E.line("const I " + sj + " = (I)__shfl_sync(0xffffffffu, " + (j < 32 ? "sa" : "sb") + ", " +
-             std::to_string(j & 31) + ");");
-      E.push();
-      Idx at;
-      at.c.push_back(sj);
-      for (auto& c : oc) at.c.push_back(c);
-      terms.push_back(E.ref(nd.operands[0], at));
-      E.pop();
-    }
-    for (int j = 0; j < 64; ++j)
-      E.line("if (" + std::to_string(j) + " < cnt) acc = __fadd_rn(acc, " + terms[j] + ");");
-    E.line("sa = na;");
-    E.line("sb = nb;");
-    E.indent -= 2;
-    E.line("}");
-  }
-  // eight sources per step: their loads are issued together, then added in
-  // ascending source order (the reference's serial order is kept exactly)
-  E.line("for (; q + 8 <= q1; q += 8) {");
-  E.indent += 2;
-  std::vector<std::string> terms;
-  for (int j = 0; j < 8; ++j) {
-    std::string sj = "s" + std::to_string(j);
-    E.line("const I " + sj + " = (I)" + E.iptr(sort.vals) + "[q + " + std::to_string(j) + "];");
-  }
-  for (int j = 0; j < 8; ++j) {
-    E.push();
-    Idx at;
-    at.c.push_back("s" + std::to_string(j));
-    for (auto& c : oc) at.c.push_back(c);
-    terms.push_back(E.ref(nd.operands[0], at));
-    E.pop();
-  }
-  for (auto& g : terms) E.line("acc = __fadd_rn(acc, " + g + ");");
-  E.indent -= 2;
-  E.line("}");
-  E.line("for (; q < q1; ++q) {");
-  E.indent += 2;
   E.line("const I s = (I)" + E.iptr(sort.vals) + "[q];");
-  E.push();
   Idx at;
   at.c.push_back("s");
   for (auto& c : oc) at.c.push_back(c);
-  std::string g = E.ref(nd.operands[0], at);
-  E.line("acc = __fadd_rn(acc, " + g + ");");
-  E.pop();
-  E.indent -= 2;
-  E.line("}");
-  E.line(E.fptr(P.info[n].buf) + "[t] = acc;");
+  std::string v = E.ref(nd.operands[0], at);
+  E.line(E.fptr(K.partial) + "[t] = " + v + ";");
   E.indent -= 2;
   E.line("}");
 }
@@ -1875,7 +1820,7 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
       K.vals = Lw.new_buffer(Storage::Arena, K.count * 4, -1);
       K.tmp_keys = Lw.new_buffer(Storage::Arena, K.count * 4, -1);
       K.tmp_vals = Lw.new_buffer(Storage::Arena, K.count * 4, -1);
-      K.counts = Lw.new_buffer(Storage::Arena, 256 * K.tiles * 4, -1);
+      K.counts = Lw.new_buffer(Storage::Arena, 256 * (K.tiles + 1) * 4, -1);
       K.rstart = Lw.new_buffer(Storage::Arena, K.rows * 4, -1);
       K.rend = Lw.new_buffer(Storage::Arena, K.rows * 4, -1);
       K.out = P.info[K.sel].buf;  // the index buffer
@@ -1895,7 +1840,22 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
       case KType::SCATTER: {
         int sk = sort_index.at(P.sort_of.at(P.nodes[K.node].operands[1]));
         K.sel = sk;
+        const Node& sn = P.nodes[K.node];
+        const Node& gn = P.nodes[sn.operands[0]];
+        const int64_t width = sn.volume() / sn.shape[0];
+        K.partial = Lw.new_buffer(Storage::Arena, gn.shape[0] * width * 4, -1);
         emit_scatter(P, K, E, P.kernels[sk]);
+        Kernel seg;
+        seg.type = KType::SEGSUM;
+        seg.node = K.node;
+        seg.partial = K.partial;
+        seg.final_out = P.info[K.node].buf;
+        seg.rstart = P.kernels[sk].rstart;
+        seg.rend = P.kernels[sk].rend;
+        seg.rows = sn.shape[0];
+        seg.final_width = width;
+        seg.exact = true;
+        finals.push_back(seg);
         break;
       }
       case KType::FOLD: emit_fold(P, K, E); break;
@@ -1928,17 +1888,14 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
       for (auto& m : K.members)
         if (P.info[m.node].buf == b && P.info[m.node].owner == m.node) written = true;
       if (b == K.a_hi || b == K.a_lo) written = true;
-      if (bf.storage == Storage::Arena && bf.node < 0 && K.type == KType::ROW) written = true;
+      if (bf.storage == Storage::Arena && bf.node < 0 &&
+          (K.type == KType::ROW || K.type == KType::SCATTER))
+        written = true;
       (written ? K.writes : K.reads).push_back(b);
     }
-    if (K.type == KType::SCATTER) {
-      const Kernel& s = P.kernels[K.sel];
-      K.reads.push_back(s.vals);
-      K.reads.push_back(s.rstart);
-      K.reads.push_back(s.rend);
-    }
+    if (K.type == KType::SCATTER) K.reads.push_back(P.kernels[K.sel].vals);
     std::ostringstream d;
-    static const char* names[] = {"ew", "row", "reduce", "prep", "gemm", "sort", "scatter", "fold", "final"};
+    static const char* names[] = {"ew", "row", "reduce", "prep", "gemm", "sort", "scatter", "fold", "final", "segsum"};
     d << names[(int)K.type] << " " << K.name << " grid=" << K.grid;
     if (!K.space.empty()) {
       d << " space=[";
@@ -1953,6 +1910,14 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
     for (auto& f : finals) {
       f.reads = {f.partial};
       f.writes = {f.final_out};
+      if (f.type == KType::SEGSUM) {
+        f.reads.push_back(f.rstart);
+        f.reads.push_back(f.rend);
+        f.describe = "segsum rows=" + std::to_string(f.rows) + " width=" +
+                     std::to_string(f.final_width) + " exact";
+        P.kernels.push_back(f);
+        continue;
+      }
       f.describe = "final partials=" + std::to_string(f.final_blocks) + "x" +
                    std::to_string(f.final_width);
       P.kernels.push_back(f);

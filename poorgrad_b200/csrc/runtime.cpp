@@ -386,6 +386,11 @@ int64_t launch_kernel(tb_plan* plan, size_t k, cudaStream_t stream) {
                                 (int)K.passes, K.tiles, stream);
       launches += 2 + 3 * K.passes;
       break;
+    case tb::KType::SEGSUM:
+      tb::launch_segment_sum(fp(plan, K.partial), ip(plan, K.rstart), ip(plan, K.rend),
+                             fp(plan, K.final_out), K.rows, K.final_width, stream);
+      launches += 1;
+      break;
     case tb::KType::FINAL:
       tb::launch_final_sum(fp(plan, K.partial), fp(plan, K.final_out), K.final_blocks,
                            K.final_width, stream);
