@@ -2,16 +2,17 @@
 //
 // C[b] = A[b] . B[b]^T over operands prepared K-major as tf32 pairs
 // (hi = rna_tf32(x), lo = x - hi): C = Ahi.Bhi + Ahi.Blo + Alo.Bhi, the f32
-// accumulator held in tensor memory (TMEM).  One CTA computes a 128 x BN tile:
-//   warp 0      TMA producer: four tiles per k-block (A hi/lo, B hi/lo), 128B
+// accumulator held in tensor memory (TMEM).  One CTA computes a 128 x 256 tile:
+//   warp 0      TMA producer: four tiles per k-block (A hi/lo, B hi/lo), 64B
 //               swizzle, into a STAGES-deep ring guarded by mbarriers;
 //   warp 1      MMA issuer: one elected thread issues tcgen05.mma kind::tf32
 //               (M=128, N=BN, K=8), three products per k-step, and commits each
 //               stage back to the producer;
-//   warps 2..5  epilogue: every CHUNK k-blocks the tensor-memory partial is
-//               read (tcgen05.ld, each warp its TMEM lane quarter) and added in
-//               IEEE f32 to register accumulators, then row-major f32 stores;
-//               warp 2 owns the TMEM allocation.
+//   warps 2..9  epilogue (two warpgroups, one per column half): every CHUNK
+//               k-blocks the tensor-memory partial is read (tcgen05.ld, each
+//               warp its TMEM lane quarter) and added in IEEE f32 to register
+//               accumulators, then row-major f32 stores; warp 2 owns the TMEM
+//               allocation.
 // The tensor cores accumulate with truncating adders, so an accumulation chain
 // of k terms drifts like k ulps; draining the accumulator every CHUNK k-blocks
 // (two TMEM buffers, the MMA warp filling one while the epilogue drains the
@@ -29,21 +30,42 @@
 #include <algorithm>
 #include <mutex>
 
+#include <cstdlib>
+
 #include "kernels.h"
 
 namespace tb {
 namespace {
 
 constexpr int BM = 128;
-constexpr int BN = 128;
-constexpr int BK = 32;               // f32 elements per k-block (128 bytes: one swizzle row)
-constexpr int STAGES = 3;
-constexpr int CHUNK = 4;             // k-blocks per tensor-memory accumulation chain
-constexpr int TILE_A = BM * BK * 4;  // bytes of one A tile (hi or lo)
-constexpr int TILE_B = BN * BK * 4;
-constexpr int STAGE_BYTES = 2 * TILE_A + 2 * TILE_B;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
-constexpr int THREADS = 192;
+
+// The two tile shapes.  128 x 128 with 32-float k-blocks (128-byte swizzle,
+// 3 stages, one epilogue warpgroup) and 128 x 256 with 16-float k-blocks
+// (64-byte swizzle, 4 stages, two epilogue warpgroups); both keep 128 k per
+// tensor-memory accumulation chain and about 192 KB of staging.
+template <int BN_>
+struct Cfg;
+template <>
+struct Cfg<128> {
+  static constexpr int BN = 128, BK = 32, STAGES = 3, CHUNK = 4, GROUPS = 1;
+  static constexpr uint64_t SWIZZLE = 2, SBO = 1024;  // 128-byte swizzle
+  static constexpr CUtensorMapSwizzle TMA_SWIZZLE = CU_TENSOR_MAP_SWIZZLE_128B;
+};
+template <>
+struct Cfg<256> {
+  static constexpr int BN = 256, BK = 16, STAGES = 4, CHUNK = 8, GROUPS = 2;
+  static constexpr uint64_t SWIZZLE = 4, SBO = 512;  // 64-byte swizzle
+  static constexpr CUtensorMapSwizzle TMA_SWIZZLE = CU_TENSOR_MAP_SWIZZLE_64B;
+};
+template <class C>
+struct Derived {
+  static constexpr int TILE_A = BM * C::BK * 4;
+  static constexpr int TILE_B = C::BN * C::BK * 4;
+  static constexpr int STAGE_BYTES = 2 * TILE_A + 2 * TILE_B;
+  static constexpr int SMEM_BYTES = C::STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int THREADS = 64 + 128 * C::GROUPS;
+  static constexpr int EPI_COLS = C::BN / C::GROUPS;  // 128 columns per epilogue warpgroup
+};
 constexpr unsigned long long WAIT_NS = 4000000000ull;  // 4 s per wait
 
 __device__ int g_gemm_error = 0;
@@ -94,14 +116,15 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       "l"((uint64_t)map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
       : "memory");
 }
-// K-major operand tile with 128-byte swizzle: 8-row atoms 1024 bytes apart.
+// K-major operand tile, swizzled rows of BK floats, 8-row atoms SBO bytes apart.
+template <class C>
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
   uint64_t d = 0;
   d |= (uint64_t)((addr >> 4) & 0x3FFF);
-  d |= (uint64_t)1 << 16;            // leading byte offset (unused for swizzled K-major): 16 B
-  d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset: 1024 B between 8-row atoms
-  d |= (uint64_t)1 << 46;            // descriptor version for tcgen05
-  d |= (uint64_t)2 << 61;            // 128-byte swizzle
+  d |= (uint64_t)1 << 16;              // leading byte offset (unused for swizzled K-major): 16 B
+  d |= (uint64_t)(C::SBO >> 4) << 32;  // stride byte offset between 8-row atoms
+  d |= (uint64_t)1 << 46;              // descriptor version for tcgen05
+  d |= C::SWIZZLE << 61;               // swizzle mode
   return d;
 }
 // kind::tf32 instruction descriptor: f32 accumulator, tf32 A and B, both K-major.
@@ -136,9 +159,10 @@ __device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t* r) {
 struct Work {
   int n0, m0, split, batch;
 };
+template <class C>
 __device__ __forceinline__ Work decode(int w, int tiles_n, int tiles_m, int splits) {
   Work r;
-  r.n0 = (w % tiles_n) * BN;
+  r.n0 = (w % tiles_n) * C::BN;
   w /= tiles_n;
   r.m0 = (w % tiles_m) * BM;
   w /= tiles_m;
@@ -150,11 +174,16 @@ __device__ __forceinline__ Work decode(int w, int tiles_n, int tiles_m, int spli
 // Persistent: each CTA walks work items blockIdx.x, +gridDim.x, ...; the
 // stage ring and the two accumulator buffers carry their phases across tiles,
 // so the epilogue of one tile overlaps the main loop of the next.
-__global__ void __launch_bounds__(THREADS, 1)
+template <class C>
+__global__ void __launch_bounds__(Derived<C>::THREADS, 1)
     k_gemm_tcgen05(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
                    const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
                    float* __restrict__ out, int m, int n, int k_blocks, int split_blocks,
                    int splits, long long split_stride, int tiles_n, int tiles_m, int work_items) {
+  using D = Derived<C>;
+  constexpr int BN = C::BN, BK = C::BK, STAGES = C::STAGES, CHUNK = C::CHUNK;
+  constexpr int TILE_A = D::TILE_A, TILE_B = D::TILE_B, STAGE_BYTES = D::STAGE_BYTES;
+  constexpr int EPI_COLS = D::EPI_COLS;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* full = (uint64_t*)(smem + STAGES * STAGE_BYTES);
@@ -173,7 +202,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 128);
+      mbar_init(&acc_empty[b], 128 * C::GROUPS);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -194,7 +223,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       uint32_t g = 0;  // k-blocks issued by this CTA so far
       for (int w = blockIdx.x; w < work_items && !*abort_flag; w += gridDim.x) {
-        const Work t = decode(w, tiles_n, tiles_m, splits);
+        const Work t = decode<C>(w, tiles_n, tiles_m, splits);
         const int kb0 = t.split * split_blocks;
         const int nkb = min(k_blocks, kb0 + split_blocks) - kb0;
         for (int i = 0; i < nkb; ++i, ++g) {
@@ -220,7 +249,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t idesc = instr_desc(BM, BN);
       uint32_t g = 0, gc = 0;  // k-blocks and chunks consumed by this CTA so far
       for (int w = blockIdx.x; w < work_items && !*abort_flag; w += gridDim.x) {
-        const Work t = decode(w, tiles_n, tiles_m, splits);
+        const Work t = decode<C>(w, tiles_n, tiles_m, splits);
         const int kb0 = t.split * split_blocks;
         const int nkb = min(k_blocks, kb0 + split_blocks) - kb0;
         const int chunks = (nkb + CHUNK - 1) / CHUNK;
@@ -248,9 +277,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int kk = 0; kk < BK / 8; ++kk) {
               const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle row
               const uint32_t first = (i > c * CHUNK || kk > 0) ? 1u : 0u;
-              umma_tf32(acc, smem_desc(a_lo + off), smem_desc(b_hi + off), idesc, first);
-              umma_tf32(acc, smem_desc(a_hi + off), smem_desc(b_lo + off), idesc, 1u);
-              umma_tf32(acc, smem_desc(a_hi + off), smem_desc(b_hi + off), idesc, 1u);
+              umma_tf32(acc, smem_desc<C>(a_lo + off), smem_desc<C>(b_hi + off), idesc, first);
+              umma_tf32(acc, smem_desc<C>(a_hi + off), smem_desc<C>(b_lo + off), idesc, 1u);
+              umma_tf32(acc, smem_desc<C>(a_hi + off), smem_desc<C>(b_hi + off), idesc, 1u);
             }
             umma_commit(&empty[s]);
           }
@@ -259,19 +288,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else {
-    // epilogue: warps 2..5 drain TMEM lane quarters (warp % 4) chunk by chunk
+    // epilogue: warps 2..9; lane quarter warp % 4, column half (warp - 2) / 4
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    const int c0 = half * EPI_COLS;
     uint32_t gc = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < work_items && ok; w += gridDim.x) {
-      const Work t = decode(w, tiles_n, tiles_m, splits);
+      const Work t = decode<C>(w, tiles_n, tiles_m, splits);
       const int kb0 = t.split * split_blocks;
       const int nkb = min(k_blocks, kb0 + split_blocks) - kb0;
       const int chunks = (nkb + CHUNK - 1) / CHUNK;
-      float total[BN];
+      float total[EPI_COLS];
 #pragma unroll
-      for (int j = 0; j < BN; ++j) total[j] = 0.0f;
+      for (int j = 0; j < EPI_COLS; ++j) total[j] = 0.0f;
       for (int c = 0; c < chunks; ++c, ++gc) {
         const int b = gc & 1;
         if (!mbar_wait(&acc_full[b], (gc >> 1) & 1, 3)) {
@@ -280,9 +311,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
-        for (int gq = 0; gq < BN / 16; ++gq) {
+        for (int gq = 0; gq < EPI_COLS / 16; ++gq) {
           uint32_t r[16];
-          tmem_ld16(tmem + lane_base + b * BN + gq * 16, r);
+          tmem_ld16(tmem + lane_base + b * BN + c0 + gq * 16, r);
 #pragma unroll
           for (int j = 0; j < 16; ++j)
             total[gq * 16 + j] = c == 0 ? __uint_as_float(r[j])
@@ -297,10 +328,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (row < m) {
         float* dst = out + (long long)t.split * split_stride + (long long)t.batch * m * n;
         const bool vec = (n % 4) == 0;
-        float* p = dst + (long long)row * n + t.n0;
+        float* p = dst + (long long)row * n + t.n0 + c0;
 #pragma unroll
-        for (int gq = 0; gq < BN / 16; ++gq) {
-          const int col = t.n0 + gq * 16;
+        for (int gq = 0; gq < EPI_COLS / 16; ++gq) {
+          const int col = t.n0 + c0 + gq * 16;
           if (vec && col + 16 <= n) {
 #pragma unroll
             for (int j = 0; j < 16; j += 4)
@@ -354,24 +385,29 @@ EncodeTiled encoder() {
 }
 
 bool make_map(CUtensorMap* map, const float* base, int64_t kp, int64_t rows, int64_t batch,
-              int box_rows) {
+              int box_rows, int bk, CUtensorMapSwizzle swizzle) {
   EncodeTiled enc = encoder();
   if (!enc) return false;
   cuuint64_t dims[3] = {(cuuint64_t)kp, (cuuint64_t)rows, (cuuint64_t)batch};
   cuuint64_t strides[2] = {(cuuint64_t)(kp * 4), (cuuint64_t)(rows * kp * 4)};
-  cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 1};
+  cuuint32_t box[3] = {(cuuint32_t)bk, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)base, dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+int g_tile_override = -1;  // TB_GEMM_TILE_N, or a test's forced choice
+
+int64_t wave_items(int64_t items, int sms) { return (items + sms - 1) / sms * sms; }
+
 }  // namespace
 
-int gemm_splits(int64_t batch, int64_t m, int64_t n, int64_t kp) {
-  const int64_t tiles = batch * ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
-  const int64_t kb = kp / BK;
+static int splits_for(int bn, int64_t batch, int64_t m, int64_t n, int64_t kp) {
+  const int bk = bn == 256 ? Cfg<256>::BK : Cfg<128>::BK;
+  const int64_t tiles = batch * ((m + BM - 1) / BM) * ((n + bn - 1) / bn);
+  const int64_t kb = kp / bk;
   if (tiles >= 120 || kb < 16) return 1;
   int64_t s = (148 + tiles - 1) / tiles;
   s = std::min<int64_t>(s, kb / 8);
@@ -381,28 +417,57 @@ int gemm_splits(int64_t batch, int64_t m, int64_t n, int64_t kp) {
   return (int)((kb + per - 1) / per);
 }
 
-bool launch_gemm_tcgen05_split(const float* a_hi, const float* a_lo, const float* b_hi,
-                               const float* b_lo, float* c, float* partial, int splits,
-                               int64_t batch, int64_t m, int64_t n, int64_t kp,
-                               cudaStream_t stream) {
-  if (kp % BK != 0 || m >= (1LL << 31) || n >= (1LL << 31) || batch > 65535) return false;
-  if (((uintptr_t)a_hi | (uintptr_t)a_lo | (uintptr_t)b_hi | (uintptr_t)b_lo) & 15) return false;
+// Tile width for a shape (from a sweep of the configs' GEMMs on B200): the
+// 256-wide tile moves 25% less operand data per flop, but it loses on narrow
+// outputs, short k, shapes it would have to split along k while 128 need not,
+// and shapes whose fewer, larger work items fill the SMs in fewer full waves.
+int gemm_tile_n(int64_t batch, int64_t m, int64_t n, int64_t kp) {
+  if (g_tile_override < 0) {
+    const char* e = getenv("TB_GEMM_TILE_N");
+    g_tile_override = e ? atoi(e) : 0;
+  }
+  if (g_tile_override == 128 || g_tile_override == 256) return g_tile_override;
+  if (n <= 64 || kp <= 128) return 128;
+  if (n > 16384 && kp <= 1024) return 128;  // very wide, short-k outputs (vocabulary logits)
+  if (splits_for(256, batch, m, n, kp) > 1 && splits_for(128, batch, m, n, kp) == 1) return 128;
+  const int64_t tm = batch * ((m + BM - 1) / BM);
+  const int64_t items128 = tm * ((n + 127) / 128), items256 = tm * ((n + 255) / 256);
+  const double eff128 = (double)items128 / wave_items(items128, 148);
+  const double eff256 = (double)items256 / wave_items(items256, 148);
+  return eff256 * 1.1 >= eff128 ? 256 : 128;
+}
+
+void set_gemm_tile_n(int tile) { g_tile_override = tile; }
+
+int gemm_splits(int64_t batch, int64_t m, int64_t n, int64_t kp) {
+  return splits_for(gemm_tile_n(batch, m, n, kp), batch, m, n, kp);
+}
+
+namespace {
+template <class C>
+bool launch_cfg(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
+                float* c, float* partial, int splits, int64_t batch, int64_t m, int64_t n,
+                int64_t kp, cudaStream_t stream) {
+  using D = Derived<C>;
+  if (kp % C::BK != 0) return false;
   CUtensorMap ma, mal, mb, mbl;
-  if (!make_map(&ma, a_hi, kp, m, batch, BM) || !make_map(&mal, a_lo, kp, m, batch, BM) ||
-      !make_map(&mb, b_hi, kp, n, batch, BN) || !make_map(&mbl, b_lo, kp, n, batch, BN))
+  if (!make_map(&ma, a_hi, kp, m, batch, BM, C::BK, C::TMA_SWIZZLE) ||
+      !make_map(&mal, a_lo, kp, m, batch, BM, C::BK, C::TMA_SWIZZLE) ||
+      !make_map(&mb, b_hi, kp, n, batch, C::BN, C::BK, C::TMA_SWIZZLE) ||
+      !make_map(&mbl, b_lo, kp, n, batch, C::BN, C::BK, C::TMA_SWIZZLE))
     return false;
   static bool configured = false;
   if (!configured) {
-    if (cudaFuncSetAttribute(k_gemm_tcgen05, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             SMEM_BYTES) != cudaSuccess)
+    if (cudaFuncSetAttribute(k_gemm_tcgen05<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             D::SMEM_BYTES) != cudaSuccess)
       return false;
     configured = true;
   }
-  const int kb = (int)(kp / BK);
+  const int kb = (int)(kp / C::BK);
   if (splits < 1 || !partial) splits = 1;
   const int per = (kb + splits - 1) / splits;
   float* target = splits > 1 ? partial : c;
-  const int tiles_n = (int)((n + BN - 1) / BN), tiles_m = (int)((m + BM - 1) / BM);
+  const int tiles_n = (int)((n + C::BN - 1) / C::BN), tiles_m = (int)((m + BM - 1) / BM);
   const long long items = (long long)tiles_n * tiles_m * batch * splits;
   if (items >= (1LL << 31)) return false;
   static int sms = 0;
@@ -413,16 +478,27 @@ bool launch_gemm_tcgen05_split(const float* a_hi, const float* a_lo, const float
     if (sms <= 0) sms = 148;
   }
   const int grid = (int)std::min<long long>(items, sms);
-  k_gemm_tcgen05<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mal, mb, mbl, target, (int)m, (int)n,
-                                                        kb, per, splits,
-                                                        (long long)(batch * m * n), tiles_n,
-                                                        tiles_m, (int)items);
+  k_gemm_tcgen05<C><<<grid, D::THREADS, D::SMEM_BYTES, stream>>>(
+      ma, mal, mb, mbl, target, (int)m, (int)n, kb, per, splits, (long long)(batch * m * n),
+      tiles_n, tiles_m, (int)items);
   if (splits > 1) {
     const long long count = batch * m * n;
     int blocks = (int)std::min<long long>((count + 255) / 256, 148 * 8);
     k_split_sum<<<blocks, 256, 0, stream>>>(partial, c, count, splits);
   }
   return cudaPeekAtLastError() == cudaSuccess;
+}
+}  // namespace
+
+bool launch_gemm_tcgen05_split(const float* a_hi, const float* a_lo, const float* b_hi,
+                               const float* b_lo, float* c, float* partial, int splits,
+                               int64_t batch, int64_t m, int64_t n, int64_t kp,
+                               cudaStream_t stream) {
+  if (m >= (1LL << 31) || n >= (1LL << 31) || batch > 65535) return false;
+  if (((uintptr_t)a_hi | (uintptr_t)a_lo | (uintptr_t)b_hi | (uintptr_t)b_lo) & 15) return false;
+  if (gemm_tile_n(batch, m, n, kp) == 256)
+    return launch_cfg<Cfg<256>>(a_hi, a_lo, b_hi, b_lo, c, partial, splits, batch, m, n, kp, stream);
+  return launch_cfg<Cfg<128>>(a_hi, a_lo, b_hi, b_lo, c, partial, splits, batch, m, n, kp, stream);
 }
 
 bool launch_gemm_tcgen05(const float* a_hi, const float* a_lo, const float* b_hi,

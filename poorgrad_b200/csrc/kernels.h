@@ -36,6 +36,9 @@ bool launch_gemm_tcgen05_split(const float* a_hi, const float* a_lo, const float
                                const float* b_lo, float* c, float* partial, int splits,
                                int64_t batch, int64_t m, int64_t n, int64_t kp,
                                cudaStream_t stream);
+// Tile width (128 or 256) the tcgen05 path uses for a shape; a test may force one.
+int gemm_tile_n(int64_t batch, int64_t m, int64_t n, int64_t kp);
+void set_gemm_tile_n(int tile);
 // Split-K factor the tcgen05 path uses for a shape (1 = no split).
 int gemm_splits(int64_t batch, int64_t m, int64_t n, int64_t kp);
 // Error code recorded by a tcgen05 GEMM whose bounded wait expired (0 = none).

@@ -28,7 +28,8 @@ def _prep(torch, x, kp):
 @pytest.mark.parametrize("batch,m,n,k,splits", [
     (1, 128, 128, 32, 1), (1, 256, 384, 96, 1), (2, 130, 70, 40, 1), (1, 1, 5, 7, 1),
     (3, 200, 136, 300, 1), (1, 512, 512, 4096, 4), (1, 128, 256, 1024, 3)])
-def test_tcgen05_matches_f64(device, batch, m, n, k, splits):
+@pytest.mark.parametrize("tile", [128, 256])
+def test_tcgen05_matches_f64(device, batch, m, n, k, splits, tile):
     import torch
     from poorgrad_b200.abi import load_library
     lib = load_library()
@@ -43,6 +44,7 @@ def test_tcgen05_matches_f64(device, batch, m, n, k, splits):
     ref = torch.bmm(a.double(), bt.double().transpose(1, 2))
     factor = 8 if k <= 1024 else 16
     tol = factor * EPS * math.sqrt(k) * (1 + ref.abs())
+    lib.tbx_set_gemm_tile_n(tile)
     for engine in (2, 1):
         c = torch.full((batch, m, n), float("nan"), device="cuda")
         part = torch.empty((max(splits, 1), batch, m, n), device="cuda")
@@ -52,3 +54,4 @@ def test_tcgen05_matches_f64(device, batch, m, n, k, splits):
         assert lib.tbx_gemm_error() == 0
         err = (c.double() - ref).abs()
         assert torch.all(err <= tol), f"engine {engine}: worst {(err / tol).max().item()}"
+    lib.tbx_set_gemm_tile_n(0)
