@@ -155,17 +155,27 @@ __device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t* r) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Work item w of tiles_n x tiles_m x (batch * splits): n fastest.
+// Work item w of tiles_n x tiles_m x (batch * splits).  The faster-varying
+// tile index is the one whose operand is smaller, so consecutive work items
+// (running concurrently on neighbouring SMs) share the larger operand's tile
+// and the smaller operand is what gets re-read from L2.
 struct Work {
   int n0, m0, split, batch;
 };
 template <class C>
-__device__ __forceinline__ Work decode(int w, int tiles_n, int tiles_m, int splits) {
+__device__ __forceinline__ Work decode(int w, int tiles_n, int tiles_m, int splits, int m_fast) {
   Work r;
-  r.n0 = (w % tiles_n) * C::BN;
-  w /= tiles_n;
-  r.m0 = (w % tiles_m) * BM;
-  w /= tiles_m;
+  if (m_fast) {
+    r.m0 = (w % tiles_m) * BM;
+    w /= tiles_m;
+    r.n0 = (w % tiles_n) * C::BN;
+    w /= tiles_n;
+  } else {
+    r.n0 = (w % tiles_n) * C::BN;
+    w /= tiles_n;
+    r.m0 = (w % tiles_m) * BM;
+    w /= tiles_m;
+  }
   r.split = w % splits;
   r.batch = w / splits;
   return r;
@@ -179,7 +189,8 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
     k_gemm_tcgen05(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
                    const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
                    float* __restrict__ out, int m, int n, int k_blocks, int split_blocks,
-                   int splits, long long split_stride, int tiles_n, int tiles_m, int work_items) {
+                   int splits, long long split_stride, int tiles_n, int tiles_m, int work_items,
+                   int m_fast) {
   using D = Derived<C>;
   constexpr int BN = C::BN, BK = C::BK, STAGES = C::STAGES, CHUNK = C::CHUNK;
   constexpr int TILE_A = D::TILE_A, TILE_B = D::TILE_B, STAGE_BYTES = D::STAGE_BYTES;
@@ -223,7 +234,7 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
     if (lane == 0) {
       uint32_t g = 0;  // k-blocks issued by this CTA so far
       for (int w = blockIdx.x; w < work_items && !*abort_flag; w += gridDim.x) {
-        const Work t = decode<C>(w, tiles_n, tiles_m, splits);
+        const Work t = decode<C>(w, tiles_n, tiles_m, splits, m_fast);
         const int kb0 = t.split * split_blocks;
         const int nkb = min(k_blocks, kb0 + split_blocks) - kb0;
         for (int i = 0; i < nkb; ++i, ++g) {
@@ -249,7 +260,7 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
       const uint32_t idesc = instr_desc(BM, BN);
       uint32_t g = 0, gc = 0;  // k-blocks and chunks consumed by this CTA so far
       for (int w = blockIdx.x; w < work_items && !*abort_flag; w += gridDim.x) {
-        const Work t = decode<C>(w, tiles_n, tiles_m, splits);
+        const Work t = decode<C>(w, tiles_n, tiles_m, splits, m_fast);
         const int kb0 = t.split * split_blocks;
         const int nkb = min(k_blocks, kb0 + split_blocks) - kb0;
         const int chunks = (nkb + CHUNK - 1) / CHUNK;
@@ -296,7 +307,7 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
     uint32_t gc = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < work_items && ok; w += gridDim.x) {
-      const Work t = decode<C>(w, tiles_n, tiles_m, splits);
+      const Work t = decode<C>(w, tiles_n, tiles_m, splits, m_fast);
       const int kb0 = t.split * split_blocks;
       const int nkb = min(k_blocks, kb0 + split_blocks) - kb0;
       const int chunks = (nkb + CHUNK - 1) / CHUNK;
@@ -480,7 +491,7 @@ bool launch_cfg(const float* a_hi, const float* a_lo, const float* b_hi, const f
   const int grid = (int)std::min<long long>(items, sms);
   k_gemm_tcgen05<C><<<grid, D::THREADS, D::SMEM_BYTES, stream>>>(
       ma, mal, mb, mbl, target, (int)m, (int)n, kb, per, splits, (long long)(batch * m * n),
-      tiles_n, tiles_m, (int)items);
+      tiles_n, tiles_m, (int)items, m > 0 && n > m ? 1 : 0);
   if (splits > 1) {
     const long long count = batch * m * n;
     int blocks = (int)std::min<long long>((count + 255) / 256, 148 * 8);

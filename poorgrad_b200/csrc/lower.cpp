@@ -1147,6 +1147,21 @@ __device__ __forceinline__ float tb_max(float a, float b) {
   if (isnan(b)) return a;
   return (b > a) ? b : a;
 }
+// Online log-sum-exp state (m = running max, s = sum of exp(x - m)).
+__device__ __forceinline__ void tb_lse_push(float& m, float& s, float x) {
+  if (x > m) {
+    s = s * expf(m - x) + 1.0f;
+    m = x;
+  } else if (x != -TB_INF) {
+    s = s + expf(x - m);
+  }
+}
+__device__ __forceinline__ void tb_lse_merge(float& m, float& s, float m2, float s2) {
+  if (s2 == 0.0f && m2 == -TB_INF) return;
+  if (s == 0.0f && m == -TB_INF) { m = m2; s = s2; return; }
+  if (m2 > m) { s = s * expf(m - m2) + s2; m = m2; }
+  else s = s + s2 * expf(m2 - m);
+}
 __device__ __forceinline__ float tb_tf32(float x) {
   unsigned r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
@@ -1226,6 +1241,36 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
   Lw.row_shape(S, T, KC, vec);
   E.vec = vec;
   int64_t teams = 256 / T;
+  // One-pass log-sum-exp: a row sum of exp(x - bcast(row max of x)) whose max
+  // is a member here is accumulated in the max's own pass, online (running
+  // max and rescaled sum), instead of a second pass over the row.
+  std::vector<int> partner(K.members.size(), -1), partner_of(K.members.size(), -1);
+  {
+    std::map<int, int> max_member;
+    for (size_t m = 0; m < K.members.size(); ++m)
+      if (K.members[m].type == MemberType::ROW_MAX) max_member[K.members[m].node] = (int)m;
+    auto virt = [&](int n) { return !P.info[n].materialized; };
+    for (size_t m = 0; m < K.members.size(); ++m) {
+      if (K.members[m].type != MemberType::ROW_SUM) continue;
+      const int e = P.nodes[K.members[m].node].operands[0];
+      if (P.nodes[e].op != TB_OP_EXP || !virt(e)) continue;
+      const int sh = P.nodes[e].operands[0];
+      if (P.nodes[sh].op != TB_OP_SUB || !virt(sh)) continue;
+      const int x = P.nodes[sh].operands[0], pb = P.nodes[sh].operands[1];
+      if (P.nodes[pb].op != TB_OP_BROADCAST_ALONG || P.info[pb].materialized) continue;
+      auto it = max_member.find(P.nodes[pb].operands[0]);
+      if (it == max_member.end() || partner[it->second] >= 0) continue;
+      if (P.nodes[K.members[it->second].node].operands[0] != x) continue;
+      partner[it->second] = (int)m;
+      partner_of[m] = it->second;
+      K.members[m].phase = K.members[it->second].phase;
+    }
+    std::set<int> used;
+    for (auto& mm : K.members) used.insert(mm.phase);
+    std::map<int, int> rank;
+    for (int ph : used) rank[ph] = (int)rank.size();
+    for (auto& mm : K.members) mm.phase = rank[mm.phase];
+  }
   bool has_col = false, has_all = false;
   int maxphase = 0;
   for (auto& m : K.members) {
@@ -1238,7 +1283,7 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
   int64_t cap = (has_col && L >= 4096) ? SMS * 2 : SMS * 4;
   K.grid = std::max<int64_t>(1, std::min<int64_t>((R + teams - 1) / teams, cap));
   if (has_col || has_all) E.exact = false;
-  E.line("__shared__ float sred[8];");
+  E.line("__shared__ float sred[8], sred2[8];");
   if (has_col) E.line("__shared__ float scol[" + lit(L) + "];");
   E.line("const int tid = threadIdx.x, team = tid / " + std::to_string(T) + ", tl = tid % " +
          std::to_string(T) + ";");
@@ -1264,7 +1309,8 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
       if (mm.phase != ph) continue;
       if (mm.type == MemberType::ROW_SUM) E.line("float ra" + std::to_string(m) + " = 0.0f;");
       if (mm.type == MemberType::ROW_MAX)
-        E.line("float ra" + std::to_string(m) + " = __int_as_float(0x7fc00000);");
+        E.line("float ra" + std::to_string(m) + " = " +
+               (partner[m] >= 0 ? "-TB_INF;" : "__int_as_float(0x7fc00000);"));
     }
     bool unroll = has_col;
     E.line(unroll ? "#pragma unroll" : "#pragma unroll 4");
@@ -1287,6 +1333,7 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
         const Member& mm = K.members[m];
         if (mm.phase != ph) continue;
         int n = mm.node;
+        if (partner_of[m] >= 0) continue;  // accumulated with its max
         std::string x;
         if (mm.type == MemberType::EW) {
           x = E.def(n, idx);
@@ -1298,7 +1345,12 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
         std::string ms = std::to_string(m);
         switch (mm.type) {
           case MemberType::ROW_SUM: E.line("ra" + ms + " = __fadd_rn(ra" + ms + ", " + x + ");"); break;
-          case MemberType::ROW_MAX: E.line("ra" + ms + " = tb_max(ra" + ms + ", " + x + ");"); break;
+          case MemberType::ROW_MAX:
+            if (partner[m] >= 0)
+              E.line("tb_lse_push(ra" + ms + ", ra" + std::to_string(partner[m]) + ", " + x + ");");
+            else
+              E.line("ra" + ms + " = tb_max(ra" + ms + ", " + x + ");");
+            break;
           case MemberType::COL_SUM:
             E.line("ca" + ms + "[kc * " + std::to_string(vec) + " + " + std::to_string(v) +
                    "] = __fadd_rn(ca" + ms + "[kc * " + std::to_string(vec) + " + " +
@@ -1331,7 +1383,32 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
       if (mm.phase != ph || (mm.type != MemberType::ROW_SUM && mm.type != MemberType::ROW_MAX))
         continue;
       E.exact = false;
+      if (partner_of[m] >= 0) continue;  // reduced with its max
       std::string ms = std::to_string(m);
+      if (partner[m] >= 0) {
+        const std::string ts = std::to_string(partner[m]);
+        E.line("float rv" + ms + " = ra" + ms + ", rv" + ts + " = ra" + ts + ";");
+        int64_t width = std::min<int64_t>(T, 32);
+        for (int64_t o = width / 2; o > 0; o /= 2)
+          E.line("{ const float m2 = __shfl_xor_sync(0xffffffffu, rv" + ms + ", " +
+                 std::to_string(o) + "), s2 = __shfl_xor_sync(0xffffffffu, rv" + ts + ", " +
+                 std::to_string(o) + "); tb_lse_merge(rv" + ms + ", rv" + ts + ", m2, s2); }");
+        if (T > 32) {
+          E.line("if ((tid & 31) == 0) { sred[tid >> 5] = rv" + ms + "; sred2[tid >> 5] = rv" + ts + "; }");
+          E.line("__syncthreads();");
+          int64_t w = T / 32;
+          E.line("{ const int w0 = team * " + std::to_string(w) + "; rv" + ms + " = sred[w0]; rv" +
+                 ts + " = sred2[w0];");
+          for (int64_t q = 1; q < w; ++q)
+            E.line("  tb_lse_merge(rv" + ms + ", rv" + ts + ", sred[w0 + " + std::to_string(q) +
+                   "], sred2[w0 + " + std::to_string(q) + "]);");
+          E.line("}");
+          E.line("__syncthreads();");
+        }
+        E.line("if (act && tl == 0) { " + E.fptr(P.info[mm.node].buf) + "[row] = rv" + ms + "; " +
+               E.fptr(P.info[K.members[partner[m]].node].buf) + "[row] = rv" + ts + "; }");
+        continue;
+      }
       std::string op = mm.type == MemberType::ROW_SUM ? "__fadd_rn" : "tb_max";
       E.line("float rv" + ms + " = ra" + ms + ";");
       int64_t width = std::min<int64_t>(T, 32);
