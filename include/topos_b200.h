@@ -150,6 +150,11 @@ int tb_params_download(const tb_params* params, int32_t slot, float* host, int64
  * device program (and an attached gradient exchange and optimizer step) is
  * launched as one CUDA graph.  Asynchronous with respect to the host. */
 int tb_plan_run(tb_plan* plan, tb_params* params, int32_t feed_count, const tb_feed* feeds);
+/* Replaces: `Run::backward(output)` then `Gradients::of(parameter)` (engine/run.rs:229-318)
+ * for a plan compiled with `backward` set: the reverse scan of every scalar readable root
+ * runs inside each `tb_plan_run`, and this answers the node whose value (read with
+ * `tb_plan_read`) is d root / d parameter. */
+int tb_plan_gradient_node(const tb_plan* plan, int64_t root, int64_t parameter, int64_t* node);
 /* Waits for the plan's stream. */
 int tb_plan_synchronize(tb_plan* plan);
 /* Copies a readable value (row-major, volume elements) to host memory (waits). */

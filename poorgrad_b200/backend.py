@@ -128,6 +128,20 @@ class DevicePlan:
                "tb_plan_read")
         return out
 
+    def gradient(self, root, parameter) -> np.ndarray:
+        """`Run::backward(root)` then `Gradients::of(parameter)` for a plan
+        compiled with ``Request(...).backward()``."""
+        r = root.index if hasattr(root, "index") else int(root)
+        p = parameter.index if hasattr(parameter, "index") else int(parameter)
+        node = C.c_int64()
+        _check(self.lib.tb_plan_gradient_node(self.handle, r, p, C.byref(node)),
+               "tb_plan_gradient_node")
+        shape = self.columns.nodes[p].shape
+        out = np.empty(shape, dtype=np.float32)
+        _check(self.lib.tb_plan_read(self.handle, node.value, fptr(out), max(out.size, 1)),
+               "tb_plan_read")
+        return out
+
     def device_pointer(self, symbol) -> int:
         index = symbol.index if hasattr(symbol, "index") else int(symbol)
         ptr = C.c_void_p()

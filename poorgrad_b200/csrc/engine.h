@@ -148,6 +148,8 @@ struct Program {
   std::vector<int> input_buffer;   // per input slot: buffer id (dense or indices)
   std::vector<int> input_node;     // per input slot: node index
   std::map<int, int> sort_of;      // selection node -> SORT kernel index
+  // engine-backward plans: (scalar root, parameter node) -> gradient node
+  std::map<std::pair<int, int>, int> gradient_of;
   std::string source;              // all generated kernels (one NVRTC program)
 };
 

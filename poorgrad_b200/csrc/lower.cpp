@@ -322,6 +322,204 @@ class Lowerer {
         P.order.push_back((int)i);
       }
     }
+    if (d->backward) append_backward(d);
+  }
+
+  // ---- engine-backward plans (`Run::backward`, engine/run.rs:229-318)
+  // For every scalar readable root, the reverse scan is appended as nodes: a
+  // `one_like` seed, the derivative rules of function/*.rs in the engine's
+  // order, and per slot a zero-seeded accumulation `g = g + c` in reverse-scan
+  // order.  The gradient of every parameter becomes a readable value.
+  int grad_node(int op, int a, int b, std::vector<int64_t> shape,
+                std::vector<int64_t> attrs = {}) {
+    Node n;
+    n.op = op;
+    n.operands[0] = a;
+    n.operands[1] = b;
+    n.rank = (int)shape.size();
+    if (n.rank > TB_MAX_RANK) fail("rank above the ABI maximum in a gradient");
+    for (int i = 0; i < n.rank; ++i) n.shape[i] = shape[i];
+    for (size_t i = 0; i < attrs.size(); ++i) n.attrs[i] = attrs[i];
+    n.wanted = true;
+    int id = add_node(n);
+    P.order.push_back(id);
+    return id;
+  }
+  std::vector<int64_t> dims(int n) const { return P.nodes[n].dims(); }
+  int constant_like(int n, float c) {
+    int id = grad_node(TB_OP_LEAF, -1, -1, dims(n));
+    P.nodes[id].payload = TB_PAYLOAD_CONSTANT;
+    P.nodes[id].constant = c;
+    return id;
+  }
+  int ew(int op, int a, int b = -1) { return grad_node(op, a, b, dims(a)); }
+  int swapped(int v) {
+    std::vector<int64_t> s = dims(v);
+    int r = (int)s.size();
+    if (r <= 2) {
+      std::reverse(s.begin(), s.end());
+      return grad_node(TB_OP_TRANSPOSE, v, -1, s);
+    }
+    std::vector<int64_t> order(r);
+    for (int i = 0; i < r; ++i) order[i] = i;
+    std::swap(order[r - 2], order[r - 1]);
+    std::swap(s[r - 2], s[r - 1]);
+    return grad_node(TB_OP_PERMUTE, v, -1, s, order);
+  }
+  int matmul(int a, int b) {
+    std::vector<int64_t> s = dims(a);
+    s.back() = P.nodes[b].shape[P.nodes[b].rank - 1];
+    return grad_node(TB_OP_MATMUL, a, b, s);
+  }
+  int sum_along(int x, int64_t axis) {
+    std::vector<int64_t> s = dims(x);
+    s.erase(s.begin() + axis);
+    return grad_node(TB_OP_SUM_ALONG, x, -1, s, {axis});
+  }
+  int bcast_along(int x, int64_t axis, int like) {
+    return grad_node(TB_OP_BROADCAST_ALONG, x, like, dims(like), {axis});
+  }
+
+  // The cotangents of node i (original indices) given output value `out`,
+  // operand values `x`, `y` and gradient `g` (function/*.rs `backward`).
+  void rule(const Node& nd, int x, int y, int out, int g, int& cx, int& cy) {
+    const int64_t* at = nd.attrs;
+    cx = cy = -1;
+    switch (nd.op) {
+      case TB_OP_ADD: cx = g; cy = g; return;
+      case TB_OP_SUB: cx = g; cy = ew(TB_OP_NEG, g); return;
+      case TB_OP_MUL: cx = ew(TB_OP_MUL, g, y); cy = ew(TB_OP_MUL, g, x); return;
+      case TB_OP_DIV: {
+        cx = ew(TB_OP_DIV, g, y);
+        int go = ew(TB_OP_MUL, g, out);
+        cy = ew(TB_OP_NEG, ew(TB_OP_DIV, go, y));
+        return;
+      }
+      case TB_OP_NEG: cx = ew(TB_OP_NEG, g); return;
+      case TB_OP_TANH: {
+        int one = constant_like(out, 1.0f);
+        int d = ew(TB_OP_SUB, one, ew(TB_OP_MUL, out, out));
+        cx = ew(TB_OP_MUL, g, d);
+        return;
+      }
+      case TB_OP_EXP: cx = ew(TB_OP_MUL, g, out); return;
+      case TB_OP_LN: cx = ew(TB_OP_DIV, g, x); return;
+      case TB_OP_SQRT: cx = ew(TB_OP_DIV, g, ew(TB_OP_ADD, out, out)); return;
+      case TB_OP_POWF: {
+        int lowered = ew(TB_OP_SUB, y, constant_like(y, 1.0f));
+        int ge = ew(TB_OP_MUL, g, y);
+        cx = ew(TB_OP_MUL, ge, ew(TB_OP_POWF, x, lowered));
+        int go = ew(TB_OP_MUL, g, out);
+        cy = ew(TB_OP_MUL, go, ew(TB_OP_LN, x));
+        return;
+      }
+      case TB_OP_MAXIMUM: {
+        int w = ew(TB_OP_STEP, x, y);
+        cx = ew(TB_OP_MUL, g, w);
+        cy = ew(TB_OP_MUL, g, ew(TB_OP_SUB, constant_like(w, 1.0f), w));
+        return;
+      }
+      case TB_OP_RELU: {
+        int z = constant_like(x, 0.0f);
+        cx = ew(TB_OP_MUL, g, ew(TB_OP_STEP, x, z));
+        return;
+      }
+      case TB_OP_STEP: return;
+      case TB_OP_MATMUL:
+        cx = matmul(g, swapped(y));
+        cy = matmul(swapped(x), g);
+        return;
+      case TB_OP_TRANSPOSE: {
+        std::vector<int64_t> s = dims(g);
+        std::reverse(s.begin(), s.end());
+        cx = grad_node(TB_OP_TRANSPOSE, g, -1, s);
+        return;
+      }
+      case TB_OP_SUM: cx = grad_node(TB_OP_BROADCAST, g, x, dims(x)); return;
+      case TB_OP_SUM_ALONG: cx = bcast_along(g, at[0], x); return;
+      case TB_OP_BROADCAST: {
+        int total = grad_node(TB_OP_SUM, g, -1, {});
+        cx = grad_node(TB_OP_BROADCAST, total, x, dims(x));
+        return;
+      }
+      case TB_OP_BROADCAST_ALONG: cx = sum_along(g, at[0]); return;
+      case TB_OP_RESHAPE: cx = grad_node(TB_OP_RESHAPE, g, -1, dims(x)); return;
+      case TB_OP_PERMUTE: {
+        std::vector<int64_t> inv(nd.rank);
+        for (int j = 0; j < nd.rank; ++j) inv[at[j]] = j;
+        cx = grad_node(TB_OP_PERMUTE, g, -1, dims(x), inv);
+        return;
+      }
+      case TB_OP_NARROW:
+        cx = grad_node(TB_OP_PAD, g, -1, dims(x), {at[0], at[1], P.nodes[x].shape[at[0]]});
+        return;
+      case TB_OP_PAD:
+        cx = grad_node(TB_OP_NARROW, g, -1, dims(x), {at[0], at[1], P.nodes[x].shape[at[0]]});
+        return;
+      case TB_OP_UNFOLD:
+        cx = grad_node(TB_OP_FOLD, g, -1, dims(x),
+                       {at[0], at[1], at[2], at[3], P.nodes[x].shape[at[0]]});
+        return;
+      case TB_OP_FOLD:
+        cx = grad_node(TB_OP_UNFOLD, g, -1, dims(x), {at[0], at[1], at[2], at[3]});
+        return;
+      case TB_OP_GATHER:
+        cx = grad_node(TB_OP_SCATTER, g, y, dims(x), {P.nodes[x].shape[0]});
+        return;
+      case TB_OP_SCATTER: {
+        std::vector<int64_t> s = dims(x);
+        cx = grad_node(TB_OP_GATHER, g, y, s);
+        return;
+      }
+      case TB_OP_LOG_SOFTMAX: {
+        int total = bcast_along(sum_along(g, at[0]), at[0], g);
+        cx = ew(TB_OP_SUB, g, ew(TB_OP_MUL, ew(TB_OP_EXP, out), total));
+        return;
+      }
+      case TB_OP_LOG_SUM_EXP: {
+        int prob = ew(TB_OP_EXP, ew(TB_OP_SUB, x, bcast_along(out, at[0], x)));
+        cx = ew(TB_OP_MUL, bcast_along(g, at[0], x), prob);
+        return;
+      }
+    }
+    fail("no derivative rule for op " + std::to_string(nd.op));
+  }
+
+  void append_backward(const tb_plan_desc* d) {
+    const int count = (int)d->node_count;
+    for (int root = 0; root < count; ++root) {
+      const tb_node& r = d->nodes[root];
+      if (!r.readable || !r.wanted || r.rank != 0) continue;
+      std::vector<int> grad(root + 1, -1);
+      std::vector<char> ancestor(root + 1, 0);
+      grad[root] = constant_like(resolve(root), 1.0f);
+      ancestor[root] = 1;
+      for (int i = root; i >= 0; --i) {
+        if (!ancestor[i]) continue;
+        const tb_node& src = d->nodes[i];
+        if (src.op == TB_OP_LEAF || src.op == TB_OP_PARAMETER || src.op == TB_OP_INPUT) continue;
+        Node nd = P.nodes[i];  // attributes; operands below are the original links
+        const int lx = src.operands[0], ly = src.operands[1];
+        const int x = lx >= 0 ? resolve(lx) : -1, y = ly >= 0 ? resolve(ly) : -1;
+        int cx, cy;
+        rule(nd, x, y, resolve(i), grad[i], cx, cy);
+        const int links[2] = {lx, ly};
+        const int cots[2] = {cx, cy};
+        for (int k = 0; k < 2; ++k) {
+          if (links[k] < 0 || cots[k] < 0) continue;
+          const int slot = links[k];
+          ancestor[slot] = 1;
+          const int seed = grad[slot] >= 0 ? grad[slot] : constant_like(resolve(slot), 0.0f);
+          grad[slot] = ew(TB_OP_ADD, seed, cots[k]);
+        }
+      }
+      for (int i = 0; i <= root; ++i) {
+        if (d->nodes[i].op != TB_OP_PARAMETER) continue;
+        int gn = grad[i] >= 0 ? grad[i] : constant_like(i, 0.0f);
+        P.nodes[gn].readable = true;
+        P.gradient_of[{root, i}] = gn;
+      }
+    }
   }
 
   // function/log_sum_exp.rs:53-63 and function/log_softmax.rs:51-65 as
@@ -1313,7 +1511,7 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
                (partner[m] >= 0 ? "-TB_INF;" : "__int_as_float(0x7fc00000);"));
     }
     bool unroll = has_col;
-    E.line(unroll ? "#pragma unroll" : "#pragma unroll 4");
+    E.line(unroll ? "#pragma unroll" : (vec == 1 ? "#pragma unroll 8" : "#pragma unroll 4"));
     E.line("for (int kc = 0; kc < " + std::to_string(KC) + "; ++kc) {");
     E.indent += 2;
     E.line("const I j0 = ((I)kc * " + std::to_string(T) + " + tl) * " + std::to_string(vec) + ";");

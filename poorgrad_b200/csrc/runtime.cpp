@@ -659,6 +659,18 @@ int tb_plan_run(tb_plan* plan, tb_params* params, int32_t feed_count, const tb_f
   });
 }
 
+int tb_plan_gradient_node(const tb_plan* plan, int64_t root, int64_t parameter, int64_t* node) {
+  return guarded([&]() {
+    auto it = plan->prog->gradient_of.find({(int)root, (int)parameter});
+    if (it == plan->prog->gradient_of.end())
+      throw Failure(TB_INVALID, "no gradient of that root with respect to that parameter: "
+                                "compile with backward set, a scalar readable root and a "
+                                "parameter node");
+    *node = it->second;
+    return (int)TB_OK;
+  }, false);
+}
+
 int tb_plan_synchronize(tb_plan* plan) {
   return guarded([&]() {
     check(cudaStreamSynchronize(plan->stream), "cudaStreamSynchronize");
