@@ -96,22 +96,25 @@ def dist_setup(gpus: int):
     return rank, world, local
 
 
-def build_workload(name: str, rank: int):
-    from poorgrad_b200 import configs
-    if name == "charmlp":
-        return configs.char_mlp(batch=16384, seed=4), {"model": "char-mlp-lm", "global_batch_per_gpu": 16384,
-                                                      "context": 8, "embedding": 64, "hidden": 512,
-                                                      "vocab": 27}
-    if name == "gpt2":
-        return configs.gpt2(), {"model": "gpt2-small-shaped", "global_batch_per_gpu": 8,
-                                "seq_len": 1024, "layers": 12, "d_model": 768}
-    if name == "mlp":
-        return configs.mlp(batch=128), {"model": "mlp-784-256-10", "global_batch_per_gpu": 128}
-    if name == "fused":
-        return configs.fused(), {"model": "fused-8192x8192"}
-    if name == "gemm":
-        return configs.gemm(), {"model": "gemm-4096^3-fwd+bwd"}
-    raise ValueError(name)
+CONFIGS = {
+    "charmlp": (lambda: __import__("poorgrad_b200.configs").configs.char_mlp(batch=16384, seed=4),
+                {"model": "char-mlp-lm", "global_batch_per_gpu": 16384, "context": 8,
+                 "embedding": 64, "hidden": 512, "vocab": 27}),
+    "gpt2": (lambda: __import__("poorgrad_b200.configs").configs.gpt2(),
+             {"model": "gpt2-small-shaped", "global_batch_per_gpu": 8, "seq_len": 1024,
+              "layers": 12, "d_model": 768}),
+    "mlp": (lambda: __import__("poorgrad_b200.configs").configs.mlp(batch=128),
+            {"model": "mlp-784-256-10", "global_batch_per_gpu": 128}),
+    "fused": (lambda: __import__("poorgrad_b200.configs").configs.fused(),
+              {"model": "fused-8192x8192"}),
+    "gemm": (lambda: __import__("poorgrad_b200.configs").configs.gemm(),
+             {"model": "gemm-4096^3-fwd+bwd"}),
+}
+
+
+def build_workload(name: str, rank: int, config_only: bool = False):
+    make, cfg = CONFIGS[name]
+    return (None if config_only else make()), dict(cfg)
 
 
 def reference_arm(args, name):
@@ -165,11 +168,14 @@ def reference_arm(args, name):
     else:
         value = cores * shard / dt
         unit = "samples/s"
-    line = {"impl": "reference", "metric": f"train {unit} ({name})", "value": value, "unit": unit,
+    _, cfg = build_workload(name, 0, config_only=True)
+    cfg.update({"workload": name, "parallelism": f"dp{args.gpus}"})
+    line = {"impl": "reference", "metric": "train samples/s" if unit == "samples/s" else f"train {unit}",
+            "value": value, "unit": unit,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded splitmix64 streams)",
-            "config": {"workload": name},
+            "config": cfg,
             "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}

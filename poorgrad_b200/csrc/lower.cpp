@@ -1478,7 +1478,7 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
   }
   K.block = 256;
   // per-block column partials cost blocks * L floats: fewer blocks for wide rows
-  int64_t cap = (has_col && L >= 4096) ? SMS * 2 : SMS * 4;
+  int64_t cap = (has_col && L >= 4096) ? SMS * 3 : SMS * 4;
   K.grid = std::max<int64_t>(1, std::min<int64_t>((R + teams - 1) / teams, cap));
   if (has_col || has_all) E.exact = false;
   E.line("__shared__ float sred[8], sred2[8];");

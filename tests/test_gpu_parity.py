@@ -309,3 +309,21 @@ def test_adam_and_adamw_steps_match_the_reference_rule(device):
             if kind == backend.ADAMW and g.ndim >= 2:
                 stepped = stepped - (p * dec) * lr
             assert_exact(dp.download(slot).reshape(g.shape), stepped.astype(np.float32))
+
+
+@pytest.mark.parametrize("op,lo", [(9, -10.0), (10, 1e-3), (27, 0.0), (8, -5.0)])
+def test_map_face_matches_libm(device, op, lo):
+    # the `Elementary::map` face (payload/elementary.rs:89-95): exp, ln, sqrt, tanh
+    import ctypes as C
+    from poorgrad_b200.abi import fptr, load_library
+    lib = load_library()
+    x = np.random.default_rng(op).uniform(lo, 10.0, 1 << 18).astype(np.float32)
+    out = np.empty_like(x)
+    assert lib.tb_map_f32(op, fptr(x), x.size, fptr(out)) == 0
+    ref = oracle.libm_map(op, x)
+    if op == 27:
+        assert_exact(out, ref)
+    else:
+        np.testing.assert_allclose(out, ref, rtol=4e-7, atol=1e-30)
+    small = np.ones(16, np.float32)
+    assert lib.tb_map_f32(op, fptr(small), 16, fptr(small)) == 5  # declined below 2^17
