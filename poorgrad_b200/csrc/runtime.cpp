@@ -169,6 +169,7 @@ struct Nccl {
   ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
   ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
   ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
   ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                             cudaStream_t) = nullptr;
   ncclResult_t (*GroupStart)() = nullptr;
@@ -190,6 +191,7 @@ Nccl* nccl() {
   n.GetUniqueId = (decltype(n.GetUniqueId))dlsym(n.handle, "ncclGetUniqueId");
   n.CommInitRank = (decltype(n.CommInitRank))dlsym(n.handle, "ncclCommInitRank");
   n.CommDestroy = (decltype(n.CommDestroy))dlsym(n.handle, "ncclCommDestroy");
+  n.CommAbort = (decltype(n.CommAbort))dlsym(n.handle, "ncclCommAbort");
   n.AllReduce = (decltype(n.AllReduce))dlsym(n.handle, "ncclAllReduce");
   n.GroupStart = (decltype(n.GroupStart))dlsym(n.handle, "ncclGroupStart");
   n.GroupEnd = (decltype(n.GroupEnd))dlsym(n.handle, "ncclGroupEnd");
@@ -231,8 +233,12 @@ struct tb_params {
 struct tb_comm {
   ncclComm_t comm = nullptr;
   int rank = 0, world = 1;
+  // Abort rather than destroy: a communicator captured into a plan's graph may
+  // still have work queued, and teardown must not wait on peers.
   ~tb_comm() {
-    if (comm && nccl() && nccl()->CommDestroy) nccl()->CommDestroy(comm);
+    if (!comm || !nccl()) return;
+    if (nccl()->CommAbort) nccl()->CommAbort(comm);
+    else if (nccl()->CommDestroy) nccl()->CommDestroy(comm);
   }
 };
 

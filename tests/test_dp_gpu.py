@@ -54,10 +54,13 @@ def _rank(rank, world, port, out):
     slots = [w.columns.nodes[p.index].slot for p in w.params]
     out[rank] = [dp.download(s) for s in slots]
     dist.barrier()
-    del opt, comm
-    dist.destroy_process_group()
+    # leave without destructors: communicators bound into a captured graph are
+    # not torn down at interpreter exit
+    sys.stdout.flush()
+    os._exit(0)
 
 
+@pytest.mark.timeout(300)
 def test_two_rank_sgd_step_matches_the_full_batch_update(device):
     import torch
     import torch.multiprocessing as mp
