@@ -110,6 +110,9 @@ struct Kernel {
   // static kernels
   int a_hi = -1, a_lo = -1, b_hi = -1, b_lo = -1, out = -1;  // GEMM buffers
   int64_t batch = 1, m = 0, n = 0, k = 0, kp = 0;
+  // GEMM operand layouts (1 = MN-major), row strides and rows per batch entry
+  int a_mn = 0, b_mn = 0;
+  int64_t a_ld = 0, b_ld = 0, a_rows = 0, b_rows = 0;
   int sel = -1;                 // SORT: selection node; SCATTER: sorted buffers via sort_of
   int keys = -1, vals = -1, tmp_keys = -1, tmp_vals = -1, counts = -1, rstart = -1, rend = -1;
   int64_t count = 0, rows = 0, passes = 0, tiles = 0;

@@ -89,7 +89,8 @@ extern "C" int tb_gemm_f32(const float* a, int64_t a_len, const int64_t a_stride
     k_prep_strided<<<grid, 256, 0, st>>>(da, a_strides[0], a_strides[1], m, k, kp, ahi, alo);
     // B^T as [n, k]: row j of B^T walks column j of B
     k_prep_strided<<<grid, 256, 0, st>>>(db, b_strides[1], b_strides[0], n, k, kp, bhi, blo);
-    tb::launch_gemm(ahi, alo, bhi, blo, dc, nullptr, 1, 1, m, n, kp, st);
+    tb::launch_gemm(tb::k_major(ahi, alo, m, kp), tb::k_major(bhi, blo, n, kp), dc, nullptr, 1,
+                    1, m, n, kp, st);
     cudaMemcpyAsync(out, dc, m * n * 4, cudaMemcpyDeviceToHost, st);
     if (cudaStreamSynchronize(st) != cudaSuccess) rc = TB_RUNTIME;
   } while (false);
@@ -120,16 +121,36 @@ extern "C" int tb_map_f32(int32_t op, const float* in, int64_t count, float* out
 
 // ---- internal hooks for tests (not part of the public ABI)
 extern "C" void tbx_set_gemm_engine(int engine) { tb::set_gemm_engine(engine); }
+// Operand layouts: a_mn / b_mn select MN-major ([batch][k rows][ld], ld a
+// multiple of 32); K-major operands are [batch][m or n][kp].
+extern "C" int tbx_gemm_prepared_layout(const float* a_hi, const float* a_lo, int a_mn,
+                                        int64_t a_ld, const float* b_hi, const float* b_lo,
+                                        int b_mn, int64_t b_ld, float* c, float* partial,
+                                        int splits, int64_t batch, int64_t m, int64_t n,
+                                        int64_t k, int64_t kp, int engine) {
+  tb::Operand a = tb::k_major(a_hi, a_lo, m, kp), b = tb::k_major(b_hi, b_lo, n, kp);
+  if (a_mn) {
+    a.mn = 1;
+    a.ld = a_ld;
+    a.rows = k;
+  }
+  if (b_mn) {
+    b.mn = 1;
+    b.ld = b_ld;
+    b.rows = k;
+  }
+  cudaStream_t st = 0;
+  if (engine == 1)
+    tb::launch_gemm_simt(a, b, c, batch, m, n, kp, st);
+  else if (!tb::launch_gemm_tcgen05_split(a, b, c, partial, splits, batch, m, n, kp, st))
+    return TB_DECLINED;
+  return cudaDeviceSynchronize() == cudaSuccess ? TB_OK : TB_RUNTIME;
+}
 extern "C" int tbx_gemm_prepared(const float* a_hi, const float* a_lo, const float* b_hi,
                                  const float* b_lo, float* c, float* partial, int splits,
                                  int64_t batch, int64_t m, int64_t n, int64_t kp, int engine) {
-  cudaStream_t st = 0;
-  if (engine == 1)
-    tb::launch_gemm_simt(a_hi, a_lo, b_hi, b_lo, c, batch, m, n, kp, st);
-  else if (!tb::launch_gemm_tcgen05_split(a_hi, a_lo, b_hi, b_lo, c, partial, splits, batch, m,
-                                          n, kp, st))
-    return TB_DECLINED;
-  return cudaDeviceSynchronize() == cudaSuccess ? TB_OK : TB_RUNTIME;
+  return tbx_gemm_prepared_layout(a_hi, a_lo, 0, kp, b_hi, b_lo, 0, kp, c, partial, splits, batch,
+                                  m, n, kp, kp, engine);
 }
 extern "C" int tbx_gemm_error(void) { return tb::gemm_error(); }
 extern "C" void tbx_set_gemm_tile_n(int tile) { tb::set_gemm_tile_n(tile); }
@@ -215,6 +236,7 @@ extern "C" int tb_gemm_f32_noalloc(const float* a, const int64_t a_strides[2], c
   const int grid = 148 * 4;
   k_prep_strided<<<grid, 256, 0, st>>>(a, a_strides[0], a_strides[1], m, k, kp, ahi, alo);
   k_prep_strided<<<grid, 256, 0, st>>>(b, b_strides[1], b_strides[0], n, k, kp, bhi, blo);
-  tb::launch_gemm(ahi, alo, bhi, blo, out, nullptr, 1, 1, m, n, kp, st);
+  tb::launch_gemm(tb::k_major(ahi, alo, m, kp), tb::k_major(bhi, blo, n, kp), out, nullptr, 1, 1,
+                  m, n, kp, st);
   return cudaPeekAtLastError() == cudaSuccess ? TB_OK : TB_RUNTIME;
 }

@@ -1,10 +1,14 @@
 // gemm_sm100.cu -- 3xTF32 GEMM on the 5th-generation tensor cores (tcgen05).
 //
-// C[b] = A[b] . B[b]^T over operands prepared K-major as tf32 pairs
-// (hi = rna_tf32(x), lo = x - hi): C = Ahi.Bhi + Ahi.Blo + Alo.Bhi, the f32
-// accumulator held in tensor memory (TMEM).  One CTA computes a 128 x 256 tile:
-//   warp 0      TMA producer: four tiles per k-block (A hi/lo, B hi/lo), 64B
-//               swizzle, into a STAGES-deep ring guarded by mbarriers;
+// C[b] = A[b] . B[b]^T over operands prepared as tf32 pairs (hi = rna_tf32(x),
+// lo = x - hi): C = Ahi.Bhi + Ahi.Blo + Alo.Bhi, the f32 accumulator held in
+// tensor memory (TMEM).  Each operand is K-major (reduction index contiguous)
+// or MN-major (output index contiguous; the same prepared buffer then serves a
+// product and its transpose).  One CTA computes a 128 x BN tile:
+//   warp 0      TMA producer: four tiles per k-block (A hi/lo, B hi/lo) into a
+//               STAGES-deep ring guarded by mbarriers.  A K-major tile is one
+//               box of BK-float rows; an MN-major tile is one box of 32-wide
+//               MN blocks (BK rows of 128 bytes each, 32-byte swizzle atoms);
 //   warp 1      MMA issuer: one elected thread issues tcgen05.mma kind::tf32
 //               (M=128, N=BN, K=8), three products per k-step, and commits each
 //               stage back to the producer;
@@ -116,6 +120,14 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       "l"((uint64_t)map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
       : "memory");
 }
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int x, int y, int z,
+                                            int w, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
+      "l"((uint64_t)map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+      : "memory");
+}
 // K-major operand tile, swizzled rows of BK floats, 8-row atoms SBO bytes apart.
 template <class C>
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
@@ -127,10 +139,26 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
   d |= C::SWIZZLE << 61;               // swizzle mode
   return d;
 }
-// kind::tf32 instruction descriptor: f32 accumulator, tf32 A and B, both K-major.
-__host__ __device__ constexpr uint32_t instr_desc(int m, int n) {
-  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) |
-         ((uint32_t)(m >> 4) << 24);
+// MN-major operand tile: 32-float (128-byte) MN blocks of BK rows each, `lbo`
+// bytes apart.  For 32-bit types the tensor cores read MN-major data only in
+// the 128-byte swizzle with 32-byte atoms (32-byte chunks of a 128-byte row
+// permuted by the row index mod 4; descriptor layout type 1, the TMA map's
+// CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B): 4-row groups of 512 bytes, so one MMA
+// k-step (8 rows) advances 1024 bytes.
+__device__ __forceinline__ uint64_t smem_desc_mn(uint32_t addr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;  // leading byte offset: next MN block
+  d |= (uint64_t)(512 >> 4) << 32;             // stride byte offset: next 4-row group
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)1 << 61;  // 128-byte swizzle, 32-byte atoms
+  return d;
+}
+// kind::tf32 instruction descriptor: f32 accumulator, tf32 A and B; bits 15/16
+// mark A/B as MN-major.
+__host__ __device__ constexpr uint32_t instr_desc(int m, int n, int a_mn, int b_mn) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 __device__ __forceinline__ void umma_tf32(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc,
                                           uint32_t accumulate) {
@@ -190,7 +218,7 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
                    const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
                    float* __restrict__ out, int m, int n, int k_blocks, int split_blocks,
                    int splits, long long split_stride, int tiles_n, int tiles_m, int work_items,
-                   int m_fast) {
+                   int m_fast, int a_mn, int b_mn) {
   using D = Derived<C>;
   constexpr int BN = C::BN, BK = C::BK, STAGES = C::STAGES, CHUNK = C::CHUNK;
   constexpr int TILE_A = D::TILE_A, TILE_B = D::TILE_B, STAGE_BYTES = D::STAGE_BYTES;
@@ -248,16 +276,32 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
           uint8_t* base = smem + s * STAGE_BYTES;
           mbar_expect_tx(&full[s], STAGE_BYTES);
           const int kx = (kb0 + i) * BK;
-          tma_load_3d(base, &ta_hi, kx, t.m0, t.batch, &full[s]);
-          tma_load_3d(base + TILE_A, &ta_lo, kx, t.m0, t.batch, &full[s]);
-          tma_load_3d(base + 2 * TILE_A, &tb_hi, kx, t.n0, t.batch, &full[s]);
-          tma_load_3d(base + 2 * TILE_A + TILE_B, &tb_lo, kx, t.n0, t.batch, &full[s]);
+          if (!a_mn) {
+            tma_load_3d(base, &ta_hi, kx, t.m0, t.batch, &full[s]);
+            tma_load_3d(base + TILE_A, &ta_lo, kx, t.m0, t.batch, &full[s]);
+          } else {  // one box: BM/32 MN blocks of BK rows
+            tma_load_4d(base, &ta_hi, 0, kx, t.m0 / 32, t.batch, &full[s]);
+            tma_load_4d(base + TILE_A, &ta_lo, 0, kx, t.m0 / 32, t.batch, &full[s]);
+          }
+          uint8_t* bb = base + 2 * TILE_A;
+          if (!b_mn) {
+            tma_load_3d(bb, &tb_hi, kx, t.n0, t.batch, &full[s]);
+            tma_load_3d(bb + TILE_B, &tb_lo, kx, t.n0, t.batch, &full[s]);
+          } else {
+            tma_load_4d(bb, &tb_hi, 0, kx, t.n0 / 32, t.batch, &full[s]);
+            tma_load_4d(bb + TILE_B, &tb_lo, 0, kx, t.n0 / 32, t.batch, &full[s]);
+          }
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = instr_desc(BM, BN);
+      const uint32_t idesc = instr_desc(BM, BN, a_mn, b_mn);
+      // operand descriptor of k-step kk: K-major steps 32 bytes along the
+      // swizzled row, MN-major steps one 1024-byte atom (8 rows of 128 bytes)
+      auto desc_of = [&](uint32_t tile, int mn, int kk) -> uint64_t {
+        return mn ? smem_desc_mn(tile + kk * 1024, BK * 128) : smem_desc<C>(tile + kk * 32);
+      };
       uint32_t g = 0, gc = 0;  // k-blocks and chunks consumed by this CTA so far
       for (int w = blockIdx.x; w < work_items && !*abort_flag; w += gridDim.x) {
         const Work t = decode<C>(w, tiles_n, tiles_m, splits, m_fast);
@@ -286,11 +330,12 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
             const uint32_t b_hi = base + 2 * TILE_A, b_lo = b_hi + TILE_B;
 #pragma unroll
             for (int kk = 0; kk < BK / 8; ++kk) {
-              const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along K inside the swizzle row
               const uint32_t first = (i > c * CHUNK || kk > 0) ? 1u : 0u;
-              umma_tf32(acc, smem_desc<C>(a_lo + off), smem_desc<C>(b_hi + off), idesc, first);
-              umma_tf32(acc, smem_desc<C>(a_hi + off), smem_desc<C>(b_lo + off), idesc, 1u);
-              umma_tf32(acc, smem_desc<C>(a_hi + off), smem_desc<C>(b_hi + off), idesc, 1u);
+              const uint64_t dah = desc_of(a_hi, a_mn, kk), dal = desc_of(a_lo, a_mn, kk);
+              const uint64_t dbh = desc_of(b_hi, b_mn, kk), dbl = desc_of(b_lo, b_mn, kk);
+              umma_tf32(acc, dal, dbh, idesc, first);
+              umma_tf32(acc, dah, dbl, idesc, 1u);
+              umma_tf32(acc, dah, dbh, idesc, 1u);
             }
             umma_commit(&empty[s]);
           }
@@ -395,13 +440,15 @@ EncodeTiled encoder() {
   return fn;
 }
 
-bool make_map(CUtensorMap* map, const float* base, int64_t kp, int64_t rows, int64_t batch,
-              int box_rows, int bk, CUtensorMapSwizzle swizzle) {
+// Tensor map over one prepared buffer [batch][rows][ld] floats; the box is
+// box_x floats along a row by box_rows rows.
+bool make_map(CUtensorMap* map, const float* base, int64_t ld, int64_t rows, int64_t batch,
+              int box_x, int box_rows, CUtensorMapSwizzle swizzle) {
   EncodeTiled enc = encoder();
   if (!enc) return false;
-  cuuint64_t dims[3] = {(cuuint64_t)kp, (cuuint64_t)rows, (cuuint64_t)batch};
-  cuuint64_t strides[2] = {(cuuint64_t)(kp * 4), (cuuint64_t)(rows * kp * 4)};
-  cuuint32_t box[3] = {(cuuint32_t)bk, (cuuint32_t)box_rows, 1};
+  cuuint64_t dims[3] = {(cuuint64_t)ld, (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 4), (cuuint64_t)(rows * ld * 4)};
+  cuuint32_t box[3] = {(cuuint32_t)box_x, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)base, dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
@@ -455,24 +502,52 @@ int gemm_splits(int64_t batch, int64_t m, int64_t n, int64_t kp) {
 }
 
 namespace {
+// Tensor map over an MN-major buffer [batch][rows][ld] seen as 32-float MN
+// blocks: dimensions (32 floats, rows, ld / 32 blocks 128 bytes apart, batch),
+// so one box of (32, bk, tile / 32) lands block after block -- the operand
+// tile the MMA reads.  Every address stays inside its row of ld floats.
+bool make_map_mn(CUtensorMap* map, const float* base, int64_t ld, int64_t rows, int64_t batch,
+                 int tile, int bk) {
+  EncodeTiled enc = encoder();
+  if (!enc) return false;
+  cuuint64_t dims[4] = {32, (cuuint64_t)rows, (cuuint64_t)(ld / 32), (cuuint64_t)batch};
+  cuuint64_t strides[3] = {(cuuint64_t)(ld * 4), 128, (cuuint64_t)(rows * ld * 4)};
+  cuuint32_t box[4] = {32, (cuuint32_t)bk, (cuuint32_t)(tile / 32), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void*)base, dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Tensor maps of one operand's hi and lo buffers: K-major boxes are BK floats
+// by the tile's rows (the config's swizzle), MN-major boxes the tile's MN
+// blocks of 32 floats by BK rows (128-byte swizzle of 32-byte atoms).
 template <class C>
-bool launch_cfg(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
-                float* c, float* partial, int splits, int64_t batch, int64_t m, int64_t n,
-                int64_t kp, cudaStream_t stream) {
+bool operand_maps(CUtensorMap* hi, CUtensorMap* lo, const Operand& o, int tile, int64_t batch) {
+  if (o.mn)
+    return make_map_mn(hi, o.hi, o.ld, o.rows, batch, tile, C::BK) &&
+           make_map_mn(lo, o.lo, o.ld, o.rows, batch, tile, C::BK);
+  return make_map(hi, o.hi, o.ld, o.rows, batch, C::BK, tile, C::TMA_SWIZZLE) &&
+         make_map(lo, o.lo, o.ld, o.rows, batch, C::BK, tile, C::TMA_SWIZZLE);
+}
+
+template <class C>
+bool launch_cfg(const Operand& a, const Operand& b, float* c, float* partial, int splits,
+                int64_t batch, int64_t m, int64_t n, int64_t kp, cudaStream_t stream) {
   using D = Derived<C>;
   if (kp % C::BK != 0) return false;
   CUtensorMap ma, mal, mb, mbl;
-  if (!make_map(&ma, a_hi, kp, m, batch, BM, C::BK, C::TMA_SWIZZLE) ||
-      !make_map(&mal, a_lo, kp, m, batch, BM, C::BK, C::TMA_SWIZZLE) ||
-      !make_map(&mb, b_hi, kp, n, batch, C::BN, C::BK, C::TMA_SWIZZLE) ||
-      !make_map(&mbl, b_lo, kp, n, batch, C::BN, C::BK, C::TMA_SWIZZLE))
+  if (!operand_maps<C>(&ma, &mal, a, BM, batch) || !operand_maps<C>(&mb, &mbl, b, C::BN, batch))
     return false;
-  static bool configured = false;
-  if (!configured) {
+  static bool configured[256] = {};  // the attribute is set per device
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 256) return false;
+  if (!configured[dev]) {
     if (cudaFuncSetAttribute(k_gemm_tcgen05<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              D::SMEM_BYTES) != cudaSuccess)
       return false;
-    configured = true;
+    configured[dev] = true;
   }
   const int kb = (int)(kp / C::BK);
   if (splits < 1 || !partial) splits = 1;
@@ -491,7 +566,7 @@ bool launch_cfg(const float* a_hi, const float* a_lo, const float* b_hi, const f
   const int grid = (int)std::min<long long>(items, sms);
   k_gemm_tcgen05<C><<<grid, D::THREADS, D::SMEM_BYTES, stream>>>(
       ma, mal, mb, mbl, target, (int)m, (int)n, kb, per, splits, (long long)(batch * m * n),
-      tiles_n, tiles_m, (int)items, m > 0 && n > m ? 1 : 0);
+      tiles_n, tiles_m, (int)items, m > 0 && n > m ? 1 : 0, a.mn, b.mn);
   if (splits > 1) {
     const long long count = batch * m * n;
     int blocks = (int)std::min<long long>((count + 255) / 256, 148 * 8);
@@ -501,21 +576,18 @@ bool launch_cfg(const float* a_hi, const float* a_lo, const float* b_hi, const f
 }
 }  // namespace
 
-bool launch_gemm_tcgen05_split(const float* a_hi, const float* a_lo, const float* b_hi,
-                               const float* b_lo, float* c, float* partial, int splits,
-                               int64_t batch, int64_t m, int64_t n, int64_t kp,
+bool launch_gemm_tcgen05_split(const Operand& a, const Operand& b, float* c, float* partial,
+                               int splits, int64_t batch, int64_t m, int64_t n, int64_t kp,
                                cudaStream_t stream) {
   if (m >= (1LL << 31) || n >= (1LL << 31) || batch > 65535) return false;
-  if (((uintptr_t)a_hi | (uintptr_t)a_lo | (uintptr_t)b_hi | (uintptr_t)b_lo) & 15) return false;
+  if (((uintptr_t)a.hi | (uintptr_t)a.lo | (uintptr_t)b.hi | (uintptr_t)b.lo) & 15) return false;
+  // row strides: 16-byte multiples for the tensor maps; an MN-major row holds
+  // whole 32-float blocks
+  for (const Operand* o : {&a, &b})
+    if (o->ld % 4 != 0 || o->rows < 1 || (o->mn && o->ld % 32 != 0)) return false;
   if (gemm_tile_n(batch, m, n, kp) == 256)
-    return launch_cfg<Cfg<256>>(a_hi, a_lo, b_hi, b_lo, c, partial, splits, batch, m, n, kp, stream);
-  return launch_cfg<Cfg<128>>(a_hi, a_lo, b_hi, b_lo, c, partial, splits, batch, m, n, kp, stream);
-}
-
-bool launch_gemm_tcgen05(const float* a_hi, const float* a_lo, const float* b_hi,
-                         const float* b_lo, float* c, int64_t batch, int64_t m, int64_t n,
-                         int64_t kp, cudaStream_t stream) {
-  return launch_gemm_tcgen05_split(a_hi, a_lo, b_hi, b_lo, c, nullptr, 1, batch, m, n, kp, stream);
+    return launch_cfg<Cfg<256>>(a, b, c, partial, splits, batch, m, n, kp, stream);
+  return launch_cfg<Cfg<128>>(a, b, c, partial, splits, batch, m, n, kp, stream);
 }
 
 int gemm_error() {

@@ -132,40 +132,44 @@ __global__ void k_segments(const int* __restrict__ keys, int* __restrict__ rstar
   }
 }
 
-// 32 columns per block: lane = column, the 8 warps take every 8th partial row;
-// the 8 per-warp sums are then combined in warp order (a fixed, deterministic
-// association).
+// CB columns per block: thread t takes column t % CB and every G-th partial row
+// starting at t / CB (G = 256 / CB groups); the G group sums are then combined
+// in group order (a fixed, deterministic association).  CB = 32 gives each
+// warp whole 128-byte rows; CB = 8 (narrow outputs) spreads the partial rows
+// over 32 groups and 4x the blocks, 32-byte sectors per group.
+template <int CB>
 __global__ void __launch_bounds__(256) k_final_sum(const float* __restrict__ part,
                                                    float* __restrict__ out, int64_t blocks,
                                                    int64_t width) {
-  __shared__ float acc_s[8][32];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t j = (int64_t)blockIdx.x * 32 + lane;
+  constexpr int G = 256 / CB;
+  __shared__ float acc_s[G][CB];
+  const int col = threadIdx.x % CB, grp = threadIdx.x / CB;
+  const int64_t j = (int64_t)blockIdx.x * CB + col;
   float acc = 0.0f;
   bool any = false;
   if (j < width) {
-    int64_t b = warp;
-    for (; b + 56 < blocks; b += 64) {  // eight rows per step: loads first, adds in order
+    int64_t b = grp;
+    for (; b + 7 * G < blocks; b += 8 * G) {  // eight rows per step: loads first, adds in order
       float v[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = part[(b + 8 * u) * width + j];
+      for (int u = 0; u < 8; ++u) v[u] = part[(b + G * u) * width + j];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         acc = any ? __fadd_rn(acc, v[u]) : v[u];
         any = true;
       }
     }
-    for (; b < blocks; b += 8) {
+    for (; b < blocks; b += G) {
       const float v = part[b * width + j];
       acc = any ? __fadd_rn(acc, v) : v;
       any = true;
     }
   }
-  acc_s[warp][lane] = acc;
+  acc_s[grp][col] = acc;
   __syncthreads();
-  if (warp == 0 && j < width) {
-    float t = acc_s[0][lane];
-    for (int w = 1; w < 8 && w < blocks; ++w) t = __fadd_rn(t, acc_s[w][lane]);
+  if (grp == 0 && j < width) {
+    float t = acc_s[0][col];
+    for (int w = 1; w < G && w < blocks; ++w) t = __fadd_rn(t, acc_s[w][col]);
     out[j] = t;
   }
 }
@@ -201,50 +205,131 @@ __global__ void k_segment_sum(const float* __restrict__ perm, const int* __restr
   }
 }
 
-// SIMT GEMM over K-major prepared operands: 64x64 tiles, 4x4 per thread.
-// The operands are reassembled as hi + lo (exactly the original f32 values).
+// Long segments (few target rows, many sources each -- an embedding table of a
+// small vocabulary): the per-output chains above would leave most SMs idle.
+// One block per (row, 32-column slice).  Warps 1..7 keep a ring of kSegSlots
+// chunks of the segment (168 source rows each) in flight with cp.async, so
+// the L2 latency is hidden behind kSegSlots - 1 chunks; warp 0 adds each
+// landed chunk in ascending order from zero, one lane per column -- the same
+// serial fold as k_segment_sum, so the result is bit-identical.
+constexpr int kSegRowsPerWarp = 24;
+constexpr int kSegStage = 7 * kSegRowsPerWarp;
+constexpr int kSegSlots = 6;
+constexpr size_t kSegSmem = sizeof(float) * kSegSlots * kSegStage * 32;
+
+__device__ __forceinline__ void cp_async4(float* dst, const float* src, bool valid) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(d), "l"(src),
+               "r"(valid ? 4 : 0));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+__global__ void __launch_bounds__(256) k_segment_sum_staged(const float* __restrict__ perm,
+                                                            const int* __restrict__ rstart,
+                                                            const int* __restrict__ rend,
+                                                            float* __restrict__ out,
+                                                            int64_t width) {
+  extern __shared__ float ring[];  // [kSegSlots][kSegStage][32]; lane = column
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t row = blockIdx.x;
+  const int64_t c = (int64_t)blockIdx.y * 32 + lane;
+  const bool live = c < width;
+  const int64_t q0 = rstart[row], q1 = rend[row];
+  const int64_t chunks = (q1 - q0 + kSegStage - 1) / kSegStage;
+  // warp w (1..7) copies its 24 rows of chunk i into slot i % kSegSlots
+  auto issue = [&](int64_t i) {
+    if (i < chunks) {
+      const int64_t base = q0 + i * kSegStage + (warp - 1) * kSegRowsPerWarp;
+      float* slot = ring + (i % kSegSlots) * (kSegStage * 32) + (warp - 1) * kSegRowsPerWarp * 32;
+#pragma unroll
+      for (int j = 0; j < kSegRowsPerWarp; ++j) {
+        const bool ok = live && base + j < q1;
+        cp_async4(slot + j * 32 + lane, ok ? perm + (base + j) * width + c : perm, ok);
+      }
+    }
+    cp_async_commit();  // an empty group past the end keeps the wait count uniform
+  };
+  if (warp > 0)
+    for (int64_t i = 0; i < kSegSlots - 1; ++i) issue(i);
+  float acc = 0.0f;
+  for (int64_t i = 0; i < chunks; ++i) {
+    if (warp > 0) cp_async_wait<kSegSlots - 2>();  // this warp's copies of chunk i landed
+    __syncthreads();  // all of chunk i visible; warp 0 is done with chunk i - 1
+    if (warp > 0) {
+      issue(i + kSegSlots - 1);  // reuses the slot of chunk i - 1
+    } else {
+      const int64_t left = q1 - q0 - i * kSegStage;
+      const float* slot = ring + (i % kSegSlots) * (kSegStage * 32);
+      if (left >= kSegStage) {
+#pragma unroll 24
+        for (int j = 0; j < kSegStage; ++j) acc = __fadd_rn(acc, slot[j * 32 + lane]);
+      } else {
+        for (int j = 0; j < left; ++j) acc = __fadd_rn(acc, slot[j * 32 + lane]);
+      }
+    }
+  }
+  cp_async_wait<0>();
+  if (warp == 0 && live) out[row * width + c] = acc;
+}
+
+// Four consecutive reduction indices k..k+3 of operand row r, as hi + lo
+// (exactly the original f32 values); zero outside the operand.
+__device__ __forceinline__ float4 simt_quad(const float* __restrict__ h,
+                                            const float* __restrict__ l, int mn, int64_t ld,
+                                            int64_t rows, int64_t r, int64_t r_end, int64_t k) {
+  float4 q = make_float4(0, 0, 0, 0);
+  if (r >= r_end) return q;
+  if (!mn) {
+    const float4 a = *(const float4*)(h + r * ld + k), b = *(const float4*)(l + r * ld + k);
+    return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+  }
+  float v[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+    v[u] = k + u < rows ? h[(k + u) * ld + r] + l[(k + u) * ld + r] : 0.0f;
+  return make_float4(v[0], v[1], v[2], v[3]);
+}
+
+// SIMT GEMM over prepared operands of either layout: 64x64 tiles, 4x4 per
+// thread.  The operands are reassembled as hi + lo (the original f32 values).
 __global__ void __launch_bounds__(256) k_gemm_simt(const float* __restrict__ ahi,
-                                                   const float* __restrict__ alo,
+                                                   const float* __restrict__ alo, int a_mn,
+                                                   int64_t a_ld, int64_t a_rows,
                                                    const float* __restrict__ bhi,
-                                                   const float* __restrict__ blo,
+                                                   const float* __restrict__ blo, int b_mn,
+                                                   int64_t b_ld, int64_t b_rows,
                                                    float* __restrict__ c, int64_t m, int64_t n,
                                                    int64_t kp) {
   __shared__ float As[16][68];
   __shared__ float Bs[16][68];
   const int64_t b = blockIdx.z;
   const int64_t m0 = (int64_t)blockIdx.y * 64, n0 = (int64_t)blockIdx.x * 64;
-  const float* Ah = ahi + b * m * kp;
-  const float* Al = alo + b * m * kp;
-  const float* Bh = bhi + b * n * kp;
-  const float* Bl = blo + b * n * kp;
+  const float* Ah = ahi + b * a_rows * a_ld;
+  const float* Al = alo + b * a_rows * a_ld;
+  const float* Bh = bhi + b * b_rows * b_ld;
+  const float* Bl = blo + b * b_rows * b_ld;
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   float acc[4][4] = {};
   const int lr = threadIdx.x >> 2;       // 0..63 row within tile
   const int lk = (threadIdx.x & 3) * 4;  // 0,4,8,12
   for (int64_t k0 = 0; k0 < kp; k0 += 16) {
     {
-      const int64_t r = m0 + lr;
-      float4 h = make_float4(0, 0, 0, 0), l = h;
-      if (r < m) {
-        h = *(const float4*)(Ah + r * kp + k0 + lk);
-        l = *(const float4*)(Al + r * kp + k0 + lk);
-      }
-      As[lk + 0][lr] = h.x + l.x;
-      As[lk + 1][lr] = h.y + l.y;
-      As[lk + 2][lr] = h.z + l.z;
-      As[lk + 3][lr] = h.w + l.w;
+      const float4 v = simt_quad(Ah, Al, a_mn, a_ld, a_rows, m0 + lr, m, k0 + lk);
+      As[lk + 0][lr] = v.x;
+      As[lk + 1][lr] = v.y;
+      As[lk + 2][lr] = v.z;
+      As[lk + 3][lr] = v.w;
     }
     {
-      const int64_t r = n0 + lr;
-      float4 h = make_float4(0, 0, 0, 0), l = h;
-      if (r < n) {
-        h = *(const float4*)(Bh + r * kp + k0 + lk);
-        l = *(const float4*)(Bl + r * kp + k0 + lk);
-      }
-      Bs[lk + 0][lr] = h.x + l.x;
-      Bs[lk + 1][lr] = h.y + l.y;
-      Bs[lk + 2][lr] = h.z + l.z;
-      Bs[lk + 3][lr] = h.w + l.w;
+      const float4 v = simt_quad(Bh, Bl, b_mn, b_ld, b_rows, n0 + lr, n, k0 + lk);
+      Bs[lk + 0][lr] = v.x;
+      Bs[lk + 1][lr] = v.y;
+      Bs[lk + 2][lr] = v.z;
+      Bs[lk + 3][lr] = v.w;
     }
     __syncthreads();
 #pragma unroll
@@ -361,30 +446,46 @@ void launch_selection_sort(const int* indices, int* keys, int* vals, int* tmp_ke
 }
 
 void launch_segment_sum(const float* perm, const int* rstart, const int* rend, float* out,
-                        int64_t rows, int64_t width, cudaStream_t stream) {
+                        int64_t rows, int64_t width, int64_t count, cudaStream_t stream) {
+  const int64_t slices = (width + 31) / 32;
+  if (count >= 64 * rows && rows <= 65535 && slices <= 65535) {  // long segments on average
+    static bool sized[256] = {};  // opt in to > 48 KB of dynamic shared memory, per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 256 && !sized[dev]) {
+      cudaFuncSetAttribute(k_segment_sum_staged, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)kSegSmem);
+      sized[dev] = true;
+    }
+    k_segment_sum_staged<<<dim3((unsigned)rows, (unsigned)slices), 256, kSegSmem, stream>>>(
+        perm, rstart, rend, out, width);
+    return;
+  }
   int grid = (int)std::max<int64_t>(1, std::min<int64_t>((rows * width + 255) / 256, 148 * 8));
   k_segment_sum<<<grid, 256, 0, stream>>>(perm, rstart, rend, out, rows, width);
 }
 
 void launch_final_sum(const float* part, float* out, int64_t blocks, int64_t width,
                       cudaStream_t stream) {
-  k_final_sum<<<(unsigned)((width + 31) / 32), 256, 0, stream>>>(part, out, blocks, width);
+  if ((width + 31) / 32 >= 148)
+    k_final_sum<32><<<(unsigned)((width + 31) / 32), 256, 0, stream>>>(part, out, blocks, width);
+  else
+    k_final_sum<8><<<(unsigned)((width + 7) / 8), 256, 0, stream>>>(part, out, blocks, width);
 }
 
-void launch_gemm_simt(const float* a_hi, const float* a_lo, const float* b_hi,
-                      const float* b_lo, float* c, int64_t batch, int64_t m, int64_t n,
-                      int64_t kp, cudaStream_t stream) {
+void launch_gemm_simt(const Operand& a, const Operand& b, float* c, int64_t batch, int64_t m,
+                      int64_t n, int64_t kp, cudaStream_t stream) {
   dim3 grid((unsigned)((n + 63) / 64), (unsigned)((m + 63) / 64), (unsigned)batch);
-  k_gemm_simt<<<grid, 256, 0, stream>>>(a_hi, a_lo, b_hi, b_lo, c, m, n, kp);
+  k_gemm_simt<<<grid, 256, 0, stream>>>(a.hi, a.lo, a.mn, a.ld, a.rows, b.hi, b.lo, b.mn, b.ld,
+                                        b.rows, c, m, n, kp);
 }
 
-void launch_gemm(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
-                 float* c, float* partial, int splits, int64_t batch, int64_t m, int64_t n,
-                 int64_t kp, cudaStream_t stream) {
-  if (g_engine != 1 && launch_gemm_tcgen05_split(a_hi, a_lo, b_hi, b_lo, c, partial, splits,
-                                                 batch, m, n, kp, stream))
+void launch_gemm(const Operand& a, const Operand& b, float* c, float* partial, int splits,
+                 int64_t batch, int64_t m, int64_t n, int64_t kp, cudaStream_t stream) {
+  if (g_engine != 1 &&
+      launch_gemm_tcgen05_split(a, b, c, partial, splits, batch, m, n, kp, stream))
     return;
-  launch_gemm_simt(a_hi, a_lo, b_hi, b_lo, c, batch, m, n, kp, stream);
+  launch_gemm_simt(a, b, c, batch, m, n, kp, stream);
 }
 
 void launch_adam_scalars(float* s, float beta1, float beta2, cudaStream_t stream) {

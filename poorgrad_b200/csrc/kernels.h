@@ -15,26 +15,42 @@ void launch_selection_sort(const int* indices, int* keys, int* vals, int* tmp_ke
 void launch_final_sum(const float* part, float* out, int64_t blocks, int64_t width,
                       cudaStream_t stream);
 
-// out[r, c] = 0 + perm[rstart[r], c] + ... + perm[rend[r]-1, c] (ascending rows).
+// out[r, c] = 0 + perm[rstart[r], c] + ... + perm[rend[r]-1, c] (ascending rows);
+// `count` (the number of source rows) selects the variant for long segments.
 void launch_segment_sum(const float* perm, const int* rstart, const int* rend, float* out,
-                        int64_t rows, int64_t width, cudaStream_t stream);
+                        int64_t rows, int64_t width, int64_t count, cudaStream_t stream);
 
-// C[b] = (Ahi+Alo)[b] . (Bhi+Blo)[b]^T over K-major prepared operands;
-// the tcgen05 path (split-K into `partial` when splits > 1), else a SIMT path.
-void launch_gemm(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
-                 float* c, float* partial, int splits, int64_t batch, int64_t m, int64_t n,
-                 int64_t kp, cudaStream_t stream);
+// A prepared GEMM operand: tf32 pairs (hi = rna_tf32(x), lo = x - hi) laid out
+// [batch][rows][ld] floats.  K-major: a row per output row (M for A, N for B),
+// the reduction index contiguous (ld = kp, zero-padded).  MN-major: a row per
+// reduction index (rows = K, no padding needed), the output index contiguous
+// (ld >= M or N, a multiple of 32).  A is M x K, B is given as N x K.
+struct Operand {
+  const float* hi = nullptr;
+  const float* lo = nullptr;
+  int mn = 0;        // 0: K-major, 1: MN-major
+  int64_t ld = 0;    // floats between consecutive rows
+  int64_t rows = 0;  // rows per batch entry
+};
+inline Operand k_major(const float* hi, const float* lo, int64_t rows, int64_t kp) {
+  Operand o;
+  o.hi = hi;
+  o.lo = lo;
+  o.ld = kp;
+  o.rows = rows;
+  return o;
+}
+
+// C[b] = (Ahi+Alo)[b] . (Bhi+Blo)[b]^T over prepared operands; the tcgen05 path
+// (split-K into `partial` when splits > 1), else a SIMT path.
+void launch_gemm(const Operand& a, const Operand& b, float* c, float* partial, int splits,
+                 int64_t batch, int64_t m, int64_t n, int64_t kp, cudaStream_t stream);
 // The SIMT path alone (tests compare the two).
-void launch_gemm_simt(const float* a_hi, const float* a_lo, const float* b_hi,
-                      const float* b_lo, float* c, int64_t batch, int64_t m, int64_t n,
-                      int64_t kp, cudaStream_t stream);
+void launch_gemm_simt(const Operand& a, const Operand& b, float* c, int64_t batch, int64_t m,
+                      int64_t n, int64_t kp, cudaStream_t stream);
 // The tcgen05 path; returns false when the shape or alignment is not served.
-bool launch_gemm_tcgen05(const float* a_hi, const float* a_lo, const float* b_hi,
-                         const float* b_lo, float* c, int64_t batch, int64_t m, int64_t n,
-                         int64_t kp, cudaStream_t stream);
-bool launch_gemm_tcgen05_split(const float* a_hi, const float* a_lo, const float* b_hi,
-                               const float* b_lo, float* c, float* partial, int splits,
-                               int64_t batch, int64_t m, int64_t n, int64_t kp,
+bool launch_gemm_tcgen05_split(const Operand& a, const Operand& b, float* c, float* partial,
+                               int splits, int64_t batch, int64_t m, int64_t n, int64_t kp,
                                cudaStream_t stream);
 // Tile width (128 or 256) the tcgen05 path uses for a shape; a test may force one.
 int gemm_tile_n(int64_t batch, int64_t m, int64_t n, int64_t kp);

@@ -994,6 +994,59 @@ class Lowerer {
     for (size_t g = 0; g < groups.size(); ++g) flush((int)g);
   }
 
+  // A value prepared for the tensor cores: its tf32 hi/lo pairs in the value's
+  // own row-major layout [batch][rows][cols rounded up to 32].  A GEMM reads it
+  // K-major when the value is its operand as is, MN-major when the operand is
+  // the value's transpose -- so a product and the weight gradient that reads
+  // the same activation transposed share one prep.
+  struct Prepared {
+    int hi = -1, lo = -1;
+    int64_t rows = 0, cols = 0, ld = 0;
+  };
+  std::map<int, Prepared> prepared;
+
+  // The value under any transposes of the last two axes (TRANSPOSE, or a
+  // PERMUTE that swaps only those); `flip` is set when their count is odd.
+  int strip_transposes(int x, bool& flip) {
+    flip = false;
+    for (;;) {
+      const Node& nd = P.nodes[x];
+      bool swap = nd.op == TB_OP_TRANSPOSE && nd.rank == 2;
+      if (nd.op == TB_OP_PERMUTE && nd.rank >= 2) {
+        swap = nd.attrs[nd.rank - 2] == nd.rank - 1 && nd.attrs[nd.rank - 1] == nd.rank - 2;
+        for (int i = 0; i < nd.rank - 2; ++i)
+          if (nd.attrs[i] != i) swap = false;
+      }
+      if (!swap) return x;
+      flip = !flip;
+      x = nd.operands[0];
+    }
+  }
+
+  Prepared prepare(int base, int64_t batch) {
+    auto it = prepared.find(base);
+    if (it != prepared.end()) return it->second;
+    const Node& b = P.nodes[base];
+    Prepared r;
+    r.rows = b.shape[b.rank - 2];
+    r.cols = b.shape[b.rank - 1];
+    r.ld = (r.cols + 31) / 32 * 32;
+    r.hi = new_buffer(Storage::Arena, batch * r.rows * r.ld * 4, -1);
+    r.lo = new_buffer(Storage::Arena, batch * r.rows * r.ld * 4, -1);
+    Kernel k;
+    k.type = KType::PREP;
+    k.node = base;
+    k.batch = batch;
+    k.m = r.rows;
+    k.k = r.cols;
+    k.kp = r.ld;
+    k.a_hi = r.hi;
+    k.a_lo = r.lo;
+    P.kernels.push_back(k);
+    prepared[base] = r;
+    return r;
+  }
+
   void matmul_kernels(int n) {
     const Node& nd = P.nodes[n];
     const Node& A = P.nodes[nd.operands[0]];
@@ -1002,38 +1055,35 @@ class Lowerer {
     int64_t batch = 1;
     for (int i = 0; i < split; ++i) batch *= A.shape[i];
     int64_t M = A.shape[split], K = A.shape[split + 1], N = B.shape[split + 1];
-    int64_t Kp = (K + 31) / 32 * 32;
-    Kernel pa, pb, g;
-    pa.type = pb.type = KType::PREP;
-    pa.node = pb.node = n;
-    pa.batch = pb.batch = g.batch = batch;
-    pa.m = g.m = M;
-    pb.m = N;
-    pa.k = pb.k = g.k = K;
-    pa.kp = pb.kp = g.kp = Kp;
-    g.n = N;
-    int ahi = new_buffer(Storage::Arena, batch * M * Kp * 4, -1);
-    int alo = new_buffer(Storage::Arena, batch * M * Kp * 4, -1);
-    int bhi = new_buffer(Storage::Arena, batch * N * Kp * 4, -1);
-    int blo = new_buffer(Storage::Arena, batch * N * Kp * 4, -1);
-    pa.a_hi = ahi;
-    pa.a_lo = alo;
-    pa.sel = 0;  // operand position
-    pb.a_hi = bhi;
-    pb.a_lo = blo;
-    pb.sel = 1;
+    bool fa = false, fb = false;
+    const int base_a = strip_transposes(nd.operands[0], fa);
+    const int base_b = strip_transposes(nd.operands[1], fb);
+    const Prepared pa = prepare(base_a, batch);
+    const Prepared pb = prepare(base_b, batch);
+    Kernel g;
     g.type = KType::GEMM;
     g.node = n;
-    g.a_hi = ahi;
-    g.a_lo = alo;
-    g.b_hi = bhi;
-    g.b_lo = blo;
+    g.batch = batch;
+    g.m = M;
+    g.n = N;
+    g.k = K;
+    g.kp = (K + 31) / 32 * 32;
+    // A (M x K) is its base as is ([M, K]: K-major) or transposed ([K, M]:
+    // MN-major); B (K x N) as is is [K, N]: MN-major for the N x K convention.
+    g.a_hi = pa.hi;
+    g.a_lo = pa.lo;
+    g.a_mn = fa ? 1 : 0;
+    g.a_ld = pa.ld;
+    g.a_rows = pa.rows;
+    g.b_hi = pb.hi;
+    g.b_lo = pb.lo;
+    g.b_mn = fb ? 0 : 1;
+    g.b_ld = pb.ld;
+    g.b_rows = pb.rows;
     g.out = P.info[n].buf;
     g.exact = false;
-    g.passes = gemm_splits(batch, M, N, Kp);  // split-K factor
+    g.passes = gemm_splits(batch, M, N, g.kp);  // split-K factor
     if (g.passes > 1) g.partial = new_buffer(Storage::Arena, g.passes * batch * M * N * 4, -1);
-    P.kernels.push_back(pa);
-    P.kernels.push_back(pb);
     P.kernels.push_back(g);
     P.gemms++;
   }
@@ -1854,16 +1904,17 @@ static int fast_axis(const Program& P, int n, int depth = 0) {
   return last;
 }
 
-// ---- GEMM operand preparation: tf32 hi/lo split into K-major [batch, R, Kp]
+// ---- GEMM operand preparation: tf32 hi/lo split of a value [batch, R, Kd]
+// into its own row-major layout [batch, R, Kp], the last axis zero-padded to
+// Kp (a multiple of 32)
 static void emit_prep(Program& P, Kernel& K, Emitter& E) {
-  const Node& mm = P.nodes[K.node];
-  int x = mm.operands[K.sel];
+  const int x = K.node;
   const Node& xn = P.nodes[x];
   int split = xn.rank - 2;
   std::vector<int64_t> bshape(xn.shape, xn.shape + split);
   int64_t R = K.m, Kd = K.k, Kp = K.kp;
-  bool is_b = K.sel == 1;
-  // transpose through shared memory when the operand is contiguous along R
+  const bool is_b = false;  // the value's own axes: R then Kd
+  // transpose through shared memory when the value is contiguous along R
   const int fa = fast_axis(P, x);
   const bool tile = fa == (is_b ? split + 1 : split);
   auto operand_idx = [&](const std::vector<std::string>& bc, const std::string& r,
@@ -2079,7 +2130,8 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
       K.exact = false;
       K.describe = "gemm3xtf32 batch=" + std::to_string(K.batch) + " m=" + std::to_string(K.m) +
                    " n=" + std::to_string(K.n) + " k=" + std::to_string(K.k) +
-                   " splits=" + std::to_string(K.passes);
+                   " splits=" + std::to_string(K.passes) + " a=" + (K.a_mn ? "mn" : "k") +
+                   " b=" + (K.b_mn ? "mn" : "k");
       P.kernels.push_back(K);
       continue;
     }
@@ -2129,6 +2181,7 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
         seg.rend = P.kernels[sk].rend;
         seg.rows = sn.shape[0];
         seg.final_width = width;
+        seg.count = gn.shape[0];
         seg.exact = true;
         finals.push_back(seg);
         break;
@@ -2180,6 +2233,8 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
     d << " members=";
     for (auto& m : K.members) d << m.node << (m.phase ? "p" + std::to_string(m.phase) : "") << " ";
     d << (K.exact ? "exact" : "tolerance");
+    if (K.type == KType::PREP)
+      d << " value=" << K.node << " [" << K.batch << "," << K.m << "," << K.kp << "]";
     K.describe = d.str();
     P.kernels.push_back(K);
     for (auto& f : finals) {

@@ -379,12 +379,23 @@ int64_t launch_kernel(tb_plan* plan, size_t k, cudaStream_t stream) {
   const tb::Kernel& K = P.kernels[k];
   int64_t launches = 0;
   switch (K.type) {
-    case tb::KType::GEMM:
-      tb::launch_gemm(fp(plan, K.a_hi), fp(plan, K.a_lo), fp(plan, K.b_hi), fp(plan, K.b_lo),
-                      fp(plan, K.out), K.partial >= 0 ? fp(plan, K.partial) : nullptr,
+    case tb::KType::GEMM: {
+      tb::Operand a, b;
+      a.hi = fp(plan, K.a_hi);
+      a.lo = fp(plan, K.a_lo);
+      a.mn = K.a_mn;
+      a.ld = K.a_ld;
+      a.rows = K.a_rows;
+      b.hi = fp(plan, K.b_hi);
+      b.lo = fp(plan, K.b_lo);
+      b.mn = K.b_mn;
+      b.ld = K.b_ld;
+      b.rows = K.b_rows;
+      tb::launch_gemm(a, b, fp(plan, K.out), K.partial >= 0 ? fp(plan, K.partial) : nullptr,
                       (int)K.passes, K.batch, K.m, K.n, K.kp, stream);
       launches += 1;
       break;
+    }
     case tb::KType::SORT:
       tb::launch_selection_sort(ip(plan, K.out), ip(plan, K.keys), ip(plan, K.vals),
                                 ip(plan, K.tmp_keys), ip(plan, K.tmp_vals), ip(plan, K.counts),
@@ -394,7 +405,7 @@ int64_t launch_kernel(tb_plan* plan, size_t k, cudaStream_t stream) {
       break;
     case tb::KType::SEGSUM:
       tb::launch_segment_sum(fp(plan, K.partial), ip(plan, K.rstart), ip(plan, K.rend),
-                             fp(plan, K.final_out), K.rows, K.final_width, stream);
+                             fp(plan, K.final_out), K.rows, K.final_width, K.count, stream);
       launches += 1;
       break;
     case tb::KType::FINAL:

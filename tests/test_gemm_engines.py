@@ -55,3 +55,50 @@ def test_tcgen05_matches_f64(device, batch, m, n, k, splits, tile):
         err = (c.double() - ref).abs()
         assert torch.all(err <= tol), f"engine {engine}: worst {(err / tol).max().item()}"
     lib.tbx_set_gemm_tile_n(0)
+
+
+@pytest.mark.parametrize("batch,m,n,k,splits", [
+    (1, 128, 128, 32, 1), (2, 130, 70, 40, 1), (1, 64, 96, 17, 1), (1, 300, 200, 1000, 3),
+    (1, 512, 27, 2048, 4)])
+@pytest.mark.parametrize("a_mn,b_mn", [(0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("tile", [128, 256])
+def test_mn_major_operands_match_f64(device, batch, m, n, k, splits, a_mn, b_mn, tile):
+    # an MN-major operand is the value [batch, k, mn] in its own row-major
+    # layout, the mn axis padded to a multiple of 32 (how the plan prepares an
+    # activation once for a product and for the transposed weight gradient)
+    import torch
+    from poorgrad_b200.abi import load_library
+    lib = load_library()
+    f = lib.tbx_gemm_prepared_layout
+    f.restype = C.c_int
+    f.argtypes = ([C.c_void_p, C.c_void_p, C.c_int, C.c_int64] * 2 + [C.c_void_p, C.c_void_p, C.c_int]
+                  + [C.c_int64] * 5 + [C.c_int])
+    g = torch.Generator(device="cuda").manual_seed(7 * batch + m + n + k)
+    a = torch.rand((batch, m, k), device="cuda", generator=g) * 2 - 1
+    bt = torch.rand((batch, n, k), device="cuda", generator=g) * 2 - 1
+    kp = (k + 31) // 32 * 32
+
+    def operand(x, mn):
+        rows = x.shape[1]
+        if not mn:
+            return _prep(torch, x, kp), kp
+        ld = (rows + 31) // 32 * 32
+        return _prep(torch, x.transpose(1, 2).contiguous(), ld), ld
+
+    (ahi, alo), a_ld = operand(a, a_mn)
+    (bhi, blo), b_ld = operand(bt, b_mn)
+    ref = torch.bmm(a.double(), bt.double().transpose(1, 2))
+    tol = 16 * EPS * math.sqrt(k) * (1 + ref.abs())
+    lib.tbx_set_gemm_tile_n(tile)
+    try:
+        for engine in (2, 1):
+            c = torch.full((batch, m, n), float("nan"), device="cuda")
+            part = torch.empty((splits, batch, m, n), device="cuda")
+            rc = f(ahi.data_ptr(), alo.data_ptr(), a_mn, a_ld, bhi.data_ptr(), blo.data_ptr(), b_mn,
+                   b_ld, c.data_ptr(), part.data_ptr(), splits, batch, m, n, k, kp, engine)
+            assert rc == 0, f"engine {engine} rc {rc}"
+            assert lib.tbx_gemm_error() == 0
+            err = (c.double() - ref).abs()
+            assert torch.all(err <= tol), f"engine {engine}: worst {(err / tol).max().item()}"
+    finally:
+        lib.tbx_set_gemm_tile_n(0)

@@ -133,10 +133,17 @@ def test_gather_and_scatter_known_rows(device):
     assert dev[scattered.index].reshape(-1).tolist() == [2, 2, 0, 0, 1, 1]
 
 
-@pytest.mark.parametrize("count,vocab,width", [(1000, 27, 64), (4097, 300, 5), (20000, 3, 7)])
+# the last three take the staged long-segment path (64+ sources per target row
+# on average): skewed targets, an empty row, chunk and column-slice edges
+@pytest.mark.parametrize("count,vocab,width", [(1000, 27, 64), (4097, 300, 5), (20000, 3, 7),
+                                               (131072, 27, 64), (60001, 27, 100),
+                                               (5000, 40, 33)])
 def test_scatter_add_is_serial_order_exact(device, count, vocab, width):
     rng = np.random.default_rng(count)
     idx = rng.integers(0, vocab, count)
+    if count > 20000:
+        idx = np.minimum(idx, rng.integers(0, vocab, count))  # skewed towards row 0
+        idx[idx == 1] = 0  # row 1 receives nothing
     g = rng.standard_normal((count, width)).astype(np.float32)
     t = Tape()
     gp = t.parameter(tensor(g.shape, g))
