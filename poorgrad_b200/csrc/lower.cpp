@@ -849,8 +849,10 @@ class Lowerer {
     return space.back() % 4 == 0 ? 4 : 1;
   }
 
-  // threads per row and chunks per thread of a row-space kernel
-  void row_shape(const std::vector<int64_t>& space, int64_t& T, int64_t& KC, int& vec) const {
+  // threads per row and chunks per thread of a row-space kernel; col_members
+  // column sums each keep KC * vec register accumulators per thread
+  void row_shape(const std::vector<int64_t>& space, int64_t& T, int64_t& KC, int& vec,
+                 int col_members = 0) const {
     int64_t L = space.empty() ? 1 : space.back();
     vec = row_vec(space);
     int64_t chunks = (L + vec - 1) / vec;
@@ -859,6 +861,11 @@ class Lowerer {
     // reductions, many rows in flight); longer rows: up to 256 threads
     if (chunks > 32 * 16)
       while (T * 2 <= chunks && T < 256) T *= 2;
+    // column sums: widen the team until the accumulators fit in 24 registers
+    // (occupancy, not the cross-warp row reductions, bounds such kernels)
+    while (col_members > 0 && T < 256 && T * 2 <= chunks &&
+           ((chunks + T - 1) / T) * vec * col_members > 24)
+      T *= 2;
     KC = (chunks + T - 1) / T;
   }
 
@@ -1486,7 +1493,9 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
   int64_t R = volume_of(S) / L;
   int64_t T, KC;
   int vec;
-  Lw.row_shape(S, T, KC, vec);
+  int col_members = 0;
+  for (auto& m : K.members) col_members += m.type == MemberType::COL_SUM;
+  Lw.row_shape(S, T, KC, vec, col_members);
   E.vec = vec;
   int64_t teams = 256 / T;
   // One-pass log-sum-exp: a row sum of exp(x - bcast(row max of x)) whose max
@@ -2194,7 +2203,10 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
     E.wide = needs_wide(P, K);
     std::ostringstream fn;
     fn << "struct PRM_NAME { void* p[" << std::max<size_t>(1, K.params.size()) << "]; };\n";
-    fn << "extern \"C\" __global__ void __launch_bounds__(256) NAME(const PRM_NAME prm) {\n";
+    // row kernels run at most four blocks per SM (their grid cap): ask for
+    // registers that let all four be resident
+    fn << "extern \"C\" __global__ void __launch_bounds__(256"
+       << (K.type == KType::ROW ? ", 4" : "") << ") NAME(const PRM_NAME prm) {\n";
     fn << "  typedef " << (E.wide ? "long long" : "int") << " I;\n";
     fn << E.body.str() << "}\n";
     std::string text = fn.str();
