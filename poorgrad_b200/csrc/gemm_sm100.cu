@@ -66,8 +66,12 @@ struct Derived {
   static constexpr int TILE_A = BM * C::BK * 4;
   static constexpr int TILE_B = C::BN * C::BK * 4;
   static constexpr int STAGE_BYTES = 2 * TILE_A + 2 * TILE_B;
-  static constexpr int SMEM_BYTES = C::STAGES * STAGE_BYTES + 1024 + 256;
   static constexpr int THREADS = 64 + 128 * C::GROUPS;
+  // per epilogue warp: a 32 x 33 float tile that turns its lanes' rows into
+  // coalesced row segments
+  static constexpr int EPI_STAGE_BYTES = 32 * 33 * 4;
+  static constexpr int SMEM_BYTES =
+      C::STAGES * STAGE_BYTES + 1024 + 256 + 4 * C::GROUPS * EPI_STAGE_BYTES;
   static constexpr int EPI_COLS = C::BN / C::GROUPS;  // 128 columns per epilogue warpgroup
 };
 constexpr unsigned long long WAIT_NS = 4000000000ull;  // 4 s per wait
@@ -231,6 +235,7 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
   uint64_t* acc_empty = acc_full + 2;    // [2]: TMEM buffer b drained by the epilogue
   uint32_t* tmem_slot = (uint32_t*)(acc_empty + 2);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  float* epi_stage = (float*)(smem + STAGES * STAGE_BYTES + 256);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -380,26 +385,24 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
                      : "memory");
       }
       if (!ok || *abort_flag) break;
-      const int row = t.m0 + q * 32 + lane;
-      if (row < m) {
-        float* dst = out + (long long)t.split * split_stride + (long long)t.batch * m * n;
-        const bool vec = (n % 4) == 0;
-        float* p = dst + (long long)row * n + t.n0 + c0;
+      // stores: 32-column slabs through this warp's staging tile, so that each
+      // store instruction writes one row's 32 consecutive floats
+      float* dst = out + (long long)t.split * split_stride + (long long)t.batch * m * n;
+      float(*st)[33] = (float(*)[33])(epi_stage + (warp - 2) * 32 * 33);
+      const int row0 = t.m0 + q * 32;
 #pragma unroll
-        for (int gq = 0; gq < EPI_COLS / 16; ++gq) {
-          const int col = t.n0 + c0 + gq * 16;
-          if (vec && col + 16 <= n) {
+      for (int g = 0; g < EPI_COLS / 32; ++g) {
 #pragma unroll
-            for (int j = 0; j < 16; j += 4)
-              *(float4*)(p + gq * 16 + j) =
-                  make_float4(total[gq * 16 + j], total[gq * 16 + j + 1], total[gq * 16 + j + 2],
-                              total[gq * 16 + j + 3]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              if (col + j < n) p[gq * 16 + j] = total[gq * 16 + j];
-          }
+        for (int j = 0; j < 32; ++j) st[lane][j] = total[g * 32 + j];
+        __syncwarp();
+        const int col = t.n0 + c0 + g * 32 + lane;
+        if (col < n) {
+          float* p = dst + (long long)row0 * n + col;
+          const int rows = min(32, m - row0);
+#pragma unroll 8
+          for (int r = 0; r < rows; ++r) p[(long long)r * n] = st[r][lane];
         }
+        __syncwarp();
       }
     }
   }
@@ -458,7 +461,6 @@ bool make_map(CUtensorMap* map, const float* base, int64_t ld, int64_t rows, int
 
 int g_tile_override = -1;  // TB_GEMM_TILE_N, or a test's forced choice
 
-int64_t wave_items(int64_t items, int sms) { return (items + sms - 1) / sms * sms; }
 
 }  // namespace
 
@@ -467,7 +469,8 @@ static int splits_for(int bn, int64_t batch, int64_t m, int64_t n, int64_t kp) {
   const int64_t tiles = batch * ((m + BM - 1) / BM) * ((n + bn - 1) / bn);
   const int64_t kb = kp / bk;
   if (tiles >= 120 || kb < 16) return 1;
-  int64_t s = (148 + tiles - 1) / tiles;
+  // as many splits as fill one wave of SMs without starting a second one
+  int64_t s = 148 / tiles;
   s = std::min<int64_t>(s, kb / 8);
   s = std::max<int64_t>(s, 1);
   // every split must own at least one k-block
@@ -475,24 +478,20 @@ static int splits_for(int bn, int64_t batch, int64_t m, int64_t n, int64_t kp) {
   return (int)((kb + per - 1) / per);
 }
 
-// Tile width for a shape (from a sweep of the configs' GEMMs on B200): the
-// 256-wide tile moves 25% less operand data per flop, but it loses on narrow
-// outputs, short k, shapes it would have to split along k while 128 need not,
-// and shapes whose fewer, larger work items fill the SMs in fewer full waves.
+// Tile width for a shape (from a sweep of the configs' GEMMs on B200, split-K
+// filling at most one wave, coalesced epilogue stores): the 256-wide tile moves
+// 25% less operand data per flop and wins everywhere except narrow outputs,
+// where half of its columns would be empty.
 int gemm_tile_n(int64_t batch, int64_t m, int64_t n, int64_t kp) {
+  (void)batch;
+  (void)m;
+  (void)kp;
   if (g_tile_override < 0) {
     const char* e = getenv("TB_GEMM_TILE_N");
     g_tile_override = e ? atoi(e) : 0;
   }
   if (g_tile_override == 128 || g_tile_override == 256) return g_tile_override;
-  if (n <= 64 || kp <= 128) return 128;
-  if (n > 16384 && kp <= 1024) return 128;  // very wide, short-k outputs (vocabulary logits)
-  if (splits_for(256, batch, m, n, kp) > 1 && splits_for(128, batch, m, n, kp) == 1) return 128;
-  const int64_t tm = batch * ((m + BM - 1) / BM);
-  const int64_t items128 = tm * ((n + 127) / 128), items256 = tm * ((n + 255) / 256);
-  const double eff128 = (double)items128 / wave_items(items128, 148);
-  const double eff256 = (double)items256 / wave_items(items256, 148);
-  return eff256 * 1.1 >= eff128 ? 256 : 128;
+  return n <= 64 ? 128 : 256;
 }
 
 void set_gemm_tile_n(int tile) { g_tile_override = tile; }
