@@ -230,10 +230,21 @@ def kernel_profile(plan, reps=20):
     return rows
 
 
-def roofline(rows):
+# DRAM read + write bytes per launch of the dominant kernel class, from one ncu
+# launch-list capture of the workload (dram__bytes_read.sum +
+# dram__bytes_write.sum; charmlp: its 63 k_gemm_tcgen05 launches average 77.3 MB).
+NCU_TRAFFIC = {"charmlp": {"gemm": 77.29e6}}
+
+
+def traffic(workload, kind):
+    return NCU_TRAFFIC.get(workload, {}).get(kind)
+
+
+def roofline(rows, workload=None):
     """Roofline of the dominant kernel: the kernel class with the largest share
     of the step (each GEMM launch is the same tcgen05 kernel).  achieved =
-    algorithmic work of its launches / their summed device time."""
+    algorithmic work of its launches / their summed device time; traffic = the
+    ncu-measured DRAM bytes per launch of that class, where one was captured."""
     hbm, bf16, bf16_sus, how = peaks()
     total = sum(r["ms"] for r in rows) or 1.0
     by = {}
@@ -246,14 +257,16 @@ def roofline(rows):
         achieved = flops / t / 1e12
         peak = bf16 / 6.0   # tf32 runs at half the bf16 rate; 3xTF32 issues three products
         return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak, "traffic": None, "launches": len(group),
+                "frac": achieved / peak, "traffic": traffic(workload, kind),
+                "traffic_unit": "bytes per launch", "launches": len(group),
                 "kernel": "k_gemm_tcgen05 (3xTF32, all GEMMs of the step)",
                 "share": t * 1e3 / total,
                 "peak_note": f"3xTF32-effective = {how} bf16 {bf16:.0f} TF/s / 6"}
     bytes_ = sum(r["read"] + r["write"] for r in group)
     achieved = bytes_ / t / 1e9
     return {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-            "frac": achieved / hbm, "traffic": None, "launches": len(group),
+            "frac": achieved / hbm, "traffic": traffic(workload, kind),
+            "traffic_unit": "bytes per launch", "launches": len(group),
             "kernel": f"{kind} kernels", "share": t * 1e3 / total,
             "peak_note": f"{how} HBM copy bandwidth"}
 
@@ -376,7 +389,7 @@ def main():
 
     stats = plan.stats()
     rows = kernel_profile(plan) if rank == 0 and not args.no_kernel_profile else []
-    roof = roofline(rows) if rows else None
+    roof = roofline(rows, args.config) if rows else None
     if rank == 0:
         cpu = None if args.no_cpu else cpu_baseline(args.config)
         arena_mb = stats["arena_bytes"] / 2**20
