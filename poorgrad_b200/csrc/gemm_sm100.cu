@@ -37,6 +37,7 @@
 #include <cstdlib>
 
 #include "kernels.h"
+#include "launch.h"
 
 namespace tb {
 namespace {
@@ -223,6 +224,7 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
                    float* __restrict__ out, int m, int n, int k_blocks, int split_blocks,
                    int splits, long long split_stride, int tiles_n, int tiles_m, int work_items,
                    int m_fast, int a_mn, int b_mn) {
+  pdl_entry();
   using D = Derived<C>;
   constexpr int BN = C::BN, BK = C::BK, STAGES = C::STAGES, CHUNK = C::CHUNK;
   constexpr int TILE_A = D::TILE_A, TILE_B = D::TILE_B, STAGE_BYTES = D::STAGE_BYTES;
@@ -416,6 +418,7 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
 
 __global__ void k_split_sum(const float* __restrict__ partial, float* __restrict__ out,
                             long long count, int splits) {
+  pdl_entry();
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < count;
        i += (long long)gridDim.x * blockDim.x) {
     float acc = partial[i];
@@ -563,13 +566,13 @@ bool launch_cfg(const Operand& a, const Operand& b, float* c, float* partial, in
     if (sms <= 0) sms = 148;
   }
   const int grid = (int)std::min<long long>(items, sms);
-  k_gemm_tcgen05<C><<<grid, D::THREADS, D::SMEM_BYTES, stream>>>(
-      ma, mal, mb, mbl, target, (int)m, (int)n, kb, per, splits, (long long)(batch * m * n),
-      tiles_n, tiles_m, (int)items, m > 0 && n > m ? 1 : 0, a.mn, b.mn);
+  launch_pdl(k_gemm_tcgen05<C>, grid, D::THREADS, D::SMEM_BYTES, stream, ma, mal, mb, mbl,
+             target, (int)m, (int)n, kb, per, splits, (long long)(batch * m * n), tiles_n, tiles_m,
+             (int)items, m > 0 && n > m ? 1 : 0, (int)a.mn, (int)b.mn);
   if (splits > 1) {
     const long long count = batch * m * n;
     int blocks = (int)std::min<long long>((count + 255) / 256, 148 * 8);
-    k_split_sum<<<blocks, 256, 0, stream>>>(partial, c, count, splits);
+    launch_pdl(k_split_sum, blocks, 256, 0, stream, partial, c, count, splits);
   }
   return cudaPeekAtLastError() == cudaSuccess;
 }

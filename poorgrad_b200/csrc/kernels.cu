@@ -8,6 +8,7 @@
 #include <algorithm>
 
 #include "kernels.h"
+#include "launch.h"
 
 namespace tb {
 namespace {
@@ -16,6 +17,7 @@ constexpr int TILE = 1024;  // selection entries per warp tile
 
 __global__ void k_sort_init(const int* __restrict__ idx, int* __restrict__ keys,
                             int* __restrict__ vals, int64_t count) {
+  pdl_entry();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count;
        i += (int64_t)gridDim.x * blockDim.x) {
     keys[i] = idx[i];
@@ -28,6 +30,7 @@ __global__ void k_sort_init(const int* __restrict__ idx, int* __restrict__ keys,
 __global__ void __launch_bounds__(TILE) k_radix_count(const int* __restrict__ keys,
                                                       int* __restrict__ counts, int64_t count,
                                                       int shift, int64_t tiles) {
+  pdl_entry();
   __shared__ int hist[256];
   const int64_t tile = blockIdx.x;
   if (threadIdx.x < 256) hist[threadIdx.x] = 0;
@@ -48,6 +51,7 @@ __global__ void __launch_bounds__(TILE) k_radix_count(const int* __restrict__ ke
 // counts[tiles][...] (accumulated by the count kernel): thread d walks the
 // tiles with coalesced loads, starting from the exclusive scan of the totals.
 __global__ void __launch_bounds__(256) k_scan_digits(int* __restrict__ counts, int64_t tiles) {
+  pdl_entry();
   __shared__ int totals[256];
   const int d = threadIdx.x;
   totals[d] = counts[tiles * 256 + d];
@@ -89,6 +93,7 @@ __global__ void __launch_bounds__(TILE) k_radix_scatter(const int* __restrict__ 
                                                         int* __restrict__ vals_out,
                                                         const int* __restrict__ offsets,
                                                         int64_t count, int shift, int64_t tiles) {
+  pdl_entry();
   __shared__ int warp_count[TILE / 32][256];
   const int64_t tile = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -124,6 +129,7 @@ __global__ void __launch_bounds__(TILE) k_radix_scatter(const int* __restrict__ 
 
 __global__ void k_segments(const int* __restrict__ keys, int* __restrict__ rstart,
                            int* __restrict__ rend, int64_t count) {
+  pdl_entry();
   for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < count;
        p += (int64_t)gridDim.x * blockDim.x) {
     const int k = keys[p];
@@ -141,6 +147,7 @@ template <int CB>
 __global__ void __launch_bounds__(256) k_final_sum(const float* __restrict__ part,
                                                    float* __restrict__ out, int64_t blocks,
                                                    int64_t width) {
+  pdl_entry();
   constexpr int G = 256 / CB;
   __shared__ float acc_s[G][CB];
   const int col = threadIdx.x % CB, grp = threadIdx.x / CB;
@@ -180,6 +187,7 @@ __global__ void __launch_bounds__(256) k_final_sum(const float* __restrict__ par
 __global__ void k_segment_sum(const float* __restrict__ perm, const int* __restrict__ rstart,
                               const int* __restrict__ rend, float* __restrict__ out,
                               int64_t rows, int64_t width) {
+  pdl_entry();
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < rows * width;
        t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t row = t / width, c = t % width;
@@ -233,6 +241,7 @@ __global__ void __launch_bounds__(256) k_segment_sum_staged(const float* __restr
                                                             const int* __restrict__ rend,
                                                             float* __restrict__ out,
                                                             int64_t width) {
+  pdl_entry();
   extern __shared__ float ring[];  // [kSegSlots][kSegStage][32]; lane = column
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t row = blockIdx.x;
@@ -304,6 +313,7 @@ __global__ void __launch_bounds__(256) k_gemm_simt(const float* __restrict__ ahi
                                                    int64_t b_ld, int64_t b_rows,
                                                    float* __restrict__ c, int64_t m, int64_t n,
                                                    int64_t kp) {
+  pdl_entry();
   __shared__ float As[16][68];
   __shared__ float Bs[16][68];
   const int64_t b = blockIdx.z;
@@ -360,6 +370,7 @@ __global__ void __launch_bounds__(256) k_gemm_simt(const float* __restrict__ ahi
 }
 
 __global__ void k_adam_scalars(float* s, float beta1, float beta2) {
+  pdl_entry();
   if (threadIdx.x == 0 && blockIdx.x == 0) {
     s[0] = __fmul_rn(s[0], beta1);
     s[1] = __fmul_rn(s[1], beta2);
@@ -374,6 +385,7 @@ __global__ void k_optimizer(const OptEntry* __restrict__ entries, int count, int
                             const float* __restrict__ s, const float* __restrict__ lr_ptr,
                             int kind, float beta1, float beta2, float share1, float share2,
                             float eps, float decay, float gscale) {
+  pdl_entry();
   const float lr = *lr_ptr;
   const float c1 = kind ? s[2] : 0.0f, c2 = kind ? s[3] : 0.0f;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -429,20 +441,20 @@ void launch_selection_sort(const int* indices, int* keys, int* vals, int* tmp_ke
   int* src_v = odd ? tmp_vals : vals;
   int* dst_k = odd ? keys : tmp_keys;
   int* dst_v = odd ? vals : tmp_vals;
-  k_sort_init<<<grid, 256, 0, stream>>>(indices, src_k, src_v, count);
+  launch_pdl(k_sort_init, grid, 256, 0, stream, indices, src_k, src_v, count);
   for (int p = 0; p < passes; ++p) {
     const int shift = 8 * p;
     cudaMemsetAsync(counts + tiles * 256, 0, 256 * 4, stream);  // digit totals
-    k_radix_count<<<(unsigned)tiles, TILE, 0, stream>>>(src_k, counts, count, shift, tiles);
-    k_scan_digits<<<1, 256, 0, stream>>>(counts, tiles);
-    k_radix_scatter<<<(unsigned)tiles, TILE, 0, stream>>>(src_k, src_v, dst_k, dst_v, counts,
-                                                        count, shift, tiles);
+    launch_pdl(k_radix_count, (unsigned)tiles, TILE, 0, stream, src_k, counts, count, shift, tiles);
+    launch_pdl(k_scan_digits, 1, 256, 0, stream, counts, tiles);
+    launch_pdl(k_radix_scatter, (unsigned)tiles, TILE, 0, stream, src_k, src_v, dst_k, dst_v,
+               counts, count, shift, tiles);
     std::swap(src_k, dst_k);
     std::swap(src_v, dst_v);
   }
   cudaMemsetAsync(rstart, 0, rows * 4, stream);
   cudaMemsetAsync(rend, 0, rows * 4, stream);  // rows without sources: empty segments
-  k_segments<<<grid, 256, 0, stream>>>(keys, rstart, rend, count);
+  launch_pdl(k_segments, grid, 256, 0, stream, keys, rstart, rend, count);
 }
 
 void launch_segment_sum(const float* perm, const int* rstart, const int* rend, float* out,
@@ -457,27 +469,29 @@ void launch_segment_sum(const float* perm, const int* rstart, const int* rend, f
                            (int)kSegSmem);
       sized[dev] = true;
     }
-    k_segment_sum_staged<<<dim3((unsigned)rows, (unsigned)slices), 256, kSegSmem, stream>>>(
-        perm, rstart, rend, out, width);
+    launch_pdl(k_segment_sum_staged, dim3((unsigned)rows, (unsigned)slices), 256, kSegSmem, stream,
+               perm, rstart, rend, out, width);
     return;
   }
   int grid = (int)std::max<int64_t>(1, std::min<int64_t>((rows * width + 255) / 256, 148 * 8));
-  k_segment_sum<<<grid, 256, 0, stream>>>(perm, rstart, rend, out, rows, width);
+  launch_pdl(k_segment_sum, grid, 256, 0, stream, perm, rstart, rend, out, rows, width);
 }
 
 void launch_final_sum(const float* part, float* out, int64_t blocks, int64_t width,
                       cudaStream_t stream) {
   if ((width + 31) / 32 >= 148)
-    k_final_sum<32><<<(unsigned)((width + 31) / 32), 256, 0, stream>>>(part, out, blocks, width);
+    launch_pdl(k_final_sum<32>, (unsigned)((width + 31) / 32), 256, 0, stream, part, out, blocks,
+               width);
   else
-    k_final_sum<8><<<(unsigned)((width + 7) / 8), 256, 0, stream>>>(part, out, blocks, width);
+    launch_pdl(k_final_sum<8>, (unsigned)((width + 7) / 8), 256, 0, stream, part, out, blocks,
+               width);
 }
 
 void launch_gemm_simt(const Operand& a, const Operand& b, float* c, int64_t batch, int64_t m,
                       int64_t n, int64_t kp, cudaStream_t stream) {
   dim3 grid((unsigned)((n + 63) / 64), (unsigned)((m + 63) / 64), (unsigned)batch);
-  k_gemm_simt<<<grid, 256, 0, stream>>>(a.hi, a.lo, a.mn, a.ld, a.rows, b.hi, b.lo, b.mn, b.ld,
-                                        b.rows, c, m, n, kp);
+  launch_pdl(k_gemm_simt, grid, 256, 0, stream, a.hi, a.lo, a.mn, a.ld, a.rows, b.hi, b.lo, b.mn,
+             b.ld, b.rows, c, m, n, kp);
 }
 
 void launch_gemm(const Operand& a, const Operand& b, float* c, float* partial, int splits,
@@ -489,15 +503,15 @@ void launch_gemm(const Operand& a, const Operand& b, float* c, float* partial, i
 }
 
 void launch_adam_scalars(float* s, float beta1, float beta2, cudaStream_t stream) {
-  k_adam_scalars<<<1, 32, 0, stream>>>(s, beta1, beta2);
+  launch_pdl(k_adam_scalars, 1, 32, 0, stream, s, beta1, beta2);
 }
 
 void launch_optimizer(const OptEntry* entries, int count, int64_t total, const float* scalars,
                       const float* lr, int kind, float beta1, float beta2, float share1,
                       float share2, float eps, float decay, float gscale, cudaStream_t stream) {
   int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 148 * 8));
-  k_optimizer<<<grid, 256, 0, stream>>>(entries, count, total, scalars, lr, kind, beta1, beta2,
-                                       share1, share2, eps, decay, gscale);
+  launch_pdl(k_optimizer, grid, 256, 0, stream, entries, count, total, scalars, lr, kind, beta1,
+             beta2, share1, share2, eps, decay, gscale);
 }
 
 }  // namespace tb

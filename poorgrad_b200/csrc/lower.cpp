@@ -2208,6 +2208,10 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
     fn << "extern \"C\" __global__ void __launch_bounds__(256"
        << (K.type == KType::ROW ? ", 4" : "") << ") NAME(const PRM_NAME prm) {\n";
     fn << "  typedef " << (E.wide ? "long long" : "int") << " I;\n";
+    // launched with programmatic stream serialization: wait for the previous
+    // kernels (and their memory) before any access, then let the next launch
+    fn << "  asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n";
+    fn << "  asm volatile(\"griddepcontrol.launch_dependents;\" ::: \"memory\");\n";
     fn << E.body.str() << "}\n";
     std::string text = fn.str();
     auto it = dedupe.find(text);

@@ -22,6 +22,7 @@
 
 #include "engine.h"
 #include "kernels.h"
+#include "launch.h"
 
 namespace {
 
@@ -47,11 +48,22 @@ struct Driver {
   CUresult (*GetErrorString)(CUresult, const char**) = nullptr;
   CUresult (*ModuleLoadData)(CUmodule*, const void*) = nullptr;
   CUresult (*ModuleGetFunction)(CUfunction*, CUmodule, const char*) = nullptr;
-  CUresult (*LaunchKernel)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned,
-                           unsigned, CUstream, void**, void**) = nullptr;
+  CUresult (*LaunchKernelEx)(const CUlaunchConfig*, CUfunction, void**, void**) = nullptr;
   CUresult (*FuncSetAttribute)(CUfunction, CUfunction_attribute, int) = nullptr;
 };
 Driver g_driver;
+
+}  // namespace
+
+bool tb::pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("TB_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+namespace {
 
 bool load_driver() {
   auto get = [](const char* name, void** fn) {
@@ -62,7 +74,7 @@ bool load_driver() {
   return get("cuGetErrorString", (void**)&g_driver.GetErrorString) &&
          get("cuModuleLoadData", (void**)&g_driver.ModuleLoadData) &&
          get("cuModuleGetFunction", (void**)&g_driver.ModuleGetFunction) &&
-         get("cuLaunchKernel", (void**)&g_driver.LaunchKernel) &&
+         get("cuLaunchKernelEx", (void**)&g_driver.LaunchKernelEx) &&
          get("cuFuncSetAttribute", (void**)&g_driver.FuncSetAttribute);
 }
 
@@ -414,10 +426,22 @@ int64_t launch_kernel(tb_plan* plan, size_t k, cudaStream_t stream) {
       launches += 1;
       break;
     default: {
+      // programmatic stream serialization: the emitted kernels begin with
+      // griddepcontrol.wait, so this launch may overlap the previous kernel's tail
       void* args[] = {plan->kparams[k].data()};
-      check(g_driver.LaunchKernel(plan->fn[k], (unsigned)K.grid, 1, 1, (unsigned)K.block, 1, 1,
-                                  (unsigned)K.smem, stream, args, nullptr),
-            "cuLaunchKernel");
+      CUlaunchAttribute attr;
+      attr.id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+      attr.value.programmaticStreamSerializationAllowed = 1;
+      CUlaunchConfig cfg = {};
+      cfg.gridDimX = (unsigned)K.grid;
+      cfg.gridDimY = cfg.gridDimZ = 1;
+      cfg.blockDimX = (unsigned)K.block;
+      cfg.blockDimY = cfg.blockDimZ = 1;
+      cfg.sharedMemBytes = (unsigned)K.smem;
+      cfg.hStream = stream;
+      cfg.attrs = &attr;
+      cfg.numAttrs = tb::pdl_enabled() ? 1 : 0;
+      check(g_driver.LaunchKernelEx(&cfg, plan->fn[k], args, nullptr), "cuLaunchKernelEx");
       launches += 1;
     }
   }
