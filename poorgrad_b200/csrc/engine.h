@@ -119,6 +119,7 @@ struct Kernel {
   int partial = -1, final_out = -1;  // FINAL
   int64_t final_blocks = 0, final_width = 0;
   std::vector<int> reads, writes;    // buffer ids touched (liveness)
+  bool side = false;                 // runs on the side stream from the program's start
   std::string describe;
 };
 
@@ -146,6 +147,10 @@ struct Program {
   int64_t arena_bytes = 0, unplanned_bytes = 0, fused_nodes = 0;
   bool exact = true;
   int gemms = 0;
+  // Side-stream kernels (the leading SORTs) run concurrently with the main
+  // kernels before side_join, the first main kernel that uses what they wrote;
+  // the main stream waits for them there (-1: no side kernels).
+  int side_join = -1;
   int parameter_slots = 0, input_slots = 0;
   std::vector<std::vector<int64_t>> parameter_shapes;
   std::vector<int> input_buffer;   // per input slot: buffer id (dense or indices)

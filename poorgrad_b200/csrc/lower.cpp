@@ -2040,12 +2040,66 @@ static void emit_prep(Program& P, Kernel& K, Emitter& E) {
 }
 
 // ---- buffer liveness and the arena layout
+// Arena invariants, checked after placement (a violation is a lowering bug
+// and fails the compile): buffers whose kernel intervals intersect do not
+// share bytes, and every buffer of a side kernel stays allocated until the
+// side stream joins.
+static void check_arena(const Program& P) {
+  std::vector<int> placed;
+  for (size_t i = 0; i < P.buffers.size(); ++i) {
+    const Buffer& b = P.buffers[i];
+    if (b.storage == Storage::Arena && b.first >= 0) placed.push_back((int)i);
+  }
+  std::sort(placed.begin(), placed.end(),
+            [&](int x, int y) { return P.buffers[x].offset < P.buffers[y].offset; });
+  for (size_t i = 0; i < placed.size(); ++i) {
+    const Buffer& a = P.buffers[placed[i]];
+    for (size_t j = i + 1; j < placed.size(); ++j) {
+      const Buffer& b = P.buffers[placed[j]];
+      if (b.offset >= a.offset + a.bytes) break;
+      if (a.first <= b.last && b.first <= a.last)
+        fail("arena: buffers " + std::to_string(placed[i]) + " and " + std::to_string(placed[j]) +
+             " overlap while both are live");
+    }
+  }
+  for (const Kernel& K : P.kernels) {
+    if (!K.side) continue;
+    for (const std::vector<int>* list : {&K.reads, &K.writes})
+      for (int b : *list)
+        if (P.buffers[b].storage == Storage::Arena && P.buffers[b].last < P.side_join)
+          fail("arena: a side-stream buffer is released before the join");
+  }
+}
+
+// The main kernel at which the side stream joins: the first that reads or
+// writes a buffer a side kernel wrote (the last kernel when none does).
+static int side_join(const Program& P) {
+  std::set<int> written;
+  bool any = false;
+  for (const Kernel& K : P.kernels)
+    if (K.side) {
+      any = true;
+      written.insert(K.writes.begin(), K.writes.end());
+    }
+  if (!any) return -1;
+  for (size_t k = 0; k < P.kernels.size(); ++k) {
+    const Kernel& K = P.kernels[k];
+    if (K.side) continue;
+    for (int b : K.reads)
+      if (written.count(b)) return (int)k;
+    for (int b : K.writes)
+      if (written.count(b)) return (int)k;
+  }
+  return (int)P.kernels.size() - 1;
+}
+
 static void plan_arena(Program& P) {
   const int never = -1;
   for (auto& b : P.buffers) {
     b.first = never;
     b.last = never;
   }
+  P.side_join = side_join(P);
   for (size_t k = 0; k < P.kernels.size(); ++k) {
     const Kernel& K = P.kernels[k];
     auto touch = [&](int buf) {
@@ -2057,6 +2111,13 @@ static void plan_arena(Program& P) {
     };
     for (int b : K.reads) touch(b);
     for (int b : K.writes) touch(b);
+  }
+  // a side kernel's buffers (its scratch included) stay allocated until the
+  // join: every main kernel before it runs concurrently with the side stream
+  for (const Kernel& K : P.kernels) {
+    if (!K.side) continue;
+    for (int b : K.reads) P.buffers[b].last = std::max(P.buffers[b].last, P.side_join);
+    for (int b : K.writes) P.buffers[b].last = std::max(P.buffers[b].last, P.side_join);
   }
   const int end = (int)P.kernels.size();
   std::vector<int> ids;
@@ -2125,6 +2186,27 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
   // codegen; FINAL kernels are inserted right after their row kernel
   std::vector<Kernel> kernels;
   kernels.swap(P.kernels);
+  // Selection sorts read only input or leaf indices: they move to the front
+  // and run on a side stream, overlapping the forward program (their buffers
+  // then live from the program's start, so the arena keeps them apart from
+  // everything that runs meanwhile).
+  {
+    std::vector<Kernel> order;
+    std::vector<int> moved(kernels.size(), -1);
+    for (size_t i = 0; i < kernels.size(); ++i)
+      if (kernels[i].type == KType::SORT) {
+        moved[i] = (int)order.size();
+        order.push_back(kernels[i]);
+        order.back().side = true;
+      }
+    for (size_t i = 0; i < kernels.size(); ++i)
+      if (kernels[i].type != KType::SORT) {
+        moved[i] = (int)order.size();
+        order.push_back(kernels[i]);
+      }
+    for (auto& [sel, k] : P.sort_of) k = moved[k];
+    kernels.swap(order);
+  }
   std::map<std::string, std::string> dedupe;  // body -> function name
   std::ostringstream all;
   all << prelude();
@@ -2276,6 +2358,7 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
   for (int n : P.order)
     if (P.info[n].kind == Kind::Expr && !P.info[n].materialized) P.fused_nodes++;
   plan_arena(P);
+  check_arena(P);
   return prog;
 }
 

@@ -276,7 +276,7 @@ struct tb_optimizer {
 struct tb_plan {
   std::unique_ptr<tb::Program> prog;
   int device = 0;
-  cudaStream_t stream = nullptr, comm_stream = nullptr;
+  cudaStream_t stream = nullptr, comm_stream = nullptr, side_stream = nullptr;
   char* arena = nullptr;
   std::vector<void*> own;              // input/leaf allocations
   std::vector<void*> buffer_ptr;       // resolved device pointer per buffer id
@@ -298,6 +298,7 @@ struct tb_plan {
     for (void* p : own) cudaFree(p);
     if (stream) cudaStreamDestroy(stream);
     if (comm_stream) cudaStreamDestroy(comm_stream);
+    if (side_stream) cudaStreamDestroy(side_stream);
   }
 };
 
@@ -463,7 +464,29 @@ void enqueue_program(tb_plan* plan, cudaStream_t stream) {
     return plan->events[next_event++];
   };
   bool comm_used = false;
+  // side kernels (selection sorts) fork off at the start; the main stream
+  // joins them at P.side_join, the first kernel that uses what they wrote --
+  // the arena keeps every side buffer allocated until that kernel
+  bool forked = false, joined = true;
   for (size_t k = 0; k < P.kernels.size(); ++k) {
+    const tb::Kernel& K = P.kernels[k];
+    if (K.side) {
+      if (!forked) {
+        cudaEvent_t e = event();
+        check(cudaEventRecord(e, stream), "cudaEventRecord");
+        check(cudaStreamWaitEvent(plan->side_stream, e, 0), "cudaStreamWaitEvent");
+        forked = true;
+        joined = false;
+      }
+      launches += launch_kernel(plan, k, plan->side_stream);
+      continue;
+    }
+    if (!joined && (int)k >= P.side_join) {
+      cudaEvent_t e = event();
+      check(cudaEventRecord(e, plan->side_stream), "cudaEventRecord");
+      check(cudaStreamWaitEvent(stream, e, 0), "cudaStreamWaitEvent");
+      joined = true;
+    }
     launches += launch_kernel(plan, k, stream);
     for (const Bucket& b : buckets) {
       if (b.after_kernel != (int)k) continue;
@@ -504,6 +527,7 @@ void instantiate(tb_plan* plan) {
   check(cudaFree(nullptr), "context init");
   check(cudaStreamCreateWithFlags(&plan->stream, cudaStreamNonBlocking), "cudaStreamCreate");
   check(cudaStreamCreateWithFlags(&plan->comm_stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  check(cudaStreamCreateWithFlags(&plan->side_stream, cudaStreamNonBlocking), "cudaStreamCreate");
   plan->buffer_ptr.assign(P.buffers.size(), nullptr);
   if (P.arena_bytes > 0) check(cudaMalloc((void**)&plan->arena, P.arena_bytes), "cudaMalloc(arena)");
   for (size_t b = 0; b < P.buffers.size(); ++b) {
@@ -895,6 +919,7 @@ int64_t tbx_lower_describe(const tb_plan_desc* desc, char* buffer, size_t capaci
     for (size_t k = 0; k < prog->kernels.size(); ++k) o << k << ": " << prog->kernels[k].describe << "\n";
     o << "arena " << prog->arena_bytes << " bytes (" << prog->unplanned_bytes << " without reuse)\n";
     o << "exact " << (prog->exact ? 1 : 0) << " fused " << prog->fused_nodes << "\n";
+    if (prog->side_join >= 0) o << "side join " << prog->side_join << "\n";
     for (size_t b = 0; b < prog->buffers.size(); ++b) {
       const tb::Buffer& buf = prog->buffers[b];
       if (!buf.keep) continue;
