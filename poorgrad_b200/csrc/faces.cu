@@ -153,6 +153,7 @@ extern "C" int tbx_gemm_prepared(const float* a_hi, const float* a_lo, const flo
                                   m, n, kp, kp, engine);
 }
 extern "C" int tbx_gemm_error(void) { return tb::gemm_error(); }
+extern "C" int tbx_segment_error(void) { return tb::segment_error(); }
 extern "C" void tbx_set_gemm_tile_n(int tile) { tb::set_gemm_tile_n(tile); }
 extern "C" int tbx_gemm_splits(int64_t batch, int64_t m, int64_t n, int64_t kp) {
   return tb::gemm_splits(batch, m, n, kp);

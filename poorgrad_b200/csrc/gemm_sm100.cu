@@ -464,6 +464,23 @@ bool make_map(CUtensorMap* map, const float* base, int64_t ld, int64_t rows, int
 
 int g_tile_override = -1;  // TB_GEMM_TILE_N, or a test's forced choice
 
+}  // namespace
+
+bool encode_rows_f32(CUtensorMap* map, const float* base, int64_t width, int64_t rows,
+                     int box_cols, int box_rows) {
+  EncodeTiled enc = encoder();
+  if (!enc || width % 4 != 0 || ((uintptr_t)base & 15)) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)width, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(width * 4)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+namespace {
+
 
 }  // namespace
 

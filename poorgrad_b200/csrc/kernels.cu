@@ -285,6 +285,121 @@ __global__ void __launch_bounds__(256) k_segment_sum_staged(const float* __restr
   if (warp == 0 && live) out[row * width + c] = acc;
 }
 
+// Long segments through TMA: one warp per (row, 32-column slice).  Lane 0 keeps
+// kSegTmaSlots chunks of the segment in flight (one 32-column x kSegTmaRows
+// box each, completing on a per-slot mbarrier); the warp adds each landed
+// chunk in ascending row order from zero -- the same serial fold, so the
+// result is bit-identical to k_segment_sum.  Rows past the segment (the next
+// segment's, or zero fill past the end) are loaded but not added.
+constexpr int kSegTmaRows = 256;
+constexpr int kSegTmaSlots = 6;
+constexpr size_t kSegTmaSmem = (size_t)kSegTmaSlots * kSegTmaRows * 32 * 4 + 128 + 64;
+constexpr unsigned long long kSegWaitNs = 2000000000ull;  // 2 s per wait
+__device__ int g_segment_error = 0;
+
+__device__ __forceinline__ bool seg_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool seg_wait(uint32_t bar, uint32_t parity) {
+  if (seg_try_wait(bar, parity)) return true;
+  unsigned long long t0, t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  while (!seg_try_wait(bar, parity)) {
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > kSegWaitNs) return false;
+  }
+  return true;
+}
+
+__global__ void __launch_bounds__(32) k_segment_sum_tma(const __grid_constant__ CUtensorMap map,
+                                                        const int* __restrict__ rstart,
+                                                        const int* __restrict__ rend,
+                                                        float* __restrict__ out,
+                                                        int64_t width) {
+  pdl_entry();
+  extern __shared__ uint8_t seg_raw[];
+  float* ring = (float*)(((uintptr_t)seg_raw + 127) & ~(uintptr_t)127);
+  uint64_t* full = (uint64_t*)(ring + (size_t)kSegTmaSlots * kSegTmaRows * 32);
+  const int lane = threadIdx.x;
+  const int64_t row = blockIdx.x;
+  const int col0 = (int)blockIdx.y * 32;
+  const int64_t c = col0 + lane;
+  const int64_t q0 = rstart[row], q1 = rend[row];
+  const int64_t chunks = (q1 - q0 + kSegTmaRows - 1) / kSegTmaRows;
+  auto bar = [&](int s) { return (uint32_t)__cvta_generic_to_shared(&full[s]); };
+  if (lane == 0) {
+    for (int s = 0; s < kSegTmaSlots; ++s)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar(s)));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  int64_t issued = 0;
+  auto issue = [&](int64_t i) {  // lane 0: chunk i into slot i % kSegTmaSlots
+    if (i >= chunks) return;
+    const int s = (int)(i % kSegTmaSlots);
+    const uint32_t dst =
+        (uint32_t)__cvta_generic_to_shared(ring + (size_t)s * kSegTmaRows * 32);
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar(s)),
+                 "r"(kSegTmaRows * 32 * 4)
+                 : "memory");
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"((uint64_t)&map), "r"(col0), "r"((int)(q0 + i * kSegTmaRows)), "r"(bar(s))
+        : "memory");
+    issued = i + 1;
+  };
+  if (lane == 0)
+    for (int64_t i = 0; i < kSegTmaSlots; ++i) issue(i);
+  float acc = 0.0f;
+  int64_t done = 0;
+  for (int64_t i = 0; i < chunks; ++i) {
+    const int s = (int)(i % kSegTmaSlots);
+    if (!seg_wait(bar(s), (uint32_t)((i / kSegTmaSlots) & 1))) {
+      if (lane == 0) atomicExch(&g_segment_error, 1);
+      break;
+    }
+    const float* slot = ring + (size_t)s * kSegTmaRows * 32;
+    const int64_t left = q1 - q0 - i * kSegTmaRows;
+    if (left >= kSegTmaRows) {
+      // software-pipelined: each register is refilled with the row 64 ahead
+      // as soon as its value is added, so loads stay ahead of the add chain
+      float v[64];
+#pragma unroll
+      for (int u = 0; u < 64; ++u) v[u] = slot[u * 32 + lane];
+#pragma unroll
+      for (int jb = 0; jb < kSegTmaRows; jb += 64) {
+#pragma unroll
+        for (int u = 0; u < 64; ++u) {
+          const float x = v[u];
+          if (jb + 64 < kSegTmaRows) v[u] = slot[(jb + 64 + u) * 32 + lane];
+          acc = __fadd_rn(acc, x);
+        }
+      }
+    } else {
+      for (int j = 0; j < left; ++j) acc = __fadd_rn(acc, slot[j * 32 + lane]);
+    }
+    done = i + 1;
+    // the slot is read: order those reads before the copy that refills it
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) issue(i + kSegTmaSlots);
+  }
+  // after an expired wait, let this warp's copies in flight land (bounded)
+  // before the shared memory is released
+  issued = __shfl_sync(0xffffffffu, issued, 0);
+  for (int64_t i = done; i < issued; ++i)
+    if (!seg_wait(bar((int)(i % kSegTmaSlots)), (uint32_t)((i / kSegTmaSlots) & 1))) break;
+  if (done == chunks && c < width) out[row * width + c] = acc;
+}
+
 // Four consecutive reduction indices k..k+3 of operand row r, as hi + lo
 // (exactly the original f32 values); zero outside the operand.
 __device__ __forceinline__ float4 simt_quad(const float* __restrict__ h,
@@ -460,6 +575,21 @@ void launch_selection_sort(const int* indices, int* keys, int* vals, int* tmp_ke
 void launch_segment_sum(const float* perm, const int* rstart, const int* rend, float* out,
                         int64_t rows, int64_t width, int64_t count, cudaStream_t stream) {
   const int64_t slices = (width + 31) / 32;
+  CUtensorMap map;
+  if (count >= 64 * rows && rows <= 65535 && slices <= 65535 && count < (1LL << 31) &&
+      encode_rows_f32(&map, perm, width, count, 32, kSegTmaRows)) {
+    static bool sized[256] = {};  // opt in to > 48 KB of dynamic shared memory, per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 256 && !sized[dev]) {
+      cudaFuncSetAttribute(k_segment_sum_tma, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)kSegTmaSmem);
+      sized[dev] = true;
+    }
+    launch_pdl(k_segment_sum_tma, dim3((unsigned)rows, (unsigned)slices), 32, kSegTmaSmem, stream,
+               map, rstart, rend, out, width);
+    return;
+  }
   if (count >= 64 * rows && rows <= 65535 && slices <= 65535) {  // long segments on average
     static bool sized[256] = {};  // opt in to > 48 KB of dynamic shared memory, per device
     int dev = 0;
@@ -475,6 +605,12 @@ void launch_segment_sum(const float* perm, const int* rstart, const int* rend, f
   }
   int grid = (int)std::max<int64_t>(1, std::min<int64_t>((rows * width + 255) / 256, 148 * 8));
   launch_pdl(k_segment_sum, grid, 256, 0, stream, perm, rstart, rend, out, rows, width);
+}
+
+int segment_error() {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_segment_error, sizeof(int));
+  return v;
 }
 
 void launch_final_sum(const float* part, float* out, int64_t blocks, int64_t width,

@@ -1,5 +1,6 @@
 // kernels.h -- host launchers of the hand-written (non-emitted) kernels.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -52,6 +53,12 @@ void launch_gemm_simt(const Operand& a, const Operand& b, float* c, int64_t batc
 bool launch_gemm_tcgen05_split(const Operand& a, const Operand& b, float* c, float* partial,
                                int splits, int64_t batch, int64_t m, int64_t n, int64_t kp,
                                cudaStream_t stream);
+// 2-D tensor map over row-major f32 [rows][width] (width a multiple of 4), no
+// swizzle, boxes of box_cols x box_rows, zero fill outside; false if refused.
+bool encode_rows_f32(CUtensorMap* map, const float* base, int64_t width, int64_t rows,
+                     int box_cols, int box_rows);
+// Error code recorded by a segment-sum kernel whose bounded wait expired (0 = none).
+int segment_error();
 // Tile width (128 or 256) the tcgen05 path uses for a shape; a test may force one.
 int gemm_tile_n(int64_t batch, int64_t m, int64_t n, int64_t kp);
 void set_gemm_tile_n(int tile);

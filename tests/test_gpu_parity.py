@@ -151,6 +151,8 @@ def test_scatter_add_is_serial_order_exact(device, count, vocab, width):
     out = gp.scatter(sel, vocab)
     ref, dev, _ = both(t, [out])
     assert_exact(dev[out.index], ref[out.index])
+    from poorgrad_b200.abi import load_library
+    assert load_library().tbx_segment_error() == 0  # no bounded wait expired
 
 
 # ------------------------------------------------------------ reductions and row ops
