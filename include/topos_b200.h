@@ -109,6 +109,7 @@ typedef struct tb_plan tb_plan;
 typedef struct tb_params tb_params;
 typedef struct tb_optimizer tb_optimizer;
 typedef struct tb_comm tb_comm;
+typedef struct tb_run tb_run;
 
 typedef struct tb_plan_stats {
   int64_t kernels;              /* launches in one run of the device program */
@@ -146,9 +147,11 @@ int tb_params_upload(tb_params* params, int32_t slot, const float* host, int64_t
 int tb_params_download(const tb_params* params, int32_t slot, float* host, int64_t count);
 
 /* ---- running (`Plan::forward` -> `Run`, engine/plan.rs:514-640; `Run::of`, run.rs:139) */
-/* Enqueues one run: feeds are copied into the plan's input buffers, then the
- * device program (and an attached gradient exchange and optimizer step) is
- * launched as one CUDA graph.  Asynchronous with respect to the host. */
+/* Enqueues one run on the plan's main instance: feeds are copied into its
+ * input buffers, then the device program (and an attached gradient exchange
+ * and optimizer step) is launched as one CUDA graph.  Asynchronous with
+ * respect to the host.  One thread at a time; concurrent runs of one plan use
+ * `tb_run_begin`. */
 int tb_plan_run(tb_plan* plan, tb_params* params, int32_t feed_count, const tb_feed* feeds);
 /* Replaces: `Run::backward(output)` then `Gradients::of(parameter)` (engine/run.rs:229-318)
  * for a plan compiled with `backward` set: the reverse scan of every scalar readable root
@@ -163,6 +166,26 @@ int tb_plan_read(tb_plan* plan, int64_t node, float* host, int64_t count);
 int tb_plan_device_pointer(tb_plan* plan, int64_t node, const float** device);
 /* The CUDA stream (cudaStream_t) the plan runs on. */
 void* tb_plan_stream(tb_plan* plan);
+
+/* ---- concurrent runs of one plan (`Plan` and `Run` are Send + Sync and run from
+ *      many threads: engine/plan.rs:20, run.rs:14, examples/makemore/mlp_parallel.rs:136-165) */
+/* Replaces: `Plan::forward(parameters, feeds) -> Run` from any thread.  Draws an
+ * instance (its own stream, arena and input buffers) from the plan's pool,
+ * creating one when all are in use, copies the feeds and launches the device
+ * program on it.  Runs drawn this way carry no optimizer or gradient
+ * exchange.  Thread-safe; asynchronous with respect to the host. */
+int tb_run_begin(tb_plan* plan, tb_params* params, int32_t feed_count, const tb_feed* feeds,
+                 tb_run** run);
+/* Waits for the run's stream. */
+int tb_run_synchronize(tb_run* run);
+/* Replaces `Run::of(node)` (run.rs:139): copies a readable value of this run to host memory (waits). */
+int tb_run_read(tb_run* run, int64_t node, float* host, int64_t count);
+/* Device address of a readable value of this run (valid until the run is released). */
+int tb_run_device_pointer(tb_run* run, int64_t node, const float** device);
+/* The CUDA stream (cudaStream_t) the run executes on. */
+void* tb_run_stream(tb_run* run);
+/* Replaces dropping the `Run`: returns its instance to the plan's pool. */
+void tb_run_release(tb_run* run);
 
 /* ---- optimizer step (graph/parameters.rs:90-146; neural/optimizer.rs:40-51; neural/adam.rs:19-171) */
 enum { TB_OPTIMIZER_SGD = 0, TB_OPTIMIZER_ADAM = 1, TB_OPTIMIZER_ADAMW = 2 };

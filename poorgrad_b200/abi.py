@@ -192,6 +192,12 @@ def load_library() -> C.CDLL:
         "tb_plan_read": (C.c_int, [P, C.c_int64, C.POINTER(C.c_float), C.c_int64]),
         "tb_plan_device_pointer": (C.c_int, [P, C.c_int64, C.POINTER(C.c_void_p)]),
         "tb_plan_stream": (P, [P]),
+        "tb_run_begin": (C.c_int, [P, P, C.c_int32, C.POINTER(TbFeed), C.POINTER(P)]),
+        "tb_run_synchronize": (C.c_int, [P]),
+        "tb_run_read": (C.c_int, [P, C.c_int64, C.POINTER(C.c_float), C.c_int64]),
+        "tb_run_device_pointer": (C.c_int, [P, C.c_int64, C.POINTER(C.c_void_p)]),
+        "tb_run_stream": (P, [P]),
+        "tb_run_release": (None, [P]),
         "tb_optimizer_create": (C.c_int, [P, P, C.POINTER(TbOptimizerDesc), C.c_int32,
                                           C.POINTER(C.c_int32), C.POINTER(C.c_int64),
                                           C.POINTER(P)]),

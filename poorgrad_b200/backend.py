@@ -120,6 +120,11 @@ class DevicePlan:
     def synchronize(self):
         _check(self.lib.tb_plan_synchronize(self.handle), "tb_plan_synchronize")
 
+    def begin(self, params: DeviceParameters, feeds: Optional[Dict] = None) -> "DeviceRun":
+        """`Plan::forward` from any thread: a run on its own pooled instance
+        (stream, arena, inputs), so runs of one plan proceed concurrently."""
+        return DeviceRun(self, params, feeds)
+
     def of(self, symbol) -> np.ndarray:
         """`Run::of`: a readable value, copied to the host."""
         index = symbol.index if hasattr(symbol, "index") else int(symbol)
@@ -167,6 +172,39 @@ class DevicePlan:
         if getattr(self, "handle", None):
             self.lib.tb_plan_destroy(self.handle)
             self.handle = None
+
+
+class DeviceRun:
+    """A run drawn from a plan's instance pool (the reference's `Run`): its
+    readable values stay available until it is released (or collected)."""
+
+    def __init__(self, plan: DevicePlan, params: DeviceParameters, feeds: Optional[Dict]):
+        self.plan = plan
+        self.lib = plan.lib
+        self._feeds = Feeds(plan.columns, feeds or {})
+        self.handle = C.c_void_p()
+        _check(self.lib.tb_run_begin(plan.handle, params.handle, self._feeds.count,
+                                     self._feeds.array, C.byref(self.handle)), "tb_run_begin")
+
+    def synchronize(self):
+        _check(self.lib.tb_run_synchronize(self.handle), "tb_run_synchronize")
+        return self
+
+    def of(self, symbol) -> np.ndarray:
+        """`Run::of`: a readable value of this run, copied to the host."""
+        index = symbol.index if hasattr(symbol, "index") else int(symbol)
+        out = np.empty(self.plan.columns.nodes[index].shape, dtype=np.float32)
+        _check(self.lib.tb_run_read(self.handle, index, fptr(out), max(out.size, 1)),
+               "tb_run_read")
+        return out
+
+    def release(self):
+        if getattr(self, "handle", None):
+            self.lib.tb_run_release(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.release()
 
 
 class Optimizer:

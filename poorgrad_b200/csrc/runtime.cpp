@@ -232,6 +232,8 @@ bool poisoned() {
 }
 }  // namespace tb
 
+struct tb_instance;
+
 struct tb_params {
   int device = 0;
   void* base = nullptr;
@@ -255,7 +257,7 @@ struct tb_comm {
 };
 
 struct tb_optimizer {
-  tb_plan* plan = nullptr;
+  tb_instance* plan = nullptr;  // the plan's main instance
   tb_params* params = nullptr;
   tb_optimizer_desc desc{};
   std::vector<int32_t> slots;
@@ -273,15 +275,20 @@ struct tb_optimizer {
   }
 };
 
-struct tb_plan {
-  std::unique_ptr<tb::Program> prog;
+// Per-run state of a plan: streams, arena, input buffers and the captured
+// graph.  A plan owns a main instance (used by tb_plan_run, the optimizer and
+// the communicator) and a pool that tb_run_begin draws from, so that runs of
+// one compiled plan proceed concurrently from several threads, each on its own
+// stream and arena.
+struct tb_instance {
+  tb_plan* owner = nullptr;
+  tb::Program* prog = nullptr;         // the plan's (shared, immutable after compile)
   int device = 0;
+  std::vector<CUfunction> fn;          // the plan's emitted kernels, per kernel
   cudaStream_t stream = nullptr, comm_stream = nullptr, side_stream = nullptr;
   char* arena = nullptr;
   std::vector<void*> own;              // input/leaf allocations
   std::vector<void*> buffer_ptr;       // resolved device pointer per buffer id
-  CUmodule module = nullptr;
-  std::vector<CUfunction> fn;          // per kernel (emitted kernels)
   std::vector<std::vector<void*>> kparams;
   tb_params* bound = nullptr;
   cudaGraphExec_t graph = nullptr;
@@ -291,7 +298,8 @@ struct tb_plan {
   int64_t bucket_bytes = 0;
   std::vector<cudaEvent_t> events;
   int64_t launches = 0;
-  ~tb_plan() {
+  ~tb_instance() {
+    if (stream) cudaStreamSynchronize(stream);
     if (graph) cudaGraphExecDestroy(graph);
     for (auto e : events) cudaEventDestroy(e);
     if (arena) cudaFree(arena);
@@ -300,6 +308,24 @@ struct tb_plan {
     if (comm_stream) cudaStreamDestroy(comm_stream);
     if (side_stream) cudaStreamDestroy(side_stream);
   }
+};
+
+struct tb_plan {
+  std::unique_ptr<tb::Program> prog;
+  int device = 0;
+  CUmodule module = nullptr;
+  std::vector<CUfunction> fn;
+  std::unique_ptr<tb_instance> main;
+  std::mutex pool_mutex;
+  std::vector<std::unique_ptr<tb_instance>> pool;
+  std::vector<tb_instance*> idle;
+};
+
+// A run drawn from the plan's pool (the reference's Run): its values stay
+// readable until it is released.
+struct tb_run {
+  tb_plan* plan = nullptr;
+  tb_instance* inst = nullptr;
 };
 
 namespace {
@@ -319,7 +345,7 @@ int readable_buffer(const tb::Program& P, int64_t node) {
   return f.buf;
 }
 
-void bind_params(tb_plan* plan, tb_params* params) {
+void bind_params(tb_instance* plan, tb_params* params) {
   tb::Program& P = *plan->prog;
   if (plan->bound == params) return;
   for (size_t b = 0; b < P.buffers.size(); ++b) {
@@ -340,8 +366,8 @@ void bind_params(tb_plan* plan, tb_params* params) {
   plan->graph_dirty = true;
 }
 
-float* fp(tb_plan* plan, int b) { return (float*)plan->buffer_ptr[b]; }
-int* ip(tb_plan* plan, int b) { return (int*)plan->buffer_ptr[b]; }
+float* fp(tb_instance* plan, int b) { return (float*)plan->buffer_ptr[b]; }
+int* ip(tb_instance* plan, int b) { return (int*)plan->buffer_ptr[b]; }
 
 // gradient ranges of the attached optimizer, issued after their last writer
 struct Bucket {
@@ -350,7 +376,7 @@ struct Bucket {
   int64_t bytes;
 };
 
-std::vector<Bucket> gradient_buckets(tb_plan* plan) {
+std::vector<Bucket> gradient_buckets(tb_instance* plan) {
   std::vector<Bucket> out;
   if (!plan->optimizer || !plan->comm) return out;
   tb::Program& P = *plan->prog;
@@ -387,7 +413,7 @@ std::vector<Bucket> gradient_buckets(tb_plan* plan) {
   return out;
 }
 
-int64_t launch_kernel(tb_plan* plan, size_t k, cudaStream_t stream) {
+int64_t launch_kernel(tb_instance* plan, size_t k, cudaStream_t stream) {
   tb::Program& P = *plan->prog;
   const tb::Kernel& K = P.kernels[k];
   int64_t launches = 0;
@@ -450,7 +476,7 @@ int64_t launch_kernel(tb_plan* plan, size_t k, cudaStream_t stream) {
   return launches;
 }
 
-void enqueue_program(tb_plan* plan, cudaStream_t stream) {
+void enqueue_program(tb_instance* plan, cudaStream_t stream) {
   tb::Program& P = *plan->prog;
   std::vector<Bucket> buckets = gradient_buckets(plan);
   int64_t launches = 0;
@@ -521,10 +547,14 @@ void enqueue_program(tb_plan* plan, cudaStream_t stream) {
   plan->launches = launches;
 }
 
-void instantiate(tb_plan* plan) {
-  tb::Program& P = *plan->prog;
-  check(cudaGetDevice(&plan->device), "cudaGetDevice");
-  check(cudaFree(nullptr), "context init");
+void run_plan(tb_instance* plan);
+
+void setup_instance(tb_plan* owner, tb_instance* plan) {
+  tb::Program& P = *owner->prog;
+  plan->owner = owner;
+  plan->prog = owner->prog.get();
+  plan->device = owner->device;
+  plan->fn = owner->fn;
   check(cudaStreamCreateWithFlags(&plan->stream, cudaStreamNonBlocking), "cudaStreamCreate");
   check(cudaStreamCreateWithFlags(&plan->comm_stream, cudaStreamNonBlocking), "cudaStreamCreate");
   check(cudaStreamCreateWithFlags(&plan->side_stream, cudaStreamNonBlocking), "cudaStreamCreate");
@@ -560,6 +590,12 @@ void instantiate(tb_plan* plan) {
       }
     }
   }
+}
+
+void instantiate(tb_plan* plan) {
+  tb::Program& P = *plan->prog;
+  check(cudaGetDevice(&plan->device), "cudaGetDevice");
+  check(cudaFree(nullptr), "context init");
   plan->module = compile_module(P.source, plan->device);
   plan->fn.assign(P.kernels.size(), nullptr);
   for (size_t k = 0; k < P.kernels.size(); ++k) {
@@ -567,9 +603,42 @@ void instantiate(tb_plan* plan) {
     if (K.name.empty()) continue;
     check(g_driver.ModuleGetFunction(&plan->fn[k], plan->module, K.name.c_str()), "cuModuleGetFunction");
   }
+  plan->main.reset(new tb_instance());
+  setup_instance(plan, plan->main.get());
 }
 
-void run_plan(tb_plan* plan) {
+// Copies the feeds into the instance's input buffers and launches its graph.
+void start_run(tb_instance* plan, tb_params* params, int32_t feed_count, const tb_feed* feeds) {
+  tb::Program& P = *plan->prog;
+  bind_params(plan, params);
+  for (int32_t f = 0; f < feed_count; ++f) {
+    const tb_feed& feed = feeds[f];
+    if (feed.slot < 0 || feed.slot >= P.input_slots)
+      throw Failure(TB_INVALID, "fed slot is not an input of the plan");
+    int b = P.input_buffer[feed.slot];
+    if (b < 0) continue;  // an input the plan does not read
+    const tb::Buffer& buf = P.buffers[b];
+    const void* src = buf.storage == tb::Storage::InputIndices ? (const void*)feed.indices
+                                                               : (const void*)feed.dense;
+    if (!src) throw Failure(TB_INVALID, "feed of the wrong payload kind");
+    check(cudaMemcpyAsync(plan->buffer_ptr[b], src, buf.bytes,
+                          feed.on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                          plan->stream),
+          "feed copy");
+  }
+  run_plan(plan);
+}
+
+void read_value(tb_instance* plan, int64_t node, float* host, int64_t count) {
+  int b = readable_buffer(*plan->prog, node);
+  if (count * 4 != plan->prog->buffers[b].bytes) throw Failure(TB_INVALID, "read size mismatch");
+  check(cudaMemcpyAsync(host, plan->buffer_ptr[b], count * 4, cudaMemcpyDeviceToHost,
+                        plan->stream),
+        "read");
+  check(cudaStreamSynchronize(plan->stream), "cudaStreamSynchronize");
+}
+
+void run_plan(tb_instance* plan) {
   if (plan->graph_dirty) {
     if (plan->graph) {
       cudaGraphExecDestroy(plan->graph);
@@ -628,14 +697,13 @@ int tb_plan_compile(const tb_plan_desc* desc, tb_plan** out) {
 
 void tb_plan_destroy(tb_plan* plan) {
   if (!plan) return;
-  if (plan->stream) cudaStreamSynchronize(plan->stream);
-  delete plan;
+  delete plan;  // each instance drains its stream before it frees its memory
 }
 
 int tb_plan_stats_get(const tb_plan* plan, tb_plan_stats* s) {
   return guarded([&]() {
     const tb::Program& P = *plan->prog;
-    s->kernels = plan->launches ? plan->launches : (int64_t)P.kernels.size();
+    s->kernels = plan->main->launches ? plan->main->launches : (int64_t)P.kernels.size();
     s->arena_bytes = P.arena_bytes;
     s->unplanned_bytes = P.unplanned_bytes;
     s->fused_nodes = P.fused_nodes;
@@ -702,24 +770,7 @@ int tb_params_download(const tb_params* params, int32_t slot, float* host, int64
 
 int tb_plan_run(tb_plan* plan, tb_params* params, int32_t feed_count, const tb_feed* feeds) {
   return guarded([&]() {
-    tb::Program& P = *plan->prog;
-    bind_params(plan, params);
-    for (int32_t f = 0; f < feed_count; ++f) {
-      const tb_feed& feed = feeds[f];
-      if (feed.slot < 0 || feed.slot >= P.input_slots)
-        throw Failure(TB_INVALID, "fed slot is not an input of the plan");
-      int b = P.input_buffer[feed.slot];
-      if (b < 0) continue;  // an input the plan does not read
-      const tb::Buffer& buf = P.buffers[b];
-      const void* src = buf.storage == tb::Storage::InputIndices ? (const void*)feed.indices
-                                                                 : (const void*)feed.dense;
-      if (!src) throw Failure(TB_INVALID, "feed of the wrong payload kind");
-      check(cudaMemcpyAsync(plan->buffer_ptr[b], src, buf.bytes,
-                            feed.on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
-                            plan->stream),
-            "feed copy");
-    }
-    run_plan(plan);
+    start_run(plan->main.get(), params, feed_count, feeds);
     return (int)TB_OK;
   });
 }
@@ -738,19 +789,14 @@ int tb_plan_gradient_node(const tb_plan* plan, int64_t root, int64_t parameter, 
 
 int tb_plan_synchronize(tb_plan* plan) {
   return guarded([&]() {
-    check(cudaStreamSynchronize(plan->stream), "cudaStreamSynchronize");
+    check(cudaStreamSynchronize(plan->main->stream), "cudaStreamSynchronize");
     return (int)TB_OK;
   });
 }
 
 int tb_plan_read(tb_plan* plan, int64_t node, float* host, int64_t count) {
   return guarded([&]() {
-    int b = readable_buffer(*plan->prog, node);
-    if (count * 4 != plan->prog->buffers[b].bytes) throw Failure(TB_INVALID, "read size mismatch");
-    check(cudaMemcpyAsync(host, plan->buffer_ptr[b], count * 4, cudaMemcpyDeviceToHost,
-                          plan->stream),
-          "read");
-    check(cudaStreamSynchronize(plan->stream), "cudaStreamSynchronize");
+    read_value(plan->main.get(), node, host, count);
     return (int)TB_OK;
   });
 }
@@ -758,17 +804,83 @@ int tb_plan_read(tb_plan* plan, int64_t node, float* host, int64_t count) {
 int tb_plan_device_pointer(tb_plan* plan, int64_t node, const float** device) {
   return guarded([&]() {
     int b = readable_buffer(*plan->prog, node);
-    *device = (const float*)plan->buffer_ptr[b];
+    *device = (const float*)plan->main->buffer_ptr[b];
     return (int)TB_OK;
   });
 }
 
-void* tb_plan_stream(tb_plan* plan) { return plan ? (void*)plan->stream : nullptr; }
+void* tb_plan_stream(tb_plan* plan) { return plan ? (void*)plan->main->stream : nullptr; }
 
-int tb_optimizer_create(tb_plan* plan, tb_params* params, const tb_optimizer_desc* desc,
+int tb_run_begin(tb_plan* plan, tb_params* params, int32_t feed_count, const tb_feed* feeds,
+                 tb_run** out) {
+  return guarded([&]() {
+    tb_instance* inst = nullptr;
+    {
+      std::lock_guard<std::mutex> lock(plan->pool_mutex);
+      if (!plan->idle.empty()) {
+        inst = plan->idle.back();
+        plan->idle.pop_back();
+      } else {
+        std::unique_ptr<tb_instance> fresh(new tb_instance());
+        setup_instance(plan, fresh.get());
+        inst = fresh.get();
+        plan->pool.push_back(std::move(fresh));
+      }
+    }
+    std::unique_ptr<tb_run> run(new tb_run());
+    run->plan = plan;
+    run->inst = inst;
+    try {
+      start_run(inst, params, feed_count, feeds);
+    } catch (...) {
+      std::lock_guard<std::mutex> lock(plan->pool_mutex);
+      plan->idle.push_back(inst);
+      throw;
+    }
+    *out = run.release();
+    return (int)TB_OK;
+  });
+}
+
+int tb_run_synchronize(tb_run* run) {
+  return guarded([&]() {
+    check(cudaStreamSynchronize(run->inst->stream), "cudaStreamSynchronize");
+    return (int)TB_OK;
+  });
+}
+
+int tb_run_read(tb_run* run, int64_t node, float* host, int64_t count) {
+  return guarded([&]() {
+    read_value(run->inst, node, host, count);
+    return (int)TB_OK;
+  });
+}
+
+int tb_run_device_pointer(tb_run* run, int64_t node, const float** device) {
+  return guarded([&]() {
+    int b = readable_buffer(*run->plan->prog, node);
+    *device = (const float*)run->inst->buffer_ptr[b];
+    return (int)TB_OK;
+  });
+}
+
+void* tb_run_stream(tb_run* run) { return run ? (void*)run->inst->stream : nullptr; }
+
+void tb_run_release(tb_run* run) {
+  if (!run) return;
+  {
+    // the next run on this instance is ordered after this one by its stream
+    std::lock_guard<std::mutex> lock(run->plan->pool_mutex);
+    run->plan->idle.push_back(run->inst);
+  }
+  delete run;
+}
+
+int tb_optimizer_create(tb_plan* owner, tb_params* params, const tb_optimizer_desc* desc,
                         int32_t count, const int32_t* slots, const int64_t* gradient_nodes,
                         tb_optimizer** out) {
   return guarded([&]() {
+    tb_instance* plan = owner->main.get();
     if (desc->kind < 0 || desc->kind > 2) throw Failure(TB_INVALID, "unknown optimizer kind");
     bind_params(plan, params);
     std::unique_ptr<tb_optimizer> o(new tb_optimizer());
@@ -838,8 +950,9 @@ int tb_optimizer_set_learning_rate(tb_optimizer* o, float lr) {
   });
 }
 
-int tb_plan_attach_optimizer(tb_plan* plan, tb_optimizer* o) {
+int tb_plan_attach_optimizer(tb_plan* owner, tb_optimizer* o) {
   return guarded([&]() {
+    tb_instance* plan = owner->main.get();
     if (o && o->plan != plan) throw Failure(TB_INVALID, "optimizer belongs to another plan");
     plan->optimizer = o;
     plan->graph_dirty = true;
@@ -892,8 +1005,9 @@ int tb_comm_init(int32_t rank, int32_t world, const uint8_t id[128], tb_comm** o
 
 void tb_comm_destroy(tb_comm* comm) { delete comm; }
 
-int tb_plan_attach_comm(tb_plan* plan, tb_comm* comm, int64_t bucket_bytes) {
+int tb_plan_attach_comm(tb_plan* owner, tb_comm* comm, int64_t bucket_bytes) {
   return guarded([&]() {
+    tb_instance* plan = owner->main.get();
     plan->comm = comm;
     plan->bucket_bytes = bucket_bytes > 0 ? bucket_bytes : (int64_t)32 << 20;
     plan->graph_dirty = true;
@@ -966,7 +1080,8 @@ int tbx_nvrtc_check(const tb_plan_desc* desc) {
 
 // Times each kernel of a bound plan on its own (after one warm launch):
 // ms[k] = average of `reps` launches.  Returns the kernel count.
-int64_t tbx_profile_kernels(tb_plan* plan, int reps, float* ms, int64_t capacity) {
+int64_t tbx_profile_kernels(tb_plan* owner, int reps, float* ms, int64_t capacity) {
+  tb_instance* plan = owner->main.get();
   int rc = guarded([&]() {
     if (!plan->bound) throw Failure(TB_INVALID, "run the plan once before profiling");
     tb::Program& P = *plan->prog;
