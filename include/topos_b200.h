@@ -215,6 +215,14 @@ void tb_comm_destroy(tb_comm* comm);
 /* Sum-allreduces the plan's gradient outputs bound by its optimizer, bucket by
  * bucket as the program finishes them, before the optimizer step. */
 int tb_plan_attach_comm(tb_plan* plan, tb_comm* comm, int64_t bucket_bytes);
+/* How the attached communicator sums gradients:
+ *  TB_REDUCTION_NCCL  ncclAllReduce (NCCL's own order; the default);
+ *  TB_REDUCTION_TREE  all-gather of the shard gradients, then the pairwise tree of `tree_sum`
+ *                     (examples/makemore/mlp_parallel.rs:59-71) over ranks in order, on every
+ *                     rank -- bit-identical to the reference's host sum of the same shard
+ *                     gradients, at the cost of N x the bucket bytes moved. */
+enum { TB_REDUCTION_NCCL = 0, TB_REDUCTION_TREE = 1 };
+int tb_plan_set_reduction(tb_plan* plan, int32_t reduction);
 int tb_comm_allreduce(tb_comm* comm, float* device, int64_t count, void* stream);
 
 /* ---- per-task faces (`Elementary::gemm` / `map`, payload/elementary.rs:74-95) */

@@ -271,9 +271,15 @@ class Comm:
         _check(lib.tb_comm_unique_id(buf), "tb_comm_unique_id")
         return bytes(buf)
 
-    def attach(self, plan: DevicePlan, bucket_bytes: int = 32 << 20):
+    def attach(self, plan: DevicePlan, bucket_bytes: int = 32 << 20, reduction: str = "nccl"):
+        """Sums the plan's optimizer-bound gradients across ranks before its
+        optimizer step: ``reduction="nccl"`` (ncclAllReduce) or ``"tree"``
+        (all-gather, then `tree_sum`'s pairwise order over ranks: bit-identical
+        to the reference's host sum of the same shard gradients)."""
         _check(self.lib.tb_plan_attach_comm(plan.handle, self.handle, bucket_bytes),
                "tb_plan_attach_comm")
+        code = {"nccl": 0, "tree": 1}[reduction]
+        _check(self.lib.tb_plan_set_reduction(plan.handle, code), "tb_plan_set_reduction")
 
     def __del__(self):
         if getattr(self, "handle", None):

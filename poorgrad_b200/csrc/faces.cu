@@ -154,6 +154,11 @@ extern "C" int tbx_gemm_prepared(const float* a_hi, const float* a_lo, const flo
 }
 extern "C" int tbx_gemm_error(void) { return tb::gemm_error(); }
 extern "C" int tbx_segment_error(void) { return tb::segment_error(); }
+extern "C" int tbx_tree_sum(const float* g, int shards, int64_t count, float* out) {
+  if (shards < 1 || shards > 64) return TB_INVALID;
+  tb::launch_tree_sum(g, shards, count, out, 0);
+  return cudaDeviceSynchronize() == cudaSuccess ? TB_OK : TB_RUNTIME;
+}
 extern "C" void tbx_set_gemm_tile_n(int tile) { tb::set_gemm_tile_n(tile); }
 extern "C" int tbx_gemm_splits(int64_t batch, int64_t m, int64_t n, int64_t kp) {
   return tb::gemm_splits(batch, m, n, kp);

@@ -607,6 +607,29 @@ void launch_segment_sum(const float* perm, const int* rstart, const int* rend, f
   launch_pdl(k_segment_sum, grid, 256, 0, stream, perm, rstart, rend, out, rows, width);
 }
 
+__global__ void k_tree_sum(const float* __restrict__ g, int shards, int64_t count,
+                           float* __restrict__ out) {
+  pdl_entry();
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float v[64];
+    for (int s = 0; s < shards; ++s) v[s] = g[(int64_t)s * count + i];
+    int n = shards;
+    while (n > 1) {
+      const int half = n / 2;
+      for (int j = 0; j < half; ++j) v[j] = __fadd_rn(v[2 * j], v[2 * j + 1]);
+      if (n & 1) v[half] = v[n - 1];
+      n = half + (n & 1);
+    }
+    out[i] = v[0];
+  }
+}
+
+void launch_tree_sum(const float* g, int shards, int64_t count, float* out, cudaStream_t stream) {
+  int grid = (int)std::max<int64_t>(1, std::min<int64_t>((count + 255) / 256, 148 * 8));
+  launch_pdl(k_tree_sum, grid, 256, 0, stream, g, shards, count, out);
+}
+
 int segment_error() {
   int v = 0;
   cudaMemcpyFromSymbol(&v, g_segment_error, sizeof(int));

@@ -85,6 +85,11 @@ struct OptEntry {
   int32_t pad;
 };
 
+// out[i] = the pairwise tree of `tree_sum` over shards[0..n) of element i, where
+// shard s is g[s * count + i]: adjacent pairs summed left + right, an odd last
+// shard carried up, until one remains (n <= 64).
+void launch_tree_sum(const float* g, int shards, int64_t count, float* out, cudaStream_t stream);
+
 // Per-step optimizer scalars: s[0]=beta1^t, s[1]=beta2^t, s[2]=1-beta1^t, s[3]=1-beta2^t.
 void launch_adam_scalars(float* s, float beta1, float beta2, cudaStream_t stream);
 // One multi-tensor step over all entries (kind: 0 SGD, 1 Adam, 2 AdamW).

@@ -184,6 +184,8 @@ struct Nccl {
   ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
   ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                             cudaStream_t) = nullptr;
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
   ncclResult_t (*GroupStart)() = nullptr;
   ncclResult_t (*GroupEnd)() = nullptr;
   const char* (*GetErrorString)(ncclResult_t) = nullptr;
@@ -205,6 +207,7 @@ Nccl* nccl() {
   n.CommDestroy = (decltype(n.CommDestroy))dlsym(n.handle, "ncclCommDestroy");
   n.CommAbort = (decltype(n.CommAbort))dlsym(n.handle, "ncclCommAbort");
   n.AllReduce = (decltype(n.AllReduce))dlsym(n.handle, "ncclAllReduce");
+  n.AllGather = (decltype(n.AllGather))dlsym(n.handle, "ncclAllGather");
   n.GroupStart = (decltype(n.GroupStart))dlsym(n.handle, "ncclGroupStart");
   n.GroupEnd = (decltype(n.GroupEnd))dlsym(n.handle, "ncclGroupEnd");
   n.GetErrorString = (decltype(n.GetErrorString))dlsym(n.handle, "ncclGetErrorString");
@@ -296,10 +299,14 @@ struct tb_instance {
   tb_optimizer* optimizer = nullptr;
   tb_comm* comm = nullptr;
   int64_t bucket_bytes = 0;
+  int reduction = TB_REDUCTION_NCCL;
+  float* gather = nullptr;             // [world][bucket] shard gradients (tree reduction)
+  int64_t gather_floats = 0;
   std::vector<cudaEvent_t> events;
   int64_t launches = 0;
   ~tb_instance() {
     if (stream) cudaStreamSynchronize(stream);
+    if (gather) cudaFree(gather);
     if (graph) cudaGraphExecDestroy(graph);
     for (auto e : events) cudaEventDestroy(e);
     if (arena) cudaFree(arena);
@@ -519,9 +526,19 @@ void enqueue_program(tb_instance* plan, cudaStream_t stream) {
       cudaEvent_t e = event();
       check(cudaEventRecord(e, stream), "cudaEventRecord");
       check(cudaStreamWaitEvent(plan->comm_stream, e, 0), "cudaStreamWaitEvent");
-      check_nccl(nccl()->AllReduce(b.begin, b.begin, b.bytes / 4, ncclFloat32, ncclSum,
-                                   plan->comm->comm, plan->comm_stream),
-                 "ncclAllReduce");
+      if (plan->reduction == TB_REDUCTION_TREE) {
+        // every rank gathers all shards' gradients and sums them in tree_sum's order
+        check_nccl(nccl()->AllGather(b.begin, plan->gather, b.bytes / 4, ncclFloat32,
+                                     plan->comm->comm, plan->comm_stream),
+                   "ncclAllGather");
+        tb::launch_tree_sum(plan->gather, plan->comm->world, b.bytes / 4, (float*)b.begin,
+                            plan->comm_stream);
+        launches += 1;
+      } else {
+        check_nccl(nccl()->AllReduce(b.begin, b.begin, b.bytes / 4, ncclFloat32, ncclSum,
+                                     plan->comm->comm, plan->comm_stream),
+                   "ncclAllReduce");
+      }
       comm_used = true;
     }
   }
@@ -639,6 +656,20 @@ void read_value(tb_instance* plan, int64_t node, float* host, int64_t count) {
 }
 
 void run_plan(tb_instance* plan) {
+  if (plan->graph_dirty && plan->comm && plan->reduction == TB_REDUCTION_TREE) {
+    // the gather buffer is allocated before capture (no allocation while capturing)
+    if (plan->comm->world > 64) throw Failure(TB_INVALID, "tree reduction supports at most 64 ranks");
+    int64_t most = 0;
+    for (const Bucket& b : gradient_buckets(plan)) most = std::max<int64_t>(most, b.bytes / 4);
+    const int64_t need = most * plan->comm->world;
+    if (need > plan->gather_floats) {
+      if (plan->gather) cudaFree(plan->gather);
+      plan->gather = nullptr;
+      plan->gather_floats = 0;
+      check(cudaMalloc((void**)&plan->gather, need * 4), "cudaMalloc(gather)");
+      plan->gather_floats = need;
+    }
+  }
   if (plan->graph_dirty) {
     if (plan->graph) {
       cudaGraphExecDestroy(plan->graph);
@@ -1011,6 +1042,20 @@ int tb_plan_attach_comm(tb_plan* owner, tb_comm* comm, int64_t bucket_bytes) {
     plan->comm = comm;
     plan->bucket_bytes = bucket_bytes > 0 ? bucket_bytes : (int64_t)32 << 20;
     plan->graph_dirty = true;
+    return (int)TB_OK;
+  });
+}
+
+int tb_plan_set_reduction(tb_plan* owner, int32_t reduction) {
+  return guarded([&]() {
+    if (reduction != TB_REDUCTION_NCCL && reduction != TB_REDUCTION_TREE)
+      throw Failure(TB_INVALID, "unknown reduction");
+    if (reduction == TB_REDUCTION_TREE && (!nccl() || !nccl()->AllGather))
+      throw Failure(TB_INITIALIZATION, "ncclAllGather is not loadable");
+    if (owner->main->comm && owner->main->comm->world > 64)
+      throw Failure(TB_INVALID, "tree reduction supports at most 64 ranks");
+    owner->main->reduction = reduction;
+    owner->main->graph_dirty = true;
     return (int)TB_OK;
   });
 }
