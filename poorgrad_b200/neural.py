@@ -102,9 +102,15 @@ class Linear:
 
 
 class LayerNorm:
-    def __init__(self, tape: Tape, features: int, epsilon: float = 1e-5):
-        self.scale = tape.parameter(Dense((features,), np.ones(features, np.float32)))
-        self.shift = tape.parameter(Dense((features,), np.zeros(features, np.float32)))
+    """`neural/layer_norm.rs:100-132`: per-sample mean and biased variance
+    along the features, ``(x - m) / sqrt(v + eps) * scale + shift``; scale
+    and shift default to ones and zeros."""
+
+    def __init__(self, tape: Tape, features: int, epsilon: float = 1e-5, scale=None, shift=None):
+        scale = np.ones(features, np.float32) if scale is None else np.asarray(scale, np.float32)
+        shift = np.zeros(features, np.float32) if shift is None else np.asarray(shift, np.float32)
+        self.scale = tape.parameter(Dense((features,), scale))
+        self.shift = tape.parameter(Dense((features,), shift))
         self.epsilon = tape.leaf(filled((), epsilon))
 
     def parameters(self) -> List[Value]:
@@ -118,6 +124,25 @@ class LayerNorm:
         deviation = (variance + self.epsilon.broadcast_like(variance)).sqrt()
         normalized = centered / deviation.broadcast_along(1, x)
         return normalized * self.scale.broadcast_along(0, x) + self.shift.broadcast_along(0, x)
+
+
+class RmsNorm:
+    """`neural/rms_norm.rs:89-114`: ``x / sqrt(mean(x^2) + eps) * scale`` per
+    sample, no centering; scale defaults to ones."""
+
+    def __init__(self, tape: Tape, features: int, epsilon: float = 1e-5, scale=None):
+        scale = np.ones(features, np.float32) if scale is None else np.asarray(scale, np.float32)
+        self.scale = tape.parameter(Dense((features,), scale))
+        self.epsilon = tape.leaf(filled((), epsilon))
+
+    def parameters(self) -> List[Value]:
+        return [self.scale]
+
+    def express(self, x: Value) -> Value:
+        assert len(x.shape) == 2
+        power = (x * x).mean_along(1)
+        root = (power + self.epsilon.broadcast_like(power)).sqrt()
+        return x / root.broadcast_along(1, x) * self.scale.broadcast_along(0, x)
 
 
 class Gelu:

@@ -188,6 +188,20 @@ def test_layer_norm_forward_and_gradients(device):
         np.testing.assert_allclose(dev[n.index], ref[n.index], rtol=2e-4, atol=2e-5)
 
 
+def test_rms_norm_forward_and_gradients(device):
+    # neural/rms_norm.rs:89-114 on a [48, 4100] input (a team of threads per row)
+    t = Tape()
+    x = t.parameter(tensor((48, 4100), rnd((48, 4100), 11, -3, 3)))
+    rms = neural.RmsNorm(t, 4100, scale=rnd((4100,), 12, 0.5, 1.5))
+    y = rms.express(x)
+    w = t.leaf(tensor((48, 4100), rnd((48, 4100), 13)))
+    loss = (y * w).sum()
+    grads = t.differentiate(loss, [x] + rms.parameters())
+    ref, dev, _ = both(t, [y] + grads)
+    for n in [y] + grads:
+        np.testing.assert_allclose(dev[n.index], ref[n.index], rtol=2e-4, atol=2e-5)
+
+
 # ------------------------------------------------------------ GEMM
 GRID = [(2, 3, 4), (5, 7, 3), (17, 33, 9), (64, 64, 64), (2, 64, 128), (129, 65, 257)]
 

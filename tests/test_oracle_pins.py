@@ -184,3 +184,44 @@ def test_plan_columns_release_like_the_reference(built):
     cols = net.compile(Request([c]))
     assert a.index in cols.releases[c.index]
     assert all(c.index not in r for r in cols.releases)
+
+
+def _norm_run(norm_cls, kw, rows, vals, grad_of_first=False):
+    t = Tape()
+    norm = norm_cls(t, 2, **kw)
+    x = t.leaf(tensor((rows, 2), vals)) if not grad_of_first else t.parameter(tensor((rows, 2), vals))
+    out = norm.express(x)
+    if not grad_of_first:
+        return run(t, [out])[out.index].reshape(-1).tolist()
+    target = out.narrow(1, 0, 1).sum()
+    grads = t.differentiate(target, [x] + norm.parameters())
+    res = run(t, grads)
+    return [res[g.index].reshape(-1).tolist() for g in grads]
+
+
+def test_layer_norm_standardizes_and_applies_the_affine(built):
+    # neural/tests/layer_norm_tests.rs:44-81
+    assert _norm_run(neural.LayerNorm, dict(epsilon=0.0), 2, [1, 3, 2, 6]) == [-1, 1, -1, 1]
+    assert _norm_run(neural.LayerNorm, dict(epsilon=0.0, scale=[2, 3], shift=[10, 20]), 2,
+                     [1, 3, 2, 6]) == [8, 23, 8, 23]
+
+
+def test_layer_norm_gradients_through_the_statistics(built):
+    # neural/tests/layer_norm_tests.rs:143-177: x = [3, 1], eps 3 -> d n0/dx = [3/16, -3/16];
+    # the scale sees the normalized value (0.5) and the shift the seed (1) on feature 0
+    gx, gscale, gshift = _norm_run(neural.LayerNorm, dict(epsilon=3.0), 1, [3, 1], True)
+    assert abs(gx[0] - 0.1875) < 1e-6 and abs(gx[1] + 0.1875) < 1e-6
+    assert gscale == [0.5, 0.0] and gshift == [1.0, 0.0]
+
+
+def test_rms_norm_normalizes_and_scales(built):
+    # neural/tests/rms_norm_tests.rs:41-73
+    assert _norm_run(neural.RmsNorm, dict(epsilon=0.0), 2, [2, 2, 3, -3]) == [1, 1, 1, -1]
+    assert _norm_run(neural.RmsNorm, dict(epsilon=0.0, scale=[2, 5]), 2,
+                     [2, 2, 3, -3]) == [2, 5, 2, -5]
+
+
+def test_rms_norm_gradients_through_the_root_mean_square(built):
+    # neural/tests/rms_norm_tests.rs:99-122: x = [2, 0], eps 2 -> [1/4, 0]; scale [1, 0]
+    gx, gscale = _norm_run(neural.RmsNorm, dict(epsilon=2.0), 1, [2, 0], True)
+    assert gx == [0.25, 0.0] and gscale == [1.0, 0.0]
