@@ -1,6 +1,6 @@
 """Benchmark of the compiled-plan training step on B200 (one process per GPU).
 
-``python bench.py --gpus N --steps K --warmup W [--config charmlp|gpt2|mlp|fused|gemm]
+``python bench.py --gpus N --steps K --warmup W [--config charmlp|gpt2|mlp|fused|gemm|gemm_skinny]
 [--impl reference]`` prints ONE JSON line on rank 0.
 
 A step is one run of the recorded-gradient training plan (loss and every
@@ -109,6 +109,8 @@ CONFIGS = {
               {"model": "fused-8192x8192"}),
     "gemm": (lambda: __import__("poorgrad_b200.configs").configs.gemm(),
              {"model": "gemm-4096^3-fwd+bwd"}),
+    "gemm_skinny": (lambda: __import__("poorgrad_b200.configs").configs.gemm(32768, 768, 3072),
+                    {"model": "gemm-32768x768x3072-fwd+bwd"}),
 }
 
 
@@ -126,13 +128,16 @@ def reference_arm(args, name):
     import oracle
     from poorgrad_b200 import configs
     cores = os.cpu_count() or 1
-    shard = {"charmlp": 64, "mlp": 128, "gpt2": None, "fused": None, "gemm": None}[name]
+    shard = {"charmlp": 64, "mlp": 128, "gpt2": None, "fused": None, "gemm": None,
+             "gemm_skinny": None}[name]
     if name == "gpt2":
         w = configs.gpt2(batch=1, seq=128)
         unit_scale = 1.0  # one short sequence per shard
         sample = "1 sequence of 128 tokens per core (full 12-layer GPT-2-small widths)"
-    elif name in ("fused", "gemm"):
-        w = configs.fused(rows=256, cols=8192) if name == "fused" else configs.gemm(256, 4096, 4096)
+    elif name in ("fused", "gemm", "gemm_skinny"):
+        w = {"fused": lambda: configs.fused(rows=256, cols=8192),
+             "gemm": lambda: configs.gemm(256, 4096, 4096),
+             "gemm_skinny": lambda: configs.gemm(256, 768, 3072)}[name]()
         sample = "256-row slice of the workload per core"
         unit_scale = 1.0
     else:
@@ -162,7 +167,7 @@ def reference_arm(args, name):
     elif name == "fused":
         value = cores * 256 / dt
         unit = "rows/s"
-    elif name == "gemm":
+    elif name in ("gemm", "gemm_skinny"):
         value = cores * 256 / dt
         unit = "rows/s"
     else:
