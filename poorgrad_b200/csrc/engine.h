@@ -75,12 +75,16 @@ struct Buffer {
   int64_t offset = 0;  // arena offset
 };
 
-enum class MemberType { EW, ROW_SUM, ROW_MAX, COL_SUM, ALL_SUM };
+// PREP: the member's value also written as the tf32 pair of a GEMM operand
+// (hi = rna_tf32(x), lo = x - hi) into `hi`/`lo`, in the value's own
+// row-major layout (its last axis a multiple of 32, so no padding).
+enum class MemberType { EW, ROW_SUM, ROW_MAX, COL_SUM, ALL_SUM, PREP };
 
 struct Member {
   int node;
   MemberType type;
   int phase = 0;
+  int hi = -1, lo = -1;  // PREP: operand buffers
 };
 
 enum class KType {

@@ -830,7 +830,7 @@ class Lowerer {
     Kernel k;
     bool reductions = false;
     for (auto& m : G.members)
-      if (m.type != MemberType::EW) reductions = true;
+      if (m.type != MemberType::EW && m.type != MemberType::PREP) reductions = true;
     k.type = reductions ? KType::ROW : KType::EW;
     k.members = G.members;
     k.space = G.space;
@@ -869,8 +869,16 @@ class Lowerer {
     KC = (chunks + T - 1) / T;
   }
 
-  void group_member(int n, MemberType type, const std::vector<int64_t>& space) {
-    auto r = refs(n);
+  // Places a member in the open group of `space` (or a new one) at the phase
+  // its reads allow.  A PREP member reads exactly its node's value (refs of
+  // the node itself, or the node when it is materialized) and is not
+  // registered as the node's producer; returns the group.
+  int group_member(int n, MemberType type, const std::vector<int64_t>& space, int hi = -1,
+                   int lo = -1) {
+    const bool prep = type == MemberType::PREP;
+    std::vector<std::pair<int, int>> r;
+    if (prep && P.info[n].materialized) r.push_back({n, ID});
+    else r = refs(n);
     // Members of open groups read in a way the group cannot serve are flushed.
     auto it = open_group.find(space);
     int g = it == open_group.end() ? -1 : it->second;
@@ -916,10 +924,13 @@ class Lowerer {
     }
     for (int og : before)
       if (groups[og].open && og != g) groups[g].after.insert(og);
-    Member m{n, type, phase};
-    groups[g].index[n] = (int)groups[g].members.size();
+    Member m{n, type, phase, hi, lo};
+    if (!prep) {
+      groups[g].index[n] = (int)groups[g].members.size();
+      group_of[n] = g;
+    }
     groups[g].members.push_back(m);
-    group_of[n] = g;
+    return g;
   }
 
   void own_kernel(int n, KType type) {
@@ -941,6 +952,18 @@ class Lowerer {
       if (source_layout(n) && !nd.readable) continue;
       switch (nd.op) {
         case TB_OP_MATMUL: {
+          // operands that open fusion groups compute get their tf32 pair from
+          // those groups, before the operands' groups are closed below
+          {
+            const Node& A = P.nodes[nd.operands[0]];
+            int64_t batch = 1;
+            for (int i = 0; i < A.rank - 2; ++i) batch *= A.shape[i];
+            for (int o = 0; o < 2; ++o) {
+              bool flip = false;
+              const int base = strip_transposes(nd.operands[o], flip);
+              if (!prepared.count(base) && fusable_prep(base)) prepare(base, batch);
+            }
+          }
           auto r = refs(n);
           flush_refs(r);
           matmul_kernels(n);
@@ -1030,6 +1053,19 @@ class Lowerer {
     }
   }
 
+  // Whether a value's prep can ride in the fusion group that computes it: an
+  // expression (virtual, or a member of a still open group of its own shape)
+  // whose last axis needs no padding.
+  bool fusable_prep(int base) const {
+    const Node& b = P.nodes[base];
+    const Info& f = P.info[base];
+    if (b.rank < 2 || b.shape[b.rank - 1] % 32 != 0 || f.kind != Kind::Expr) return false;
+    if (!f.materialized) return true;
+    const int g = group_of[base];
+    return g >= 0 && groups[g].open && groups[g].space == b.dims() &&
+           groups[g].members[groups[g].index.at(base)].type == MemberType::EW;
+  }
+
   Prepared prepare(int base, int64_t batch) {
     auto it = prepared.find(base);
     if (it != prepared.end()) return it->second;
@@ -1040,6 +1076,14 @@ class Lowerer {
     r.ld = (r.cols + 31) / 32 * 32;
     r.hi = new_buffer(Storage::Arena, batch * r.rows * r.ld * 4, -1);
     r.lo = new_buffer(Storage::Arena, batch * r.rows * r.ld * 4, -1);
+    if (fusable_prep(base)) {
+      // the group that computes the value also writes its tf32 pair; it is
+      // closed now, before the GEMM that reads the pair
+      const int g = group_member(base, MemberType::PREP, b.dims(), r.hi, r.lo);
+      flush(g);
+      prepared[base] = r;
+      return r;
+    }
     Kernel k;
     k.type = KType::PREP;
     k.node = base;
@@ -1122,7 +1166,8 @@ class Emitter {
 
   Emitter(Program& p, Kernel& k, int id) : P(p), K(k), kid(id) {
     memo.emplace_back();
-    for (size_t i = 0; i < K.members.size(); ++i) member_of[K.members[i].node] = (int)i;
+    for (size_t i = 0; i < K.members.size(); ++i)
+      if (K.members[i].type != MemberType::PREP) member_of[K.members[i].node] = (int)i;
   }
 
   std::string pad() const { return std::string(indent, ' '); }
@@ -1444,6 +1489,27 @@ const int SMS = 148;
 }  // namespace
 
 // ---- flat elementwise group
+// Stores a PREP member's values (one or four consecutive elements at `off`)
+// as their tf32 pairs.
+static void emit_prep_store(Emitter& E, const Member& mm, const std::string& off,
+                            const std::vector<std::string>& x) {
+  const std::string hi = E.fptr(mm.hi), lo = E.fptr(mm.lo);
+  E.line("{");
+  E.indent += 2;
+  for (size_t v = 0; v < x.size(); ++v)
+    E.line("const float h" + std::to_string(v) + " = tb_tf32(" + x[v] + ");");
+  if (x.size() == 4) {
+    E.line("*(float4*)(" + hi + " + " + off + ") = make_float4(h0, h1, h2, h3);");
+    E.line("*(float4*)(" + lo + " + " + off + ") = make_float4(__fsub_rn(" + x[0] + ", h0), __fsub_rn(" +
+           x[1] + ", h1), __fsub_rn(" + x[2] + ", h2), __fsub_rn(" + x[3] + ", h3));");
+  } else {
+    E.line(hi + "[" + off + "] = h0;");
+    E.line(lo + "[" + off + "] = __fsub_rn(" + x[0] + ", h0);");
+  }
+  E.indent -= 2;
+  E.line("}");
+}
+
 static void emit_ew(Program& P, Kernel& K, Emitter& E) {
   const std::vector<int64_t>& S = K.space;
   int64_t total = volume_of(S);
@@ -1467,12 +1533,20 @@ static void emit_ew(Program& P, Kernel& K, Emitter& E) {
     }
     for (size_t m = 0; m < K.members.size(); ++m) {
       int n = K.members[m].node;
+      if (K.members[m].type == MemberType::PREP) {
+        vals[m].push_back(E.ref(n, idx));
+        continue;
+      }
       std::string x = E.def(n, idx);
       E.memo.back()[Emitter::key(n, idx)] = x;
       vals[m].push_back(x);
     }
   }
   for (size_t m = 0; m < K.members.size(); ++m) {
+    if (K.members[m].type == MemberType::PREP) {
+      emit_prep_store(E, K.members[m], "lin", vals[m]);
+      continue;
+    }
     int buf = P.info[K.members[m].node].buf;
     if (E.vec == 4) {
       E.line("*(float4*)(" + E.fptr(buf) + " + lin) = make_float4(" + vals[m][0] + ", " +
@@ -1595,6 +1669,8 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
         if (mm.type == MemberType::EW) {
           x = E.def(n, idx);
           E.memo.back()[Emitter::key(n, idx)] = x;
+        } else if (mm.type == MemberType::PREP) {
+          x = E.ref(n, idx);
         } else {
           x = E.ref(P.nodes[n].operands[0], idx);
         }
@@ -1617,6 +1693,11 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
           default: break;
         }
       }
+    }
+    for (size_t m = 0; m < K.members.size(); ++m) {
+      const Member& mm = K.members[m];
+      if (mm.phase != ph || mm.type != MemberType::PREP) continue;
+      emit_prep_store(E, mm, "row * " + lit(L) + " + j0", vals[m]);
     }
     for (size_t m = 0; m < K.members.size(); ++m) {
       const Member& mm = K.members[m];
@@ -2311,8 +2392,13 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
     for (int b : K.params) {
       const Buffer& bf = P.buffers[b];
       bool written = false;
-      for (auto& m : K.members)
+      for (auto& m : K.members) {
+        if (m.type == MemberType::PREP) {
+          if (b == m.hi || b == m.lo) written = true;
+          continue;
+        }
         if (P.info[m.node].buf == b && P.info[m.node].owner == m.node) written = true;
+      }
       if (b == K.a_hi || b == K.a_lo) written = true;
       if (bf.storage == Storage::Arena && bf.node < 0 &&
           (K.type == KType::ROW || K.type == KType::SCATTER))
@@ -2329,7 +2415,9 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
       d << "]";
     }
     d << " members=";
-    for (auto& m : K.members) d << m.node << (m.phase ? "p" + std::to_string(m.phase) : "") << " ";
+    for (auto& m : K.members)
+      d << m.node << (m.type == MemberType::PREP ? "prep" : "")
+        << (m.phase ? "p" + std::to_string(m.phase) : "") << " ";
     d << (K.exact ? "exact" : "tolerance");
     if (K.type == KType::PREP)
       d << " value=" << K.node << " [" << K.batch << "," << K.m << "," << K.kp << "]";
