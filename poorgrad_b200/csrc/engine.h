@@ -122,6 +122,10 @@ struct Kernel {
   int64_t count = 0, rows = 0, passes = 0, tiles = 0;
   int partial = -1, final_out = -1;  // FINAL
   int64_t final_blocks = 0, final_width = 0;
+  // FINAL of several outputs in one launch (same partial-row count): per entry
+  // its partials, output and width
+  std::vector<int> final_parts, final_outs;
+  std::vector<int64_t> final_widths;
   std::vector<int> reads, writes;    // buffer ids touched (liveness)
   bool side = false;                 // runs on the side stream from the program's start
   std::string describe;

@@ -144,14 +144,13 @@ __global__ void k_segments(const int* __restrict__ keys, int* __restrict__ rstar
 // warp whole 128-byte rows; CB = 8 (narrow outputs) spreads the partial rows
 // over 32 groups and 4x the blocks, 32-byte sectors per group.
 template <int CB>
-__global__ void __launch_bounds__(256) k_final_sum(const float* __restrict__ part,
-                                                   float* __restrict__ out, int64_t blocks,
-                                                   int64_t width) {
-  pdl_entry();
+__device__ __forceinline__ void final_sum_body(const float* __restrict__ part,
+                                               float* __restrict__ out, int64_t blocks,
+                                               int64_t width, int64_t block) {
   constexpr int G = 256 / CB;
   __shared__ float acc_s[G][CB];
   const int col = threadIdx.x % CB, grp = threadIdx.x / CB;
-  const int64_t j = (int64_t)blockIdx.x * CB + col;
+  const int64_t j = block * CB + col;
   float acc = 0.0f;
   bool any = false;
   if (j < width) {
@@ -179,6 +178,28 @@ __global__ void __launch_bounds__(256) k_final_sum(const float* __restrict__ par
     for (int w = 1; w < G && w < blocks; ++w) t = __fadd_rn(t, acc_s[w][col]);
     out[j] = t;
   }
+}
+
+// CB columns per block: thread t takes column t % CB and every G-th partial row
+// starting at t / CB (G = 256 / CB groups); the G group sums are then combined
+// in group order (a fixed, deterministic association).  CB = 32 gives each
+// warp whole 128-byte rows; CB = 8 (narrow outputs) spreads the partial rows
+// over 32 groups and 4x the blocks, 32-byte sectors per group.
+template <int CB>
+__global__ void __launch_bounds__(256) k_final_sum(const float* __restrict__ part,
+                                                   float* __restrict__ out, int64_t blocks,
+                                                   int64_t width) {
+  pdl_entry();
+  final_sum_body<CB>(part, out, blocks, width, blockIdx.x);
+}
+
+// Several narrow finals of one row kernel in one launch: block ranges
+// [start[e], start[e + 1]) serve entry e.
+__global__ void __launch_bounds__(256) k_final_sum_multi(const FinalSet set, int64_t blocks) {
+  pdl_entry();
+  int e = 0;
+  while (e + 1 < set.count && (int)blockIdx.x >= set.start[e + 1]) ++e;
+  final_sum_body<8>(set.part[e], set.out[e], blocks, set.width[e], blockIdx.x - set.start[e]);
 }
 
 // One thread per output; the segment's rows are contiguous, loaded 64 at a
@@ -634,6 +655,10 @@ int segment_error() {
   int v = 0;
   cudaMemcpyFromSymbol(&v, g_segment_error, sizeof(int));
   return v;
+}
+
+void launch_final_sum_multi(const FinalSet& set, int64_t blocks, cudaStream_t stream) {
+  launch_pdl(k_final_sum_multi, (unsigned)set.start[set.count], 256, 0, stream, set, blocks);
 }
 
 void launch_final_sum(const float* part, float* out, int64_t blocks, int64_t width,

@@ -16,6 +16,18 @@ void launch_selection_sort(const int* indices, int* keys, int* vals, int* tmp_ke
 void launch_final_sum(const float* part, float* out, int64_t blocks, int64_t width,
                       cudaStream_t stream);
 
+// Up to kFinalSetMax narrow column finals sharing a partial-row count, one
+// launch: entry e owns blocks [start[e], start[e + 1]), 8 columns each.
+constexpr int kFinalSetMax = 8;
+struct FinalSet {
+  const float* part[kFinalSetMax];
+  float* out[kFinalSetMax];
+  int64_t width[kFinalSetMax];
+  int start[kFinalSetMax + 1];
+  int count;
+};
+void launch_final_sum_multi(const FinalSet& set, int64_t blocks, cudaStream_t stream);
+
 // out[r, c] = 0 + perm[rstart[r], c] + ... + perm[rend[r]-1, c] (ascending rows);
 // `count` (the number of source rows) selects the variant for long segments.
 void launch_segment_sum(const float* perm, const int* rstart, const int* rend, float* out,

@@ -2434,6 +2434,24 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
         P.kernels.push_back(f);
         continue;
       }
+      // narrow finals of this row kernel share one launch (8-column blocks)
+      Kernel* prev = P.kernels.empty() ? nullptr : &P.kernels.back();
+      const bool narrow = (f.final_width + 31) / 32 < SMS;
+      if (narrow && prev && prev->type == KType::FINAL && !prev->final_parts.empty() &&
+          prev->final_blocks == f.final_blocks && prev->final_parts.size() < 8) {
+        prev->final_parts.push_back(f.partial);
+        prev->final_outs.push_back(f.final_out);
+        prev->final_widths.push_back(f.final_width);
+        prev->reads.push_back(f.partial);
+        prev->writes.push_back(f.final_out);
+        prev->describe += "," + std::to_string(f.final_width);
+        continue;
+      }
+      if (narrow) {
+        f.final_parts = {f.partial};
+        f.final_outs = {f.final_out};
+        f.final_widths = {f.final_width};
+      }
       f.describe = "final partials=" + std::to_string(f.final_blocks) + "x" +
                    std::to_string(f.final_width);
       P.kernels.push_back(f);

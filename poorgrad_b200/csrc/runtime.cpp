@@ -455,8 +455,21 @@ int64_t launch_kernel(tb_instance* plan, size_t k, cudaStream_t stream) {
       launches += 1;
       break;
     case tb::KType::FINAL:
-      tb::launch_final_sum(fp(plan, K.partial), fp(plan, K.final_out), K.final_blocks,
-                           K.final_width, stream);
+      if (!K.final_parts.empty()) {
+        tb::FinalSet set{};
+        set.count = (int)K.final_parts.size();
+        set.start[0] = 0;
+        for (int e = 0; e < set.count; ++e) {
+          set.part[e] = fp(plan, K.final_parts[e]);
+          set.out[e] = fp(plan, K.final_outs[e]);
+          set.width[e] = K.final_widths[e];
+          set.start[e + 1] = set.start[e] + (int)((K.final_widths[e] + 7) / 8);
+        }
+        tb::launch_final_sum_multi(set, K.final_blocks, stream);
+      } else {
+        tb::launch_final_sum(fp(plan, K.partial), fp(plan, K.final_out), K.final_blocks,
+                             K.final_width, stream);
+      }
       launches += 1;
       break;
     default: {
