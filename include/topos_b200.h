@@ -204,6 +204,13 @@ void tb_optimizer_destroy(tb_optimizer* optimizer);
 int tb_optimizer_set_learning_rate(tb_optimizer* optimizer, float learning_rate);
 /* Runs the step inside every later `tb_plan_run` of its plan (one graph launch per step). */
 int tb_plan_attach_optimizer(tb_plan* plan, tb_optimizer* optimizer);
+/* Replaces: `Parameters::step(&gradients, &mut optimizer)` (graph/parameters.rs:90-146) called by
+ * the caller: one update of the bound parameters now, on `stream` (a cudaStream_t; NULL = the
+ * plan's).  `gradients` NULL steps with the bound gradient values of the plan's last
+ * `tb_plan_run`; otherwise it holds one device pointer per bound slot, in binding order (for
+ * example gradients summed over several `tb_run_begin` runs).  Updates the same moments and
+ * beta powers as the in-graph step. */
+int tb_optimizer_step(tb_optimizer* optimizer, const float* const* gradients, void* stream);
 /* Downloads Adam moments of a slot (first, second); count elements each. */
 int tb_optimizer_state(const tb_optimizer* optimizer, int32_t slot, float* first, float* second, int64_t count);
 

@@ -199,6 +199,7 @@ def load_library() -> C.CDLL:
         "tb_run_stream": (P, [P]),
         "tb_run_release": (None, [P]),
         "tb_plan_set_reduction": (C.c_int, [P, C.c_int32]),
+        "tb_optimizer_step": (C.c_int, [P, C.POINTER(C.c_void_p), P]),
         "tb_optimizer_create": (C.c_int, [P, P, C.POINTER(TbOptimizerDesc), C.c_int32,
                                           C.POINTER(C.c_int32), C.POINTER(C.c_int64),
                                           C.POINTER(P)]),

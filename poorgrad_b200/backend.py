@@ -237,6 +237,16 @@ class Optimizer:
                    "tb_plan_attach_optimizer")
         self.params = params
 
+    def step(self, gradients=None, stream: int = 0):
+        """`Parameters::step(&gradients, &mut optimizer)` now: with the plan's
+        last gradients (``None``) or with one device pointer per bound slot."""
+        arr = None
+        if gradients is not None:
+            ptrs = [int(g) for g in gradients]
+            arr = (C.c_void_p * len(ptrs))(*ptrs)
+        _check(self.lib.tb_optimizer_step(self.handle, arr, C.c_void_p(stream) if stream else None),
+               "tb_optimizer_step")
+
     def set_learning_rate(self, lr: float):
         _check(self.lib.tb_optimizer_set_learning_rate(self.handle, lr), "set_learning_rate")
 

@@ -267,12 +267,14 @@ struct tb_optimizer {
   std::vector<int> grad_buffers;       // plan buffer ids
   std::vector<tb::OptEntry> host_entries;
   tb::OptEntry* entries = nullptr;     // device table
+  tb::OptEntry* custom = nullptr;      // device table for caller-given gradients
   float* state = nullptr;              // moments (Adam): first then second per slot
   float* scalars = nullptr;            // beta powers and corrections, learning rate
   int64_t total = 0;
   std::vector<int64_t> state_offset;   // per entry
   ~tb_optimizer() {
     if (entries) cudaFree(entries);
+    if (custom) cudaFree(custom);
     if (state) cudaFree(state);
     if (scalars) cudaFree(scalars);
   }
@@ -990,6 +992,36 @@ int tb_optimizer_set_learning_rate(tb_optimizer* o, float lr) {
                           o->plan->stream),
           "upload learning rate");
     check(cudaStreamSynchronize(o->plan->stream), "sync");
+    return (int)TB_OK;
+  });
+}
+
+int tb_optimizer_step(tb_optimizer* o, const float* const* gradients, void* stream) {
+  return guarded([&]() {
+    cudaStream_t st = stream ? (cudaStream_t)stream : o->plan->stream;
+    const tb::OptEntry* table = o->entries;
+    if (gradients && !o->host_entries.empty()) {
+      if (!o->custom)
+        check(cudaMalloc((void**)&o->custom, o->host_entries.size() * sizeof(tb::OptEntry)),
+              "cudaMalloc(entries)");
+      std::vector<tb::OptEntry> e = o->host_entries;
+      for (size_t i = 0; i < e.size(); ++i) {
+        if (!gradients[i]) throw Failure(TB_INVALID, "missing gradient pointer");
+        e[i].g = gradients[i];
+      }
+      // synchronous: the table is tiny and must not outlive this call's host copy
+      check(cudaStreamSynchronize(st), "sync");
+      check(cudaMemcpy(o->custom, e.data(), e.size() * sizeof(tb::OptEntry),
+                       cudaMemcpyHostToDevice),
+            "upload entries");
+      table = o->custom;
+    }
+    if (o->desc.kind != TB_OPTIMIZER_SGD) tb::launch_adam_scalars(o->scalars, o->desc.beta1, o->desc.beta2, st);
+    tb::launch_optimizer(table, (int)o->host_entries.size(), o->total, o->scalars, o->scalars + 4,
+                         o->desc.kind, o->desc.beta1, o->desc.beta2, 1.0f - o->desc.beta1,
+                         1.0f - o->desc.beta2, o->desc.epsilon, o->desc.decay,
+                         o->desc.gradient_scale, st);
+    check(cudaGetLastError(), "optimizer launch");
     return (int)TB_OK;
   });
 }

@@ -350,3 +350,30 @@ def test_map_face_matches_libm(device, op, lo):
         np.testing.assert_allclose(out, ref, rtol=4e-7, atol=1e-30)
     small = np.ones(16, np.float32)
     assert lib.tb_map_f32(op, fptr(small), 16, fptr(small)) == 5  # declined below 2^17
+
+
+def test_standalone_optimizer_step_matches_the_reference_rule(device):
+    # Parameters::step(&gradients, &mut optimizer) called by the caller
+    # (graph/parameters.rs:90-146): once with the plan's own gradients, once
+    # with caller-given device gradients (twice the plan's)
+    import torch
+    w = configs.mlp(batch=128)
+    feeds = w.feeds(0)
+    params = w.network.parameters()
+    plan = backend.DevicePlan(w.columns)
+    dp = backend.DeviceParameters(plan, params)
+    opt = backend.Optimizer(plan, dp, backend.SGD, zip(w.params, w.grads), 0.1, attach=False)
+    plan.forward(dp, feeds, sync=True)
+    grads = [plan.of(g) for g in w.grads]
+    opt.step()
+    torch.cuda.synchronize()
+    slots = [w.columns.nodes[p.index].slot for p in w.params]
+    stepped = neural.sgd_reference([p.reshape(g.shape) for p, g in zip(params, grads)], grads, 0.1)
+    for s, e in zip(slots, stepped):
+        assert_exact(dp.download(s).reshape(e.shape), e)
+    doubled = [torch.from_numpy(g * np.float32(2)).cuda() for g in grads]
+    opt.step([d.data_ptr() for d in doubled])
+    torch.cuda.synchronize()
+    again = neural.sgd_reference(stepped, [g * np.float32(2) for g in grads], 0.1)
+    for s, e in zip(slots, again):
+        assert_exact(dp.download(s).reshape(e.shape), e)
