@@ -145,6 +145,41 @@ class RmsNorm:
         return x / root.broadcast_along(1, x) * self.scale.broadcast_along(0, x)
 
 
+def conv2d(x: Value, weights: Value, bias: Value, stride: int = 1, padding: int = 0) -> Value:
+    """`neural/convolution.rs:53-131`: zero padding (`pad`), two single-axis
+    unfolds into windows ``[batch, channels, out_h, kernel_h, out_w, kernel_w]``,
+    the im2col matrix (window-major rows over ``[channels, kernel]``), one GEMM
+    against the ``[columns, filters]`` weights, the bias along rows, back to
+    ``[batch, filters, out_h, out_w]``."""
+    batch, channels, height, width = x.shape
+    filters, _, kh, kw = weights.shape
+    padded = x
+    if padding > 0:
+        padded = padded.pad(2, padding, height + 2 * padding)
+        padded = padded.pad(3, padding, width + 2 * padding)
+    windows = padded.unfold(2, kh, stride, 1).unfold(4, kw, stride, 1)
+    out_h, out_w = windows.shape[2], windows.shape[4]
+    patches = windows.permute([0, 2, 4, 1, 3, 5]).reshape(
+        (batch * out_h * out_w, channels * kh * kw))
+    kernel = weights.permute([1, 2, 3, 0]).reshape((channels * kh * kw, filters))
+    product = patches.matmul(kernel)
+    shifted = product + bias.broadcast_along(0, product)
+    return shifted.reshape((batch, out_h, out_w, filters)).permute([0, 3, 1, 2])
+
+
+def max_pool(x: Value, size: int, stride: int) -> Value:
+    """`neural/pooling.rs:16-61`: the window lanes (two unfolds, then
+    ``[batch, channels, out_h, out_w, size*size]``) folded left with
+    `maximum` in row-major window order (ties route to the earliest lane)."""
+    windows = x.unfold(2, size, stride, 1).unfold(4, size, stride, 1)
+    a = windows.shape
+    lanes = windows.permute([0, 1, 2, 4, 3, 5]).reshape((a[0], a[1], a[2], a[4], size * size))
+    largest = lanes.narrow(4, 0, 1)
+    for lane in range(1, size * size):
+        largest = largest.maximum(lanes.narrow(4, lane, 1))
+    return largest.squeeze(4)
+
+
 class Gelu:
     """``0.5 x (1 + tanh(0.7978846 (x + 0.044715 x^3)))`` with scalar leaves."""
 

@@ -377,3 +377,24 @@ def test_standalone_optimizer_step_matches_the_reference_rule(device):
     again = neural.sgd_reference(stepped, [g * np.float32(2) for g in grads], 0.1)
     for s, e in zip(slots, again):
         assert_exact(dp.download(s).reshape(e.shape), e)
+
+
+def test_conv_pool_network_forward_and_gradients(device):
+    # the mnist/cifar-style stack of the reference's examples: conv2d
+    # (neural/convolution.rs:53-131: pad, unfolds, im2col GEMM), relu,
+    # max_pool (neural/pooling.rs:49-61), linear head, cross-entropy
+    t = Tape()
+    rng = np.random.default_rng(21)
+    x = t.input(tensor((8, 3, 16, 16), rng.uniform(-1, 1, (8, 3, 16, 16)).astype(np.float32)))
+    y = t.input(selection(rng.integers(0, 10, 8), 10))
+    w = t.parameter(tensor((8, 3, 3, 3), rng.uniform(-0.3, 0.3, (8, 3, 3, 3)).astype(np.float32)))
+    b = t.parameter(tensor((8,), np.zeros(8, np.float32)))
+    head = neural.Linear(t, rng.uniform(-0.1, 0.1, (8 * 8 * 8, 10)).astype(np.float32),
+                         np.zeros(10, np.float32))
+    h = neural.max_pool(neural.conv2d(x, w, b, 1, 1).relu(), 2, 2).reshape((8, 8 * 8 * 8))
+    loss = neural.cross_entropy(head.express(h), y)
+    grads = t.differentiate(loss, [w, b] + head.parameters())
+    ref, dev, _ = both(t, [loss] + grads)
+    for n in [loss] + grads:
+        scale = np.abs(ref[n.index]).max() + 1e-30
+        np.testing.assert_allclose(dev[n.index], ref[n.index], rtol=1e-3, atol=1e-4 * scale)

@@ -225,3 +225,50 @@ def test_rms_norm_gradients_through_the_root_mean_square(built):
     # neural/tests/rms_norm_tests.rs:99-122: x = [2, 0], eps 2 -> [1/4, 0]; scale [1, 0]
     gx, gscale = _norm_run(neural.RmsNorm, dict(epsilon=2.0), 1, [2, 0], True)
     assert gx == [0.25, 0.0] and gscale == [1.0, 0.0]
+
+
+def _conv(ishape, ivals, wshape, wvals, bvals, stride, padding):
+    t = Tape()
+    x = t.leaf(tensor(ishape, ivals))
+    w = t.leaf(tensor(wshape, wvals))
+    b = t.leaf(tensor((wshape[0],), bvals))
+    out = neural.conv2d(x, w, b, stride, padding)
+    return out.shape, run(t, [out])[out.index].reshape(-1).tolist()
+
+
+def test_conv2d_known_answers(built):
+    # neural/tests/convolution_tests.rs:6-81
+    assert _conv((1, 1, 3, 3), list(range(1, 10)), (1, 1, 2, 2), [1, 0, 0, 1], [10], 1, 0) == \
+        ((1, 1, 2, 2), [16, 18, 22, 24])
+    assert _conv((1, 2, 2, 2), [1, 2, 3, 4, 10, 20, 30, 40], (2, 2, 1, 1), [1, 1, 2, 3], [0, 0],
+                 1, 0) == ((1, 2, 2, 2), [11, 22, 33, 44, 32, 64, 96, 128])
+    assert _conv((1, 1, 1, 5), [1, 2, 3, 4, 5], (1, 1, 1, 2), [1, 1], [0], 2, 0) == \
+        ((1, 1, 1, 2), [3, 7])
+    assert _conv((1, 1, 2, 2), [1, 2, 3, 4], (1, 1, 3, 3), [1] * 9, [0], 1, 1) == \
+        ((1, 1, 2, 2), [10, 10, 10, 10])
+
+
+def test_conv2d_gradients_known_answers(built):
+    # neural/tests/convolution_tests.rs:84-114: window coverage counts, summed inputs, seeds
+    t = Tape()
+    x = t.parameter(tensor((1, 1, 3, 3), list(range(1, 10))))
+    w = t.parameter(tensor((1, 1, 2, 2), [1, 1, 1, 1]))
+    b = t.parameter(tensor((1,), [0]))
+    loss = neural.conv2d(x, w, b, 1, 0).sum()
+    gx, gw, gb = t.differentiate(loss, [x, w, b])
+    out = run(t, [gx, gw, gb])
+    assert out[gx.index].reshape(-1).tolist() == [1, 2, 1, 2, 4, 2, 1, 2, 1]
+    assert out[gw.index].reshape(-1).tolist() == [12, 16, 24, 28]
+    assert out[gb.index].reshape(-1).tolist() == [4]
+
+
+def test_max_pool_takes_window_maxima_and_routes_ties_left(built):
+    # neural/pooling.rs:49-61: a left fold of maximum over the window lanes
+    t = Tape()
+    x = t.parameter(tensor((1, 1, 2, 4), [1, 5, 2, 2, 3, 4, 2, 2]))
+    pooled = neural.max_pool(x, 2, 2)
+    (g,) = t.differentiate(pooled.sum(), [x])
+    out = run(t, [pooled, g])
+    assert out[pooled.index].reshape(-1).tolist() == [5, 2]
+    # the second window's four 2s tie: the gradient goes to its first lane only
+    assert out[g.index].reshape(-1).tolist() == [0, 1, 1, 0, 0, 0, 0, 0]
