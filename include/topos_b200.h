@@ -243,6 +243,15 @@ int tb_gemm_f32(const float* a, int64_t a_len, const int64_t a_strides[2],
 /* Replaces: `MapTask` offers (payload/elementary.rs:89-95): op is TB_OP_EXP,
  * TB_OP_LN, TB_OP_SQRT or TB_OP_TANH; host buffers. */
 int tb_map_f32(int32_t op, const float* in, int64_t count, float* out);
+/* Replaces: `Elementary::batch_norm` offers (payload/elementary.rs:107-113, `BatchNormTask`,
+ * payload/normalized.rs:18-98): training-mode batch normalization of the row-major
+ * [batch, features] input over the batch axis, with the operation order of the recorded
+ * formula (payload/tensorial.rs:240-258) -- bit-identical to it.  Writes the output and the
+ * per-feature mean and biased variance (`Normalized`); host buffers.  TB_DECLINED below
+ * 2^17 elements. */
+int tb_batch_norm_f32(const float* input, const float* scale, const float* shift, float epsilon,
+                      int64_t batch, int64_t features, float* output, float* mean,
+                      float* variance);
 
 /* ---- allocation-free GEMM (no counterpart in the reference: topos's cuda backend always
  *      allocates device buffers from its pool for each product).

@@ -200,6 +200,8 @@ def load_library() -> C.CDLL:
         "tb_run_release": (None, [P]),
         "tb_plan_set_reduction": (C.c_int, [P, C.c_int32]),
         "tb_optimizer_step": (C.c_int, [P, C.POINTER(C.c_void_p), P]),
+        "tb_batch_norm_f32": (C.c_int, [C.POINTER(C.c_float)] * 3 + [C.c_float, C.c_int64, C.c_int64]
+                              + [C.POINTER(C.c_float)] * 3),
         "tb_optimizer_create": (C.c_int, [P, P, C.POINTER(TbOptimizerDesc), C.c_int32,
                                           C.POINTER(C.c_int32), C.POINTER(C.c_int64),
                                           C.POINTER(P)]),

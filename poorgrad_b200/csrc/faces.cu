@@ -54,6 +54,35 @@ __global__ void k_map(int op, const float* __restrict__ in, float* __restrict__ 
   }
 }
 
+// One thread per feature: the statistics fold down the batch in row order,
+// seeded with the first row, exactly as the recorded formula's sum_along(0).
+__global__ void k_batch_norm(const float* __restrict__ x, const float* __restrict__ scale,
+                             const float* __restrict__ shift, float epsilon, int64_t batch,
+                             int64_t features, float* __restrict__ out, float* __restrict__ mean,
+                             float* __restrict__ variance) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= features) return;
+  const float count = (float)batch;
+  float s = x[j];
+  for (int64_t b = 1; b < batch; ++b) s = __fadd_rn(s, x[b * features + j]);
+  const float m = __fdiv_rn(s, count);
+  float c = __fsub_rn(x[j], m);
+  float q = __fmul_rn(c, c);
+  for (int64_t b = 1; b < batch; ++b) {
+    c = __fsub_rn(x[b * features + j], m);
+    q = __fadd_rn(q, __fmul_rn(c, c));
+  }
+  const float v = __fdiv_rn(q, count);
+  const float dev = __fsqrt_rn(__fadd_rn(v, epsilon));
+  const float g = scale[j], h = shift[j];
+  for (int64_t b = 0; b < batch; ++b) {
+    const float n = __fdiv_rn(__fsub_rn(x[b * features + j], m), dev);
+    out[b * features + j] = __fadd_rn(__fmul_rn(n, g), h);
+  }
+  mean[j] = m;
+  variance[j] = v;
+}
+
 int64_t span_of(int64_t rows, int64_t cols, const int64_t s[2]) {
   return (rows - 1) * s[0] + (cols - 1) * s[1] + 1;
 }
@@ -114,6 +143,32 @@ extern "C" int tb_map_f32(int32_t op, const float* in, int64_t count, float* out
   cudaMemcpy(d, in, count * 4, cudaMemcpyHostToDevice);
   k_map<<<148 * 8, 256>>>(op, d, d + count, count);
   cudaMemcpy(out, d + count, count * 4, cudaMemcpyDeviceToHost);
+  cudaError_t e = cudaGetLastError();
+  cudaFree(d);
+  return e == cudaSuccess ? TB_OK : TB_RUNTIME;
+}
+
+extern "C" int tb_batch_norm_f32(const float* input, const float* scale, const float* shift,
+                                 float epsilon, int64_t batch, int64_t features, float* output,
+                                 float* mean, float* variance) {
+  char msg[8];
+  int s = tb_status(msg, sizeof msg);
+  if (s != TB_OK) return s;
+  if (batch < 1 || features < 1) return TB_INVALID;
+  if (batch * features < (1 << 17)) return TB_DECLINED;
+  const int64_t n = batch * features;
+  float* d = nullptr;
+  if (cudaMalloc(&d, (2 * n + 4 * features) * 4) != cudaSuccess) return TB_RUNTIME;
+  float *dx = d, *dout = d + n, *dscale = d + 2 * n, *dshift = dscale + features,
+        *dmean = dshift + features, *dvar = dmean + features;
+  cudaMemcpy(dx, input, n * 4, cudaMemcpyHostToDevice);
+  cudaMemcpy(dscale, scale, features * 4, cudaMemcpyHostToDevice);
+  cudaMemcpy(dshift, shift, features * 4, cudaMemcpyHostToDevice);
+  k_batch_norm<<<(unsigned)((features + 127) / 128), 128>>>(dx, dscale, dshift, epsilon, batch,
+                                                            features, dout, dmean, dvar);
+  cudaMemcpy(output, dout, n * 4, cudaMemcpyDeviceToHost);
+  cudaMemcpy(mean, dmean, features * 4, cudaMemcpyDeviceToHost);
+  cudaMemcpy(variance, dvar, features * 4, cudaMemcpyDeviceToHost);
   cudaError_t e = cudaGetLastError();
   cudaFree(d);
   return e == cudaSuccess ? TB_OK : TB_RUNTIME;

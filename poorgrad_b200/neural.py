@@ -180,6 +180,32 @@ def max_pool(x: Value, size: int, stride: int) -> Value:
     return largest.squeeze(4)
 
 
+class BatchNorm:
+    """`neural/batch_norm.rs:104-160` (training mode): per-feature mean and
+    biased variance over the batch axis, ``(x - m) / sqrt(v + eps) * scale +
+    shift``; `express` returns (output, mean, variance)."""
+
+    def __init__(self, tape: Tape, features: int, epsilon: float = 1e-5, scale=None, shift=None):
+        scale = np.ones(features, np.float32) if scale is None else np.asarray(scale, np.float32)
+        shift = np.zeros(features, np.float32) if shift is None else np.asarray(shift, np.float32)
+        self.scale = tape.parameter(Dense((features,), scale))
+        self.shift = tape.parameter(Dense((features,), shift))
+        self.epsilon = tape.leaf(filled((), epsilon))
+
+    def parameters(self) -> List[Value]:
+        return [self.scale, self.shift]
+
+    def express(self, x: Value):
+        mean = x.mean_along(0)
+        centered = x - mean.broadcast_along(0, x)
+        variance = (centered * centered).mean_along(0)
+        deviation = (variance + self.epsilon.broadcast_like(variance)).sqrt()
+        normalized = centered / deviation.broadcast_along(0, centered)
+        out = normalized * self.scale.broadcast_along(0, centered) + \
+            self.shift.broadcast_along(0, centered)
+        return out, mean, variance
+
+
 class Gelu:
     """``0.5 x (1 + tanh(0.7978846 (x + 0.044715 x^3)))`` with scalar leaves."""
 

@@ -398,3 +398,32 @@ def test_conv_pool_network_forward_and_gradients(device):
     for n in [loss] + grads:
         scale = np.abs(ref[n.index]).max() + 1e-30
         np.testing.assert_allclose(dev[n.index], ref[n.index], rtol=1e-3, atol=1e-4 * scale)
+
+
+def test_batch_norm_face_is_bitwise_the_recorded_formula(device):
+    # the `Elementary::batch_norm` face against the recorded formula
+    # (payload/tensorial.rs:240-258) run by the oracle
+    from poorgrad_b200.abi import fptr, load_library
+    lib = load_library()
+    batch, features = 512, 300
+    rng = np.random.default_rng(31)
+    x = rng.normal(0.5, 2.0, (batch, features)).astype(np.float32)
+    scale = rng.uniform(0.5, 1.5, features).astype(np.float32)
+    shift = rng.uniform(-1, 1, features).astype(np.float32)
+    t = Tape()
+    xv = t.leaf(tensor(x.shape, x))
+    bn = neural.BatchNorm(t, features, 1e-5, scale, shift)
+    out, mean, var = bn.express(xv)
+    net = t.into_network()
+    ref = oracle.run(net.compile(Request([out, mean, var])), net.parameters())
+    o = np.empty_like(x)
+    m = np.empty(features, np.float32)
+    v = np.empty(features, np.float32)
+    assert lib.tb_batch_norm_f32(fptr(x), fptr(scale), fptr(shift), np.float32(1e-5), batch,
+                                 features, fptr(o), fptr(m), fptr(v)) == 0
+    assert_exact(m, ref[mean.index].reshape(-1))
+    assert_exact(v, ref[var.index].reshape(-1))
+    assert_exact(o, ref[out.index].reshape(x.shape))
+    small = np.zeros((4, 4), np.float32)  # below the size threshold: declined (TB_DECLINED)
+    assert lib.tb_batch_norm_f32(fptr(small), fptr(scale), fptr(shift), np.float32(1e-5), 4, 4,
+                                 fptr(small), fptr(m), fptr(v)) == 5
