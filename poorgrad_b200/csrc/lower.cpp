@@ -1447,14 +1447,18 @@ __device__ __forceinline__ float tb_max(float a, float b) {
   if (isnan(b)) return a;
   return (b > a) ? b : a;
 }
-// Online log-sum-exp state (m = running max, s = sum of exp(x - m)).
+// Online log-sum-exp state (m = running max, s = sum of exp(x - m)).  Branch
+// free, so a row loop's loads are not held behind a divergent branch: one
+// e = exp(-|x - m|) serves both cases -- a new maximum rescales the sum by
+// exp(m - x) and adds 1, otherwise exp(x - m) is added (nothing for -inf);
+// s * 1 is exact, so the result equals the branching form bit for bit.
 __device__ __forceinline__ void tb_lse_push(float& m, float& s, float x) {
-  if (x > m) {
-    s = s * expf(m - x) + 1.0f;
-    m = x;
-  } else if (x != -TB_INF) {
-    s = s + expf(x - m);
-  }
+  const bool up = x > m;
+  const float e = expf(-fabsf(x - m));
+  const float scale = up ? e : 1.0f;
+  const float add = up ? 1.0f : (x != -TB_INF ? e : 0.0f);
+  s = s * scale + add;
+  m = up ? x : m;
 }
 __device__ __forceinline__ void tb_lse_merge(float& m, float& s, float m2, float s2) {
   if (s2 == 0.0f && m2 == -TB_INF) return;
@@ -1517,10 +1521,12 @@ static void emit_ew(Program& P, Kernel& K, Emitter& E) {
   int64_t units = total / E.vec;
   K.block = 256;
   K.grid = std::max<int64_t>(1, std::min<int64_t>((units + 255) / 256, SMS * 8));
-  E.line("for (I t = (I)blockIdx.x * 256 + threadIdx.x; t < " + lit(units) +
-         "; t += (I)gridDim.x * 256) {");
+  // one unit of work: the element(s) at lin = t * vec, in its own scope
+  auto emit_unit = [&](const std::string& t) {
+  E.line("{");
   E.indent += 2;
-  E.line("const I lin = t * " + std::to_string(E.vec) + ";");
+  E.push();
+  E.line("const I lin = " + t + " * " + std::to_string(E.vec) + ";");
   std::vector<std::string> base = E.unravel("lin", S, "i");
   std::vector<std::vector<std::string>> vals(K.members.size());
   for (int v = 0; v < E.vec; ++v) {
@@ -1555,6 +1561,25 @@ static void emit_ew(Program& P, Kernel& K, Emitter& E) {
       E.line(E.fptr(buf) + "[lin] = " + vals[m][0] + ";");
     }
   }
+  E.pop();
+  E.indent -= 2;
+  E.line("}");
+  };
+  E.line("const I stride = (I)gridDim.x * 256;");
+  E.line("I t = (I)blockIdx.x * 256 + threadIdx.x;");
+  // (the unrolled trip's index t + 3 * stride must not overflow a 32-bit I)
+  if (E.vec == 1 && units >= 4 * K.grid * 256 && units + 4 * K.grid * 256 < (int64_t(1) << 31)) {
+    // scalar elements: four strides per trip with no bounds test between
+    // them, so each thread has four loads of each operand in flight
+    E.line("for (; t + 3 * stride < " + lit(units) + "; t += 4 * stride) {");
+    E.indent += 2;
+    for (int u = 0; u < 4; ++u) emit_unit(u == 0 ? "t" : "(t + " + std::to_string(u) + " * stride)");
+    E.indent -= 2;
+    E.line("}");
+  }
+  E.line("for (; t < " + lit(units) + "; t += stride) {");
+  E.indent += 2;
+  emit_unit("t");
   E.indent -= 2;
   E.line("}");
 }
@@ -1643,13 +1668,11 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
         E.line("float ra" + std::to_string(m) + " = " +
                (partner[m] >= 0 ? "-TB_INF;" : "__int_as_float(0x7fc00000);"));
     }
-    bool unroll = has_col;
-    E.line(unroll ? "#pragma unroll" : (vec == 1 ? "#pragma unroll 8" : "#pragma unroll 4"));
-    E.line("for (int kc = 0; kc < " + std::to_string(KC) + "; ++kc) {");
-    E.indent += 2;
-    E.line("const I j0 = ((I)kc * " + std::to_string(T) + " + tl) * " + std::to_string(vec) + ";");
-    E.line("if (act && j0 < " + lit(L) + ") {");
-    E.indent += 2;
+    // Full passes over the row need no bounds test, so the unrolled loads of
+    // several passes are issued before their results are used; only a last
+    // partial pass (row length not a multiple of the team's stride) is guarded.
+    const int64_t kc_full = L / (T * vec);
+    auto emit_pass = [&]() {
     E.push();
     std::vector<std::vector<std::string>> vals(K.members.size());
     for (int v = 0; v < vec; ++v) {
@@ -1711,10 +1734,33 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
       }
     }
     E.pop();
-    E.indent -= 2;
-    E.line("}");
-    E.indent -= 2;
-    E.line("}");
+    };
+    if (kc_full > 0) {
+      E.line("if (act) {");
+      E.indent += 2;
+      E.line(has_col ? "#pragma unroll" : (vec == 1 ? "#pragma unroll 8" : "#pragma unroll 4"));
+      E.line("for (int kc = 0; kc < " + std::to_string(kc_full) + "; ++kc) {");
+      E.indent += 2;
+      E.line("const I j0 = ((I)kc * " + std::to_string(T) + " + tl) * " + std::to_string(vec) + ";");
+      emit_pass();
+      E.indent -= 2;
+      E.line("}");
+      E.indent -= 2;
+      E.line("}");
+    }
+    if (kc_full < KC) {
+      E.line("{");
+      E.indent += 2;
+      E.line("const int kc = " + std::to_string(kc_full) + ";");
+      E.line("const I j0 = ((I)kc * " + std::to_string(T) + " + tl) * " + std::to_string(vec) + ";");
+      E.line("if (act && j0 < " + lit(L) + ") {");
+      E.indent += 2;
+      emit_pass();
+      E.indent -= 2;
+      E.line("}");
+      E.indent -= 2;
+      E.line("}");
+    }
     // team reductions of this phase
     for (size_t m = 0; m < K.members.size(); ++m) {
       const Member& mm = K.members[m];
