@@ -10,6 +10,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <functional>
 #include <sstream>
 #include <stdexcept>
 #include <unordered_map>
@@ -1493,6 +1494,120 @@ const int SMS = 148;
 }  // namespace
 
 // ---- flat elementwise group
+// Evaluates once, before a kernel's element loop, every rank-0 value its
+// members read that does not depend on the element: constants, scalars other
+// kernels wrote, and expressions of those (a loss scale, a 1 / count).  The
+// loop body then finds them in the outer memo scope instead of recomputing
+// them per element.
+static void hoist_uniform_scalars(Program& P, Kernel& K, Emitter& E) {
+  std::map<int, bool> uniform;
+  std::function<bool(int)> is_uniform = [&](int n) -> bool {
+    auto it = uniform.find(n);
+    if (it != uniform.end()) return it->second;
+    const Node& nd = P.nodes[n];
+    const Info& f = P.info[n];
+    bool u = false;
+    if (nd.rank == 0 && !E.member_of.count(n)) {
+      if (f.kind == Kind::Const) u = true;
+      else if (f.materialized && f.owner == n) u = true;  // read from its buffer
+      else if (f.kind == Kind::Expr && !f.materialized && is_elementwise(nd.op)) {
+        u = true;
+        for (int o : {nd.operands[0], nd.operands[1]})
+          if (o >= 0 && !is_uniform(o)) u = false;
+      }
+    }
+    uniform[n] = u;
+    return u;
+  };
+  std::set<int> seen;
+  std::vector<int> order;
+  std::function<void(int)> visit = [&](int n) {
+    if (!seen.insert(n).second) return;
+    const Info& f = P.info[n];
+    if (is_uniform(n)) {
+      if (f.kind != Kind::Const) order.push_back(n);
+      return;
+    }
+    // a value read from a buffer (other than this kernel's members) ends the walk
+    if ((f.materialized || f.kind == Kind::Layout) && !E.member_of.count(n)) return;
+    const Node& nd = P.nodes[n];
+    for (int o : {nd.operands[0], nd.operands[1]})
+      if (o >= 0) visit(o);
+  };
+  for (auto& m : K.members) {
+    const Node& nd = P.nodes[m.node];
+    if (m.type == MemberType::EW || m.type == MemberType::PREP) {
+      if (m.type == MemberType::PREP && !E.member_of.count(m.node) && P.info[m.node].materialized)
+        continue;
+      for (int o : {nd.operands[0], nd.operands[1]})
+        if (o >= 0) visit(o);
+    } else if (nd.operands[0] >= 0) {
+      visit(nd.operands[0]);
+    }
+  }
+  for (int n : order) E.ref(n, Idx{});
+}
+
+// In a row kernel, evaluates once per row (before the passes over its
+// elements) every row-shaped value the members read that depends only on
+// buffers other kernels wrote and constants -- per-row statistics such as
+// sqrt(variance + eps) -- so the passes find it in the row's memo scope.
+// Only when every team row is in range (R a multiple of the rows per block):
+// the hoisted loads are not behind the `act` guard.
+static void hoist_row_uniform(Program& P, Kernel& K, Emitter& E,
+                              const std::vector<int64_t>& lead,
+                              const std::vector<std::string>& rc) {
+  std::map<int, bool> memo;
+  std::function<bool(int)> row_uniform = [&](int n) -> bool {
+    auto it = memo.find(n);
+    if (it != memo.end()) return it->second;
+    const Node& nd = P.nodes[n];
+    const Info& f = P.info[n];
+    bool u = false;
+    if (!E.member_of.count(n)) {
+      if (f.kind == Kind::Const) u = true;
+      else if (nd.rank == 0 && f.materialized && f.owner == n) u = true;
+      else if (nd.dims() == lead && f.materialized && f.owner == n) u = true;
+      else if ((nd.rank == 0 || nd.dims() == lead) && f.kind == Kind::Expr && !f.materialized &&
+               is_elementwise(nd.op)) {
+        u = true;
+        for (int o : {nd.operands[0], nd.operands[1]})
+          if (o >= 0 && !row_uniform(o)) u = false;
+      }
+    }
+    memo[n] = u;
+    return u;
+  };
+  std::set<int> seen;
+  std::vector<int> order;
+  std::function<void(int)> visit = [&](int n) {
+    if (!seen.insert(n).second) return;
+    const Node& nd = P.nodes[n];
+    const Info& f = P.info[n];
+    if (nd.dims() == lead && !lead.empty() && row_uniform(n)) {
+      if (f.kind != Kind::Const) order.push_back(n);
+      return;
+    }
+    if ((f.materialized || f.kind == Kind::Layout) && !E.member_of.count(n)) return;
+    for (int o : {nd.operands[0], nd.operands[1]})
+      if (o >= 0) visit(o);
+  };
+  for (auto& m : K.members) {
+    const Node& nd = P.nodes[m.node];
+    if (m.type == MemberType::EW || m.type == MemberType::PREP) {
+      if (m.type == MemberType::PREP && !E.member_of.count(m.node) && P.info[m.node].materialized)
+        continue;
+      for (int o : {nd.operands[0], nd.operands[1]})
+        if (o >= 0) visit(o);
+    } else if (nd.operands[0] >= 0) {
+      visit(nd.operands[0]);
+    }
+  }
+  Idx idx;
+  idx.c = rc;
+  for (int n : order) E.ref(n, idx);
+}
+
 // Stores a PREP member's values (one or four consecutive elements at `off`)
 // as their tf32 pairs.
 static void emit_prep_store(Emitter& E, const Member& mm, const std::string& off,
@@ -1565,6 +1680,7 @@ static void emit_ew(Program& P, Kernel& K, Emitter& E) {
   E.indent -= 2;
   E.line("}");
   };
+  hoist_uniform_scalars(P, K, E);
   E.line("const I stride = (I)gridDim.x * 256;");
   E.line("I t = (I)blockIdx.x * 256 + threadIdx.x;");
   // (the unrolled trip's index t + 3 * stride must not overflow a 32-bit I)
@@ -1649,6 +1765,7 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
       E.line("float ca" + std::to_string(m) + "[" + std::to_string(KC * vec) + "] = {0};");
     if (K.members[m].type == MemberType::ALL_SUM) E.line("float fa" + std::to_string(m) + " = 0.0f;");
   }
+  hoist_uniform_scalars(P, K, E);
   E.line("for (I base = (I)blockIdx.x * " + std::to_string(teams) + "; base < " + lit(R) +
          "; base += (I)gridDim.x * " + std::to_string(teams) + ") {");
   E.indent += 2;
@@ -1657,6 +1774,7 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
   std::vector<int64_t> lead(S.begin(), S.end() - 1);
   std::vector<std::string> rc = lead.empty() ? std::vector<std::string>{}
                                              : E.unravel("row", lead, "i");
+  if (R % teams == 0) hoist_row_uniform(P, K, E, lead, rc);
   for (int ph = 0; ph <= maxphase; ++ph) {
     E.phase = ph;
     E.line("// phase " + std::to_string(ph));
