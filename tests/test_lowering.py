@@ -1,0 +1,63 @@
+"""Lowering decisions, checked on the host (no GPU): how the charmlp (C4)
+training plan is split into kernels, which GEMM operands are read K-major or
+MN-major, which operand preps ride inside the fusion group that computes the
+value, and how column finals share launches.  These are the structure the
+bench numbers depend on; the GPU tests check the values."""
+import ctypes as C
+import re
+
+import pytest
+
+from poorgrad_b200 import backend, configs
+
+
+@pytest.fixture(scope="module")
+def charmlp_lines(built):
+    w = configs.char_mlp()
+    return [l for l in backend.lower_describe(w.columns).splitlines() if re.match(r"\d+: ", l)]
+
+
+def test_weight_gradients_read_the_forward_preps_transposed(charmlp_lines):
+    gemms = [l for l in charmlp_lines if "gemm3xtf32" in l]
+    assert len(gemms) == 9
+    # dW = h^T . dY (m=n=512, k=batch): both operands are the activations'
+    # own row-major preps, read MN-major -- no transposing prep exists
+    dw = [l for l in gemms if "m=512 n=512 k=16384" in l]
+    assert len(dw) == 2 and all("a=mn b=mn" in l for l in dw)
+    # every prepared value is prepared once (9 GEMMs, fewer than 18 preps)
+    preps = [l for l in charmlp_lines if ": prep " in l]
+    fused = [l for l in charmlp_lines if "prep" in l and (": row " in l or ": ew " in l)]
+    assert len(preps) + len(fused) < 18
+
+
+def test_activation_preps_ride_in_their_producing_row_kernels(charmlp_lines):
+    # the LayerNorm forward (tanh output) and backward (dX) row kernels write
+    # the tf32 pair of the GEMM operand they compute
+    rows = [l for l in charmlp_lines if ": row " in l and "space=[16384,512]" in l]
+    assert sum("prep" in l for l in rows) == 4
+    standalone = [l for l in charmlp_lines if ": prep " in l and "[1,16384,512]" in l]
+    assert not standalone
+
+
+def test_narrow_column_finals_share_a_launch(charmlp_lines):
+    finals = [l for l in charmlp_lines if ": final " in l]
+    assert any(l.count(",") >= 2 for l in finals)  # three 512-wide finals in one launch
+    assert len(finals) <= 6
+
+
+def test_the_selection_sort_leads_the_program(charmlp_lines):
+    assert " sort selection" in charmlp_lines[0]
+
+
+def test_gemm_tile_and_split_rules(built):
+    from poorgrad_b200.abi import load_library
+    lib = load_library()
+    lib.tbx_gemm_splits.restype = C.c_int
+    lib.tbx_gemm_splits.argtypes = [C.c_int64] * 4
+    # split-K fills one wave of 148 SMs at most: 512x512 outputs in 256-wide
+    # tiles are 8 tiles -> 18 splits (144 work items)
+    assert lib.tbx_gemm_splits(1, 512, 512, 16384) == 18
+    # long-M products need no split
+    assert lib.tbx_gemm_splits(1, 16384, 512, 512) == 1
+    # narrow outputs take the 128-wide tile: 4 tiles -> 37 splits
+    assert lib.tbx_gemm_splits(1, 512, 27, 16384) == 37
