@@ -91,7 +91,7 @@ enum class KType {
   EW,         // flat elementwise group
   ROW,        // row-space group with reductions
   REDUCE,     // generic serial reduction (thread per output)
-  PREP,       // GEMM operand split into tf32 hi/lo, K-major
+  PREP,       // a GEMM operand value split into tf32 hi/lo, in its own row-major layout
   GEMM,       // 3xTF32 GEMM over prepared operands
   SORT,       // stable index sort of a selection (scatter)
   SCATTER,    // serial-order scatter-add

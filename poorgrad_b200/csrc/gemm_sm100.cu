@@ -12,11 +12,12 @@
 //   warp 1      MMA issuer: one elected thread issues tcgen05.mma kind::tf32
 //               (M=128, N=BN, K=8), three products per k-step, and commits each
 //               stage back to the producer;
-//   warps 2..9  epilogue (two warpgroups, one per column half): every CHUNK
-//               k-blocks the tensor-memory partial is read (tcgen05.ld, each
-//               warp its TMEM lane quarter) and added in IEEE f32 to register
-//               accumulators, then row-major f32 stores; warp 2 owns the TMEM
-//               allocation.
+//   warps 2..   epilogue (one warpgroup per 128 columns of the tile): every
+//               CHUNK k-blocks the tensor-memory partial is read (tcgen05.ld,
+//               each warp its TMEM lane quarter) and added in IEEE f32 to
+//               register accumulators; the finished tile goes out through a
+//               per-warp 32 x 33 staging tile, one 128-byte row segment per
+//               store instruction; warp 2 owns the TMEM allocation.
 // The tensor cores accumulate with truncating adders, so an accumulation chain
 // of k terms drifts like k ulps; draining the accumulator every CHUNK k-blocks
 // (two TMEM buffers, the MMA warp filling one while the epilogue drains the
@@ -26,6 +27,8 @@
 // No TMA multicast is used anywhere (operands may live on any GPU's arena).
 // Every mbarrier wait is bounded by the global timer: on expiry the kernel
 // records an error code, stops issuing work and releases its TMEM.
+// Launched with programmatic stream serialization: the kernel waits for its
+// predecessors (griddepcontrol.wait) before touching global memory.
 #include <cuda.h>
 #include <cuda_runtime.h>
 

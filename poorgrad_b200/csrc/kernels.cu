@@ -1,7 +1,9 @@
 // kernels.cu -- hand-written kernels that are not emitted per plan:
-// the stable selection sort behind deterministic scatter-add, the partial-sum
-// finalizer of fused column/full reductions, the SIMT GEMM path and the
-// multi-tensor optimizer steps.
+// the stable selection sort and the segment sums behind deterministic
+// scatter-add (a TMA-fed folding warp for long segments), the partial-sum
+// finalizers of fused column/full reductions, the SIMT GEMM path, the
+// pairwise tree sum of the deterministic gradient reduction and the
+// multi-tensor optimizer steps.  Every kernel begins with pdl_entry().
 #include <cstdio>
 #include <cstdlib>
 
