@@ -286,7 +286,14 @@ class Lowerer {
       n.op = s.op;
       n.rank = s.rank;
       if (s.rank < 0 || s.rank > TB_MAX_RANK) fail("node rank out of range");
-      for (int k = 0; k < s.rank; ++k) n.shape[k] = s.shape[k];
+      if (s.op < 0 || s.op >= TB_OP_COUNT) fail("unknown opcode " + std::to_string(s.op));
+      for (int k = 0; k < s.rank; ++k) {
+        // the reference has no empty values (payload/tensor.rs rejects them)
+        if (s.shape[k] < 1) fail("node " + std::to_string(i) + " has an empty extent");
+        n.shape[k] = s.shape[k];
+      }
+      if ((s.op == TB_OP_PARAMETER || s.op == TB_OP_INPUT) && s.slot < 0)
+        fail("node " + std::to_string(i) + " has no slot");
       for (int k = 0; k < TB_MAX_RANK; ++k) n.attrs[k] = s.attrs[k];
       n.operands[0] = s.operands[0];
       n.operands[1] = s.operands[1];

@@ -56,3 +56,25 @@ def test_missing_library_fails_loudly(monkeypatch):
     monkeypatch.setattr(abi, "library_path", lambda: "/nonexistent/libtopos_b200.so")
     with pytest.raises(RuntimeError, match="not built"):
         abi.load_library()
+
+
+@pytest.mark.parametrize("field,value,message", [
+    ("shape", 0, b"empty extent"), ("op", 999, b"unknown opcode"), ("slot", -1, b"no slot")])
+def test_invalid_descriptor_fields_are_rejected(built, field, value, message):
+    # the reference has no empty values, no unknown functions and no unslotted
+    # parameters: a descriptor with one answers TB_INVALID and poisons nothing
+    lib = abi.load_library()
+    lib.tbx_lower_describe.restype = C.c_int64
+    t = Tape()
+    x = t.parameter(tensor([2], [1.0, 2.0]))
+    y = x.exp()
+    packed = abi.PackedPlan(t.into_network().compile(Request([y])))
+    node = packed.array[0]  # the parameter
+    if field == "shape":
+        node.shape[0] = value
+    else:
+        setattr(node, field, value)
+    assert lib.tbx_lower_describe(C.byref(packed.desc), None, 0, 0) == -1
+    assert message in lib.tb_last_error()
+    code, _ = backend.status()
+    assert code in (0, 2)
