@@ -427,3 +427,20 @@ def test_batch_norm_face_is_bitwise_the_recorded_formula(device):
     small = np.zeros((4, 4), np.float32)  # below the size threshold: declined (TB_DECLINED)
     assert lib.tb_batch_norm_f32(fptr(small), fptr(scale), fptr(shift), np.float32(1e-5), 4, 4,
                                  fptr(small), fptr(m), fptr(v)) == 5
+
+
+@pytest.mark.parametrize("row,cls", [([1000.0, -1000.0], 0), ([-3.0e38, 3.0e38], 1),
+                                     ([3.0e38, -3.0e38], 0)])
+def test_cross_entropy_edge_rows(device, row, cls):
+    # neural/tests/loss_tests.rs:21-133 on the device, one row per plan as
+    # there: a confidently correct or extreme finite row costs exactly 0 and
+    # its gradient stays finite (in f32 two such rows in one batch would
+    # overflow the loss's own sums, in the interpreter as well)
+    t = Tape()
+    logits = t.parameter(tensor((1, 2), row))
+    loss = neural.cross_entropy(logits, t.input(selection([cls], 2)))
+    (g,) = t.differentiate(loss, [logits])
+    ref, dev, _ = both(t, [loss, g])
+    assert dev[loss.index] == 0.0 and ref[loss.index] == 0.0
+    assert np.all(np.isfinite(dev[g.index]))
+    np.testing.assert_allclose(dev[g.index], ref[g.index], rtol=1e-6, atol=1e-7)

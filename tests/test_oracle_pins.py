@@ -272,3 +272,40 @@ def test_max_pool_takes_window_maxima_and_routes_ties_left(built):
     assert out[pooled.index].reshape(-1).tolist() == [5, 2]
     # the second window's four 2s tie: the gradient goes to its first lane only
     assert out[g.index].reshape(-1).tolist() == [0, 1, 1, 0, 0, 0, 0, 0]
+
+
+def test_linear_records_the_affine_alone(built):
+    # neural/tests/linear_tests.rs:41-56: [1, 1] x [[1, 2], [3, 4]] + [10, 20]
+    t = Tape()
+    lin = neural.Linear(t, np.array([[1, 2], [3, 4]], np.float32), np.array([10, 20], np.float32))
+    out = lin.express(t.leaf(tensor((1, 2), [1, 1])))
+    assert run(t, [out])[out.index].reshape(-1).tolist() == [14, 26]
+
+
+def test_confident_correct_logits_cost_nothing(built):
+    # neural/tests/loss_tests.rs:21-36
+    t = Tape()
+    loss = neural.cross_entropy(t.leaf(tensor((1, 2), [1000.0, -1000.0])),
+                                t.input(selection([0], 2)))
+    assert run(t, [loss])[loss.index] == 0.0
+
+
+def test_extreme_f32_logits_keep_loss_zero_and_gradients_finite(built):
+    # neural/tests/loss_tests.rs:100-133 (the f32 range): either class order
+    for row, cls in (([-3.0e38, 3.0e38], 1), ([3.0e38, -3.0e38], 0)):
+        t = Tape()
+        logits = t.parameter(tensor((1, 2), row))
+        loss = neural.cross_entropy(logits, t.input(selection([cls], 2)))
+        (g,) = t.differentiate(loss, [logits])
+        out = run(t, [loss, g])
+        assert out[loss.index] == 0.0
+        assert np.all(np.isfinite(out[g.index]))
+
+
+def test_zero_target_lanes_contribute_exact_zero(built):
+    # neural/tests/loss_tests.rs:136-148: a dense soft target's zero lane
+    # against an underflowing log-probability adds 0, never 0 * -inf
+    t = Tape()
+    loss = neural.cross_entropy(t.leaf(tensor((1, 2), [-3.0e38, 3.0e38])),
+                                t.input(tensor((1, 2), [0.0, 1.0])))
+    assert run(t, [loss])[loss.index] == 0.0
