@@ -5,7 +5,6 @@ written twice: on the tape (differentiated, then run by the f32 oracle) and in
 numpy float64 (differenced numerically).  The bar is relative 2e-3: the
 analytic side is f32."""
 import numpy as np
-import pytest
 
 import oracle
 from poorgrad_b200 import neural
