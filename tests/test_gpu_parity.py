@@ -438,3 +438,25 @@ def test_cross_entropy_edge_rows(device, row, cls):
     assert dev[loss.index] == 0.0 and ref[loss.index] == 0.0
     assert np.all(np.isfinite(dev[g.index]))
     np.testing.assert_allclose(dev[g.index], ref[g.index], rtol=1e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("row", [[-3.0e38, 3.0e38], [3.0e38, -3.0e38], [1000.0, 1000.0],
+                                 [1.0, 2.0, 3.0]])
+def test_log_sum_exp_and_log_softmax_extreme_rows(device, row):
+    # function/tests/log_sum_exp_tests.rs:18-40, 62-75 and
+    # log_softmax_tests.rs:19-30 on the device: a finite row whose
+    # differences overflow keeps a finite normalizer, the losing lane's
+    # gradient is exactly zero and the winner's is one
+    t = Tape()
+    x = t.parameter(tensor((1, len(row)), row))
+    lse = x.logsumexp(1)
+    lp = x.log_softmax(1)
+    (g,) = t.differentiate(lse.sum(), [x])
+    ref, dev, _ = both(t, [lse, lp, g])
+    assert np.all(np.isfinite(dev[lse.index]))
+    assert_rel(dev[lse.index], ref[lse.index])
+    assert_rel(dev[lp.index], ref[lp.index])
+    assert np.all(np.isfinite(dev[g.index]))
+    assert_rel(dev[g.index], ref[g.index])
+    if abs(row[0]) == 3.0e38:
+        assert set(dev[g.index].reshape(-1).tolist()) == {0.0, 1.0}

@@ -309,3 +309,48 @@ def test_zero_target_lanes_contribute_exact_zero(built):
     loss = neural.cross_entropy(t.leaf(tensor((1, 2), [-3.0e38, 3.0e38])),
                                 t.input(tensor((1, 2), [0.0, 1.0])))
     assert run(t, [loss])[loss.index] == 0.0
+
+
+def test_log_sum_exp_known_answers(built):
+    # function/tests/log_sum_exp_tests.rs:6-16, 31-40 (f32), 42-60, 62-75
+    t = Tape()
+    x = t.parameter(tensor([1, 3], [1.0, 2.0, 3.0]))
+    lse = x.logsumexp(1)
+    (g,) = t.differentiate((lse * t.leaf(filled([1], 2.0))).sum(), [x])
+    out = run(t, [lse, g])
+    z = math.exp(1) + math.exp(2) + math.exp(3)
+    assert out[lse.index].shape == (1,)
+    assert abs(float(out[lse.index][0]) - math.log(z)) < 1e-6
+    assert np.allclose(out[g.index].reshape(-1), [2 * math.exp(v) / z for v in (1, 2, 3)],
+                       atol=1e-6)
+    for row in ([-3.0e38, 3.0e38], [3.0e38, -3.0e38]):
+        t = Tape()
+        x = t.parameter(tensor([2], row))
+        lse = x.logsumexp(0)
+        (g,) = t.differentiate(lse, [x])
+        out = run(t, [lse, g])
+        value = float(out[lse.index])
+        assert math.isfinite(value) and abs(value - 3.0e38) < 3.0e31
+        grad = out[g.index].tolist()
+        winner = row.index(3.0e38)
+        assert grad[1 - winner] == 0.0 and abs(grad[winner] - 1.0) < 1e-6
+
+
+def test_log_softmax_known_answers(built):
+    # function/tests/log_softmax_tests.rs:6-17, 19-30, 32-41, 43-68
+    t = Tape()
+    x = t.parameter(tensor([1, 3], [1.0, 2.0, 3.0]))
+    lp = x.log_softmax(1)
+    (g,) = t.differentiate((lp * t.leaf(tensor([1, 3], [1.0, 0.0, 0.0]))).sum(), [x])
+    out = run(t, [lp, g])
+    z = math.log(math.exp(1) + math.exp(2) + math.exp(3))
+    assert np.allclose(out[lp.index].reshape(-1), [1 - z, 2 - z, 3 - z], atol=1e-6)
+    soft = np.exp(out[lp.index].reshape(-1))
+    assert np.allclose(out[g.index].reshape(-1), np.array([1.0, 0.0, 0.0]) - soft, atol=1e-6)
+    t = Tape()
+    lp = t.leaf(tensor([1, 2], [1000.0, 1000.0])).log_softmax(1)
+    assert np.allclose(run(t, [lp])[lp.index], math.log(0.5), atol=1e-6)
+    t = Tape()
+    lp = t.leaf(tensor([2, 2], [0.0, 5.0, 0.0, -5.0])).log_softmax(0)
+    p = np.exp(run(t, [lp])[lp.index].astype(np.float64))
+    assert np.allclose(p.sum(axis=0), 1.0, atol=1e-6)
