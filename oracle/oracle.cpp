@@ -442,6 +442,8 @@ int oracle_run(const tb_plan_desc* desc, const float* const* params, int32_t par
           const tb_feed* f =
               node.slot < (int32_t)feed_of.size() ? feed_of[node.slot] : nullptr;
           tb_node copy = node;
+          // a feed replaces the initial payload whole, its kind included
+          if (f) copy.payload = f->indices ? TB_PAYLOAD_SELECTION : TB_PAYLOAD_DENSE;
           if (copy.payload == TB_PAYLOAD_NONE) copy.payload = TB_PAYLOAD_DENSE;
           values[i] = source_payload(copy, f ? f->dense : node.dense,
                                      f ? f->indices : node.indices);

@@ -614,8 +614,16 @@ void setup_instance(tb_plan* owner, tb_instance* plan) {
           init = node->dense;
         else
           init = node->indices;
-        if (init) check(cudaMemcpy(p, init, buf.bytes, cudaMemcpyHostToDevice), "upload source");
-        else check(cudaMemset(p, 0, buf.bytes), "cudaMemset(source)");
+        if (init) {
+          check(cudaMemcpy(p, init, buf.bytes, cudaMemcpyHostToDevice), "upload source");
+        } else if (buf.storage == tb::Storage::Input && node->payload == TB_PAYLOAD_CONSTANT) {
+          // an input whose initial payload is one value spread over its shape
+          // (a dropout mask before its first feed) starts as that value
+          std::vector<float> filled((size_t)(buf.bytes / 4), node->constant);
+          check(cudaMemcpy(p, filled.data(), buf.bytes, cudaMemcpyHostToDevice), "upload source");
+        } else {
+          check(cudaMemset(p, 0, buf.bytes), "cudaMemset(source)");
+        }
         if ((buf.storage == tb::Storage::Leaf || buf.storage == tb::Storage::LeafIndices) && !init)
           throw Failure(TB_INVALID, "leaf without payload");
         break;

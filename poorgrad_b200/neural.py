@@ -81,6 +81,18 @@ def unit_uniform(seed: int):
     return draw
 
 
+def dropout(seed: int, keep: float):
+    """`init::dropout` (neural/init.rs:119-130): one stream across calls; per
+    element ``1 / keep`` where the unit draw is below ``keep``, else 0."""
+    assert 0.0 < keep <= 1.0, f"the keep probability must lie within (0, 1], got {keep}"
+    stream = Stream(seed)
+
+    def draw(shape) -> np.ndarray:
+        n = int(np.prod(shape)) if len(shape) else 1
+        return np.where(stream.unit(n) < keep, 1.0 / keep, 0.0).astype(np.float32).reshape(shape)
+    return draw
+
+
 def integers(seed: int, high: int, n: int) -> np.ndarray:
     """Uniform integers ``0..high`` from one stream: ``floor(unit * high)``."""
     u = Stream(seed).unit(n)
@@ -99,6 +111,18 @@ class Linear:
     def express(self, x: Value) -> Value:
         product = x.matmul(self.weights)
         return product + self.bias.broadcast_along(0, product)
+
+
+class Dropout:
+    """`neural/dropout.rs`: an input mask of the given shape, all ones until
+    fed, multiplied into the expression; a training loop feeds a fresh
+    `dropout` mask each step, an unfed run is the identity."""
+
+    def __init__(self, tape: Tape, shape):
+        self.mask = tape.input(counted(tuple(shape), 1))
+
+    def express(self, x: Value) -> Value:
+        return x * self.mask
 
 
 class LayerNorm:
