@@ -223,11 +223,24 @@ class BatchNorm:
         mean = x.mean_along(0)
         centered = x - mean.broadcast_along(0, x)
         variance = (centered * centered).mean_along(0)
+        return self._normalize(centered, variance), mean, variance
+
+    def express_with(self, x: Value, mean: Value, variance: Value) -> Value:
+        """Inference mode (`neural/batch_norm.rs:136-145`): normalization by
+        supplied ``[features]`` statistics, typically per-run inputs fed with
+        the running estimates."""
+        return self._normalize(x - mean.broadcast_along(0, x), variance)
+
+    def _normalize(self, centered: Value, variance: Value) -> Value:
+        # the shared tail (`neural/batch_norm.rs:149-177`)
+        assert len(centered.shape) == 2, \
+            f"batch-norm input must be rank 2 [batch, features], got {centered.shape}"
+        assert centered.shape[1] == self.scale.shape[0], \
+            f"batch-norm input {centered.shape} and scale {self.scale.shape} disagree on features"
         deviation = (variance + self.epsilon.broadcast_like(variance)).sqrt()
         normalized = centered / deviation.broadcast_along(0, centered)
-        out = normalized * self.scale.broadcast_along(0, centered) + \
+        return normalized * self.scale.broadcast_along(0, centered) + \
             self.shift.broadcast_along(0, centered)
-        return out, mean, variance
 
 
 class Gelu:
