@@ -6,7 +6,8 @@ CPU path).  The product never imports it.
 
 ``oracle.cpp`` restates the topos default-build interpreter (see its header
 for the reference file:line each part follows); ``run`` executes a packed plan
-descriptor on the host and returns the requested values.  The reference is
+descriptor on the host and returns the requested values, and ``backward`` runs
+the engine's reverse scan over them.  ``optim.py`` restates the optimizers.  The reference is
 Rust and cannot be built here (no cargo/rustc), so parity of this restatement
 is pinned by the known-answer assertions of the reference's own test files
 (``tests/test_oracle_pins.py``).
@@ -43,6 +44,7 @@ def lib():
         build()
         _LIB = C.CDLL(LIB_PATH)
         _LIB.oracle_run.restype = C.c_int
+        _LIB.oracle_backward.restype = C.c_int
         _LIB.oracle_last_error.restype = C.c_char_p
         _LIB.oracle_gemm.restype = None
         _LIB.oracle_map.restype = None
@@ -69,6 +71,27 @@ def run(columns, parameters, feeds=None, read=None):
     if rc != 0:
         raise RuntimeError("oracle: " + lib().oracle_last_error().decode())
     return dict(zip(read, outs))
+
+
+def backward(columns, parameters, root, nodes, feeds=None):
+    """The engine's reverse scan (`Run::backward`, engine/run.rs:229-318) from
+    scalar ``root`` over the plan's forward values; returns the gradient of
+    each of ``nodes`` in order (zeros for non-ancestors)."""
+    from poorgrad_b200.abi import PackedPlan, Feeds, fptr
+    packed = PackedPlan(columns)
+    feeds = Feeds(columns, feeds or {})
+    params = [np.ascontiguousarray(p, dtype=np.float32).reshape(-1) for p in parameters]
+    param_ptrs = (C.POINTER(C.c_float) * max(1, len(params)))(*[fptr(p) for p in params])
+    nodes = [n.index if hasattr(n, "index") else int(n) for n in nodes]
+    outs = [np.empty(columns.nodes[n].shape, dtype=np.float32) for n in nodes]
+    out_ptrs = (C.POINTER(C.c_float) * max(1, len(outs)))(*[fptr(o) for o in outs])
+    index = (C.c_int64 * max(1, len(nodes)))(*nodes)
+    root = root.index if hasattr(root, "index") else int(root)
+    rc = lib().oracle_backward(C.byref(packed.desc), param_ptrs, len(params), feeds.count,
+                               feeds.array, C.c_int64(root), len(nodes), index, out_ptrs)
+    if rc != 0:
+        raise RuntimeError("oracle: " + lib().oracle_last_error().decode())
+    return outs
 
 
 def gemm(a: np.ndarray, b: np.ndarray) -> np.ndarray:

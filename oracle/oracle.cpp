@@ -24,6 +24,7 @@
 // Values are independent of storage representation (payload/tests/
 // tensor_tests.rs:1209-1240), so every value is held densely except constants
 // (one scalar) and selections (indices), which gather/scatter need.
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -404,6 +405,226 @@ Val forward(const tb_node& n, const Val* x, const Val* y) {
   }
 }
 
+// Evaluates every wanted node of a plan in index order (`Plan::forward`,
+// engine/plan.rs:514-640) and returns all values.
+std::vector<Val> evaluate(const tb_plan_desc* desc, const float* const* params,
+                          int32_t param_count, int32_t feed_count, const tb_feed* feeds) {
+  const int64_t n = desc->node_count;
+  std::vector<Val> values(n);
+  std::vector<const tb_feed*> feed_of;
+  for (int32_t f = 0; f < feed_count; ++f) {
+    if ((int32_t)feed_of.size() <= feeds[f].slot) feed_of.resize(feeds[f].slot + 1, nullptr);
+    feed_of[feeds[f].slot] = &feeds[f];
+  }
+  // release bookkeeping of forward-only plans is irrelevant to values; the
+  // oracle keeps everything so any readable value can be read back.
+  for (int64_t i = 0; i < n; ++i) {
+    const tb_node& node = desc->nodes[i];
+    if (!node.wanted) continue;
+    switch (node.op) {
+      case TB_OP_LEAF: values[i] = source_payload(node, node.dense, node.indices); break;
+      case TB_OP_PARAMETER:
+        if (node.slot >= param_count) throw std::runtime_error("missing parameter slot");
+        values[i] = source_payload(node, params[node.slot], nullptr);
+        values[i].kind = TB_PAYLOAD_DENSE;
+        break;
+      case TB_OP_INPUT: {
+        const tb_feed* f =
+            node.slot < (int32_t)feed_of.size() ? feed_of[node.slot] : nullptr;
+        tb_node copy = node;
+        // a feed replaces the initial payload whole, its kind included
+        if (f) copy.payload = f->indices ? TB_PAYLOAD_SELECTION : TB_PAYLOAD_DENSE;
+        if (copy.payload == TB_PAYLOAD_NONE) copy.payload = TB_PAYLOAD_DENSE;
+        values[i] = source_payload(copy, f ? f->dense : node.dense,
+                                   f ? f->indices : node.indices);
+        break;
+      }
+      default: {
+        const Val* x = node.operands[0] >= 0 ? &values[node.operands[0]] : nullptr;
+        const Val* y = node.operands[1] >= 0 ? &values[node.operands[1]] : nullptr;
+        values[i] = forward(node, x, y);
+      }
+    }
+  }
+  return values;
+}
+
+// ---- the engine's reverse scan (`Run::backward`, engine/run.rs:229-318)
+
+// One forward operation applied to computed values, as the derivative rules
+// compose payload methods.
+Val apply(int op, const Val* x, const Val* y, const std::vector<int64_t>& shape,
+          std::initializer_list<int64_t> attrs = {}) {
+  tb_node n{};
+  n.op = op;
+  n.rank = (int32_t)shape.size();
+  for (int i = 0; i < n.rank; ++i) n.shape[i] = shape[i];
+  int k = 0;
+  for (int64_t a : attrs) n.attrs[k++] = a;
+  return forward(n, x, y);
+}
+Val add(const Val& a, const Val& b) { return apply(TB_OP_ADD, &a, &b, a.shape); }
+Val sub(const Val& a, const Val& b) { return apply(TB_OP_SUB, &a, &b, a.shape); }
+Val mul(const Val& a, const Val& b) { return apply(TB_OP_MUL, &a, &b, a.shape); }
+Val div(const Val& a, const Val& b) { return apply(TB_OP_DIV, &a, &b, a.shape); }
+Val neg(const Val& a) { return apply(TB_OP_NEG, &a, nullptr, a.shape); }
+Val un(int op, const Val& a) { return apply(op, &a, nullptr, a.shape); }
+
+// function/matmul.rs:89-97: the last two axes exchanged
+Val swapped(const Val& v) {
+  std::vector<int64_t> s = v.shape;
+  const int r = (int)s.size();
+  if (r <= 2) {
+    std::reverse(s.begin(), s.end());
+    return apply(TB_OP_TRANSPOSE, &v, nullptr, s);
+  }
+  std::swap(s[r - 2], s[r - 1]);
+  tb_node n{};
+  n.op = TB_OP_PERMUTE;
+  n.rank = r;
+  for (int i = 0; i < r; ++i) {
+    n.shape[i] = s[i];
+    n.attrs[i] = i;
+  }
+  std::swap(n.attrs[r - 2], n.attrs[r - 1]);
+  return forward(n, &v, nullptr);
+}
+
+Val matmul_of(const Val& a, const Val& b) {
+  std::vector<int64_t> s = a.shape;
+  s.back() = b.shape.back();
+  return apply(TB_OP_MATMUL, &a, &b, s);
+}
+
+// The cotangents of one node (function/*.rs `backward`); an absent
+// cotangent (a shape-only or selection operand, `Step`) is `present = false`.
+void cotangents(const tb_node& n, const Val* x, const Val* y, const Val& out, const Val& g,
+                Val c[2], bool present[2]) {
+  const int64_t* at = n.attrs;
+  present[0] = present[1] = false;
+  auto one = [](const Val& v) { return constant(v.shape, 1.0f); };
+  auto give = [&](int k, Val v) {
+    c[k] = std::move(v);
+    present[k] = true;
+  };
+  switch (n.op) {
+    case TB_OP_ADD: give(0, g); give(1, g); return;                     // add.rs
+    case TB_OP_SUB: give(0, g); give(1, neg(g)); return;                // sub.rs
+    case TB_OP_MUL: give(0, mul(g, *y)); give(1, mul(g, *x)); return;   // mul.rs
+    case TB_OP_DIV:                                                     // div.rs:46-52
+      give(0, div(g, *y));
+      give(1, neg(div(mul(g, out), *y)));
+      return;
+    case TB_OP_NEG: give(0, neg(g)); return;
+    case TB_OP_TANH: give(0, mul(g, sub(one(out), mul(out, out)))); return;  // tanh.rs:41-44
+    case TB_OP_EXP: give(0, mul(g, out)); return;
+    case TB_OP_LN: give(0, div(g, *x)); return;
+    case TB_OP_SQRT: give(0, div(g, add(out, out))); return;           // sqrt.rs:43-45
+    case TB_OP_POWF: {                                                 // powf.rs:48-54
+      Val lowered = sub(*y, one(*y));
+      give(0, mul(mul(g, *y), apply(TB_OP_POWF, x, &lowered, x->shape)));
+      give(1, mul(mul(g, out), un(TB_OP_LN, *x)));
+      return;
+    }
+    case TB_OP_MAXIMUM: {                                              // maximum.rs:45-51
+      Val winners = apply(TB_OP_STEP, x, y, x->shape);
+      give(0, mul(g, winners));
+      give(1, mul(g, sub(one(winners), winners)));
+      return;
+    }
+    case TB_OP_RELU: {                                                 // relu.rs
+      Val zero = constant(x->shape, 0.0f);
+      give(0, mul(g, apply(TB_OP_STEP, x, &zero, x->shape)));
+      return;
+    }
+    case TB_OP_STEP: return;
+    case TB_OP_MATMUL:                                                 // matmul.rs
+      give(0, matmul_of(g, swapped(*y)));
+      give(1, matmul_of(swapped(*x), g));
+      return;
+    case TB_OP_TRANSPOSE: give(0, apply(TB_OP_TRANSPOSE, &g, nullptr, x->shape)); return;
+    case TB_OP_SUM: give(0, apply(TB_OP_BROADCAST, &g, x, x->shape)); return;
+    case TB_OP_SUM_ALONG: give(0, apply(TB_OP_BROADCAST_ALONG, &g, x, x->shape, {at[0]})); return;
+    case TB_OP_BROADCAST: {                                            // broadcast.rs
+      Val total = apply(TB_OP_SUM, &g, nullptr, {});
+      give(0, apply(TB_OP_BROADCAST, &total, x, x->shape));
+      return;
+    }
+    case TB_OP_BROADCAST_ALONG: give(0, apply(TB_OP_SUM_ALONG, &g, nullptr, x->shape, {at[0]})); return;
+    case TB_OP_RESHAPE: give(0, apply(TB_OP_RESHAPE, &g, nullptr, x->shape)); return;
+    case TB_OP_PERMUTE: {                                              // permute.rs:53-60
+      tb_node p{};
+      p.op = TB_OP_PERMUTE;
+      p.rank = n.rank;
+      for (int i = 0; i < n.rank; ++i) {
+        p.shape[i] = x->shape[i];
+        p.attrs[at[i]] = i;
+      }
+      give(0, forward(p, &g, nullptr));
+      return;
+    }
+    case TB_OP_NARROW:
+      give(0, apply(TB_OP_PAD, &g, nullptr, x->shape, {at[0], at[1], x->shape[at[0]]}));
+      return;
+    case TB_OP_PAD:
+      give(0, apply(TB_OP_NARROW, &g, nullptr, x->shape, {at[0], at[1], x->shape[at[0]]}));
+      return;
+    case TB_OP_UNFOLD:
+      give(0, apply(TB_OP_FOLD, &g, nullptr, x->shape, {at[0], at[1], at[2], at[3], x->shape[at[0]]}));
+      return;
+    case TB_OP_FOLD:
+      give(0, apply(TB_OP_UNFOLD, &g, nullptr, x->shape, {at[0], at[1], at[2], at[3]}));
+      return;
+    case TB_OP_GATHER: give(0, apply(TB_OP_SCATTER, &g, y, x->shape, {x->shape[0]})); return;
+    case TB_OP_SCATTER: give(0, apply(TB_OP_GATHER, &g, y, x->shape)); return;
+    case TB_OP_LOG_SOFTMAX: {                                          // log_softmax.rs
+      std::vector<int64_t> reduced = without(g.shape, (int)at[0]);
+      Val rows = apply(TB_OP_SUM_ALONG, &g, nullptr, reduced, {at[0]});
+      Val total = apply(TB_OP_BROADCAST_ALONG, &rows, &g, g.shape, {at[0]});
+      give(0, sub(g, mul(un(TB_OP_EXP, out), total)));
+      return;
+    }
+    case TB_OP_LOG_SUM_EXP: {                                          // log_sum_exp.rs
+      Val spread = apply(TB_OP_BROADCAST_ALONG, &out, x, x->shape, {at[0]});
+      Val probabilities = un(TB_OP_EXP, sub(*x, spread));
+      give(0, mul(apply(TB_OP_BROADCAST_ALONG, &g, x, x->shape, {at[0]}), probabilities));
+      return;
+    }
+  }
+  throw std::runtime_error("oracle: no derivative rule for op " + std::to_string(n.op));
+}
+
+// engine/run.rs:264-317: zero gradients, a `one_like` seed at the scalar
+// root, one reverse scan that marks ancestors as it goes, and `g = g + c`
+// per present cotangent.
+std::vector<Val> reverse_scan(const tb_plan_desc* desc, const std::vector<Val>& values,
+                              int64_t root) {
+  if (root < 0 || root >= desc->node_count || desc->nodes[root].rank != 0)
+    throw std::runtime_error("backward requires a scalar target; reduce it with `sum` first");
+  std::vector<Val> grads(root + 1);
+  for (int64_t i = 0; i <= root; ++i) grads[i] = constant(node_shape(desc->nodes[i]), 0.0f);
+  grads[root] = constant({}, 1.0f);
+  std::vector<char> ancestor(root + 1, 0);
+  ancestor[root] = 1;
+  for (int64_t i = root; i >= 0; --i) {
+    if (!ancestor[i]) continue;
+    const tb_node& n = desc->nodes[i];
+    if (n.op == TB_OP_LEAF || n.op == TB_OP_PARAMETER || n.op == TB_OP_INPUT) continue;
+    const int64_t lx = n.operands[0], ly = n.operands[1];
+    Val c[2];
+    bool present[2];
+    cotangents(n, lx >= 0 ? &values[lx] : nullptr, ly >= 0 ? &values[ly] : nullptr, values[i],
+               grads[i], c, present);
+    const int64_t links[2] = {lx, ly};
+    for (int k = 0; k < 2; ++k) {
+      if (!present[k] || links[k] < 0) continue;
+      ancestor[links[k]] = 1;
+      grads[links[k]] = add(grads[links[k]], c[k]);
+    }
+  }
+  return grads;
+}
+
 thread_local std::string g_error;
 
 }  // namespace
@@ -419,45 +640,32 @@ int oracle_run(const tb_plan_desc* desc, const float* const* params, int32_t par
                int32_t feed_count, const tb_feed* feeds, int32_t read_count,
                const int64_t* read_nodes, float* const* outputs) {
   try {
-    const int64_t n = desc->node_count;
-    std::vector<Val> values(n);
-    std::vector<const tb_feed*> feed_of;
-    for (int32_t f = 0; f < feed_count; ++f) {
-      if ((int32_t)feed_of.size() <= feeds[f].slot) feed_of.resize(feeds[f].slot + 1, nullptr);
-      feed_of[feeds[f].slot] = &feeds[f];
-    }
-    // release bookkeeping of forward-only plans is irrelevant to values; the
-    // oracle keeps everything so any readable value can be read back.
-    for (int64_t i = 0; i < n; ++i) {
-      const tb_node& node = desc->nodes[i];
-      if (!node.wanted) continue;
-      switch (node.op) {
-        case TB_OP_LEAF: values[i] = source_payload(node, node.dense, node.indices); break;
-        case TB_OP_PARAMETER:
-          if (node.slot >= param_count) throw std::runtime_error("missing parameter slot");
-          values[i] = source_payload(node, params[node.slot], nullptr);
-          values[i].kind = TB_PAYLOAD_DENSE;
-          break;
-        case TB_OP_INPUT: {
-          const tb_feed* f =
-              node.slot < (int32_t)feed_of.size() ? feed_of[node.slot] : nullptr;
-          tb_node copy = node;
-          // a feed replaces the initial payload whole, its kind included
-          if (f) copy.payload = f->indices ? TB_PAYLOAD_SELECTION : TB_PAYLOAD_DENSE;
-          if (copy.payload == TB_PAYLOAD_NONE) copy.payload = TB_PAYLOAD_DENSE;
-          values[i] = source_payload(copy, f ? f->dense : node.dense,
-                                     f ? f->indices : node.indices);
-          break;
-        }
-        default: {
-          const Val* x = node.operands[0] >= 0 ? &values[node.operands[0]] : nullptr;
-          const Val* y = node.operands[1] >= 0 ? &values[node.operands[1]] : nullptr;
-          values[i] = forward(node, x, y);
-        }
-      }
-    }
+    std::vector<Val> values = evaluate(desc, params, param_count, feed_count, feeds);
     for (int32_t r = 0; r < read_count; ++r) {
       const Val& v = values[read_nodes[r]];
+      for (int64_t i = 0; i < v.volume(); ++i) outputs[r][i] = v.get(i);
+    }
+    return 0;
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return 1;
+  }
+}
+
+// `Run::backward(root)` then `Gradients::of(node)` for each of `nodes`
+// (engine/run.rs:229-318) over the plan's forward values: the engine's own
+// reverse scan, against which recorded-gradient plans close bitwise.
+int oracle_backward(const tb_plan_desc* desc, const float* const* params, int32_t param_count,
+                    int32_t feed_count, const tb_feed* feeds, int64_t root, int32_t count,
+                    const int64_t* nodes, float* const* outputs) {
+  try {
+    std::vector<Val> values = evaluate(desc, params, param_count, feed_count, feeds);
+    std::vector<Val> grads = reverse_scan(desc, values, root);
+    for (int32_t r = 0; r < count; ++r) {
+      if (nodes[r] < 0 || nodes[r] >= desc->node_count)
+        throw std::runtime_error("gradient of a node outside the plan");
+      const Val v = nodes[r] <= root ? grads[nodes[r]]
+                                     : constant(node_shape(desc->nodes[nodes[r]]), 0.0f);
       for (int64_t i = 0; i < v.volume(); ++i) outputs[r][i] = v.get(i);
     }
     return 0;

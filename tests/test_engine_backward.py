@@ -3,7 +3,8 @@ engine/run.rs:229-318) on the device: the reverse scan runs inside the plan
 and its parameter gradients agree with the recorded-gradient plan of the same
 graph (`Tape::differentiate`), which the reference pins bitwise to the engine
 (graph/tests/differentiate_tests.rs:520); here both are checked against the
-oracle's run of the recorded-gradient columns."""
+oracle's run of the recorded-gradient columns and the oracle's own reverse
+scan."""
 import numpy as np
 import pytest
 
@@ -44,10 +45,13 @@ def test_engine_backward_matches_the_recorded_gradients(device):
     engine = net.compile(Request([loss]).backward())
     ref = oracle.run(net.compile(Request([loss] + recorded)), net.parameters(),
                      read=[g.index for g in recorded])
+    scan = oracle.backward(engine, net.parameters(), loss, params)
     plan = backend.DevicePlan(engine)
     dp = backend.DeviceParameters(plan, net.parameters())
     plan.forward(dp, sync=True)
     for p, g in zip(params, recorded):
         got = plan.gradient(loss, p)
         np.testing.assert_allclose(got, ref[g.index], rtol=1e-4, atol=1e-6)
+    for p, e in zip(params, scan):
+        np.testing.assert_allclose(plan.gradient(loss, p), e, rtol=1e-4, atol=1e-6)
     assert n_forward < len(t)
