@@ -213,6 +213,16 @@ int tb_plan_attach_optimizer(tb_plan* plan, tb_optimizer* optimizer);
 int tb_optimizer_step(tb_optimizer* optimizer, const float* const* gradients, void* stream);
 /* Downloads Adam moments of a slot (first, second); count elements each. */
 int tb_optimizer_state(const tb_optimizer* optimizer, int32_t slot, float* first, float* second, int64_t count);
+/* Checkpoints of the optimizer state (the `first`/`second` fields and beta powers that
+ * neural/adam.rs:19-31 keeps between steps; the reference's checkpoint.rs snapshots
+ * parameters only, and a resumed run needs both).  tb_optimizer_powers reads beta1^t and
+ * beta2^t; tb_optimizer_restore writes a slot's moments; tb_optimizer_restore_powers writes
+ * the powers, so the next step continues the saved trajectory bitwise.  Adam and AdamW only
+ * (TB_INVALID for SGD); each waits for the device first. */
+int tb_optimizer_powers(const tb_optimizer* optimizer, float powers[2]);
+int tb_optimizer_restore(tb_optimizer* optimizer, int32_t slot, const float* first,
+                         const float* second, int64_t count);
+int tb_optimizer_restore_powers(tb_optimizer* optimizer, const float powers[2]);
 
 /* ---- data parallel gradient exchange (new: the reference has no communication backend;
  *      replaces the host `tree_sum` of examples/makemore/mlp_parallel.rs:59-71) */

@@ -210,6 +210,10 @@ def load_library() -> C.CDLL:
         "tb_plan_attach_optimizer": (C.c_int, [P, P]),
         "tb_optimizer_state": (C.c_int, [P, C.c_int32, C.POINTER(C.c_float),
                                          C.POINTER(C.c_float), C.c_int64]),
+        "tb_optimizer_powers": (C.c_int, [P, C.POINTER(C.c_float)]),
+        "tb_optimizer_restore": (C.c_int, [P, C.c_int32, C.POINTER(C.c_float),
+                                           C.POINTER(C.c_float), C.c_int64]),
+        "tb_optimizer_restore_powers": (C.c_int, [P, C.POINTER(C.c_float)]),
         "tb_comm_unique_id": (C.c_int, [C.POINTER(C.c_uint8)]),
         "tb_comm_init": (C.c_int, [C.c_int32, C.c_int32, C.POINTER(C.c_uint8), C.POINTER(P)]),
         "tb_comm_destroy": (None, [P]),

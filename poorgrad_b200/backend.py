@@ -258,6 +258,26 @@ class Optimizer:
                "tb_optimizer_state")
         return m, v
 
+    def state_snapshot(self) -> dict:
+        """The Adam/AdamW state a resumed run needs: per bound slot its
+        moments, and the beta powers (``beta1^t``, ``beta2^t``)."""
+        powers = (C.c_float * 2)()
+        _check(self.lib.tb_optimizer_powers(self.handle, powers), "tb_optimizer_powers")
+        return {"moments": {slot: self.moments(slot) for slot in self.slots},
+                "powers": (powers[0], powers[1])}
+
+    def state_restore(self, state: dict):
+        """Writes a ``state_snapshot`` back: the next step continues the saved
+        trajectory."""
+        for slot, (m, v) in state["moments"].items():
+            m = np.ascontiguousarray(m, np.float32).reshape(-1)
+            v = np.ascontiguousarray(v, np.float32).reshape(-1)
+            _check(self.lib.tb_optimizer_restore(self.handle, slot, fptr(m), fptr(v), m.size),
+                   "tb_optimizer_restore")
+        powers = (C.c_float * 2)(*state["powers"])
+        _check(self.lib.tb_optimizer_restore_powers(self.handle, powers),
+               "tb_optimizer_restore_powers")
+
     def __del__(self):
         if getattr(self, "handle", None):
             self.lib.tb_optimizer_destroy(self.handle)

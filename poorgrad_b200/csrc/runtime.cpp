@@ -1061,6 +1061,44 @@ int tb_optimizer_state(const tb_optimizer* o, int32_t slot, float* first, float*
   });
 }
 
+int tb_optimizer_powers(const tb_optimizer* o, float powers[2]) {
+  return guarded([&]() {
+    if (!o->state) throw Failure(TB_INVALID, "optimizer has no moments");
+    check(cudaDeviceSynchronize(), "sync");
+    check(cudaMemcpy(powers, o->scalars, 2 * 4, cudaMemcpyDeviceToHost), "download");
+    return (int)TB_OK;
+  });
+}
+
+int tb_optimizer_restore(tb_optimizer* o, int32_t slot, const float* first, const float* second,
+                         int64_t count) {
+  return guarded([&]() {
+    if (!o->state) throw Failure(TB_INVALID, "optimizer has no moments");
+    for (size_t i = 0; i < o->slots.size(); ++i) {
+      if (o->slots[i] != slot) continue;
+      const tb::OptEntry& e = o->host_entries[i];
+      if (e.count != count) throw Failure(TB_INVALID, "size mismatch");
+      check(cudaDeviceSynchronize(), "sync");
+      check(cudaMemcpy(e.m, first, count * 4, cudaMemcpyHostToDevice), "upload");
+      check(cudaMemcpy(e.v, second, count * 4, cudaMemcpyHostToDevice), "upload");
+      return (int)TB_OK;
+    }
+    throw Failure(TB_INVALID, "slot not bound to the optimizer");
+  });
+}
+
+int tb_optimizer_restore_powers(tb_optimizer* o, const float powers[2]) {
+  return guarded([&]() {
+    if (!o->state) throw Failure(TB_INVALID, "optimizer has no moments");
+    // s[0..1] are the powers the next step multiplies; s[2..3] their
+    // corrections, recomputed by that step before use
+    const float s[4] = {powers[0], powers[1], 1.0f - powers[0], 1.0f - powers[1]};
+    check(cudaDeviceSynchronize(), "sync");
+    check(cudaMemcpy(o->scalars, s, sizeof s, cudaMemcpyHostToDevice), "upload");
+    return (int)TB_OK;
+  });
+}
+
 int tb_comm_unique_id(uint8_t id[128]) {
   return guarded([&]() {
     Nccl* n = nccl();

@@ -112,6 +112,11 @@ class Linear:
         product = x.matmul(self.weights)
         return product + self.bias.broadcast_along(0, product)
 
+    def visit(self, visitor) -> None:
+        # neural/linear.rs:107-110
+        visitor.parameter("weights", self.weights)
+        visitor.parameter("bias", self.bias)
+
 
 class Dropout:
     """`neural/dropout.rs`: an input mask of the given shape, all ones until
@@ -123,6 +128,50 @@ class Dropout:
 
     def express(self, x: Value) -> Value:
         return x * self.mask
+
+    def visit(self, visitor) -> None:
+        pass  # a mask input, no parameters
+
+
+class Activation:
+    """`neural/activation.rs:13-61`: a stateless stage, ``tanh`` or ``relu``."""
+    TANH, RELU = "tanh", "relu"
+
+    def __init__(self, kind: str):
+        assert kind in (self.TANH, self.RELU), kind
+        self.kind = kind
+
+    def express(self, x: Value) -> Value:
+        return x.tanh() if self.kind == self.TANH else x.relu()
+
+    def visit(self, visitor) -> None:
+        pass
+
+
+class Sequential:
+    """`neural/sequential.rs`: stages applied in order; `visit` announces each
+    stage's parameters under its index (`sequential.rs:57-63`)."""
+
+    def __init__(self):
+        self.stages = []
+
+    def then(self, stage) -> "Sequential":
+        self.stages.append(stage)
+        return self
+
+    def __len__(self):
+        return len(self.stages)
+
+    def express(self, x: Value) -> Value:
+        for stage in self.stages:
+            x = stage.express(x)
+        return x
+
+    def visit(self, visitor) -> None:
+        for index, stage in enumerate(self.stages):
+            visitor.enter(index)
+            stage.visit(visitor)
+            visitor.leave()
 
 
 class LayerNorm:
@@ -149,6 +198,11 @@ class LayerNorm:
         normalized = centered / deviation.broadcast_along(1, x)
         return normalized * self.scale.broadcast_along(0, x) + self.shift.broadcast_along(0, x)
 
+    def visit(self, visitor) -> None:
+        # neural/layer_norm.rs:148-151
+        visitor.parameter("scale", self.scale)
+        visitor.parameter("shift", self.shift)
+
 
 class RmsNorm:
     """`neural/rms_norm.rs:89-114`: ``x / sqrt(mean(x^2) + eps) * scale`` per
@@ -167,6 +221,10 @@ class RmsNorm:
         power = (x * x).mean_along(1)
         root = (power + self.epsilon.broadcast_like(power)).sqrt()
         return x / root.broadcast_along(1, x) * self.scale.broadcast_along(0, x)
+
+    def visit(self, visitor) -> None:
+        # neural/rms_norm.rs:130-132
+        visitor.parameter("scale", self.scale)
 
 
 def conv2d(x: Value, weights: Value, bias: Value, stride: int = 1, padding: int = 0) -> Value:
