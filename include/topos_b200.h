@@ -65,6 +65,13 @@ enum { TB_PAYLOAD_NONE = 0, TB_PAYLOAD_DENSE = 1, TB_PAYLOAD_CONSTANT = 2, TB_PA
 
 /* ---- numerics posture (backend/numerics.rs:25-43) */
 enum { TB_NUMERICS_FAST = 0, TB_NUMERICS_EXACT = 1 };
+/* Payload element types (`Tensor<f32>`, `Tensor<Bf16>`: payload/bf16.rs).  A bf16 network
+ * rounds every payload operation's f32 result once to the nearest bf16 (ties to even,
+ * bf16.rs:39-50) and accumulates products, sums, folds and scatters in f32 before one
+ * rounding (tensor.rs:1015-1022, 1055-1093, 1431-1451, 1605-1616; gemm.rs:149-161).  Values
+ * cross this ABI in f32 containers holding bf16 values.  The device does not lower bf16
+ * plans yet: tb_plan_compile answers TB_DECLINED for them. */
+enum { TB_ELEMENT_F32 = 0, TB_ELEMENT_BF16 = 1 };
 
 #define TB_MAX_RANK 8
 
@@ -95,6 +102,7 @@ typedef struct tb_plan_desc {
   const tb_node* nodes;
   int32_t backward;             /* Request::backward (engine/request.rs:70) */
   int32_t numerics;             /* TB_NUMERICS_* (engine/request.rs:84) */
+  int32_t element;              /* TB_ELEMENT_*: the network's payload element type */
 } tb_plan_desc;
 
 /* One fed input (`Plan::forward` feeds, engine/plan.rs:534-564). */

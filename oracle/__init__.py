@@ -48,6 +48,7 @@ def lib():
         _LIB.oracle_last_error.restype = C.c_char_p
         _LIB.oracle_gemm.restype = None
         _LIB.oracle_map.restype = None
+        _LIB.oracle_round_bf16.restype = None
     return _LIB
 
 
@@ -104,6 +105,15 @@ def gemm(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     c = np.empty((m, n), dtype=np.float32)
     lib().oracle_gemm(fptr(a), fptr(b), fptr(c), C.c_int64(m), C.c_int64(k), C.c_int64(n))
     return c
+
+
+def round_bf16(x: np.ndarray) -> np.ndarray:
+    """`Bf16::from_f32(x).to_f32()` per element."""
+    from poorgrad_b200.abi import fptr
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty_like(x)
+    lib().oracle_round_bf16(fptr(x), C.c_int64(x.size), fptr(out))
+    return out
 
 
 def libm_map(op: int, x: np.ndarray) -> np.ndarray:

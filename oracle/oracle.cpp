@@ -18,6 +18,10 @@
 //     pad / unfold / fold (1292-1463),
 //   * scalar semantics of payload/elementary.rs:116-143 (libm expf/logf/tanhf/
 //     powf, sqrtf, `f32::max` for maximum, `x >= t` for step).
+//   * bf16 networks (payload/bf16.rs): every payload operation rounds its f32
+//     result once to bf16; products, sums, folds and scatters accumulate in
+//     f32 and round once (tensor.rs:1015-1022, 1055-1093, 1431-1451,
+//     1605-1616; gemm.rs:149-161).
 // Compiled with -O2 -ffp-contract=off and without fast-math: no contraction,
 // no reassociation, exactly as the Rust source is evaluated.
 //
@@ -66,6 +70,30 @@ inline float fmax_ref(float a, float b) {
   return (b > a) ? b : a;
 }
 
+// Element type of the running plan: a bf16 network rounds each payload
+// operation's f32 result once (payload/bf16.rs:131-170, 206-257) and each
+// accumulation (sums, folds, scatters, products) once at its end.
+thread_local bool g_bf16 = false;
+
+// payload/bf16.rs:39-55: the nearest bf16 with ties to even, carried into the
+// exponent; a NaN keeps its top half with a mantissa bit forced on.
+inline float round_bf16(float v) {
+  uint32_t bits;
+  std::memcpy(&bits, &v, 4);
+  uint32_t out;
+  if (std::isnan(v)) {
+    out = ((bits >> 16) | 0x0040u) << 16;
+  } else {
+    out = ((bits + 0x7FFFu + ((bits >> 16) & 1u)) >> 16) << 16;
+  }
+  float r;
+  std::memcpy(&r, &out, 4);
+  return r;
+}
+
+// One payload result in the running element type.
+inline float el(float v) { return g_bf16 ? round_bf16(v) : v; }
+
 Val dense(std::vector<int64_t> shape) {
   Val v;
   v.kind = TB_PAYLOAD_DENSE;
@@ -88,9 +116,9 @@ std::vector<int64_t> node_shape(const tb_node& n) {
 
 template <class F>
 Val map1(const Val& a, F f) {
-  if (a.kind == TB_PAYLOAD_CONSTANT) return constant(a.shape, f(a.c));
+  if (a.kind == TB_PAYLOAD_CONSTANT) return constant(a.shape, el(f(a.c)));
   Val out = dense(a.shape);
-  for (int64_t i = 0; i < out.volume(); ++i) out.data[i] = f(a.get(i));
+  for (int64_t i = 0; i < out.volume(); ++i) out.data[i] = el(f(a.get(i)));
   return out;
 }
 
@@ -98,9 +126,9 @@ template <class F>
 Val zip(const Val& a, const Val& b, F f) {
   if (a.shape != b.shape) throw std::runtime_error("tensors have different shapes");
   if (a.kind == TB_PAYLOAD_CONSTANT && b.kind == TB_PAYLOAD_CONSTANT)
-    return constant(a.shape, f(a.c, b.c));
+    return constant(a.shape, el(f(a.c, b.c)));
   Val out = dense(a.shape);
-  for (int64_t i = 0; i < out.volume(); ++i) out.data[i] = f(a.get(i), b.get(i));
+  for (int64_t i = 0; i < out.volume(); ++i) out.data[i] = el(f(a.get(i), b.get(i)));
   return out;
 }
 
@@ -129,7 +157,7 @@ Val sum_along(const Val& a, int axis) {
     for (int64_t in = 0; in < inner; ++in) {
       float total = a.get((o * extent + 0) * inner + in);
       for (int64_t s = 1; s < extent; ++s) total = total + a.get((o * extent + s) * inner + in);
-      out.data[o * inner + in] = total;
+      out.data[o * inner + in] = el(total);
     }
   return out;
 }
@@ -222,6 +250,7 @@ Val matmul(const Val& a, const Val& b) {
       }
     }
   }
+  for (float& v : out.data) v = el(v);  // f32 accumulators, one rounding
   return out;
 }
 
@@ -235,10 +264,10 @@ Val source_payload(const tb_node& n, const float* dense_ptr, const int32_t* idx_
   v.shape = node_shape(n);
   if (n.payload == TB_PAYLOAD_CONSTANT) {
     v.kind = TB_PAYLOAD_CONSTANT;
-    v.c = n.constant;
+    v.c = el(n.constant);
   } else if (n.payload == TB_PAYLOAD_SELECTION) {
     v.kind = TB_PAYLOAD_SELECTION;
-    v.c = n.constant;
+    v.c = el(n.constant);
     v.vocab = n.shape[1];
     if (!idx_ptr) throw std::runtime_error("selection without indices");
     v.idx.assign(idx_ptr, idx_ptr + n.shape[0]);
@@ -246,6 +275,7 @@ Val source_payload(const tb_node& n, const float* dense_ptr, const int32_t* idx_
     v.kind = TB_PAYLOAD_DENSE;
     if (!dense_ptr) throw std::runtime_error("dense source without elements");
     v.data.assign(dense_ptr, dense_ptr + v.volume());
+    for (float& e : v.data) e = el(e);  // a bf16 network holds bf16 sources
   }
   return v;
 }
@@ -281,7 +311,7 @@ Val forward(const tb_node& n, const Val* x, const Val* y) {
     case TB_OP_SUM: {  // payload/tensor.rs:1055-1063
       float total = x->get(0);
       for (int64_t i = 1; i < x->volume(); ++i) total = total + x->get(i);
-      return constant({}, total);
+      return constant({}, el(total));
     }
     case TB_OP_SUM_ALONG: return sum_along(*x, (int)at[0]);
     case TB_OP_BROADCAST: return constant(shape, x->get(0));
@@ -358,7 +388,7 @@ Val forward(const tb_node& n, const Val* x, const Val* y) {
               if (window >= count) continue;
               total = total + x->get(((o * count + window) * size + k) * inner + in);
             }
-            out.data[w++] = total;
+            out.data[w++] = el(total);
           }
       return out;
     }
@@ -381,6 +411,7 @@ Val forward(const tb_node& n, const Val* x, const Val* y) {
           int64_t p = (int64_t)y->idx[s] * row + o;
           out.data[p] = out.data[p] + x->get(s * row + o);
         }
+      for (float& v : out.data) v = el(v);  // f32 accumulators, one rounding
       return out;
     }
     case TB_OP_LOG_SOFTMAX: {  // function/log_softmax.rs:51-65
@@ -406,9 +437,12 @@ Val forward(const tb_node& n, const Val* x, const Val* y) {
 }
 
 // Evaluates every wanted node of a plan in index order (`Plan::forward`,
-// engine/plan.rs:514-640) and returns all values.
+// engine/plan.rs:514-640) in the plan's element type and returns all values.
 std::vector<Val> evaluate(const tb_plan_desc* desc, const float* const* params,
                           int32_t param_count, int32_t feed_count, const tb_feed* feeds) {
+  if (desc->element != TB_ELEMENT_F32 && desc->element != TB_ELEMENT_BF16)
+    throw std::runtime_error("unknown element type");
+  g_bf16 = desc->element == TB_ELEMENT_BF16;
   const int64_t n = desc->node_count;
   std::vector<Val> values(n);
   std::vector<const tb_feed*> feed_of;
@@ -691,6 +725,11 @@ void oracle_gemm(const float* a, const float* b, float* c, int64_t m, int64_t k,
 }
 
 // libm scalar maps of payload/elementary.rs:116-143, for ulp measurements.
+// `Bf16::from_f32(x).to_f32()` per element (payload/bf16.rs:39-55).
+void oracle_round_bf16(const float* in, int64_t count, float* out) {
+  for (int64_t i = 0; i < count; ++i) out[i] = round_bf16(in[i]);
+}
+
 void oracle_map(int32_t op, const float* in, int64_t count, float* out) {
   for (int64_t i = 0; i < count; ++i) {
     float v = in[i];

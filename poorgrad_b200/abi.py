@@ -33,7 +33,7 @@ class TbNode(C.Structure):
 
 class TbPlanDesc(C.Structure):
     _fields_ = [("node_count", C.c_int64), ("nodes", C.POINTER(TbNode)),
-                ("backward", C.c_int32), ("numerics", C.c_int32)]
+                ("backward", C.c_int32), ("numerics", C.c_int32), ("element", C.c_int32)]
 
 
 class TbFeed(C.Structure):
@@ -91,7 +91,7 @@ class PackedPlan:
             rec.readable = columns.readable[index]
             rec.required = columns.required[index]
         self.desc = TbPlanDesc(len(nodes), self.array, int(columns.backward),
-                               int(columns.numerics))
+                               int(columns.numerics), int(getattr(columns, "element", 0)))
 
     def _payload(self, rec, payload):
         if isinstance(payload, Constant):

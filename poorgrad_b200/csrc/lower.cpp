@@ -278,6 +278,7 @@ class Lowerer {
 
   // ---- pass 1: load columns, expand LogSumExp / LogSoftmax into primitives
   void load(const tb_plan_desc* d) {
+    if (d->element != TB_ELEMENT_F32) fail("bf16 networks are not lowered for the device");
     const int64_t count = d->node_count;
     P.nodes.reserve(count * 2);
     for (int64_t i = 0; i < count; ++i) {

@@ -245,10 +245,18 @@ def infer_shape(name: str, attrs, shapes: List[tuple]) -> tuple:
     raise ValueError(name)
 
 
-class Tape:
-    """Records a static graph (`graph/tape.rs:49`)."""
+F32, BF16 = 0, 1  # payload element types (`Tensor<f32>`, `Tensor<Bf16>`: payload/bf16.rs)
 
-    def __init__(self):
+
+class Tape:
+    """Records a static graph (`graph/tape.rs:49`).  ``element`` is the
+    payload element type of the whole tape, as `Tape<Tensor<E>>` fixes it
+    in the reference: ``F32`` or ``BF16`` (payloads still travel as f32
+    arrays; a bf16 network rounds them on entry)."""
+
+    def __init__(self, element: int = F32):
+        assert element in (F32, BF16), element
+        self.element = element
         self.nodes: List[Node] = []
         self.parameter_payloads: List[Dense] = []
         self.input_payloads: list = []

@@ -60,6 +60,7 @@ class PlanColumns:
         self.observed = list(request.observe_)
         self.backward = bool(request.backward_)
         self.numerics = int(request.numerics_)
+        self.element = int(getattr(network.tape, "element", 0))
         wanted = [False] * length
         readable = [False] * length
         for index in self.roots + self.observed:
