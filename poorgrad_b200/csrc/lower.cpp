@@ -740,11 +740,14 @@ class Lowerer {
       if (nd.op == TB_OP_GATHER && k == 1) continue;
       if ((nd.op == TB_OP_BROADCAST || nd.op == TB_OP_BROADCAST_ALONG) && k == 1) continue;
       const Info& fo = P.info[o];
+      // a buffer is heavy for this value when it holds at least as many
+      // elements as the value: a per-row vector broadcast over a matrix is not
       if (fo.materialized || fo.kind == Kind::Layout) {
-        if (P.buffers[fo.buf].bytes / 4 * 4 >= vol) heavy.push_back(fo.buf);
+        if (P.buffers[fo.buf].bytes / 4 >= vol) heavy.push_back(fo.buf);
       } else if (fo.kind == Kind::Expr) {
         f.ops += fo.ops;
-        heavy.insert(heavy.end(), fo.heavy.begin(), fo.heavy.end());
+        for (int hb : fo.heavy)
+          if (P.buffers[hb].bytes / 4 >= vol) heavy.push_back(hb);
       }
     }
     std::sort(heavy.begin(), heavy.end());
