@@ -85,6 +85,9 @@ struct Member {
   MemberType type;
   int phase = 0;
   int hi = -1, lo = -1;  // PREP: operand buffers
+  // EW member of a row kernel that no other kernel reads: later phases take
+  // it from the thread's registers instead of a store and a reload
+  bool reg = false;
 };
 
 enum class KType {
@@ -105,6 +108,7 @@ struct Kernel {
   std::vector<Member> members;  // EW / ROW / REDUCE / SCATTER / FOLD
   std::vector<int64_t> space;   // iteration shape (EW/ROW)
   int node = -1;                // REDUCE/SCATTER/FOLD/GEMM: the node computed
+  int group = -1;               // EW/ROW: the fusion group it was flushed from
   // generated kernels
   std::string name, source;
   std::vector<int> params;      // buffer ids, in kernel parameter order

@@ -769,6 +769,11 @@ class Lowerer {
   std::vector<Group> groups;
   std::map<std::vector<int64_t>, int> open_group;
   std::vector<int> group_of;  // node -> group id
+  // materialized node -> the groups that read it (-1: a kernel of its own)
+  std::map<int, std::set<int>> readers;
+  void read_by(const std::vector<std::pair<int, int>>& r, int g) {
+    for (auto& nc : r) readers[nc.first].insert(g);
+  }
 
   void walk(int n, int ctx, std::set<std::pair<int, int>>& seen,
             std::vector<std::pair<int, int>>& out, bool is_root) {
@@ -846,6 +851,7 @@ class Lowerer {
     k.type = reductions ? KType::ROW : KType::EW;
     k.members = G.members;
     k.space = G.space;
+    k.group = g;
     P.kernels.push_back(k);
   }
 
@@ -936,6 +942,7 @@ class Lowerer {
     }
     for (int og : before)
       if (groups[og].open && og != g) groups[g].after.insert(og);
+    read_by(r, g);
     Member m{n, type, phase, hi, lo};
     if (!prep) {
       groups[g].index[n] = (int)groups[g].members.size();
@@ -947,6 +954,7 @@ class Lowerer {
 
   void own_kernel(int n, KType type) {
     auto r = refs(n);
+    read_by(r, -1);
     flush_refs(r);
     Kernel k;
     k.type = type;
@@ -976,6 +984,8 @@ class Lowerer {
               if (!prepared.count(base) && fusable_prep(base)) prepare(base, batch);
             }
           }
+          // the GEMM reads only tf32 pairs; what a pair is made from is read by
+          // the group or the prep kernel that writes it
           auto r = refs(n);
           flush_refs(r);
           matmul_kernels(n);
@@ -983,6 +993,7 @@ class Lowerer {
         }
         case TB_OP_SCATTER: {
           auto r = refs(n);
+          read_by(r, -1);
           flush_refs(r);
           int sel = nd.operands[1];
           if (!P.sort_of.count(sel)) {
@@ -1034,6 +1045,30 @@ class Lowerer {
       }
     }
     for (size_t g = 0; g < groups.size(); ++g) flush((int)g);
+    mark_register_members();
+  }
+
+  // An EW member of a row kernel read by no other kernel, not readable and
+  // not a view's storage, can stay in registers across the kernel's phases.
+  void mark_register_members() {
+    std::set<int> viewed;  // buffers other values are views of
+    for (size_t i = 0; i < P.nodes.size(); ++i) {
+      const Info& f = P.info[i];
+      if (f.kind == Kind::Layout && f.owner >= 0 && f.owner != (int)i) viewed.insert(f.owner);
+    }
+    for (Kernel& K : P.kernels) {
+      if (K.type != KType::ROW || K.group < 0) continue;
+      for (Member& m : K.members) {
+        if (m.type != MemberType::EW || P.nodes[m.node].readable || viewed.count(m.node)) continue;
+        if (P.info[m.node].owner != m.node) continue;
+        auto it = readers.find(m.node);
+        bool only_here = true;
+        if (it != readers.end())
+          for (int g : it->second)
+            if (g != K.group) only_here = false;
+        m.reg = only_here;
+      }
+    }
   }
 
   // A value prepared for the tensor cores: its tf32 hi/lo pairs in the value's
@@ -1096,6 +1131,8 @@ class Lowerer {
       prepared[base] = r;
       return r;
     }
+    if (P.info[base].materialized) readers[base].insert(-1);
+    else read_by(refs(base), -1);
     Kernel k;
     k.type = KType::PREP;
     k.node = base;
@@ -1169,6 +1206,7 @@ class Emitter {
   std::vector<std::unordered_map<std::string, std::string>> memo;
   std::map<int, int> param_of;   // buffer -> parameter position
   std::map<int, int> member_of;  // node -> member index (current kernel)
+  std::set<int> in_registers;    // member indices held in `kr<m>[kc * vec + lane]`
   int phase = 0;
   int tmp = 0;
   int indent = 2;
@@ -1259,6 +1297,9 @@ class Emitter {
       const Member& m = K.members[mit->second];
       if ((m.type == MemberType::ROW_SUM || m.type == MemberType::ROW_MAX) && m.phase < phase)
         return "rv" + std::to_string(mit->second);
+      if (in_registers.count(mit->second) && m.phase < phase)
+        return "kr" + std::to_string(mit->second) + "[kc * " + std::to_string(vec) + " + " +
+               std::to_string(idx.lane >= 0 ? idx.lane : 0) + "]";
     }
     if (f.kind == Kind::Sel && !f.materialized) {
       std::string v = var();
@@ -1776,6 +1817,15 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
       E.line("float ca" + std::to_string(m) + "[" + std::to_string(KC * vec) + "] = {0};");
     if (K.members[m].type == MemberType::ALL_SUM) E.line("float fa" + std::to_string(m) + " = 0.0f;");
   }
+  // EW members no other kernel reads and that a later phase uses stay in
+  // registers (fully unrolled passes index the arrays with constants)
+  for (size_t m = 0; m < K.members.size(); ++m) {
+    Member& mm = K.members[m];
+    if (KC * vec > 32) mm.reg = false;
+    if (!mm.reg) continue;
+    E.in_registers.insert((int)m);
+    E.line("float kr" + std::to_string(m) + "[" + std::to_string(KC * vec) + "];");
+  }
   hoist_uniform_scalars(P, K, E);
   E.line("for (I base = (I)blockIdx.x * " + std::to_string(teams) + "; base < " + lit(R) +
          "; base += (I)gridDim.x * " + std::to_string(teams) + ") {");
@@ -1854,6 +1904,12 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
     for (size_t m = 0; m < K.members.size(); ++m) {
       const Member& mm = K.members[m];
       if (mm.phase != ph || mm.type != MemberType::EW) continue;
+      if (E.in_registers.count((int)m)) {
+        for (int v = 0; v < vec; ++v)
+          E.line("kr" + std::to_string(m) + "[kc * " + std::to_string(vec) + " + " +
+                 std::to_string(v) + "] = " + vals[m][v] + ";");
+        continue;
+      }
       int buf = P.info[mm.node].buf;
       if (vec == 4) {
         E.line("*(float4*)(" + E.fptr(buf) + " + row * " + lit(L) + " + j0) = make_float4(" +
@@ -1867,7 +1923,8 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
     if (kc_full > 0) {
       E.line("if (act) {");
       E.indent += 2;
-      E.line(has_col ? "#pragma unroll" : (vec == 1 ? "#pragma unroll 8" : "#pragma unroll 4"));
+      E.line(has_col || !E.in_registers.empty() ? "#pragma unroll"
+                                                 : (vec == 1 ? "#pragma unroll 8" : "#pragma unroll 4"));
       E.line("for (int kc = 0; kc < " + std::to_string(kc_full) + "; ++kc) {");
       E.indent += 2;
       E.line("const I j0 = ((I)kc * " + std::to_string(T) + " + tl) * " + std::to_string(vec) + ";");
@@ -2300,6 +2357,21 @@ static void emit_prep(Program& P, Kernel& K, Emitter& E) {
 // and fails the compile): buffers whose kernel intervals intersect do not
 // share bytes, and every buffer of a side kernel stays allocated until the
 // side stream joins.
+// A row member held in registers has no storage: no kernel, its own
+// included, may name its buffer.  Checked before any device memory exists.
+static void check_register_members(const Program& P) {
+  std::set<int> held;
+  for (const Kernel& K : P.kernels)
+    for (const Member& m : K.members)
+      if (m.reg) held.insert(P.info[m.node].buf);
+  if (held.empty()) return;
+  for (const Kernel& K : P.kernels)
+    for (const std::vector<int>* list : {&K.reads, &K.writes})
+      for (int b : *list)
+        if (held.count(b))
+          fail("internal: the buffer of a register-held value is named by kernel " + K.name);
+}
+
 static void check_arena(const Program& P) {
   std::vector<int> placed;
   for (size_t i = 0; i < P.buffers.size(); ++i) {
@@ -2638,6 +2710,7 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
   P.fused_nodes = 0;
   for (int n : P.order)
     if (P.info[n].kind == Kind::Expr && !P.info[n].materialized) P.fused_nodes++;
+  check_register_members(P);
   plan_arena(P);
   check_arena(P);
   return prog;
