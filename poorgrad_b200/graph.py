@@ -501,13 +501,47 @@ class Value:
 
     def mean_along(self, axis):
         shape = self.shape
+        assert axis < len(shape), f"axis {axis} is out of rank for {shape}"
         extent = shape[axis]
         return self.sum_along(axis) / self.literal(counted(_without(shape, axis), extent))
+
+    def broadcast_to(self, shape):
+        """`graph/composite.rs:77-131`: right-aligned broadcasting composed
+        from `reshape` (prepended unit axes) and one `broadcast_along` per
+        repeated axis, or a single `broadcast_like` for one element."""
+        target, source = tuple(shape), self.shape
+        if source == target:
+            return self
+        assert len(target) >= len(source), f"broadcast to {target} from {source} lowers the rank"
+        offset = len(target) - len(source)
+        for axis, extent in enumerate(source):
+            aligned = target[offset + axis]
+            assert extent in (aligned, 1), \
+                (f"broadcast to {target} from {source} cannot align source axis {axis} "
+                 f"of extent {extent} to extent {aligned}")
+        if int(np.prod(source)) == 1:
+            return self.broadcast_like(self.literal(counted(target, 0)))
+        current = self if offset == 0 else self.reshape((1,) * offset + source)
+        for axis in range(len(target)):
+            if current.shape[axis] == target[axis]:
+                continue
+            widened = list(current.shape)
+            widened[axis] = target[axis]
+            current = current.squeeze(axis).broadcast_along(
+                axis, self.literal(counted(tuple(widened), 0)))
+        return current
 
 
 def concat(values: Sequence[Value], axis: int) -> Value:
     """`graph/composite.rs:142-176`: the sum of zero-padded windows."""
+    assert values, "concat needs at least one value"
     first = values[0]
+    assert axis < len(first.shape), f"concat axis {axis} is out of rank for {first.shape}"
+    for v in values:
+        off = [e for i, e in enumerate(v.shape) if i != axis]
+        assert len(v.shape) == len(first.shape) and off == [
+            e for i, e in enumerate(first.shape) if i != axis], \
+            "concat needs equal shapes off the axis"
     if len(values) == 1:
         return first
     combined = sum(v.shape[axis] for v in values)
