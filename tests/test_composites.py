@@ -172,3 +172,33 @@ def test_attention_heads_compose_with_a_loop_and_concat(built):
     assert np.allclose(out[output.index].reshape(-1)[:4], [1.0, 2.0, 2.0, 2.0], atol=1e-6)
     for g in grads[0::2]:
         assert np.any(g != 0.0)
+
+
+@pytest.mark.gpu
+def test_composites_on_the_device(device):
+    # the same compositions in one engine-backward plan on the device,
+    # against the oracle's values and reverse scan
+    from poorgrad_b200 import backend
+    rng = np.random.default_rng(4)
+    t = Tape()
+    a = t.parameter(tensor((2, 1, 8), rng.uniform(-1, 1, 16)))
+    b = t.parameter(tensor((8,), rng.uniform(-1, 1, 8)))
+    s = t.parameter(tensor((4, 8), rng.uniform(-2, 2, 32)))
+    mask = t.leaf(tensor((8,), [0.0] * 6 + [-np.inf] * 2))
+    grid = a.broadcast_to((2, 4, 8)) + b.broadcast_to((2, 4, 8))
+    probs = (s + mask.broadcast_to((4, 8))).softmax(1)
+    joined = concat([grid.reshape((8, 8)), probs.abs()], 0)
+    stacked = stack([probs, s.mean_along(0).broadcast_to((4, 8))], 0)
+    loss = (joined.tanh().sum() + stacked.logsumexp(2).sum())
+    net = t.into_network()
+    cols = net.compile(Request([loss, joined, stacked]).backward())
+    params = net.parameters()
+    ref = oracle.run(cols, params)
+    grads = oracle.backward(cols, params, loss, [a, b, s])
+    plan = backend.DevicePlan(cols)
+    dp = backend.DeviceParameters(plan, params)
+    plan.forward(dp, sync=True)
+    for v in (joined, stacked, loss):
+        np.testing.assert_allclose(plan.of(v), ref[v.index], rtol=4e-6, atol=1e-7)
+    for p, g in zip((a, b, s), grads):
+        np.testing.assert_allclose(plan.gradient(loss, p), g, rtol=1e-5, atol=1e-6)
