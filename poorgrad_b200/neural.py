@@ -93,6 +93,43 @@ def dropout(seed: int, keep: float):
     return draw
 
 
+def _fan_initializer(name: str, seed: int, weights):
+    """Rank-2 ``[inputs, outputs]`` weights drawn by ``weights(stream, shape)``
+    in f64, rank-1 biases zero (`neural/init.rs:145-216`); ``draw(shape,
+    f64=True)`` returns the f64 values, the default rounds them once to f32."""
+    stream = Stream(seed)
+
+    def draw(shape, f64: bool = False) -> np.ndarray:
+        shape = tuple(shape)
+        if len(shape) == 1:
+            out = np.zeros(shape)
+        elif len(shape) == 2:
+            out = weights(stream, shape).reshape(shape)
+        else:
+            raise AssertionError(f"{name} initialization expects rank-2 weights or rank-1 "
+                                 f"biases, got {shape}")
+        return out if f64 else out.astype(np.float32)
+    return draw
+
+
+def xavier(seed: int):
+    """`init::xavier`: uniform within ``±sqrt(6 / (inputs + outputs))``."""
+    return _fan_initializer("xavier", seed, lambda st, sh: (st.unit(sh[0] * sh[1]) * 2.0 - 1.0)
+                            * math.sqrt(6.0 / float(sh[0] + sh[1])))
+
+
+def kaiming(seed: int):
+    """`init::kaiming`: normal with deviation ``sqrt(2 / inputs)``."""
+    return _fan_initializer("kaiming", seed, lambda st, sh: st.standard_normal(sh[0] * sh[1])
+                            * math.sqrt(2.0 / float(sh[0])))
+
+
+def scaled(seed: int, gain: float):
+    """`init::scaled`: normal with deviation ``gain / sqrt(inputs)``."""
+    return _fan_initializer("scaled", seed, lambda st, sh: st.standard_normal(sh[0] * sh[1])
+                            * (gain / math.sqrt(float(sh[0]))))
+
+
 def integers(seed: int, high: int, n: int) -> np.ndarray:
     """Uniform integers ``0..high`` from one stream: ``floor(unit * high)``."""
     u = Stream(seed).unit(n)
@@ -144,6 +181,10 @@ class Activation:
     def express(self, x: Value) -> Value:
         return x.tanh() if self.kind == self.TANH else x.relu()
 
+    def gain(self) -> float:
+        """`Activation::gain` (activation.rs:31-36)."""
+        return 5.0 / 3.0 if self.kind == self.TANH else math.sqrt(2.0)
+
     def visit(self, visitor) -> None:
         pass
 
@@ -165,6 +206,37 @@ class Sequential:
     def express(self, x: Value) -> Value:
         for stage in self.stages:
             x = stage.express(x)
+        return x
+
+    def visit(self, visitor) -> None:
+        for index, stage in enumerate(self.stages):
+            visitor.enter(index)
+            stage.visit(visitor)
+            visitor.leave()
+
+
+class Mlp:
+    """`neural/mlp.rs`: Linear stages over consecutive widths, tanh between
+    them and none after the last; ``initializer(shape)`` draws each weight,
+    then its bias."""
+
+    def __init__(self, tape: Tape, sizes, initializer):
+        assert len(sizes) >= 2, "an MLP topology needs an input and an output width"
+        self.stages = []
+        for inputs, outputs in zip(sizes[:-1], sizes[1:]):
+            weights = np.asarray(initializer((inputs, outputs)), np.float32)
+            bias = np.asarray(initializer((outputs,)), np.float32)
+            self.stages.append(Linear(tape, weights, bias))
+
+    def parameters(self) -> List[Value]:
+        return [p for stage in self.stages for p in stage.parameters()]
+
+    def express(self, x: Value) -> Value:
+        last = len(self.stages) - 1
+        for index, stage in enumerate(self.stages):
+            x = stage.express(x)
+            if index != last:
+                x = x.tanh()
         return x
 
     def visit(self, visitor) -> None:
