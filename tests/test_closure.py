@@ -223,3 +223,37 @@ def test_engine_backward_plans_on_the_device_follow_the_engine_scan(device, name
     plan.forward(dp, sync=True)
     for p, e in zip(wrt, engine):
         np.testing.assert_allclose(plan.gradient(loss, p), e, rtol=1e-5, atol=1e-6)
+
+
+def test_a_recorded_training_loop_matches_the_engine_bitwise(built):
+    # differentiate_tests.rs:519-587: twelve SGD generations through the
+    # engine's reverse scan and through the recorded-gradient plan agree bit
+    # for bit
+    def build(t):
+        x = t.input(varied((4, 3), 1))
+        w = P(t, (3, 4), 2)
+        b = P(t, (4,), 3)
+        product = x.matmul(w)
+        hidden = (product + b.broadcast_along(0, product)).tanh()
+        head = P(t, (4, 2), 4)
+        return x, [w, b, head], hidden.matmul(head).log_softmax(1).sum()
+
+    te = Tape()
+    xe, pe, le = build(te)
+    ne = te.into_network()
+    engine_cols = ne.compile(Request([le]).backward())
+    tr = Tape()
+    xr, pr, lr = build(tr)
+    grads = tr.differentiate(lr, pr)
+    nr = tr.into_network()
+    recorded_cols = nr.compile(Request([lr] + grads))
+    es, rs = ne.parameters(), nr.parameters()
+    rate = np.float32(0.05)
+    for step in range(12):
+        batch = varied((4, 3), 10 + step).to_numpy().astype(np.float32)
+        eg = oracle.backward(engine_cols, es, le, pe, {xe: batch})
+        out = oracle.run(recorded_cols, rs, {xr: batch}, read=grads)
+        es = [(p - g.reshape(-1) * rate).astype(np.float32) for p, g in zip(es, eg)]
+        rs = [(p - out[g.index].reshape(-1) * rate).astype(np.float32) for p, g in zip(rs, grads)]
+        for a, b in zip(es, rs):
+            assert a.tobytes() == b.tobytes(), f"step {step}"
