@@ -49,3 +49,15 @@ def test_c2_is_one_fused_pass_over_x(built):
     text = backend.lower_describe(w.columns)
     first = text.splitlines()[0]
     assert first.startswith("0: row") and len(first.split("members=")[1].split()) >= 4
+
+
+def test_the_documented_rust_binding_declares_every_entry_point():
+    # the reference-side binding a maintainer adds stays
+    # in step with the header
+    import os
+    import re
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    text = open(os.path.join(root, "INTEGRATION.md")).read()
+    bound = set(re.findall(r"pub fn (tb_\w+)\(", text))
+    missing = sorted(set(abi.header_symbols()) - bound)
+    assert not missing, missing
