@@ -2664,7 +2664,7 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
     d << " members=";
     for (auto& m : K.members)
       d << m.node << (m.type == MemberType::PREP ? "prep" : "")
-        << (m.phase ? "p" + std::to_string(m.phase) : "") << " ";
+        << (m.phase ? "p" + std::to_string(m.phase) : "") << (m.reg ? "reg" : "") << " ";
     d << (K.exact ? "exact" : "tolerance");
     if (K.type == KType::PREP)
       d << " value=" << K.node << " [" << K.batch << "," << K.m << "," << K.kp << "]";
