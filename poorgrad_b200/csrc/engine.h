@@ -158,6 +158,9 @@ struct Program {
   std::vector<int> order;  // processing order (synthetic nodes included)
   int64_t arena_bytes = 0, unplanned_bytes = 0, fused_nodes = 0;
   bool exact = true;
+  // a bf16 network (payload/bf16.rs): values are bf16 numbers held in f32
+  // storage; every operation rounds its result once, accumulations round once
+  bool bf16 = false;
   int gemms = 0;
   // Side-stream kernels (the leading SORTs) run concurrently with the main
   // kernels before side_join, the first main kernel that uses what they wrote;
@@ -175,5 +178,7 @@ struct Program {
 
 // Lowers a plan descriptor; throws std::runtime_error on malformed input.
 std::unique_ptr<Program> lower(const tb_plan_desc* desc);
+// payload/bf16.rs:39-55: the nearest bf16 as an f32 (ties to even)
+float round_bf16(float v);
 
 }  // namespace tb

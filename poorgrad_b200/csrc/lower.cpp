@@ -278,7 +278,9 @@ class Lowerer {
 
   // ---- pass 1: load columns, expand LogSumExp / LogSoftmax into primitives
   void load(const tb_plan_desc* d) {
-    if (d->element != TB_ELEMENT_F32) fail("bf16 networks are not lowered for the device");
+    if (d->element != TB_ELEMENT_F32 && d->element != TB_ELEMENT_BF16)
+      fail("unknown element type " + std::to_string(d->element));
+    P.bf16 = d->element == TB_ELEMENT_BF16;
     const int64_t count = d->node_count;
     P.nodes.reserve(count * 2);
     for (int64_t i = 0; i < count; ++i) {
@@ -607,10 +609,10 @@ class Lowerer {
         case TB_OP_LEAF:
           if (nd.payload == TB_PAYLOAD_CONSTANT) {
             f.kind = Kind::Const;
-            f.c = nd.constant;
+            f.c = P.bf16 ? round_bf16(nd.constant) : nd.constant;
           } else if (nd.payload == TB_PAYLOAD_SELECTION) {
             f.kind = Kind::Sel;
-            f.one = nd.constant;
+            f.one = P.bf16 ? round_bf16(nd.constant) : nd.constant;
             f.buf = new_buffer(Storage::LeafIndices, nd.shape[0] * 4, n);
           } else if (nd.payload == TB_PAYLOAD_DENSE) {
             f.kind = Kind::Layout;
@@ -630,7 +632,7 @@ class Lowerer {
         case TB_OP_INPUT:
           if (nd.payload == TB_PAYLOAD_SELECTION) {
             f.kind = Kind::Sel;
-            f.one = nd.constant;
+            f.one = P.bf16 ? round_bf16(nd.constant) : nd.constant;
             f.buf = new_buffer(Storage::InputIndices, nd.shape[0] * 4, n, nd.slot);
           } else {
             f.kind = Kind::Layout;
@@ -659,6 +661,7 @@ class Lowerer {
       if (fa->kind == Kind::Const && (!binary || fb->kind == Kind::Const)) {
         f.kind = Kind::Const;
         f.c = fold_scalar(nd.op, fa->c, binary ? fb->c : 0.0f);
+        if (P.bf16) f.c = round_bf16(f.c);
         return;
       }
       expression(n);
@@ -707,7 +710,7 @@ class Lowerer {
           for (int64_t s = 1; s < extent; ++s)
             acc = nd.op == TB_OP_MAX_ALONG ? fmax_ref(acc, fa->c) : acc + fa->c;
           f.kind = Kind::Const;
-          f.c = acc;
+          f.c = P.bf16 ? round_bf16(acc) : acc;  // f32 accumulation, one rounding
           return;
         }
         f.kind = Kind::Expr;
@@ -1220,6 +1223,19 @@ class Emitter {
       if (K.members[i].type != MemberType::PREP) member_of[K.members[i].node] = (int)i;
   }
 
+  // a bf16 network holds bf16 values: a loaded value (a source, or a
+  // library kernel's f32 accumulation) and each operation's result round once;
+  // rounding is idempotent, so values already rounded pass unchanged
+  std::string rounded(const std::string& v) {
+    if (!P.bf16) return v;
+    const std::string k = "rb|" + v;
+    if (const std::string* hit = find(k)) return *hit;
+    std::string r = var("b");
+    line("const float " + r + " = tb_rb(" + v + ");");
+    memo.back()[k] = r;
+    return r;
+  }
+
   std::string pad() const { return std::string(indent, ' '); }
   void line(const std::string& s) { body << pad() << s << "\n"; }
   std::string var(const char* p = "v") { return std::string(p) + std::to_string(tmp++); }
@@ -1318,7 +1334,7 @@ class Emitter {
     }
     if (f.materialized || f.kind == Kind::Layout) {
       std::string v = load(f.buf, f.lay, idx);
-      return v;
+      return rounded(v);
     }
     std::string v = def(n, idx);
     memo.back()[k] = v;
@@ -1354,7 +1370,7 @@ class Emitter {
       int src = -1;
       for (size_t i = 0; i < P.buffers.size(); ++i)
         if (P.buffers[i].node == n && P.buffers[i].storage != Storage::Arena) src = (int)i;
-      return load(src, l, idx);
+      return rounded(load(src, l, idx));
     }
     if (is_elementwise(nd.op)) {
       std::string x = ref(a, idx);
@@ -1377,7 +1393,7 @@ class Emitter {
       }
       if (is_transcendental(nd.op)) exact = false;
       std::string v = var();
-      line("const float " + v + " = " + e + ";");
+      line("const float " + v + " = " + (P.bf16 ? "tb_rb(" + e + ")" : e) + ";");
       return v;
     }
     const Node& on = P.nodes[a >= 0 ? a : n];
@@ -1523,6 +1539,13 @@ __device__ __forceinline__ float tb_tf32(float x) {
   unsigned r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return __uint_as_float(r);
+}
+// the nearest bf16 as an f32 (ties to even; a NaN keeps its top half with a
+// mantissa bit forced on): a bf16 network's rounding of every result
+__device__ __forceinline__ float tb_rb(float x) {
+  const unsigned b = __float_as_uint(x);
+  return __uint_as_float(isnan(x) ? ((b >> 16) | 0x40u) << 16
+                                  : ((b + 0x7fffu + ((b >> 16) & 1u)) >> 16) << 16);
 }
 )";
 }
@@ -1774,7 +1797,9 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
     for (size_t m = 0; m < K.members.size(); ++m)
       if (K.members[m].type == MemberType::ROW_MAX) max_member[K.members[m].node] = (int)m;
     auto virt = [&](int n) { return !P.info[n].materialized; };
-    for (size_t m = 0; m < K.members.size(); ++m) {
+    // a bf16 network rounds exp(x - max) per element against the final max,
+    // which the online update cannot: its rows keep the two-pass form
+    for (size_t m = 0; m < K.members.size() && !P.bf16; ++m) {
       if (K.members[m].type != MemberType::ROW_SUM) continue;
       const int e = P.nodes[K.members[m].node].operands[0];
       if (P.nodes[e].op != TB_OP_EXP || !virt(e)) continue;
@@ -1995,6 +2020,8 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
         E.line("}");
         E.line("__syncthreads();");
       }
+      // f32 accumulation, one rounding (payload/tensor.rs:1085-1089)
+      if (P.bf16 && mm.type == MemberType::ROW_SUM) E.line("rv" + ms + " = tb_rb(rv" + ms + ");");
       E.line("if (act && tl == 0) " + E.fptr(P.info[mm.node].buf) + "[row] = rv" + ms + ";");
     }
   }
@@ -2091,7 +2118,7 @@ static void emit_reduce(Program& P, Kernel& K, Emitter& E) {
   E.pop();
   E.indent -= 2;
   E.line("}");
-  E.line(E.fptr(P.info[n].buf) + "[t] = acc;");
+  E.line(E.fptr(P.info[n].buf) + (P.bf16 ? "[t] = tb_rb(acc);" : "[t] = acc;"));
   E.indent -= 2;
   E.line("}");
 }
@@ -2164,7 +2191,7 @@ static void emit_fold(Program& P, Kernel& K, Emitter& E) {
   E.pop();
   E.indent -= 2;
   E.line("}");
-  E.line(E.fptr(P.info[n].buf) + "[t] = acc;");
+  E.line(E.fptr(P.info[n].buf) + (P.bf16 ? "[t] = tb_rb(acc);" : "[t] = acc;"));
   E.indent -= 2;
   E.line("}");
 }
@@ -2714,6 +2741,18 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
   plan_arena(P);
   check_arena(P);
   return prog;
+}
+
+// payload/bf16.rs:39-55: the nearest bf16 (ties to even, carried into the
+// exponent), as an f32; a NaN keeps its top half with a mantissa bit forced on.
+float round_bf16(float v) {
+  uint32_t bits;
+  std::memcpy(&bits, &v, 4);
+  const uint32_t out = std::isnan(v) ? ((bits >> 16) | 0x0040u) << 16
+                                     : ((bits + 0x7FFFu + ((bits >> 16) & 1u)) >> 16) << 16;
+  float r;
+  std::memcpy(&r, &out, 4);
+  return r;
 }
 
 }  // namespace tb

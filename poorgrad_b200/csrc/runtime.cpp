@@ -676,6 +676,10 @@ void read_value(tb_instance* plan, int64_t node, float* host, int64_t count) {
                         plan->stream),
         "read");
   check(cudaStreamSynchronize(plan->stream), "cudaStreamSynchronize");
+  // a bf16 network's values are bf16: a value a library kernel wrote (a GEMM,
+  // a column final, a segment sum) holds its f32 accumulation, rounded here
+  if (plan->prog->bf16)
+    for (int64_t i = 0; i < count; ++i) host[i] = tb::round_bf16(host[i]);
 }
 
 void run_plan(tb_instance* plan) {
@@ -737,7 +741,7 @@ int tb_status(char* message, size_t capacity) {
 int tb_plan_compile(const tb_plan_desc* desc, tb_plan** out) {
   return guarded([&]() {
     if (desc->element != TB_ELEMENT_F32) {
-      g_error = "bf16 networks are not lowered for the device; the caller computes them";
+      g_error = "bf16 networks are lowered but not yet run on the device; the caller computes them";
       return (int)TB_DECLINED;
     }
     auto prog = tb::lower(desc);
@@ -940,6 +944,7 @@ int tb_optimizer_create(tb_plan* owner, tb_params* params, const tb_optimizer_de
   return guarded([&]() {
     tb_instance* plan = owner->main.get();
     if (desc->kind < 0 || desc->kind > 2) throw Failure(TB_INVALID, "unknown optimizer kind");
+    if (plan->prog->bf16) throw Failure(TB_DECLINED, "the device optimizer steps f32 parameters");
     bind_params(plan, params);
     std::unique_ptr<tb_optimizer> o(new tb_optimizer());
     o->plan = plan;
@@ -1134,6 +1139,7 @@ void tb_comm_destroy(tb_comm* comm) { delete comm; }
 int tb_plan_attach_comm(tb_plan* owner, tb_comm* comm, int64_t bucket_bytes) {
   return guarded([&]() {
     tb_instance* plan = owner->main.get();
+    if (plan->prog->bf16) throw Failure(TB_DECLINED, "the gradient exchange sums f32 gradients");
     plan->comm = comm;
     plan->bucket_bytes = bucket_bytes > 0 ? bucket_bytes : (int64_t)32 << 20;
     plan->graph_dirty = true;

@@ -2,8 +2,10 @@
 of payload/tests/bf16_tests.rs: rounding to nearest with ties to even, each
 payload operation rounding its f32 result once, products, reductions and
 scatters accumulating in f32 and rounding once, and networks differentiating
-in bf16.  The device declines bf16 plans (the reference's `None`): the
-caller computes them."""
+in bf16.  The device lowering of bf16 plans rounds every result and load in
+the generated kernels; until that path has run against the oracle on a GPU,
+the device declines bf16 plans (the reference's `None`) and the caller
+computes them."""
 import struct
 
 import numpy as np
@@ -181,3 +183,34 @@ def test_the_device_declines_bf16_networks(device):
     with pytest.raises(backend.BackendError) as declined:
         backend.DevicePlan(t.into_network().compile(Request([y])))
     assert declined.value.code == 5 and "bf16" in str(declined.value)
+
+
+def _mixed_network(element):
+    from poorgrad_b200 import neural
+    rng = np.random.default_rng(6)
+    t = Tape(element)
+    x = t.input(tensor((64, 32), rng.uniform(-1, 1, 64 * 32)))
+    w = t.parameter(tensor((32, 32), rng.uniform(-0.3, 0.3, 32 * 32)))
+    ln = neural.LayerNorm(t, 32)
+    h = ln.express(x.matmul(w)).tanh()
+    table = t.parameter(tensor((10, 32), rng.uniform(-1, 1, 320)))
+    sel = t.input(selection(rng.integers(0, 10, 64).tolist(), 10))
+    g = h + table.gather(sel)
+    loss = (g.log_softmax(1) * g).sum() + g.logsumexp(1).sum()
+    grads = t.differentiate(loss, [w, table] + ln.parameters())
+    return t.into_network().compile(Request([loss] + grads))
+
+
+def test_bf16_plans_lower_with_rounding_and_compile(built):
+    # the device lowering of a bf16 network: every generated kernel rounds
+    # its results (`tb_rb`), log-sum-exp rows keep the two-pass form, and the
+    # source compiles for sm_100a; f32 plans carry no rounding
+    from poorgrad_b200 import backend
+    bf = _mixed_network(BF16)
+    text = backend.lower_describe(bf, with_source=True)
+    bodies = text.split("extern \"C\" __global__")[1:]
+    assert bodies and all("tb_rb(" in b for b in bodies)
+    assert "tb_lse_push(" not in "".join(bodies)
+    backend.nvrtc_check(bf)
+    f32 = backend.lower_describe(_mixed_network(0), with_source=True)
+    assert all("tb_rb(" not in b for b in f32.split("extern \"C\" __global__")[1:])
