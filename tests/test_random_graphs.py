@@ -11,17 +11,17 @@ import pytest
 
 import oracle
 from poorgrad_b200 import backend
-from poorgrad_b200.graph import Tape, selection, tensor
+from poorgrad_b200.graph import BF16, Tape, selection, tensor
 from poorgrad_b200.plan import Request
 
 SEEDS = list(range(24))
 
 
-def random_graph(seed):
+def random_graph(seed, element=0):
     rng = np.random.default_rng(seed)
     rows = int(rng.choice([4, 64, 96]))
     cols = int(rng.choice([8, 32, 48]))
-    t = Tape()
+    t = Tape(element)
     params = [t.parameter(tensor((rows, cols), rng.uniform(-1, 1, rows * cols))),
               t.parameter(tensor((cols,), rng.uniform(-1, 1, cols))),
               t.parameter(tensor((cols, cols), rng.uniform(-0.5, 0.5, cols * cols)))]
@@ -73,6 +73,17 @@ def test_random_graph_lowers_and_compiles(built, seed):
     backend.nvrtc_check(cols)
     out = oracle.run(cols, net.parameters(), read=[loss] + grads)
     assert np.isfinite(out[loss.index]).all()
+
+
+@pytest.mark.parametrize("seed", SEEDS[:8])
+def test_random_bf16_graph_lowers_with_rounding_and_compiles(built, seed):
+    net, cols, loss, grads = random_graph(seed, BF16)
+    text = backend.lower_describe(cols, with_source=True)
+    assert text.count("tb_rb(") > 1  # beyond the prelude's definition
+    backend.nvrtc_check(cols)
+    out = oracle.run(cols, net.parameters(), read=[loss] + grads)
+    for v in out.values():
+        assert oracle.round_bf16(v).tobytes() == v.tobytes()
 
 
 @pytest.mark.gpu
