@@ -18,6 +18,7 @@
 #include <sstream>
 #include <stdexcept>
 #include <string>
+#include <set>
 #include <vector>
 
 #include "engine.h"
@@ -1189,6 +1190,24 @@ int64_t tbx_lower_describe(const tb_plan_desc* desc, char* buffer, size_t capaci
           if (w == (int)b) writer = (int)k;
       o << "keep buffer " << b << " node " << buf.node << " offset " << buf.offset << " bytes "
         << buf.bytes << " writer " << writer << "\n";
+    }
+    // a value's buffer written by a kernel and read by no other kernel, and not
+    // a result: a store nobody needs, or a round trip through memory inside its
+    // own kernel (a kernel's parameter is listed as written when it writes it).
+    // Scratch such as split-K partials is used inside its own launch and is not
+    // listed.
+    for (size_t b = 0; b < prog->buffers.size(); ++b) {
+      const tb::Buffer& buf = prog->buffers[b];
+      if (buf.keep || buf.node < 0) continue;
+      std::set<int> writers, readers;
+      for (size_t k = 0; k < prog->kernels.size(); ++k) {
+        for (int w : prog->kernels[k].writes)
+          if (w == (int)b) writers.insert((int)k);
+        for (int r : prog->kernels[k].reads)
+          if (r == (int)b) readers.insert((int)k);
+      }
+      if (!writers.empty() && readers.empty())
+        o << "dead buffer " << b << " node " << buf.node << " bytes " << buf.bytes << "\n";
     }
     if (with_source) o << prog->source;
     std::string s = o.str();

@@ -61,3 +61,16 @@ def test_gemm_tile_and_split_rules(built):
     assert lib.tbx_gemm_splits(1, 16384, 512, 512) == 1
     # narrow outputs take the 128-wide tile: 4 tiles -> 37 splits
     assert lib.tbx_gemm_splits(1, 512, 27, 16384) == 37
+
+
+@pytest.mark.parametrize("name", ["mlp", "fused", "gemm", "charmlp", "gpt2"])
+def test_no_config_stores_a_large_value_nobody_reads(built, name):
+    # a full-size value that no other kernel reads (not a result) is a store
+    # nobody needs or a round trip through memory inside its own kernel: the
+    # waste of materializing broadcast row statistics and phase-crossing
+    # values.  What remains are per-row statistics the kernel also keeps in
+    # registers.
+    from poorgrad_b200 import backend, configs
+    w = configs.BUILDERS[name]()
+    dead = [l for l in backend.lower_describe(w.columns).splitlines() if l.startswith("dead")]
+    assert all(int(l.split()[-1]) < (1 << 20) for l in dead), dead
