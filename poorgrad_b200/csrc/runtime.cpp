@@ -721,6 +721,37 @@ void run_plan(tb_instance* plan) {
 
 }  // namespace
 
+namespace {
+void json_str(std::ostringstream& o, const std::string& s) {
+  o << '"';
+  for (char c : s) {
+    switch (c) {
+      case '"': o << "\\\""; break;
+      case '\\': o << "\\\\"; break;
+      case '\n': o << "\\n"; break;
+      case '\t': o << "\\t"; break;
+      default:
+        if ((unsigned char)c < 0x20) {
+          char b[8];
+          snprintf(b, sizeof b, "\\u%04x", c);
+          o << b;
+        } else {
+          o << c;
+        }
+    }
+  }
+  o << '"';
+}
+
+template <class T>
+void json_list(std::ostringstream& o, const std::vector<T>& v) {
+  o << '[';
+  for (size_t i = 0; i < v.size(); ++i) o << (i ? "," : "") << v[i];
+  o << ']';
+}
+
+}  // namespace
+
 extern "C" {
 
 const char* tb_last_error(void) { return g_error.c_str(); }
@@ -1210,6 +1241,65 @@ int64_t tbx_lower_describe(const tb_plan_desc* desc, char* buffer, size_t capaci
         o << "dead buffer " << b << " node " << buf.node << " bytes " << buf.bytes << "\n";
     }
     if (with_source) o << prog->source;
+    std::string s = o.str();
+    if (buffer && capacity) snprintf(buffer, capacity, "%s", s.c_str());
+    return (int64_t)s.size() + 1;
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return -1;
+  }
+}
+
+// The lowered program as JSON, for the host-side kernel emulator of the
+// tests: kernels in order with their buffers and launch shapes, the buffer
+// table, the buffers of readable values, and the emitted source.
+int64_t tbx_lower_json(const tb_plan_desc* desc, char* buffer, size_t capacity) {
+  try {
+    auto prog = tb::lower(desc);
+    static const char* types[] = {"ew", "row", "reduce", "prep", "gemm", "sort", "scatter",
+                                  "fold", "final", "segsum"};
+    std::ostringstream o;
+    o << "{\"bf16\":" << (prog->bf16 ? 1 : 0) << ",\"kernels\":[";
+    for (size_t k = 0; k < prog->kernels.size(); ++k) {
+      const tb::Kernel& K = prog->kernels[k];
+      o << (k ? "," : "") << "{\"type\":\"" << types[(int)K.type] << "\",\"name\":";
+      json_str(o, K.name);
+      o << ",\"grid\":" << K.grid << ",\"block\":" << K.block << ",\"params\":";
+      json_list(o, K.params);
+      o << ",\"a_hi\":" << K.a_hi << ",\"a_lo\":" << K.a_lo << ",\"b_hi\":" << K.b_hi
+        << ",\"b_lo\":" << K.b_lo << ",\"out\":" << K.out << ",\"batch\":" << K.batch
+        << ",\"m\":" << K.m << ",\"n\":" << K.n << ",\"k\":" << K.k << ",\"kp\":" << K.kp
+        << ",\"a_mn\":" << K.a_mn << ",\"b_mn\":" << K.b_mn << ",\"a_ld\":" << K.a_ld
+        << ",\"b_ld\":" << K.b_ld << ",\"a_rows\":" << K.a_rows << ",\"b_rows\":" << K.b_rows
+        << ",\"keys\":" << K.keys << ",\"vals\":" << K.vals << ",\"rstart\":" << K.rstart
+        << ",\"rend\":" << K.rend << ",\"count\":" << K.count << ",\"rows\":" << K.rows
+        << ",\"partial\":" << K.partial << ",\"final_out\":" << K.final_out
+        << ",\"final_blocks\":" << K.final_blocks << ",\"final_width\":" << K.final_width
+        << ",\"final_parts\":";
+      json_list(o, K.final_parts);
+      o << ",\"final_outs\":";
+      json_list(o, K.final_outs);
+      o << ",\"final_widths\":";
+      json_list(o, K.final_widths);
+      o << "}";
+    }
+    o << "],\"buffers\":[";
+    for (size_t b = 0; b < prog->buffers.size(); ++b) {
+      const tb::Buffer& B = prog->buffers[b];
+      o << (b ? "," : "") << "{\"storage\":" << (int)B.storage << ",\"bytes\":" << B.bytes
+        << ",\"slot\":" << B.slot << ",\"node\":" << B.node << "}";
+    }
+    o << "],\"readable\":{";
+    bool first = true;
+    for (size_t n = 0; n < prog->nodes.size(); ++n) {
+      const tb::Info& f = prog->info[n];
+      if (!prog->nodes[n].readable || !f.materialized || f.owner != (int)n) continue;
+      o << (first ? "" : ",") << "\"" << n << "\":" << f.buf;
+      first = false;
+    }
+    o << "},\"source\":";
+    json_str(o, prog->source);
+    o << "}";
     std::string s = o.str();
     if (buffer && capacity) snprintf(buffer, capacity, "%s", s.c_str());
     return (int64_t)s.size() + 1;

@@ -1,0 +1,58 @@
+"""Whole lowered device programs run on the host by the kernel emulator
+(`tests/kernel_emulator.py`), against the oracle: the emitted kernels (fusion
+groups and their phases, register-held values, column and full sums, preps,
+gather and scatter) and the data flow between them, checked without a GPU.
+The library kernels are restated in the emulator from their contracts, so
+GEMM results agree within the product's tolerance, not bitwise.
+
+bf16 networks, which the device declines until they have run on a GPU, are
+checked here end to end: their emulated programs equal the bf16 oracle
+bitwise on these cases."""
+import numpy as np
+import pytest
+
+import kernel_emulator
+import oracle
+from poorgrad_b200 import configs
+from poorgrad_b200.graph import BF16
+
+from test_bf16 import _mixed_network
+from test_random_graphs import random_graph
+
+
+def compare(cols, params, feeds=None, tol=3e-5, bitwise=False):
+    out = kernel_emulator.run_program(cols, params, feeds)
+    ref = oracle.run(cols, params, feeds)
+    assert out
+    for node, v in out.items():
+        r = ref[node]
+        if bitwise:
+            assert v.tobytes() == r.tobytes(), node
+        else:
+            scale = max(1.0, float(np.abs(r).max()))
+            np.testing.assert_allclose(v, r, rtol=0, atol=tol * scale, err_msg=str(node))
+
+
+@pytest.mark.parametrize("name,kw", [
+    ("mlp", dict(batch=16)), ("charmlp", dict(batch=32)), ("fused", dict(rows=32, cols=64)),
+    ("gpt2", dict(batch=1, seq=8, layers=1, d=16, heads=2, vocab=11, mlp=32))])
+def test_config_programs_follow_the_oracle(built, name, kw):
+    w = configs.BUILDERS[name](**kw)
+    compare(w.columns, w.network.parameters(), w.feeds(0) if w.feeds else None)
+
+
+@pytest.mark.parametrize("seed", [0, 3, 7, 11, 17, 22])
+def test_random_programs_follow_the_oracle(built, seed):
+    net, cols, _, _ = random_graph(seed)
+    compare(cols, net.parameters())
+
+
+@pytest.mark.parametrize("seed", [1, 4, 8, 12, 18, 23])
+def test_random_bf16_programs_equal_the_bf16_oracle(built, seed):
+    net, cols, _, _ = random_graph(seed, BF16)
+    compare(cols, net.parameters(), bitwise=True)
+
+
+def test_bf16_layer_norm_gather_and_softmax_program_equals_the_bf16_oracle(built):
+    cols = _mixed_network(BF16)
+    compare(cols, cols.network.parameters(), bitwise=True)
