@@ -1294,10 +1294,19 @@ int64_t tbx_lower_json(const tb_plan_desc* desc, char* buffer, size_t capacity) 
     for (size_t n = 0; n < prog->nodes.size(); ++n) {
       const tb::Info& f = prog->info[n];
       if (!prog->nodes[n].readable || !f.materialized || f.owner != (int)n) continue;
-      o << (first ? "" : ",") << "\"" << n << "\":" << f.buf;
+      o << (first ? "" : ",") << "\"" << n << "\":[" << f.buf << ",";
+      json_list(o, prog->nodes[n].dims());
+      o << "]";
       first = false;
     }
-    o << "},\"source\":";
+    o << "},\"gradients\":[";
+    bool any = false;
+    for (const auto& g : prog->gradient_of) {
+      o << (any ? "," : "") << "[" << g.first.first << "," << g.first.second << "," << g.second
+        << "]";
+      any = true;
+    }
+    o << "],\"source\":";
     json_str(o, prog->source);
     o << "}";
     std::string s = o.str();

@@ -106,9 +106,11 @@ def _operand(hi, lo, mn, ld, rows, batch, outer, inner):
     return h[:, :outer, :inner], l_[:, :outer, :inner]
 
 
-def run_program(columns, parameters, feeds=None) -> dict:
+def run_program(columns, parameters, feeds=None, gradients=False):
     """Runs the lowered program of `columns` on the host; returns
-    ``{node_index: ndarray}`` for every readable value."""
+    ``{node_index: ndarray}`` for every readable value (the lowered program's
+    node numbering: an engine-backward plan's gradients are appended nodes).
+    With ``gradients``, also ``{(root, parameter): node}`` of such a plan."""
     from poorgrad_b200.graph import Constant, Dense, Selection
     prog = lowered(columns)
     kernels, buffers = prog["kernels"], prog["buffers"]
@@ -198,8 +200,10 @@ def run_program(columns, parameters, feeds=None) -> dict:
             raise NotImplementedError(f"kernel type {t}")
 
     results = {}
-    for node, b in prog["readable"].items():
-        shape = nodes[int(node)].shape
+    for node, (b, shape) in prog["readable"].items():
+        shape = tuple(shape)
         v = f32(b)[: int(np.prod(shape)) if shape else 1].copy().reshape(shape)
         results[int(node)] = _round_bf16(v) if prog["bf16"] else v
+    if gradients:
+        return results, {(r, p): n for r, p, n in prog["gradients"]}
     return results

@@ -7,16 +7,19 @@ GEMM results agree within the product's tolerance, not bitwise.
 
 bf16 networks, which the device declines until they have run on a GPU, are
 checked here end to end: their emulated programs equal the bf16 oracle
-bitwise on these cases."""
+bitwise on these cases.  Engine-backward plans (the reverse scan appended by
+the lowering) follow the oracle's restatement of `Run::backward`."""
 import numpy as np
 import pytest
 
 import kernel_emulator
 import oracle
 from poorgrad_b200 import configs
-from poorgrad_b200.graph import BF16
+from poorgrad_b200.graph import BF16, Tape
+from poorgrad_b200.plan import Request
 
 from test_bf16 import _mixed_network
+from test_closure import CASES
 from test_random_graphs import random_graph
 
 
@@ -56,3 +59,19 @@ def test_random_bf16_programs_equal_the_bf16_oracle(built, seed):
 def test_bf16_layer_norm_gather_and_softmax_program_equals_the_bf16_oracle(built):
     cols = _mixed_network(BF16)
     compare(cols, cols.network.parameters(), bitwise=True)
+
+
+@pytest.mark.parametrize("name", sorted(CASES))
+def test_engine_backward_programs_follow_the_engine_scan(built, name):
+    # the reverse scan the lowering appends for `Request::backward`, run on
+    # the host, against the oracle's restatement of `Run::backward`
+    t = Tape()
+    loss, wrt = CASES[name](t)
+    net = t.into_network()
+    cols = net.compile(Request([loss]).backward())
+    params = net.parameters()
+    out, grads = kernel_emulator.run_program(cols, params, gradients=True)
+    scan = oracle.backward(cols, params, loss, wrt)
+    for p, ref in zip(wrt, scan):
+        got = out[grads[(loss.index, p.index)]]
+        np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-6)
