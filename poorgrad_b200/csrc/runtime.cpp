@@ -1292,8 +1292,10 @@ int64_t tbx_lower_json(const tb_plan_desc* desc, char* buffer, size_t capacity) 
     o << "],\"readable\":{";
     bool first = true;
     for (size_t n = 0; n < prog->nodes.size(); ++n) {
-      const tb::Info& f = prog->info[n];
-      if (!prog->nodes[n].readable || !f.materialized || f.owner != (int)n) continue;
+      // as readable_buffer answers: through the alias of an expanded node
+      const int r = resolve_node(*prog, (int64_t)n);
+      const tb::Info& f = prog->info[r];
+      if (!prog->nodes[r].readable || !f.materialized || f.owner != r) continue;
       o << (first ? "" : ",") << "\"" << n << "\":[" << f.buf << ",";
       json_list(o, prog->nodes[n].dims());
       o << "]";
