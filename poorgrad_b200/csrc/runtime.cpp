@@ -1259,7 +1259,8 @@ int64_t tbx_lower_json(const tb_plan_desc* desc, char* buffer, size_t capacity) 
     static const char* types[] = {"ew", "row", "reduce", "prep", "gemm", "sort", "scatter",
                                   "fold", "final", "segsum"};
     std::ostringstream o;
-    o << "{\"bf16\":" << (prog->bf16 ? 1 : 0) << ",\"kernels\":[";
+    o << "{\"bf16\":" << (prog->bf16 ? 1 : 0) << ",\"arena_bytes\":" << prog->arena_bytes
+      << ",\"kernels\":[";
     for (size_t k = 0; k < prog->kernels.size(); ++k) {
       const tb::Kernel& K = prog->kernels[k];
       o << (k ? "," : "") << "{\"type\":\"" << types[(int)K.type] << "\",\"name\":";
@@ -1287,7 +1288,8 @@ int64_t tbx_lower_json(const tb_plan_desc* desc, char* buffer, size_t capacity) 
     for (size_t b = 0; b < prog->buffers.size(); ++b) {
       const tb::Buffer& B = prog->buffers[b];
       o << (b ? "," : "") << "{\"storage\":" << (int)B.storage << ",\"bytes\":" << B.bytes
-        << ",\"slot\":" << B.slot << ",\"node\":" << B.node << "}";
+        << ",\"slot\":" << B.slot << ",\"node\":" << B.node << ",\"offset\":" << B.offset
+        << ",\"placed\":" << (B.first >= 0 ? 1 : 0) << "}";
     }
     o << "],\"readable\":{";
     bool first = true;

@@ -13,9 +13,9 @@ kernels are restated here in numpy from their contracts:
 - column finals: the per-block partials summed in f32.
 
 Buffers start as the runtime stages them (parameters, feeds or initial
-payloads, leaves; the arena zeroed), but each buffer gets its own memory: the
-arena's reuse is checked by the lowering itself, not here.  The product never
-uses this module.
+payloads, leaves), and the arena's buffers sit at their planned offsets in one
+array, as on the device: a buffer reused while still live clobbers a value and
+shows as a wrong result.  The product never uses this module.
 """
 from __future__ import annotations
 
@@ -131,10 +131,14 @@ def run_program(columns, parameters, feeds=None, gradients=False):
         a = np.asarray(payload)
         return np.ascontiguousarray(a, np.int32 if a.dtype == np.int32 else np.float32).reshape(-1)
 
+    arena = np.zeros(max(prog["arena_bytes"], 16), np.uint8)
     mem = []
     for b in buffers:
-        raw = np.zeros(max(b["bytes"], 16), np.uint8)
         st, n = b["storage"], b["node"]
+        if st == ARENA and b["placed"]:
+            mem.append(arena[b["offset"]: b["offset"] + max(b["bytes"], 4)])
+            continue
+        raw = np.zeros(max(b["bytes"], 16), np.uint8)
         if st == PARAMETER:
             src = np.ascontiguousarray(parameters[b["slot"]], np.float32).reshape(-1)
         elif st in (INPUT, INPUT_INDICES):
