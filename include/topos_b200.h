@@ -69,9 +69,9 @@ enum { TB_NUMERICS_FAST = 0, TB_NUMERICS_EXACT = 1 };
  * rounds every payload operation's f32 result once to the nearest bf16 (ties to even,
  * bf16.rs:39-50) and accumulates products, sums, folds and scatters in f32 before one
  * rounding (tensor.rs:1015-1022, 1055-1093, 1431-1451, 1605-1616; gemm.rs:149-161).  Values
- * cross this ABI in f32 containers holding bf16 values.  The lowering handles bf16 plans
- * (rounded results and loads in every generated kernel), but tb_plan_compile still answers
- * TB_DECLINED for them until the device path has been checked against the oracle on a GPU. */
+ * cross this ABI in f32 containers holding bf16 values: every generated kernel rounds its
+ * results and loads, reads round on the host.  The optimizer (tb_optimizer_create) and the
+ * gradient exchange (tb_plan_attach_comm) answer TB_DECLINED for bf16 plans. */
 enum { TB_ELEMENT_F32 = 0, TB_ELEMENT_BF16 = 1 };
 
 #define TB_MAX_RANK 8

@@ -772,10 +772,6 @@ int tb_status(char* message, size_t capacity) {
 
 int tb_plan_compile(const tb_plan_desc* desc, tb_plan** out) {
   return guarded([&]() {
-    if (desc->element != TB_ELEMENT_F32) {
-      g_error = "bf16 networks are lowered but not yet run on the device; the caller computes them";
-      return (int)TB_DECLINED;
-    }
     auto prog = tb::lower(desc);
     if (desc->numerics == TB_NUMERICS_EXACT && !prog->exact) {
       g_error = "the plan holds kernels that are not bit-identical to the interpreter";

@@ -3,9 +3,10 @@ of payload/tests/bf16_tests.rs: rounding to nearest with ties to even, each
 payload operation rounding its f32 result once, products, reductions and
 scatters accumulating in f32 and rounding once, and networks differentiating
 in bf16.  The device lowering of bf16 plans rounds every result and load in
-the generated kernels; until that path has run against the oracle on a GPU,
-the device declines bf16 plans (the reference's `None`) and the caller
-computes them."""
+the generated kernels; on the device a bf16 plan follows the bf16 oracle
+within a few bf16 ulps (the reassociated f32 accumulations may round the
+other way), and the emulated programs equal it bitwise
+(`tests/test_emulated_programs.py`)."""
 import struct
 
 import numpy as np
@@ -175,14 +176,26 @@ def test_recorded_gradients_close_in_bf16(built):
 
 
 @pytest.mark.gpu
-def test_the_device_declines_bf16_networks(device):
+def test_bf16_plans_on_the_device_follow_the_bf16_oracle(device):
+    # values and gradients are bf16 numbers and agree with the oracle within
+    # a few bf16 ulps of each output's scale; the optimizer declines
     from poorgrad_b200 import backend
-    t = Tape(BF16)
-    x = t.parameter(tensor((4,), [1.0, 2.0, 3.0, 4.0]))
-    y = (x * x).sum()
+    cols = _mixed_network(BF16)
+    params = cols.network.parameters()
+    ref = oracle.run(cols, params)
+    plan = backend.DevicePlan(cols)
+    dp = backend.DeviceParameters(plan, params)
+    plan.forward(dp, sync=True)
+    for node, r in ref.items():
+        if not cols.readable[node]:
+            continue
+        got = plan.of(node)
+        assert oracle.round_bf16(got).tobytes() == got.tobytes()
+        scale = max(1.0, float(np.abs(r).max()))
+        np.testing.assert_allclose(got, r, rtol=0, atol=2.0 ** -5 * scale)
     with pytest.raises(backend.BackendError) as declined:
-        backend.DevicePlan(t.into_network().compile(Request([y])))
-    assert declined.value.code == 5 and "bf16" in str(declined.value)
+        backend.Optimizer(plan, dp, backend.SGD, [], 0.1)
+    assert declined.value.code == 5
 
 
 def _mixed_network(element):
