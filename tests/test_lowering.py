@@ -74,3 +74,17 @@ def test_no_config_stores_a_large_value_nobody_reads(built, name):
     w = configs.BUILDERS[name]()
     dead = [l for l in backend.lower_describe(w.columns).splitlines() if l.startswith("dead")]
     assert all(int(l.split()[-1]) < (1 << 20) for l in dead), dead
+
+
+def test_values_past_two_to_the_31_elements_index_in_64_bits(built):
+    # a [65536, 40000] input (2.6e9 elements; a constant payload, so nothing
+    # is allocated): its kernels take 64-bit indices and still compile
+    from poorgrad_b200.graph import Tape, filled
+    from poorgrad_b200.plan import Request
+    t = Tape()
+    x = t.input(filled((65536, 40000), 1.0))
+    rows = (x * x.literal(filled((65536, 40000), 0.5))).tanh().sum_along(1)
+    cols = t.into_network().compile(Request([rows]))
+    text = backend.lower_describe(cols, with_source=True)
+    assert "typedef long long I;" in text
+    backend.nvrtc_check(cols)
