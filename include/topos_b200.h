@@ -70,8 +70,9 @@ enum { TB_NUMERICS_FAST = 0, TB_NUMERICS_EXACT = 1 };
  * bf16.rs:39-50) and accumulates products, sums, folds and scatters in f32 before one
  * rounding (tensor.rs:1015-1022, 1055-1093, 1431-1451, 1605-1616; gemm.rs:149-161).  Values
  * cross this ABI in f32 containers holding bf16 values: every generated kernel rounds its
- * results and loads, reads round on the host.  The optimizer (tb_optimizer_create) and the
- * gradient exchange (tb_plan_attach_comm) answer TB_DECLINED for bf16 plans. */
+ * results and loads, parameter uploads and reads round on the host, and the optimizer steps
+ * in bf16 with bf16 hyperparameters (note that 0.999 rounds to 1 in bf16).  The gradient
+ * exchange (tb_plan_attach_comm) answers TB_DECLINED for bf16 plans. */
 enum { TB_ELEMENT_F32 = 0, TB_ELEMENT_BF16 = 1 };
 
 #define TB_MAX_RANK 8

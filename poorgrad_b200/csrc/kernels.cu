@@ -11,6 +11,7 @@
 
 #include "kernels.h"
 #include "launch.h"
+#include "optimizer_rule.h"
 
 namespace tb {
 namespace {
@@ -507,25 +508,32 @@ __global__ void __launch_bounds__(256) k_gemm_simt(const float* __restrict__ ahi
   }
 }
 
+template <bool BF16>
 __global__ void k_adam_scalars(float* s, float beta1, float beta2) {
   pdl_entry();
-  if (threadIdx.x == 0 && blockIdx.x == 0) {
-    s[0] = __fmul_rn(s[0], beta1);
-    s[1] = __fmul_rn(s[1], beta2);
-    s[2] = __fsub_rn(1.0f, s[0]);
-    s[3] = __fsub_rn(1.0f, s[1]);
-  }
+  if (threadIdx.x == 0 && blockIdx.x == 0) advance_powers<BF16>(s, beta1, beta2);
 }
 
-// Multi-tensor optimizer step; op order follows neural/optimizer.rs:40-51 (SGD)
-// and neural/adam.rs:62-85, 137-157 (Adam, AdamW).
+// Multi-tensor optimizer step: each element follows optimizer_update
+// (optimizer_rule.h) in the element type of the parameters.
+template <bool BF16>
 __global__ void k_optimizer(const OptEntry* __restrict__ entries, int count, int64_t total,
                             const float* __restrict__ s, const float* __restrict__ lr_ptr,
                             int kind, float beta1, float beta2, float share1, float share2,
                             float eps, float decay, float gscale) {
   pdl_entry();
-  const float lr = *lr_ptr;
-  const float c1 = kind ? s[2] : 0.0f, c2 = kind ? s[3] : 0.0f;
+  OptimizerScalars sc;
+  sc.kind = kind;
+  sc.lr = *lr_ptr;
+  sc.beta1 = beta1;
+  sc.beta2 = beta2;
+  sc.share1 = share1;
+  sc.share2 = share2;
+  sc.eps = eps;
+  sc.decay = decay;
+  sc.gscale = gscale;
+  sc.c1 = kind ? s[2] : 0.0f;
+  sc.c2 = kind ? s[3] : 0.0f;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     int lo = 0, hi = count - 1;
@@ -535,26 +543,17 @@ __global__ void k_optimizer(const OptEntry* __restrict__ entries, int count, int
     }
     const OptEntry& e = entries[lo];
     const int64_t j = i - e.start;
-    float g = e.g[j];
-    if (gscale != 1.0f) g = __fmul_rn(g, gscale);
-    const float p = e.p[j];
+    float p = e.p[j];
     if (kind == 0) {
-      e.p[j] = __fsub_rn(p, __fmul_rn(g, lr));
-      continue;
-    }
-    const float first = __fadd_rn(__fmul_rn(e.m[j], beta1), __fmul_rn(g, share1));
-    const float second = __fadd_rn(__fmul_rn(e.v[j], beta2), __fmul_rn(__fmul_rn(g, g), share2));
-    e.m[j] = first;
-    e.v[j] = second;
-    const float cf = __fdiv_rn(first, c1);
-    const float cs = __fdiv_rn(second, c2);
-    const float d = __fdiv_rn(cf, __fadd_rn(__fsqrt_rn(cs), eps));
-    const float stepped = __fsub_rn(p, __fmul_rn(d, lr));
-    if (kind == 2 && e.decay) {
-      e.p[j] = __fsub_rn(stepped, __fmul_rn(__fmul_rn(p, decay), lr));
+      float unused = 0.0f;
+      optimizer_update<BF16>(p, unused, unused, e.g[j], false, sc);
     } else {
-      e.p[j] = stepped;
+      float m = e.m[j], v = e.v[j];
+      optimizer_update<BF16>(p, m, v, e.g[j], e.decay != 0, sc);
+      e.m[j] = m;
+      e.v[j] = v;
     }
+    e.p[j] = p;
   }
 }
 
@@ -688,16 +687,22 @@ void launch_gemm(const Operand& a, const Operand& b, float* c, float* partial, i
   launch_gemm_simt(a, b, c, batch, m, n, kp, stream);
 }
 
-void launch_adam_scalars(float* s, float beta1, float beta2, cudaStream_t stream) {
-  launch_pdl(k_adam_scalars, 1, 32, 0, stream, s, beta1, beta2);
+void launch_adam_scalars(float* s, float beta1, float beta2, bool bf16, cudaStream_t stream) {
+  if (bf16) launch_pdl(k_adam_scalars<true>, 1, 32, 0, stream, s, beta1, beta2);
+  else launch_pdl(k_adam_scalars<false>, 1, 32, 0, stream, s, beta1, beta2);
 }
 
 void launch_optimizer(const OptEntry* entries, int count, int64_t total, const float* scalars,
                       const float* lr, int kind, float beta1, float beta2, float share1,
-                      float share2, float eps, float decay, float gscale, cudaStream_t stream) {
+                      float share2, float eps, float decay, float gscale, bool bf16,
+                      cudaStream_t stream) {
   int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 148 * 8));
-  launch_pdl(k_optimizer, grid, 256, 0, stream, entries, count, total, scalars, lr, kind, beta1,
-             beta2, share1, share2, eps, decay, gscale);
+  if (bf16)
+    launch_pdl(k_optimizer<true>, grid, 256, 0, stream, entries, count, total, scalars, lr, kind,
+               beta1, beta2, share1, share2, eps, decay, gscale);
+  else
+    launch_pdl(k_optimizer<false>, grid, 256, 0, stream, entries, count, total, scalars, lr,
+               kind, beta1, beta2, share1, share2, eps, decay, gscale);
 }
 
 }  // namespace tb

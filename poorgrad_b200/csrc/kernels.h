@@ -103,10 +103,11 @@ struct OptEntry {
 void launch_tree_sum(const float* g, int shards, int64_t count, float* out, cudaStream_t stream);
 
 // Per-step optimizer scalars: s[0]=beta1^t, s[1]=beta2^t, s[2]=1-beta1^t, s[3]=1-beta2^t.
-void launch_adam_scalars(float* s, float beta1, float beta2, cudaStream_t stream);
+void launch_adam_scalars(float* s, float beta1, float beta2, bool bf16, cudaStream_t stream);
 // One multi-tensor step over all entries (kind: 0 SGD, 1 Adam, 2 AdamW).
 void launch_optimizer(const OptEntry* entries, int count, int64_t total, const float* scalars,
                       const float* lr, int kind, float beta1, float beta2, float share1,
-                      float share2, float eps, float decay, float gscale, cudaStream_t stream);
+                      float share2, float eps, float decay, float gscale, bool bf16,
+                      cudaStream_t stream);
 
 }  // namespace tb

@@ -240,6 +240,7 @@ struct tb_instance;
 
 struct tb_params {
   int device = 0;
+  bool bf16 = false;  // the plan's network holds bf16 numbers: uploads round
   void* base = nullptr;
   std::vector<float*> slot;
   std::vector<int64_t> count;
@@ -271,6 +272,7 @@ struct tb_optimizer {
   tb::OptEntry* custom = nullptr;      // device table for caller-given gradients
   float* state = nullptr;              // moments (Adam): first then second per slot
   float* scalars = nullptr;            // beta powers and corrections, learning rate
+  bool bf16 = false;                   // the plan's parameters are bf16 numbers
   int64_t total = 0;
   std::vector<int64_t> state_offset;   // per entry
   ~tb_optimizer() {
@@ -280,6 +282,12 @@ struct tb_optimizer {
     if (scalars) cudaFree(scalars);
   }
 };
+
+// 1 - beta (adam.rs:46-47) in the parameters' element type.
+float optimizer_share(const tb_optimizer* o, float beta) {
+  const float s = 1.0f - beta;
+  return o->bf16 ? tb::round_bf16(s) : s;
+}
 
 // Per-run state of a plan: streams, arena, input buffers and the captured
 // graph.  A plan owns a main instance (used by tb_plan_run, the optimizer and
@@ -566,14 +574,14 @@ void enqueue_program(tb_instance* plan, cudaStream_t stream) {
   if (plan->optimizer) {
     tb_optimizer* o = plan->optimizer;
     if (o->desc.kind != TB_OPTIMIZER_SGD) {
-      tb::launch_adam_scalars(o->scalars, o->desc.beta1, o->desc.beta2, stream);
+      tb::launch_adam_scalars(o->scalars, o->desc.beta1, o->desc.beta2, o->bf16, stream);
       launches += 1;
     }
-    float share1 = 1.0f - o->desc.beta1;
-    float share2 = 1.0f - o->desc.beta2;
     tb::launch_optimizer(o->entries, (int)o->host_entries.size(), o->total, o->scalars,
-                         o->scalars + 4, o->desc.kind, o->desc.beta1, o->desc.beta2, share1,
-                         share2, o->desc.epsilon, o->desc.decay, o->desc.gradient_scale, stream);
+                         o->scalars + 4, o->desc.kind, o->desc.beta1, o->desc.beta2,
+                         optimizer_share(o, o->desc.beta1), optimizer_share(o, o->desc.beta2),
+                         o->desc.epsilon, o->desc.decay, o->desc.gradient_scale, o->bf16,
+                         stream);
     launches += 1;
     check(cudaGetLastError(), "optimizer launch");
   }
@@ -818,6 +826,7 @@ int tb_params_create(const tb_plan* plan, tb_params** out) {
     const tb::Program& P = *plan->prog;
     std::unique_ptr<tb_params> p(new tb_params());
     check(cudaGetDevice(&p->device), "cudaGetDevice");
+    p->bf16 = P.bf16;
     int slots = P.parameter_slots;
     std::vector<int64_t> offset(slots);
     int64_t total = 0;
@@ -843,6 +852,14 @@ int tb_params_upload(tb_params* params, int32_t slot, const float* host, int64_t
   return guarded([&]() {
     if (slot < 0 || slot >= (int)params->slot.size() || count != params->count[slot])
       throw Failure(TB_INVALID, "parameter slot or size mismatch");
+    if (params->bf16) {
+      // a bf16 network's parameters are bf16 numbers (payload/bf16.rs:39-55)
+      std::vector<float> rounded(host, host + count);
+      for (float& v : rounded) v = tb::round_bf16(v);
+      check(cudaMemcpy(params->slot[slot], rounded.data(), count * 4, cudaMemcpyHostToDevice),
+            "upload");
+      return (int)TB_OK;
+    }
     check(cudaMemcpy(params->slot[slot], host, count * 4, cudaMemcpyHostToDevice), "upload");
     return (int)TB_OK;
   });
@@ -972,12 +989,20 @@ int tb_optimizer_create(tb_plan* owner, tb_params* params, const tb_optimizer_de
   return guarded([&]() {
     tb_instance* plan = owner->main.get();
     if (desc->kind < 0 || desc->kind > 2) throw Failure(TB_INVALID, "unknown optimizer kind");
-    if (plan->prog->bf16) throw Failure(TB_DECLINED, "the device optimizer steps f32 parameters");
     bind_params(plan, params);
     std::unique_ptr<tb_optimizer> o(new tb_optimizer());
     o->plan = plan;
     o->params = params;
     o->desc = *desc;
+    o->bf16 = plan->prog->bf16;
+    if (o->bf16) {
+      // Adam<Bf16> and the rate hold bf16 scalars (neural/adam.rs:40-56)
+      if (desc->gradient_scale != 1.0f)
+        throw Failure(TB_DECLINED, "a bf16 step takes no gradient scale");
+      for (float* h : {&o->desc.learning_rate, &o->desc.beta1, &o->desc.beta2,
+                       &o->desc.epsilon, &o->desc.decay})
+        *h = tb::round_bf16(*h);
+    }
     int64_t total = 0;
     for (int32_t i = 0; i < count; ++i) {
       int slot = slots[i];
@@ -1032,7 +1057,7 @@ void tb_optimizer_destroy(tb_optimizer* o) {
 
 int tb_optimizer_set_learning_rate(tb_optimizer* o, float lr) {
   return guarded([&]() {
-    o->desc.learning_rate = lr;
+    o->desc.learning_rate = o->bf16 ? tb::round_bf16(lr) : lr;
     check(cudaMemcpyAsync(o->scalars + 4, &o->desc.learning_rate, 4, cudaMemcpyHostToDevice,
                           o->plan->stream),
           "upload learning rate");
@@ -1061,11 +1086,12 @@ int tb_optimizer_step(tb_optimizer* o, const float* const* gradients, void* stre
             "upload entries");
       table = o->custom;
     }
-    if (o->desc.kind != TB_OPTIMIZER_SGD) tb::launch_adam_scalars(o->scalars, o->desc.beta1, o->desc.beta2, st);
+    if (o->desc.kind != TB_OPTIMIZER_SGD)
+      tb::launch_adam_scalars(o->scalars, o->desc.beta1, o->desc.beta2, o->bf16, st);
     tb::launch_optimizer(table, (int)o->host_entries.size(), o->total, o->scalars, o->scalars + 4,
-                         o->desc.kind, o->desc.beta1, o->desc.beta2, 1.0f - o->desc.beta1,
-                         1.0f - o->desc.beta2, o->desc.epsilon, o->desc.decay,
-                         o->desc.gradient_scale, st);
+                         o->desc.kind, o->desc.beta1, o->desc.beta2,
+                         optimizer_share(o, o->desc.beta1), optimizer_share(o, o->desc.beta2),
+                         o->desc.epsilon, o->desc.decay, o->desc.gradient_scale, o->bf16, st);
     check(cudaGetLastError(), "optimizer launch");
     return (int)TB_OK;
   });
