@@ -75,3 +75,29 @@ def test_engine_backward_programs_follow_the_engine_scan(built, name):
     for p, ref in zip(wrt, scan):
         got = out[grads[(loss.index, p.index)]]
         np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-6)
+
+
+def test_decode_carry_programs_follow_the_oracle(built):
+    # the full-context and one-token decode programs of the decode-carry test
+    # (scatter-appended caches carried as feeds, a -inf mask), emulated
+    from test_decode_carry import carry_loop, record
+    net, full, decode, n = record()
+    params = net.parameters()
+    keys = [n["row"]] + [c for pair in n["updated"] for c in pair]
+
+    def run_full(feeds):
+        got = kernel_emulator.run_program(full, params, feeds)[n["full_out"].index]
+        ref = oracle.run(full, params, feeds)[n["full_out"].index]
+        np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-6)
+        return got
+
+    def run_decode(feeds):
+        got = kernel_emulator.run_program(decode, params, feeds)
+        ref = oracle.run(decode, params, feeds, read=keys)
+        for k in keys:
+            np.testing.assert_allclose(got[k.index], ref[k.index], rtol=1e-5, atol=1e-6)
+        return {k: got[k.index] for k in keys}
+
+    full_rows, decode_rows = carry_loop(run_full, run_decode, n)
+    for f, d in zip(full_rows, decode_rows):
+        np.testing.assert_allclose(d, f, rtol=1e-5, atol=1e-6)
