@@ -101,3 +101,43 @@ def test_decode_carry_programs_follow_the_oracle(built):
     full_rows, decode_rows = carry_loop(run_full, run_decode, n)
     for f, d in zip(full_rows, decode_rows):
         np.testing.assert_allclose(d, f, rtol=1e-5, atol=1e-6)
+
+
+def test_dropout_programs_follow_the_oracle(built):
+    # a fed mask each run and an unfed run that is the identity
+    from poorgrad_b200 import neural
+    from test_dropout import masked_network
+    net, cols, w, x, drop, loss, g = masked_network(64, 16, 32)
+    params = net.parameters()
+    for feeds in ({}, {drop.mask: neural.dropout(3, 0.75)((64, 32))}):
+        out = kernel_emulator.run_program(cols, params, feeds)
+        ref = oracle.run(cols, params, feeds)
+        for v in (loss, g):
+            scale = max(1.0, float(np.abs(ref[v.index]).max()))
+            np.testing.assert_allclose(out[v.index], ref[v.index], rtol=0, atol=3e-5 * scale)
+
+
+def test_composite_engine_backward_program_follows_the_oracle(built):
+    # the compositions of the device composites test (broadcast_to, concat,
+    # stack, masked softmax) in one engine-backward plan
+    from poorgrad_b200.graph import concat, stack, tensor
+    rng = np.random.default_rng(4)
+    t = Tape()
+    a = t.parameter(tensor((2, 1, 8), rng.uniform(-1, 1, 16)))
+    b = t.parameter(tensor((8,), rng.uniform(-1, 1, 8)))
+    s = t.parameter(tensor((4, 8), rng.uniform(-2, 2, 32)))
+    mask = t.leaf(tensor((8,), [0.0] * 6 + [-np.inf] * 2))
+    grid = a.broadcast_to((2, 4, 8)) + b.broadcast_to((2, 4, 8))
+    probs = (s + mask.broadcast_to((4, 8))).softmax(1)
+    joined = concat([grid.reshape((8, 8)), probs.abs()], 0)
+    stacked = stack([probs, s.mean_along(0).broadcast_to((4, 8))], 0)
+    loss = joined.tanh().sum() + stacked.logsumexp(2).sum()
+    net = t.into_network()
+    cols = net.compile(Request([loss, joined, stacked]).backward())
+    params = net.parameters()
+    out, grads = kernel_emulator.run_program(cols, params, gradients=True)
+    ref = oracle.run(cols, params)
+    for v in (joined, stacked, loss):
+        np.testing.assert_allclose(out[v.index], ref[v.index], rtol=1e-5, atol=1e-6)
+    for p, r in zip((a, b, s), oracle.backward(cols, params, loss, [a, b, s])):
+        np.testing.assert_allclose(out[grads[(loss.index, p.index)]], r, rtol=1e-5, atol=1e-6)
