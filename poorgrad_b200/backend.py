@@ -10,7 +10,7 @@ every call goes to the CUDA library, and a missing library or device raises.
 from __future__ import annotations
 
 import ctypes as C
-from typing import Dict, Iterable, List, Optional, Sequence
+from typing import Dict, Iterable, Optional, Sequence
 
 import numpy as np
 

@@ -16,7 +16,7 @@ from typing import Callable, Dict, List
 import numpy as np
 
 from . import neural
-from .graph import Dense, Selection, Tape, Value, concat, counted, filled, selection
+from .graph import Dense, Selection, Tape, Value, counted, filled, selection
 from .plan import Request
 
 

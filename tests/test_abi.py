@@ -2,7 +2,6 @@
 symbol include/topos_b200.h declares, reports PlatformUnsupported, and the
 host half of the backend (lowering, NVRTC compilation of the emitted kernels
 for sm_100a) runs."""
-import ctypes as C
 
 import pytest
 

@@ -4,7 +4,6 @@ emulator against the oracle: 256-thread teams with cross-warp reductions
 (`vec = 1`) rows of odd width, the four-stride unrolled flat loop (more than
 4 · 1184 · 256 elements), and column sums of wide rows."""
 import numpy as np
-import pytest
 
 import kernel_emulator
 import oracle

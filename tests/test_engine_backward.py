@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 
 import oracle
-from poorgrad_b200 import backend, configs, neural
+from poorgrad_b200 import backend, neural
 from poorgrad_b200.graph import Tape, tensor, selection
 from poorgrad_b200.plan import Request
 

@@ -3,7 +3,6 @@
 to run without its CUDA library (no CPU fallback)."""
 import ctypes as C
 
-import numpy as np
 import pytest
 
 from poorgrad_b200 import abi, backend

@@ -17,7 +17,7 @@ import pytest
 import oracle
 from oracle import optim
 from poorgrad_b200 import backend, configs, neural
-from poorgrad_b200.graph import Dense, Tape, concat, filled, selection, tensor
+from poorgrad_b200.graph import Tape, concat, filled, selection, tensor
 from poorgrad_b200.plan import Request
 
 pytestmark = pytest.mark.gpu

@@ -6,7 +6,6 @@ import math
 import struct
 
 import numpy as np
-import pytest
 
 import oracle
 from poorgrad_b200 import neural
