@@ -20,7 +20,6 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -42,51 +41,82 @@ def peaks():
 
 
 class Clocks:
-    """Samples SM clocks and throttle reasons during the timed region."""
+    """Samples the SM clock and the throttle reasons of this process's GPU
+    in-process through read-only NVML queries every ``period`` seconds, across
+    the untimed replay and the timed region."""
 
-    def __init__(self, index: int):
-        self.index = index
-        self.samples = []
-        self.proc = None
+    REASONS = [("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+               ("hw_power_brake", "nvmlClocksEventReasonHwPowerBrakeSlowdown")]
+
+    def __init__(self, local: int, period: float = 0.005):
+        self.local = local
+        self.period = period
+        self.samples = []       # (t, sm_mhz, reasons bitmask)
+        self.stop = threading.Event()
+        self.nvml = None
+        self.handle = None
+        self.max_mhz = None
+        self.error = None
+        self.marks = {}
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), "--query-gpu=clocks.sm,clocks.max.sm,"
-                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(self.local).uuid)
+            try:
+                self.handle = pynvml.nvmlDeviceGetHandleByUUID(
+                    uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(self.local)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self.nvml = pynvml
+            self.thread = threading.Thread(target=self._run, daemon=True)
             self.thread.start()
-        except OSError:
-            self.proc = None
+        except Exception as e:  # no NVML: the line says so
+            self.error = f"{type(e).__name__}: {e}"
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 6:
-                self.samples.append(parts)
+    def _run(self):
+        n = self.nvml
+        while not self.stop.is_set():
+            try:
+                sm = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+                why = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.samples.append((time.perf_counter(), sm, why))
+            except Exception as e:
+                self.error = f"{type(e).__name__}: {e}"
+                return
+            time.sleep(self.period)
+
+    def mark(self, name):
+        self.marks[name] = time.perf_counter()
 
     def __exit__(self, *exc):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=2)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self.stop.set()
+        if self.nvml is not None:
+            self.thread.join(timeout=2)
 
     def summary(self):
         if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
-        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for s in self.samples for i in range(4)
-                          if s[2 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(sm)}
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"],
+                    "error": self.error}
+        n = self.nvml
+        t0 = self.marks.get("timed_start", 0.0)
+        t1 = self.marks.get("timed_end", float("inf"))
+        timed = [s for s in self.samples if t0 <= s[0] <= t1]
+        names = sorted({name for _, _, why in self.samples for name, attr in self.REASONS
+                        if why & getattr(n, attr, 0)})
+        return {"sm_mhz": statistics.median(s[1] for s in self.samples),
+                "sm_max_mhz": self.max_mhz, "reasons": names,
+                "samples": len(self.samples), "samples_timed": len(timed),
+                "sm_mhz_timed": statistics.median(s[1] for s in timed) if timed else None,
+                "source": f"NVML in-process every {self.period * 1e3:.0f} ms over the untimed "
+                          "replay and the timed steps"}
 
 
 def dist_setup(gpus: int):
@@ -119,64 +149,92 @@ def build_workload(name: str, rank: int, config_only: bool = False):
     return (None if config_only else make()), dict(cfg)
 
 
+def metric_of(name):
+    """(metric, unit, units per sample) of a config's line: GPT-2 counts
+    tokens, the microbenches rows of their workload, the rest samples."""
+    if name == "gpt2":
+        return "train tokens/s", "tokens/s"
+    if name in ("fused", "gemm", "gemm_skinny"):
+        return "train rows/s", "rows/s"
+    return "train samples/s", "samples/s"
+
+
+def tree_sum(parts):
+    """`tree_sum` of examples/makemore/mlp_parallel.rs:59-71: left + right in
+    pairs, an odd last shard carried up."""
+    while len(parts) > 1:
+        nxt = [parts[i] + parts[i + 1] for i in range(0, len(parts) - 1, 2)]
+        if len(parts) % 2:
+            nxt.append(parts[-1])
+        parts = nxt
+    return parts[0]
+
+
 def reference_arm(args, name):
     """Times the reference interpreter's arithmetic (the oracle port) on the
-    host cores: shards of a bounded sample, one per core, run concurrently."""
+    host cores, in the reference's own data-parallel idiom
+    (examples/makemore/mlp_parallel.rs): each step splits the workload's batch
+    into one shard per core, runs the shards' plans on concurrent threads, sums
+    the shard gradients in `tree_sum` order, scales by 1/shards and applies the
+    config's optimizer on the host."""
     rank, world, local = dist_setup(args.gpus)
     if rank != 0:
         return
     import oracle
+    from oracle import optim
     from poorgrad_b200 import configs
     cores = os.cpu_count() or 1
-    shard = {"charmlp": 64, "mlp": 128, "gpt2": None, "fused": None, "gemm": None,
-             "gemm_skinny": None}[name]
+    metric, unit = metric_of(name)
     if name == "gpt2":
+        # a full 8 x 1024 step would take the host cores many minutes: one
+        # 128-token sequence per core at the full model widths
         w = configs.gpt2(batch=1, seq=128)
-        unit_scale = 1.0  # one short sequence per shard
-        sample = "1 sequence of 128 tokens per core (full 12-layer GPT-2-small widths)"
+        per_shard, sample = 128, f"{cores} shards x 1 sequence of 128 tokens (full GPT-2-small widths) per step"
     elif name in ("fused", "gemm", "gemm_skinny"):
         w = {"fused": lambda: configs.fused(rows=256, cols=8192),
              "gemm": lambda: configs.gemm(256, 4096, 4096),
              "gemm_skinny": lambda: configs.gemm(256, 768, 3072)}[name]()
-        sample = "256-row slice of the workload per core"
-        unit_scale = 1.0
+        per_shard, sample = 256, f"{cores} shards x a 256-row slice of the workload per step"
     else:
-        w = configs.char_mlp(batch=shard) if name == "charmlp" else configs.mlp(batch=shard)
-        sample = f"batch {shard} of the same graph per core"
+        full = 16384 if name == "charmlp" else 128
+        per_shard = max(1, full // cores)
+        w = (configs.char_mlp(batch=per_shard, seed=4) if name == "charmlp"
+             else configs.mlp(batch=per_shard))
+        sample = f"the full batch {per_shard * cores} as {cores} shards of {per_shard} per step"
     oracle.build()
-    params = w.network.parameters()
-    feeds = [w.feeds(i) for i in range(cores)]
+    params = [p.reshape(w.columns.nodes[s.index].shape).copy()
+              for p, s in zip(w.network.parameters(), w.params)]
+    opt = w.optimizer
+    host = optim.make(opt["kind"], opt) if opt else None
+    results = [None] * cores
 
-    def one_step():
-        threads = [threading.Thread(target=oracle.run, args=(w.columns, params, feeds[i]))
+    def shard(i, feeds):
+        results[i] = oracle.run(w.columns, params, feeds, read=[g.index for g in w.grads])
+
+    def one_step(step):
+        nonlocal params
+        threads = [threading.Thread(target=shard, args=(i, w.feeds(step * cores + i)))
                    for i in range(cores)]
         for t in threads:
             t.start()
         for t in threads:
             t.join()
+        if host is not None:
+            grads = [tree_sum([results[i][g.index] for i in range(cores)]) * np.float32(1.0 / cores)
+                     for g in w.grads]
+            params = host.step(params, [g.astype(np.float32) for g in grads], opt["lr"])
 
-    for _ in range(max(1, min(args.warmup, 1))):
-        one_step()
+    for i in range(max(1, min(args.warmup, 1))):
+        one_step(i)
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        one_step()
+    for i in range(args.steps):
+        one_step(i + 1)
     dt = (time.perf_counter() - t0) / args.steps
-    if name == "gpt2":
-        value = cores * 1 / dt
-        unit = "sequences/s"
-    elif name == "fused":
-        value = cores * 256 / dt
-        unit = "rows/s"
-    elif name in ("gemm", "gemm_skinny"):
-        value = cores * 256 / dt
-        unit = "rows/s"
-    else:
-        value = cores * shard / dt
-        unit = "samples/s"
+    value = cores * per_shard / dt
     _, cfg = build_workload(name, 0, config_only=True)
-    cfg.update({"workload": name, "parallelism": f"dp{args.gpus}"})
-    line = {"impl": "reference", "metric": "train samples/s" if unit == "samples/s" else f"train {unit}",
-            "value": value, "unit": unit,
+    cfg.update({"workload": name, "parallelism": f"dp{args.gpus}",
+                "optimizer": opt.get("kind") if opt else None})
+    line = {"impl": "reference", "metric": metric, "value": value, "unit": unit,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded splitmix64 streams)",
@@ -194,10 +252,10 @@ def cpu_baseline(name):
     oracle.build()
     if name == "gpt2":
         w = configs.gpt2(batch=1, seq=128)
-        n, unit, sample = 1, "sequences/s", "1 sequence of 128 tokens, full model widths"
+        n, unit, sample = 128, "tokens/s", "1 sequence of 128 tokens, full model widths"
     elif name == "charmlp":
-        w = configs.char_mlp(batch=256)
-        n, unit, sample = 256, "samples/s", "batch 256 of the same graph, 1 step"
+        w = configs.char_mlp(batch=1024, seed=4)
+        n, unit, sample = 1024, "samples/s", "batch 1024 of the same graph, 1 step"
     elif name == "mlp":
         w = configs.mlp(batch=128)
         n, unit, sample = 128, "samples/s", "the full batch-128 step"
@@ -213,6 +271,140 @@ def cpu_baseline(name):
         reps += 1
     dt = (time.perf_counter() - t0) / reps
     return {"value": n / dt, "unit": unit, "cores": 1, "kind": "port", "sample": sample}
+
+
+def tolerance(name, w, plan, dp, feeds):
+    """Measured error of the timed config against the oracle, outside the
+    timed region: the current device parameters are read back, one more step
+    runs on the device (its loss and gradients come from those parameters),
+    and the oracle computes the same loss and gradients on every host core.
+    Reported per output as max |dev - oracle| / max |oracle|."""
+    import oracle
+    if name not in ("charmlp", "mlp"):
+        return None
+    oracle.build()
+    oracle.set_threads(os.cpu_count() or 1)
+    params = [dp.download(slot) for slot in range(len(dp.shapes))]
+    plan.forward(dp, feeds, sync=True)
+    dev = {g.index: plan.of(g) for g in [w.loss] + list(w.grads)}
+    t0 = time.perf_counter()
+    ref = oracle.run(w.columns, params, feeds, read=list(dev))
+    oracle_s = time.perf_counter() - t0
+    oracle.set_threads(1)
+    loss_rel = float(abs(dev[w.loss.index] - ref[w.loss.index]) / abs(ref[w.loss.index]))
+    grad_rel = max(float(np.abs(dev[g.index] - ref[g.index]).max() /
+                         (np.abs(ref[g.index]).max() + 1e-30)) for g in w.grads)
+    return {"loss_rel": loss_rel, "grads_max_rel_to_scale": grad_rel,
+            "bar": "loss and every gradient within rtol 1e-3 + atol 1e-4 of its scale "
+                   "(tests/test_full_size_parity.py)",
+            "sample": f"one full-size step ({w.samples} samples) from the parameters after the "
+                      f"timed steps; oracle {oracle_s:.1f} s on {os.cpu_count()} threads"}
+
+
+def cublas_baseline(m, k, n, reps=5):
+    """The reference's cuda arm for C3 (backend/cuda/kernels/gemm.rs:54-163,
+    context.rs:217-288): a fresh cuBLAS handle in its default math mode (no
+    TF32), `cublasSgemm_v2` on row-major operands through the column-major
+    swap, for C = A.B, dA = dC.B^T and dB = A^T.dC.  Timed device-only (CUDA
+    events around the three calls, operands resident) and with the reference's
+    per-product copies (pageable host -> device for both operands, the call,
+    device -> host of the product, device synchronize; wall clock).  A
+    baseline only: nothing of the product path calls cuBLAS."""
+    import torch
+    lib = None
+    for cand in ("libcublas.so.12", "libcublas.so"):
+        try:
+            lib = C.CDLL(cand)
+            break
+        except OSError:
+            continue
+    if lib is None:
+        return {"unavailable": "libcublas not found"}
+    handle = C.c_void_p()
+    if lib.cublasCreate_v2(C.byref(handle)) != 0:
+        return {"unavailable": "cublasCreate failed"}
+    N, T = 0, 1
+    one, zero = C.c_float(1.0), C.c_float(0.0)
+    rng = np.random.default_rng(0)
+    A = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    B = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    dC = rng.standard_normal((m, n)).astype(np.float32)
+
+    def sgemm(opb, opa, nn, mm, kk, b, ldb, a, lda, c, ldc):
+        rc = lib.cublasSgemm_v2(handle, opb, opa, nn, mm, kk, C.byref(one), C.c_void_p(b), ldb,
+                                C.c_void_p(a), lda, C.byref(zero), C.c_void_p(c), ldc)
+        assert rc == 0, rc
+
+    # row-major products through the column-major swap: C^T = op(B)^T op(A)^T
+    products = [  # (left host, right host, out shape, call)
+        (A, B, (m, n), lambda l, r, o: sgemm(N, N, n, m, k, r, n, l, k, o, n)),
+        (dC, B, (m, k), lambda l, r, o: sgemm(T, N, k, m, n, r, n, l, n, o, k)),
+        (A, dC, (k, n), lambda l, r, o: sgemm(N, T, n, k, m, r, n, l, k, o, n)),
+    ]
+    dev = [(torch.from_numpy(l).cuda(), torch.from_numpy(r).cuda(),
+            torch.empty(shape, device="cuda")) for l, r, shape, _ in products]
+    torch.cuda.synchronize()
+    flops = 3 * 2.0 * m * n * k
+
+    def device_only():
+        for (l, r, o), (_, _, _, call) in zip(dev, products):
+            call(l.data_ptr(), r.data_ptr(), o.data_ptr())
+
+    for _ in range(2):
+        device_only()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(torch.cuda.default_stream())
+    for _ in range(reps):
+        device_only()
+    e.record(torch.cuda.default_stream())
+    torch.cuda.synchronize()
+    ms_dev = s.elapsed_time(e) / reps
+
+    def with_copies():
+        for (l, r, o), (lh, rh, shape, call) in zip(dev, products):
+            l.copy_(torch.from_numpy(lh))
+            r.copy_(torch.from_numpy(rh))
+            call(l.data_ptr(), r.data_ptr(), o.data_ptr())
+            out = o.cpu()
+            torch.cuda.synchronize()
+        return out
+
+    with_copies()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        with_copies()
+    ms_copy = (time.perf_counter() - t0) * 1e3 / reps
+    lib.cublasDestroy_v2(handle)
+    return {"device_only": {"ms_per_step": ms_dev, "tflops": flops / ms_dev / 1e9},
+            "with_copies": {"ms_per_step": ms_copy, "tflops": flops / ms_copy / 1e9,
+                            "copies": "pageable H2D of both operands and D2H of the product, "
+                                      "per product"},
+            "math_mode": "cuBLAS default (f32, no TF32)", "reps": reps}
+
+
+def face_with_copies(m, k, n, reps=5):
+    """This library's per-task face `tb_gemm_f32` (host slices in, owned
+    product out) timed through the same three products as `cublas_baseline`'s
+    copy arm (wall clock)."""
+    from poorgrad_b200 import backend
+    rng = np.random.default_rng(0)
+    A = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    B = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    dC = rng.standard_normal((m, n)).astype(np.float32)
+
+    def step():
+        backend.gemm_f32(A, B)
+        backend.gemm_f32(dC, B.T)
+        backend.gemm_f32(A.T, dC)
+
+    step()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        step()
+    ms = (time.perf_counter() - t0) * 1e3 / reps
+    return {"ms_per_step": ms, "tflops": 3 * 2.0 * m * n * k / ms / 1e9,
+            "copies": "pageable H2D of both operands and D2H of the product, per product"}
 
 
 KTYPES = ["ew", "row", "reduce", "prep", "gemm", "sort", "scatter", "fold", "final", "segsum"]
@@ -235,14 +427,16 @@ def kernel_profile(plan, reps=20):
     return rows
 
 
-# DRAM read + write bytes per launch of the dominant kernel class, from one ncu
-# launch-list capture of the workload (dram__bytes_read.sum +
-# dram__bytes_write.sum; charmlp: its 63 k_gemm_tcgen05 launches average 77.3 MB).
-NCU_TRAFFIC = {"charmlp": {"gemm": 77.29e6}}
+# DRAM read + write bytes per launch of the dominant kernel class, averaged
+# over that class's launches in one ncu capture of the workload
+# (dram__bytes_read.sum + dram__bytes_write.sum), with the profile summary it
+# comes from.
+NCU_TRAFFIC = {"charmlp": {"gemm": (77.29e6, "profiles/charmlp_step_launches.md: the 63 "
+                                    "k_gemm_tcgen05 launches of 7 steps")}}
 
 
 def traffic(workload, kind):
-    return NCU_TRAFFIC.get(workload, {}).get(kind)
+    return NCU_TRAFFIC.get(workload, {}).get(kind, (None, None))
 
 
 def roofline(rows, workload=None):
@@ -262,16 +456,20 @@ def roofline(rows, workload=None):
         achieved = flops / t / 1e12
         peak = bf16 / 6.0   # tf32 runs at half the bf16 rate; 3xTF32 issues three products
         return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak, "traffic": traffic(workload, kind),
-                "traffic_unit": "bytes per launch", "launches": len(group),
+                "frac": achieved / peak, "traffic": traffic(workload, kind)[0],
+                "traffic_unit": "bytes per launch", "traffic_source": traffic(workload, kind)[1],
+                "timing": "per-kernel CUDA-event replay of the step's kernels, hot cache "
+                          "(tbx_profile_kernels)", "launches": len(group),
                 "kernel": "k_gemm_tcgen05 (3xTF32, all GEMMs of the step)",
                 "share": t * 1e3 / total,
                 "peak_note": f"3xTF32-effective = {how} bf16 {bf16:.0f} TF/s / 6"}
     bytes_ = sum(r["read"] + r["write"] for r in group)
     achieved = bytes_ / t / 1e9
     return {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-            "frac": achieved / hbm, "traffic": traffic(workload, kind),
-            "traffic_unit": "bytes per launch", "launches": len(group),
+            "frac": achieved / hbm, "traffic": traffic(workload, kind)[0],
+            "traffic_unit": "bytes per launch", "traffic_source": traffic(workload, kind)[1],
+            "timing": "per-kernel CUDA-event replay of the step's kernels, hot cache "
+                      "(tbx_profile_kernels)", "launches": len(group),
             "kernel": f"{kind} kernels", "share": t * 1e3 / total,
             "peak_note": f"{how} HBM copy bandwidth"}
 
@@ -284,6 +482,8 @@ def main():
     ap.add_argument("--impl", default="b200")
     ap.add_argument("--config", default=DEFAULT_CONFIG)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--replay-s", type=float, default=1.5,
+                    help="untimed replay before the timed steps (clock sampling)")
     ap.add_argument("--no-kernel-profile", action="store_true",
                     help="skip the per-kernel timing pass (for runs under a profiler)")
     args = ap.parse_args()
@@ -358,7 +558,7 @@ def main():
     torch.cuda.synchronize()
     stream = torch.cuda.ExternalStream(plan.stream())
 
-    def timed(host):
+    def timed(host, clocks=None):
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
@@ -366,6 +566,8 @@ def main():
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
         loss_host = np.empty((), np.float32)
+        if clocks:
+            clocks.mark("timed_start")
         t_wall = time.perf_counter()
         with torch.cuda.stream(stream):
             start.record(stream)
@@ -376,8 +578,10 @@ def main():
             end.record(stream)
         plan.synchronize()
         torch.cuda.synchronize()
-        ms = start.elapsed_time(end)
         wall = (time.perf_counter() - t_wall) * 1e3
+        if clocks:
+            clocks.mark("timed_end")
+        ms = start.elapsed_time(end)
         t = torch.tensor([ms], device="cuda")
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -385,10 +589,22 @@ def main():
         return float(t.item()), wall, loss_host
 
     with Clocks(local) as clocks:
-        ms, wall, _ = timed(False)
+        # untimed replay of the same step for >= 1.5 s right before the timed
+        # region, so that the clock samples (and any external sampler) see the
+        # GPU under this load
+        t_end = time.perf_counter() + args.replay_s
+        i = 0
+        while time.perf_counter() < t_end:
+            for _ in range(32):
+                step(i)
+                i += 1
+            plan.synchronize()
+        ms, wall, _ = timed(False, clocks)
     ms_e2e, wall_e2e, last_loss = timed(True)
     per_step = ms / args.steps
-    samples = w.samples * world
+    metric, unit = metric_of(args.config)
+    per_sample = 1024 if args.config == "gpt2" else 1   # tokens per GPT-2 sequence
+    samples = w.samples * per_sample * world
     value = samples / (per_step * 1e-3)
     e2e_value = samples / (ms_e2e / args.steps * 1e-3)
 
@@ -397,21 +613,27 @@ def main():
     roof = roofline(rows, args.config) if rows else None
     if rank == 0:
         cpu = None if args.no_cpu else cpu_baseline(args.config)
+        tol = None if args.no_cpu else tolerance(args.config, w, plan, dp, host_batches[0])
         arena_mb = stats["arena_bytes"] / 2**20
         cfg.update({"workload": args.config, "parallelism": f"dp{world}",
                     "l2": f"working set > L2: arena {arena_mb:.0f} MiB per step, no flush",
                     "optimizer": opt_cfg.get("kind") if opt_cfg else None})
-        line = {"metric": "train samples/s", "value": value, "unit": "samples/s",
+        line = {"metric": metric, "value": value, "unit": unit,
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": per_step, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded splitmix64 streams)",
                 "config": cfg,
-                "e2e": {"value": e2e_value, "unit": "samples/s", "h2d_bytes_per_step": h2d,
+                "e2e": {"value": e2e_value, "unit": unit, "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": 4, "wall_ms": wall_e2e},
                 "gpu_launches": stats["kernels"] * args.steps,
                 "roofline": roof, "cpu_baseline": cpu, "clocks": clocks.summary(),
+                "tolerance": tol,
                 "loss": float(last_loss), "wall_ms_timed": wall,
                 "kernels_per_step": stats["kernels"], "gemms_per_step": stats["gemms"]}
+        if args.config in ("gemm", "gemm_skinny") and not args.no_cpu:
+            shape = (4096, 4096, 4096) if args.config == "gemm" else (32768, 768, 3072)
+            line["cublas_baseline"] = cublas_baseline(*shape)
+            line["face_with_copies"] = face_with_copies(*shape)
         if os.environ.get("TB_PROFILE_OUT"):
             with open(os.environ["TB_PROFILE_OUT"], "w") as f:
                 json.dump({"rows": rows, "describe": plan.describe()}, f, indent=1)

@@ -256,7 +256,10 @@ int tb_comm_allreduce(tb_comm* comm, float* device, int64_t count, void* stream)
 /* Replaces: `executed_f32` of the cuda backend (backend/cuda/kernels/gemm.rs:54-163).
  * out[m, n] = a[m, k] . b[k, n] with element (i, j) of a at a[i*a_strides[0] + j*a_strides[1]]
  * (`GemmTask`, payload/gemm.rs:40-125); host buffers.  TB_DECLINED below the size
- * threshold or for unsupported strides. */
+ * threshold or for unsupported strides.  The device workspace is kept per device and grown on
+ * demand; calls on one device are serialized.  A CUDA failure answers TB_RUNTIME and poisons
+ * the library (backend/cuda/kernels/mod.rs:94-105), as it does for tb_map_f32 and
+ * tb_batch_norm_f32. */
 int tb_gemm_f32(const float* a, int64_t a_len, const int64_t a_strides[2],
                 const float* b, int64_t b_len, const int64_t b_strides[2],
                 int64_t m, int64_t k, int64_t n, float* out);
@@ -281,8 +284,14 @@ int tb_batch_norm_f32(const float* input, const float* scale, const float* shift
  * enqueued on `stream` (a cudaStream_t; 0 = the legacy default stream), asynchronous.
  * The only scratch is a fixed 16 MiB device array inside the library: requests needing more
  * than 2*(m+n)*roundup(k,32) <= 4,194,304 floats answer TB_INVALID (tb_last_error says so).
- * The first call on each device resolves the array's address with that device current.
- * Calls that overlap on the GPU share the array and race; the caller serializes them. */
+ * Every call resolves the array's address with the calling device current.  The array is
+ * committed when the library's device code loads on a device (under CUDA's lazy loading, at the
+ * first call that needs it), so make the first call on each device before any stream capture.
+ * Calls that overlap on the GPU share the array and race; the caller serializes them.
+ * TB_OK means the work was enqueued; a launch failure answers TB_RUNTIME and poisons the
+ * library.  A tensor-core wait that expires on the device (a hung copy, 4 s) leaves the output
+ * unwritten and is reported by the next tb_plan_synchronize / tb_run_synchronize, or at once by
+ * the internal hook tbx_gemm_error() read after the caller synchronizes the stream. */
 int tb_gemm_f32_noalloc(const float* a, const int64_t a_strides[2], const float* b,
                         const int64_t b_strides[2], int64_t m, int64_t k, int64_t n, float* out,
                         void* stream);

@@ -30,7 +30,7 @@ def build(force: bool = False) -> str:
     src = os.path.join(HERE, "oracle.cpp")
     if force or not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(src):
         subprocess.check_call([
-            "g++", "-O2", "-std=c++17", "-ffp-contract=off", "-fno-fast-math", "-fPIC",
+            "g++", "-O2", "-std=c++17", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-pthread",
             "-shared", "-o", LIB_PATH, src])
     return LIB_PATH
 
@@ -49,7 +49,15 @@ def lib():
         _LIB.oracle_gemm.restype = None
         _LIB.oracle_map.restype = None
         _LIB.oracle_round_bf16.restype = None
+        _LIB.oracle_set_threads.restype = None
     return _LIB
+
+
+def set_threads(threads: int) -> None:
+    """Host threads for the oracle's GEMMs (default 1, the interpreter's own
+    single thread).  Each output row stays one serial chain, so the results
+    are bit-identical for every thread count."""
+    lib().oracle_set_threads(C.c_int(int(threads)))
 
 
 def run(columns, parameters, feeds=None, read=None):

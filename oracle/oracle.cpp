@@ -34,6 +34,7 @@
 #include <cstring>
 #include <stdexcept>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../include/topos_b200.h"
@@ -217,6 +218,26 @@ Val strided(const Val& a, const std::vector<int64_t>& shape, int64_t offset,
   return out;
 }
 
+// Worker threads for the row-parallel GEMM (1 = the interpreter's single
+// thread).  Set by oracle_set_threads; the test harness may use every core.
+int g_threads = 1;
+
+template <class F>
+void parallel_rows(int64_t total_rows, int64_t work, F&& body) {
+  const int64_t t = std::min<int64_t>(g_threads, total_rows);
+  if (t <= 1 || work * total_rows < (int64_t(1) << 22)) {
+    body(0, total_rows);
+    return;
+  }
+  std::vector<std::thread> pool;
+  const int64_t per = (total_rows + t - 1) / t;
+  for (int64_t i = 0; i < t; ++i) {
+    const int64_t a = i * per, b = std::min(total_rows, a + per);
+    if (a < b) pool.emplace_back([=, &body]() { body(a, b); });
+  }
+  for (auto& th : pool) th.join();
+}
+
 // payload/tensor.rs:921-1027 and payload/gemm.rs:140-211
 Val matmul(const Val& a, const Val& b) {
   int rank = (int)a.shape.size();
@@ -235,12 +256,14 @@ Val matmul(const Val& a, const Val& b) {
   std::vector<float> A(a.volume()), B(b.volume());
   for (int64_t i = 0; i < a.volume(); ++i) A[i] = a.get(i);
   for (int64_t i = 0; i < b.volume(); ++i) B[i] = b.get(i);
-  for (int64_t bt = 0; bt < batches; ++bt) {
-    const float* Ab = A.data() + bt * rows * inner;
-    const float* Bb = B.data() + bt * inner * cols;
-    float* Cb = out.data.data() + bt * rows * cols;
-    for (int64_t r = 0; r < rows; ++r) {
-      float* acc = Cb + r * cols;
+  // Every output row is its own serial chain, so rows may be computed on
+  // several threads (oracle_set_threads) with bit-identical results.
+  auto rows_of = [&](int64_t first_row, int64_t last_row) {
+    for (int64_t q = first_row; q < last_row; ++q) {
+      const int64_t bt = q / rows, r = q % rows;
+      const float* Ab = A.data() + bt * rows * inner;
+      const float* Bb = B.data() + bt * inner * cols;
+      float* acc = out.data.data() + bt * rows * cols + r * cols;
       const float first = Ab[r * inner];
       for (int64_t c = 0; c < cols; ++c) acc[c] = first * Bb[c];
       for (int64_t s = 1; s < inner; ++s) {
@@ -249,7 +272,8 @@ Val matmul(const Val& a, const Val& b) {
         for (int64_t c = 0; c < cols; ++c) acc[c] = acc[c] + av * brow[c];
       }
     }
-  }
+  };
+  parallel_rows(batches * rows, rows * inner * cols, rows_of);
   for (float& v : out.data) v = el(v);  // f32 accumulators, one rounding
   return out;
 }
@@ -711,8 +735,11 @@ int oracle_backward(const tb_plan_desc* desc, const float* const* params, int32_
 
 // The interpreter's serial-order GEMM alone (payload/gemm.rs:140-211) over
 // dense row-major operands: the CPU baseline of the GEMM configs.
+void oracle_set_threads(int threads) { g_threads = threads < 1 ? 1 : threads; }
+
 void oracle_gemm(const float* a, const float* b, float* c, int64_t m, int64_t k, int64_t n) {
-  for (int64_t r = 0; r < m; ++r) {
+  parallel_rows(m, k * n, [&](int64_t r0, int64_t r1) {
+  for (int64_t r = r0; r < r1; ++r) {
     float* acc = c + r * n;
     const float first = a[r * k];
     for (int64_t j = 0; j < n; ++j) acc[j] = first * b[j];
@@ -722,6 +749,7 @@ void oracle_gemm(const float* a, const float* b, float* c, int64_t m, int64_t k,
       for (int64_t j = 0; j < n; ++j) acc[j] = acc[j] + av * brow[j];
     }
   }
+  });
 }
 
 // libm scalar maps of payload/elementary.rs:116-143, for ulp measurements.

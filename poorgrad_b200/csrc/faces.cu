@@ -87,6 +87,61 @@ int64_t span_of(int64_t rows, int64_t cols, const int64_t s[2]) {
   return (rows - 1) * s[0] + (cols - 1) * s[1] + 1;
 }
 
+// Device workspace of the host-buffer faces, one per device, grown on demand
+// and kept for the process: a face call allocates only when a task is larger
+// than every earlier one on that device.  The mutex serializes face calls on a
+// device (the reference shares one cuBLAS handle behind a mutex the same way,
+// backend/cuda/kernels/context.rs:203-212).
+struct FaceDevice {
+  std::mutex mutex;
+  cudaStream_t stream = nullptr;
+  void* buffer = nullptr;
+  size_t bytes = 0;
+};
+FaceDevice g_face[64];
+
+// Poisons the library for a CUDA failure inside a face: one runtime failure
+// disables the backend for good (backend/cuda/kernels/mod.rs:94-105).
+int face_failed(const char* face, cudaError_t e) {
+  char text[256];
+  snprintf(text, sizeof text, "%s: %s", face, cudaGetErrorString(e));
+  tb::poison_library(text);
+  return TB_RUNTIME;
+}
+
+// Claims the calling device's face workspace of at least `bytes` (lock held).
+cudaError_t face_workspace(FaceDevice*& fd, std::unique_lock<std::mutex>& lock, size_t bytes,
+                           void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  fd = &g_face[dev];
+  lock = std::unique_lock<std::mutex>(fd->mutex);
+  if (!fd->stream && (e = cudaStreamCreateWithFlags(&fd->stream, cudaStreamNonBlocking)))
+    return e;
+  if (fd->bytes < bytes) {
+    if (fd->buffer) cudaFree(fd->buffer);
+    fd->buffer = nullptr;
+    fd->bytes = 0;
+    if ((e = cudaMalloc(&fd->buffer, bytes)) != cudaSuccess) return e;
+    fd->bytes = bytes;
+  }
+  *out = fd->buffer;
+  return cudaSuccess;
+}
+
+// Checks the work a face enqueued: launch errors, the stream, and the tcgen05
+// GEMM's wait-expiry flag.
+cudaError_t face_finish(cudaStream_t st) {
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e == cudaSuccess && tb::gemm_error() != 0) e = cudaErrorLaunchTimeout;
+  return e;
+}
+
+size_t round256(size_t bytes) { return (bytes + 255) / 256 * 256; }
+
 }  // namespace
 
 extern "C" int tb_gemm_f32(const float* a, int64_t a_len, const int64_t a_strides[2],
@@ -95,40 +150,42 @@ extern "C" int tb_gemm_f32(const float* a, int64_t a_len, const int64_t a_stride
   char msg[8];
   int s = tb_status(msg, sizeof msg);
   if (s != TB_OK) return s;
-  if (m <= 1 || n <= 1 || 2 * m * n * k < kMinFlops) return TB_DECLINED;
+  if (m <= 1 || n <= 1 || k < 1 || 2 * m * n * k < kMinFlops) return TB_DECLINED;
   if (a_strides[0] < 0 || a_strides[1] < 0 || b_strides[0] < 0 || b_strides[1] < 0)
     return TB_DECLINED;
   if (span_of(m, k, a_strides) > a_len || span_of(k, n, b_strides) > b_len) return TB_INVALID;
   const int64_t kp = (k + 31) / 32 * 32;
-  float *da = nullptr, *db = nullptr, *dc = nullptr, *ws = nullptr;
   const int64_t al = span_of(m, k, a_strides), bl = span_of(k, n, b_strides);
-  cudaStream_t st = nullptr;
-  int rc = TB_OK;
-  do {
-    if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) { rc = TB_RUNTIME; break; }
-    if (cudaMalloc(&da, al * 4) || cudaMalloc(&db, bl * 4) || cudaMalloc(&dc, m * n * 4) ||
-        cudaMalloc(&ws, (2 * m * kp + 2 * n * kp) * 4)) { rc = TB_RUNTIME; break; }
-    cudaMemcpyAsync(da, a, al * 4, cudaMemcpyHostToDevice, st);
-    cudaMemcpyAsync(db, b, bl * 4, cudaMemcpyHostToDevice, st);
-    float* ahi = ws;
-    float* alo = ahi + m * kp;
-    float* bhi = alo + m * kp;
-    float* blo = bhi + n * kp;
-    int grid = 148 * 4;
-    k_prep_strided<<<grid, 256, 0, st>>>(da, a_strides[0], a_strides[1], m, k, kp, ahi, alo);
-    // B^T as [n, k]: row j of B^T walks column j of B
-    k_prep_strided<<<grid, 256, 0, st>>>(db, b_strides[1], b_strides[0], n, k, kp, bhi, blo);
-    tb::launch_gemm(tb::k_major(ahi, alo, m, kp), tb::k_major(bhi, blo, n, kp), dc, nullptr, 1,
-                    1, m, n, kp, st);
-    cudaMemcpyAsync(out, dc, m * n * 4, cudaMemcpyDeviceToHost, st);
-    if (cudaStreamSynchronize(st) != cudaSuccess) rc = TB_RUNTIME;
-  } while (false);
-  if (da) cudaFree(da);
-  if (db) cudaFree(db);
-  if (dc) cudaFree(dc);
-  if (ws) cudaFree(ws);
-  if (st) cudaStreamDestroy(st);
-  return rc;
+  const size_t ab = round256(al * 4), bb = round256(bl * 4), cb = round256(m * n * 4);
+  const size_t wb = (size_t)(2 * m * kp + 2 * n * kp) * 4;
+  FaceDevice* fd = nullptr;
+  std::unique_lock<std::mutex> lock;
+  void* base = nullptr;
+  cudaGetLastError();  // an earlier call's launch error is not this call's
+  cudaError_t e = face_workspace(fd, lock, ab + bb + cb + wb, &base);
+  if (e != cudaSuccess) return face_failed("tb_gemm_f32", e);
+  cudaStream_t st = fd->stream;
+  float* da = (float*)base;
+  float* db = (float*)((char*)base + ab);
+  float* dc = (float*)((char*)base + ab + bb);
+  float* ahi = (float*)((char*)base + ab + bb + cb);
+  float* alo = ahi + m * kp;
+  float* bhi = alo + m * kp;
+  float* blo = bhi + n * kp;
+  if ((e = cudaMemcpyAsync(da, a, al * 4, cudaMemcpyHostToDevice, st)) ||
+      (e = cudaMemcpyAsync(db, b, bl * 4, cudaMemcpyHostToDevice, st)))
+    return face_failed("tb_gemm_f32", e);
+  const int grid = 148 * 4;
+  k_prep_strided<<<grid, 256, 0, st>>>(da, a_strides[0], a_strides[1], m, k, kp, ahi, alo);
+  // B^T as [n, k]: row j of B^T walks column j of B
+  k_prep_strided<<<grid, 256, 0, st>>>(db, b_strides[1], b_strides[0], n, k, kp, bhi, blo);
+  tb::launch_gemm(tb::k_major(ahi, alo, m, kp), tb::k_major(bhi, blo, n, kp), dc, nullptr, 1, 1,
+                  m, n, kp, st);
+  if ((e = cudaGetLastError()) != cudaSuccess ||
+      (e = cudaMemcpyAsync(out, dc, m * n * 4, cudaMemcpyDeviceToHost, st)) != cudaSuccess ||
+      (e = face_finish(st)) != cudaSuccess)
+    return face_failed("tb_gemm_f32", e);
+  return TB_OK;
 }
 
 extern "C" int tb_map_f32(int32_t op, const float* in, int64_t count, float* out) {
@@ -138,14 +195,22 @@ extern "C" int tb_map_f32(int32_t op, const float* in, int64_t count, float* out
   if (op != TB_OP_EXP && op != TB_OP_LN && op != TB_OP_SQRT && op != TB_OP_TANH)
     return TB_DECLINED;
   if (count < (1 << 17)) return TB_DECLINED;
-  float *d = nullptr;
-  if (cudaMalloc(&d, count * 8) != cudaSuccess) return TB_RUNTIME;
-  cudaMemcpy(d, in, count * 4, cudaMemcpyHostToDevice);
-  k_map<<<148 * 8, 256>>>(op, d, d + count, count);
-  cudaMemcpy(out, d + count, count * 4, cudaMemcpyDeviceToHost);
-  cudaError_t e = cudaGetLastError();
-  cudaFree(d);
-  return e == cudaSuccess ? TB_OK : TB_RUNTIME;
+  FaceDevice* fd = nullptr;
+  std::unique_lock<std::mutex> lock;
+  void* base = nullptr;
+  cudaGetLastError();
+  cudaError_t e = face_workspace(fd, lock, (size_t)count * 8, &base);
+  if (e != cudaSuccess) return face_failed("tb_map_f32", e);
+  float* d = (float*)base;
+  cudaStream_t st = fd->stream;
+  if ((e = cudaMemcpyAsync(d, in, count * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess)
+    return face_failed("tb_map_f32", e);
+  k_map<<<148 * 8, 256, 0, st>>>(op, d, d + count, count);
+  if ((e = cudaGetLastError()) != cudaSuccess ||
+      (e = cudaMemcpyAsync(out, d + count, count * 4, cudaMemcpyDeviceToHost, st)) ||
+      (e = face_finish(st)) != cudaSuccess)
+    return face_failed("tb_map_f32", e);
+  return TB_OK;
 }
 
 extern "C" int tb_batch_norm_f32(const float* input, const float* scale, const float* shift,
@@ -157,21 +222,29 @@ extern "C" int tb_batch_norm_f32(const float* input, const float* scale, const f
   if (batch < 1 || features < 1) return TB_INVALID;
   if (batch * features < (1 << 17)) return TB_DECLINED;
   const int64_t n = batch * features;
-  float* d = nullptr;
-  if (cudaMalloc(&d, (2 * n + 4 * features) * 4) != cudaSuccess) return TB_RUNTIME;
+  FaceDevice* fd = nullptr;
+  std::unique_lock<std::mutex> lock;
+  void* base = nullptr;
+  cudaGetLastError();
+  cudaError_t e = face_workspace(fd, lock, (size_t)(2 * n + 4 * features) * 4, &base);
+  if (e != cudaSuccess) return face_failed("tb_batch_norm_f32", e);
+  float* d = (float*)base;
   float *dx = d, *dout = d + n, *dscale = d + 2 * n, *dshift = dscale + features,
         *dmean = dshift + features, *dvar = dmean + features;
-  cudaMemcpy(dx, input, n * 4, cudaMemcpyHostToDevice);
-  cudaMemcpy(dscale, scale, features * 4, cudaMemcpyHostToDevice);
-  cudaMemcpy(dshift, shift, features * 4, cudaMemcpyHostToDevice);
-  k_batch_norm<<<(unsigned)((features + 127) / 128), 128>>>(dx, dscale, dshift, epsilon, batch,
-                                                            features, dout, dmean, dvar);
-  cudaMemcpy(output, dout, n * 4, cudaMemcpyDeviceToHost);
-  cudaMemcpy(mean, dmean, features * 4, cudaMemcpyDeviceToHost);
-  cudaMemcpy(variance, dvar, features * 4, cudaMemcpyDeviceToHost);
-  cudaError_t e = cudaGetLastError();
-  cudaFree(d);
-  return e == cudaSuccess ? TB_OK : TB_RUNTIME;
+  cudaStream_t st = fd->stream;
+  if ((e = cudaMemcpyAsync(dx, input, n * 4, cudaMemcpyHostToDevice, st)) ||
+      (e = cudaMemcpyAsync(dscale, scale, features * 4, cudaMemcpyHostToDevice, st)) ||
+      (e = cudaMemcpyAsync(dshift, shift, features * 4, cudaMemcpyHostToDevice, st)))
+    return face_failed("tb_batch_norm_f32", e);
+  k_batch_norm<<<(unsigned)((features + 127) / 128), 128, 0, st>>>(
+      dx, dscale, dshift, epsilon, batch, features, dout, dmean, dvar);
+  if ((e = cudaGetLastError()) ||
+      (e = cudaMemcpyAsync(output, dout, n * 4, cudaMemcpyDeviceToHost, st)) ||
+      (e = cudaMemcpyAsync(mean, dmean, features * 4, cudaMemcpyDeviceToHost, st)) ||
+      (e = cudaMemcpyAsync(variance, dvar, features * 4, cudaMemcpyDeviceToHost, st)) ||
+      (e = face_finish(st)))
+    return face_failed("tb_batch_norm_f32", e);
+  return TB_OK;
 }
 
 // ---- internal hooks for tests (not part of the public ABI)
@@ -226,8 +299,10 @@ extern "C" int tbx_gemm_splits(int64_t batch, int64_t m, int64_t n, int64_t kp) 
 // code that must never allocate after start-up.  tb_gemm_f32_noalloc serves
 // them: the caller passes device inputs and output, and the only scratch --
 // the tf32 hi/lo split of both operands -- lives in the fixed array below.
-// The array is a file-scope device variable: every GPU that loads the library
-// holds its 16 MiB until the process exits.  All calls on a device share it,
+// The array is a file-scope device variable of 16 MiB.  It is committed on a
+// device when the library's device code loads there (with CUDA's lazy module
+// loading, at the first call that needs it, e.g. this entry point's first
+// call) and is held until the process exits.  All calls on a device share it,
 // so calls that overlap on the GPU (different streams, or different host
 // threads) race on it; callers serialize them.  Each call rewrites every
 // scratch element it reads (padding included), so nothing needs clearing.
@@ -235,27 +310,38 @@ namespace {
 constexpr int64_t kNoAllocScratchFloats = int64_t(4) << 20;  // 16 MiB of f32
 __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
 
-std::mutex g_noalloc_mutex;
-float* g_noalloc_ptr[256] = {};  // per device: the array's device address
-
-// Host code cannot use the array's name as a device address: resolve it once
-// per device, with that device current.
-float* noalloc_scratch(int device) {
-  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (device < 0 || device >= 256) return nullptr;
-  if (!g_noalloc_ptr[device]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) return nullptr;
-    g_noalloc_ptr[device] = (float*)p;
-  }
-  return g_noalloc_ptr[device];
+// Host code cannot use the array's name as a device address: it is resolved
+// on every call, with the calling device current, so a cached address can
+// never outlive its context (a device reset, another context).
+float* noalloc_scratch() {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) return nullptr;
+  return (float*)p;
 }
 }  // namespace
 
 extern "C" int tb_gemm_f32_noalloc(const float* a, const int64_t a_strides[2], const float* b,
                                    const int64_t b_strides[2], int64_t m, int64_t k, int64_t n,
                                    float* out, void* stream) {
-  // readiness without the library's lazy set-up (which initializes the context
+  // the request first: a malformed or oversized one is refused before any CUDA call
+  if (!a || !b || !out || m < 1 || n < 1 || k < 1 || a_strides[0] < 0 || a_strides[1] < 0 ||
+      b_strides[0] < 0 || b_strides[1] < 0) {
+    tb::set_last_error("tb_gemm_f32_noalloc: invalid pointers, shape or strides");
+    return TB_INVALID;
+  }
+  // each extent alone must fit before any product is formed, so that the size
+  // arithmetic below cannot overflow
+  if (m > kNoAllocScratchFloats || n > kNoAllocScratchFloats || k > kNoAllocScratchFloats ||
+      2 * (m + n) * ((k + 31) / 32 * 32) > kNoAllocScratchFloats) {
+    char text[240];
+    snprintf(text, sizeof text,
+             "tb_gemm_f32_noalloc: m=%lld k=%lld n=%lld needs 2*(m+n)*roundup(k,32) floats of "
+             "scratch; the fixed scratch holds %lld (16 MiB)",
+             (long long)m, (long long)k, (long long)n, (long long)kNoAllocScratchFloats);
+    tb::set_last_error(text);
+    return TB_INVALID;
+  }
+  // then readiness, without the library's lazy set-up (which initializes the context
   // through a cudaFree(nullptr) call this entry point must not make)
   int count = 0;
   if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
@@ -266,25 +352,8 @@ extern "C" int tb_gemm_f32_noalloc(const float* a, const int64_t a_strides[2], c
     tb::set_last_error("tb_gemm_f32_noalloc: the backend is poisoned");
     return TB_POISONED;
   }
-  if (m < 1 || n < 1 || k < 1 || a_strides[0] < 0 || a_strides[1] < 0 || b_strides[0] < 0 ||
-      b_strides[1] < 0) {
-    tb::set_last_error("tb_gemm_f32_noalloc: invalid shape or strides");
-    return TB_INVALID;
-  }
   const int64_t kp = (k + 31) / 32 * 32;
-  const int64_t need = 2 * (m + n) * kp;
-  if (need > kNoAllocScratchFloats) {
-    char text[200];
-    snprintf(text, sizeof text,
-             "tb_gemm_f32_noalloc: needs %lld floats of scratch (2*(m+n)*roundup(k,32)); the "
-             "fixed scratch holds %lld (16 MiB)",
-             (long long)need, (long long)kNoAllocScratchFloats);
-    tb::set_last_error(text);
-    return TB_INVALID;
-  }
-  int device = 0;
-  if (cudaGetDevice(&device) != cudaSuccess) return TB_RUNTIME;
-  float* ws = noalloc_scratch(device);
+  float* ws = noalloc_scratch();
   if (!ws) {
     tb::set_last_error("tb_gemm_f32_noalloc: cudaGetSymbolAddress failed");
     return TB_RUNTIME;
@@ -295,9 +364,12 @@ extern "C" int tb_gemm_f32_noalloc(const float* a, const int64_t a_strides[2], c
   float* bhi = alo + m * kp;
   float* blo = bhi + n * kp;
   const int grid = 148 * 4;
+  cudaGetLastError();  // a launch error left by earlier, unrelated work is not this call's
   k_prep_strided<<<grid, 256, 0, st>>>(a, a_strides[0], a_strides[1], m, k, kp, ahi, alo);
   k_prep_strided<<<grid, 256, 0, st>>>(b, b_strides[1], b_strides[0], n, k, kp, bhi, blo);
   tb::launch_gemm(tb::k_major(ahi, alo, m, kp), tb::k_major(bhi, blo, n, kp), out, nullptr, 1, 1,
                   m, n, kp, st);
-  return cudaPeekAtLastError() == cudaSuccess ? TB_OK : TB_RUNTIME;
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return face_failed("tb_gemm_f32_noalloc", e);
+  return TB_OK;
 }

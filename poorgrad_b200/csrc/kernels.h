@@ -82,6 +82,9 @@ int gemm_error();
 void set_last_error(const char* message);
 // Whether an earlier runtime failure poisoned the library.
 bool poisoned();
+// Records a runtime failure of a per-task face: the library answers
+// TB_POISONED from then on (backend/cuda/kernels/mod.rs:94-105).
+void poison_library(const char* why);
 // Selects the GEMM engine: 0 = automatic, 1 = SIMT only, 2 = tcgen05 only.
 void set_gemm_engine(int engine);
 int gemm_engine();

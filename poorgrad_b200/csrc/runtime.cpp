@@ -234,6 +234,10 @@ bool poisoned() {
   std::lock_guard<std::mutex> lock(g_mutex);
   return g_state == TB_POISONED;
 }
+void poison_library(const char* why) {
+  g_error = why;
+  poison(why);
+}
 }  // namespace tb
 
 struct tb_instance;
@@ -894,9 +898,19 @@ int tb_plan_gradient_node(const tb_plan* plan, int64_t root, int64_t parameter, 
   }, false);
 }
 
+// A kernel whose bounded wait expired recorded a code instead of hanging: the
+// run's values are not to be trusted, which is a runtime failure (poisons).
+static void check_device_flags() {
+  const int g = tb::gemm_error(), s = tb::segment_error();
+  if (g || s)
+    runtime_fail("a device wait expired (gemm code " + std::to_string(g) + ", segment code " +
+                 std::to_string(s) + ")");
+}
+
 int tb_plan_synchronize(tb_plan* plan) {
   return guarded([&]() {
     check(cudaStreamSynchronize(plan->main->stream), "cudaStreamSynchronize");
+    check_device_flags();
     return (int)TB_OK;
   });
 }
@@ -952,6 +966,7 @@ int tb_run_begin(tb_plan* plan, tb_params* params, int32_t feed_count, const tb_
 int tb_run_synchronize(tb_run* run) {
   return guarded([&]() {
     check(cudaStreamSynchronize(run->inst->stream), "cudaStreamSynchronize");
+    check_device_flags();
     return (int)TB_OK;
   });
 }

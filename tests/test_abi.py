@@ -50,13 +50,15 @@ def test_c2_is_one_fused_pass_over_x(built):
     assert first.startswith("0: row") and len(first.split("members=")[1].split()) >= 4
 
 
-def test_the_documented_rust_binding_declares_every_entry_point():
-    # the reference-side binding a maintainer adds stays
-    # in step with the header
-    import os
-    import re
-    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    text = open(os.path.join(root, "INTEGRATION.md")).read()
-    bound = set(re.findall(r"pub fn (tb_\w+)\(", text))
-    missing = sorted(set(abi.header_symbols()) - bound)
-    assert not missing, missing
+def test_noalloc_gemm_refuses_oversized_requests_before_any_cuda_call():
+    # the size check comes first and cannot overflow: an absurd extent is an
+    # invalid request, answered without touching a device
+    import ctypes as C
+    lib = abi.load_library()
+    s = (C.c_int64 * 2)(1, 1)
+    big = (1 << 58) - 1
+    for m, k, n in [(big, 1, 1), (1, big, 1), (1, 1, big), (4096, 1024, 4096)]:
+        rc = lib.tb_gemm_f32_noalloc(C.c_void_p(256), s, C.c_void_p(256), s, m, k, n,
+                                     C.c_void_p(256), None)
+        assert rc == 6, (m, k, n)
+        assert b"fixed scratch holds" in lib.tb_last_error()

@@ -1,0 +1,166 @@
+"""Device parity at the benchmarked sizes, against the CPU oracle.
+
+Each config of the benchmark runs at its full size through the C ABI and is
+compared with the oracle (the interpreter's arithmetic, `oracle/oracle.cpp`)
+on the same seeded inputs (plan == interpreter, engine/tests/plan_tests.rs:9-22):
+
+  * C4 char-MLP at batch 16384 (the bench's headline step): loss and every
+    gradient, and an 8-step Adam trajectory;
+  * C2 fused microbench at 8192 x 8192: row sums and every gradient;
+  * C3 GEMMs at 4096^3 and 32768 x 768 x 3072: a sampled block of 64 rows x 64
+    columns of C, dA and dB against the serial-k product of the same slices;
+  * C5 GPT-2-small at full widths (12 layers, d 768, vocab 50257) at batch 1,
+    sequence 128: loss and every gradient.
+
+Bars (each assertion states its own):
+  * whole configs: |dev - ref| <= rtol |ref| + atol max|ref| per output, the
+    values of the test-size config tests (rtol 1e-3, atol 1e-4; C2 rtol 2e-5,
+    atol 1e-5);
+  * GEMM blocks: within 8 eps sqrt(k) (1 + |exact|) of the f64 product
+    (backend/cuda/tests/cuda_tests.rs:141-150), and within that bar plus the
+    oracle's own distance from the f64 product of the oracle (its serial f32
+    chain drifts past the bar for k >= 4096);
+  * trajectory: loss drift per step <= 2e-3 relative, parameters after the
+    last step within 50x that of their scale (tests/test_trajectories.py).
+
+The oracle's GEMMs run on every host core (`oracle.set_threads`); each output
+row stays one serial chain, so its results do not depend on the thread count.
+With TB_PARITY_REPORT=<path> the measured errors are appended there as JSON
+lines."""
+import json
+import math
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from oracle import optim
+from poorgrad_b200 import backend, configs, neural
+
+pytestmark = pytest.mark.gpu
+EPS = float(np.finfo(np.float32).eps)
+
+
+@pytest.fixture(scope="module", autouse=True)
+def oracle_threads(built):
+    oracle.set_threads(os.cpu_count() or 1)
+    yield
+    oracle.set_threads(1)
+
+
+def report(config, **fields):
+    path = os.environ.get("TB_PARITY_REPORT")
+    if path:
+        with open(path, "a") as f:
+            f.write(json.dumps({"config": config, **fields}) + "\n")
+
+
+def scaled_errors(dev, ref, rtol, atol):
+    """Per output: max |d - r| / (rtol |r| + atol max|r|); <= 1 passes."""
+    worst = {}
+    for i, r in ref.items():
+        d = dev[i]
+        scale = float(np.abs(r).max()) + 1e-30
+        worst[i] = float(np.max(np.abs(d - r) / (rtol * np.abs(r) + atol * scale)))
+    return worst
+
+
+def run_both(w, feeds, rtol, atol, config):
+    params = w.network.parameters()
+    ref = oracle.run(w.columns, params, feeds)
+    plan = backend.DevicePlan(w.columns)
+    dp = backend.DeviceParameters(plan, params)
+    plan.forward(dp, feeds, sync=True)
+    dev = {i: plan.of(i) for i in ref}
+    worst = scaled_errors(dev, ref, rtol, atol)
+    rel = {i: float(np.abs(dev[i] - ref[i]).max() / (np.abs(ref[i]).max() + 1e-30)) for i in ref}
+    report(config, outputs=len(ref), worst_scaled=max(worst.values()),
+           max_rel_to_scale=max(rel.values()), rtol=rtol, atol=atol)
+    bad = {i: v for i, v in worst.items() if v > 1.0}
+    assert not bad, f"outputs beyond the bar (ratio): {bad}"
+    return plan, dp
+
+
+def test_c4_char_mlp_at_batch_16384(device):
+    w = configs.char_mlp(batch=16384, seed=4)
+    run_both(w, w.feeds(0), rtol=1e-3, atol=1e-4, config="C4 batch 16384")
+
+
+def test_c4_adam_trajectory_at_batch_16384(device):
+    w = configs.char_mlp(batch=16384, seed=4)
+    opt = w.optimizer
+    params0 = w.network.parameters()
+    plan = backend.DevicePlan(w.columns)
+    dp = backend.DeviceParameters(plan, params0)
+    optimizer = backend.Optimizer(plan, dp, backend.ADAM, zip(w.params, w.grads), opt["lr"],
+                                  opt["beta1"], opt["beta2"], opt["eps"])
+    params = [p.reshape(w.columns.nodes[s.index].shape).copy() for p, s in zip(params0, w.params)]
+    host = optim.make("adam", opt)
+    drift = []
+    for step in range(8):
+        feeds = w.feeds(step)
+        plan.forward(dp, feeds, sync=True)
+        dev_loss = float(plan.of(w.loss))
+        ref = oracle.run(w.columns, params, feeds, read=[w.loss.index] + [g.index for g in w.grads])
+        ref_loss = float(ref[w.loss.index])
+        drift.append(abs(dev_loss - ref_loss) / max(abs(ref_loss), 1e-30))
+        params = host.step(params, [ref[g.index] for g in w.grads], opt["lr"])
+    worst_param = 0.0
+    for p_ref, sym in zip(params, w.params):
+        got = dp.download(w.columns.nodes[sym.index].slot).reshape(p_ref.shape)
+        worst_param = max(worst_param,
+                          float(np.abs(got - p_ref).max() / (np.abs(p_ref).max() + 1e-30)))
+    report("C4 batch 16384, 8 Adam steps", loss_drift=drift, param_rel_to_scale=worst_param)
+    assert max(drift) <= 2e-3, drift
+    assert worst_param <= 50 * 2e-3
+    del optimizer
+
+
+def test_c2_fused_at_8192_squared(device):
+    w = configs.fused()
+    run_both(w, {}, rtol=2e-5, atol=1e-5, config="C2 8192x8192")
+
+
+@pytest.mark.parametrize("m,k,n", [(4096, 4096, 4096), (32768, 768, 3072)])
+def test_c3_gemm_sampled_blocks(device, m, k, n):
+    w = configs.gemm(m, k, n)
+    params = w.network.parameters()
+    A = params[0].reshape(m, k)
+    B = params[1].reshape(k, n)
+    dC = neural.normal(3 + 2, 1.0)((m, n)).reshape(m, n)
+    plan = backend.DevicePlan(w.columns)
+    dp = backend.DeviceParameters(plan, params)
+    plan.forward(dp, {}, sync=True)
+    Cd = plan.of(w.extra["C"])
+    dAd = plan.of(w.grads[0])
+    dBd = plan.of(w.grads[1])
+    rng = np.random.default_rng(11)
+    worst = {}
+    for name, dev, left, right, depth in [
+            ("C", Cd, lambda I: A[I, :], lambda J: B[:, J], k),
+            ("dA", dAd, lambda I: dC[I, :], lambda J: B[J, :].T, n),
+            ("dB", dBd, lambda I: A[:, I].T, lambda J: dC[:, J], m)]:
+        rows, cols = dev.shape
+        I = np.sort(rng.choice(rows, 64, replace=False))
+        J = np.sort(rng.choice(cols, 64, replace=False))
+        L = np.ascontiguousarray(left(I))
+        R = np.ascontiguousarray(right(J))
+        exact = L.astype(np.float64) @ R.astype(np.float64)
+        serial = oracle.gemm(L, R).astype(np.float64)
+        got = dev[np.ix_(I, J)].astype(np.float64)
+        bar = 8 * EPS * math.sqrt(depth) * (1 + np.abs(exact))
+        vs_exact = float(np.max(np.abs(got - exact) / bar))
+        vs_oracle = float(np.max(np.abs(got - serial) / (bar + np.abs(serial - exact))))
+        oracle_own = float(np.max(np.abs(serial - exact) / bar))
+        worst[name] = (vs_exact, vs_oracle, oracle_own)
+    report(f"C3 {m}x{k}x{n}", blocks={k_: {"dev_vs_f64": v[0], "dev_vs_oracle": v[1],
+                                           "oracle_vs_f64": v[2]} for k_, v in worst.items()})
+    for name, (vs_exact, vs_oracle, _) in worst.items():
+        assert vs_exact <= 1.0, (name, vs_exact)
+        assert vs_oracle <= 1.0, (name, vs_oracle)
+
+
+def test_c5_gpt2_full_widths_one_sequence_of_128(device):
+    w = configs.gpt2(batch=1, seq=128)
+    run_both(w, w.feeds(0), rtol=1e-3, atol=1e-4, config="C5 full widths, 1 x 128")
