@@ -11,6 +11,8 @@
 #include <cstdio>
 #include <cstring>
 #include <functional>
+#include <map>
+#include <set>
 #include <sstream>
 #include <stdexcept>
 #include <unordered_map>
@@ -1226,6 +1228,16 @@ class Emitter {
   // a bf16 network holds bf16 values: a loaded value (a source, or a
   // library kernel's f32 accumulation) and each operation's result round once;
   // rounding is idempotent, so values already rounded pass unchanged
+  // Variables known never to hold -0 (results of a sum with a +0 literal), and
+  // the operand of each emitted negation.
+  std::set<std::string> no_negative_zero;
+  std::map<std::string, std::string> negation_of;
+  bool never_negative_zero(const std::string& v) const {
+    if (no_negative_zero.count(v)) return true;
+    // a literal other than -0
+    return v.rfind("__int_as_float(0x", 0) == 0 && v != flit(-0.0f);
+  }
+
   std::string rounded(const std::string& v) {
     if (!P.bf16) return v;
     const std::string k = "rb|" + v;
@@ -1375,6 +1387,20 @@ class Emitter {
     if (is_elementwise(nd.op)) {
       std::string x = ref(a, idx);
       std::string y = b >= 0 ? ref(b, idx) : "";
+      // Exact identities (f32 only): 1*y is y; 0+y is y when y is never -0
+      // (the sum of anything and +0 is never -0, so only the first of a chain
+      // of `0 + ...` seeds is kept); -(-y) is y.
+      if (!P.bf16) {
+        const std::string one = flit(1.0f), zero = flit(0.0f);
+        if (nd.op == TB_OP_MUL && (x == one || y == one)) return x == one ? y : x;
+        if (nd.op == TB_OP_ADD && ((x == zero && never_negative_zero(y)) ||
+                                   (y == zero && never_negative_zero(x))))
+          return x == zero ? y : x;
+        if (nd.op == TB_OP_NEG) {
+          auto it = negation_of.find(x);
+          if (it != negation_of.end()) return it->second;
+        }
+      }
       std::string e;
       switch (nd.op) {
         case TB_OP_ADD: e = "__fadd_rn(" + x + ", " + y + ")"; break;
@@ -1394,6 +1420,10 @@ class Emitter {
       if (is_transcendental(nd.op)) exact = false;
       std::string v = var();
       line("const float " + v + " = " + (P.bf16 ? "tb_rb(" + e + ")" : e) + ";");
+      if (!P.bf16) {
+        if (nd.op == TB_OP_ADD && (x == flit(0.0f) || y == flit(0.0f))) no_negative_zero.insert(v);
+        if (nd.op == TB_OP_NEG) negation_of[v] = x;
+      }
       return v;
     }
     const Node& on = P.nodes[a >= 0 ? a : n];

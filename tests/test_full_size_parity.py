@@ -118,8 +118,36 @@ def test_c4_adam_trajectory_at_batch_16384(device):
 
 
 def test_c2_fused_at_8192_squared(device):
+    # the gradient of the scalar `a` is one sum over all 67M elements: the
+    # oracle's serial f32 fold of that many terms is itself far from the exact
+    # sum, so that output is held to the f64 sum of the same terms instead,
+    # within 1e-6 of the sum of their magnitudes, and to the oracle within that
+    # bar plus the oracle's own distance from the f64 sum
     w = configs.fused()
-    run_both(w, {}, rtol=2e-5, atol=1e-5, config="C2 8192x8192")
+    params = w.network.parameters()
+    ref = oracle.run(w.columns, params, {})
+    plan = backend.DevicePlan(w.columns)
+    dp = backend.DeviceParameters(plan, params)
+    plan.forward(dp, {}, sync=True)
+    da = w.grads[2].index
+    dev = {i: plan.of(i) for i in ref}
+    worst = scaled_errors({i: v for i, v in dev.items() if i != da},
+                          {i: v for i, v in ref.items() if i != da}, 2e-5, 1e-5)
+    X = params[0].reshape(8192, 8192).astype(np.float64)
+    b = params[1].astype(np.float64)
+    a = float(params[2])
+    t = np.tanh(a * X + b[None, :])
+    terms = (1.0 / (1.0 + np.exp(-X))) * (1.0 - t * t) * X
+    exact = float(terms.sum())
+    magnitude = float(np.abs(terms).sum())
+    bar = 1e-6 * magnitude
+    got, serial = float(dev[da]), float(ref[da])
+    report("C2 8192x8192", outputs=len(ref), worst_scaled=max(worst.values()),
+           da={"dev_vs_f64": abs(got - exact) / bar, "oracle_vs_f64": abs(serial - exact) / bar,
+               "exact": exact, "sum_of_magnitudes": magnitude})
+    assert max(worst.values()) <= 1.0, worst
+    assert abs(got - exact) <= bar, (got, exact, bar)
+    assert abs(got - serial) <= bar + abs(serial - exact)
 
 
 @pytest.mark.parametrize("m,k,n", [(4096, 4096, 4096), (32768, 768, 3072)])
