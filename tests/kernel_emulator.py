@@ -55,6 +55,9 @@ def _host_source(source: str, names) -> str:
             continue
         if 'asm("cvt.rna.tf32.f32' in line:
             line = "  r = emu_tf32_bits(x);"
+        if 'asm("rcp.approx.f32' in line:
+            # the hardware reciprocal estimate, restated as the rounded reciprocal
+            line = "  r = 1.0f / y;"
         out.append(line)
     for name in sorted(names):
         out.append(
