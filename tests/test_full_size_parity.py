@@ -135,7 +135,7 @@ def test_c2_fused_at_8192_squared(device):
                           {i: v for i, v in ref.items() if i != da}, 2e-5, 1e-5)
     X = params[0].reshape(8192, 8192).astype(np.float64)
     b = params[1].astype(np.float64)
-    a = float(params[2])
+    a = float(np.asarray(params[2]).reshape(-1)[0])
     t = np.tanh(a * X + b[None, :])
     terms = (1.0 / (1.0 + np.exp(-X))) * (1.0 - t * t) * X
     exact = float(terms.sum())
