@@ -1217,10 +1217,21 @@ class Emitter {
   int indent = 2;
   bool exact = true;
   // Set for a kernel already known to carry a tolerance (a transcendental or a
-  // reassociated reduction): its divisions use tb_div (about 1 ulp instead of
+  // reassociated reduction): its divisions multiply by tb_rcp (about 2 ulp instead of
   // correctly rounded) and `0 + x` gradient seeds are dropped (they differ
   // from x only in the sign of a zero).  Exact kernels never set it.
   bool relaxed = false;
+  // Values that already carry a tolerance: results of transcendentals, row
+  // reductions, and anything computed from them.  A kernel whose every member
+  // is such a value (or a reduction) may be emitted relaxed: no exact output
+  // can observe the relaxation.
+  std::set<std::string> tainted;
+  std::set<int> tainted_members;
+  bool exact_member_seen = false;
+  bool is_tainted(const std::string& v) const { return tainted.count(v) || v.rfind("rv", 0) == 0; }
+  void note_member_value(const std::string& v) {
+    if (!is_tainted(v)) exact_member_seen = true;
+  }
   bool wide = false;             // 64-bit indices
   int vec = 1;
 
@@ -1330,9 +1341,13 @@ class Emitter {
       const Member& m = K.members[mit->second];
       if ((m.type == MemberType::ROW_SUM || m.type == MemberType::ROW_MAX) && m.phase < phase)
         return "rv" + std::to_string(mit->second);
-      if (in_registers.count(mit->second) && m.phase < phase)
-        return "kr" + std::to_string(mit->second) + "[kc * " + std::to_string(vec) + " + " +
-               std::to_string(idx.lane >= 0 ? idx.lane : 0) + "]";
+      if (in_registers.count(mit->second) && m.phase < phase) {
+        const std::string r = "kr" + std::to_string(mit->second) + "[kc * " +
+                              std::to_string(vec) + " + " +
+                              std::to_string(idx.lane >= 0 ? idx.lane : 0) + "]";
+        if (tainted_members.count(mit->second)) tainted.insert(r);
+        return r;
+      }
     }
     if (f.kind == Kind::Sel && !f.materialized) {
       std::string v = var();
@@ -1414,7 +1429,8 @@ class Emitter {
         case TB_OP_SUB: e = "__fsub_rn(" + x + ", " + y + ")"; break;
         case TB_OP_MUL: e = "__fmul_rn(" + x + ", " + y + ")"; break;
         case TB_OP_DIV:
-          e = (relaxed && !P.bf16 ? "tb_div(" : "__fdiv_rn(") + x + ", " + y + ")";
+          e = relaxed && !P.bf16 ? "__fmul_rn(" + x + ", tb_rcp(" + y + "))"
+                                 : "__fdiv_rn(" + x + ", " + y + ")";
           break;
         case TB_OP_NEG: e = "(-" + x + ")"; break;
         case TB_OP_TANH: e = "tanhf(" + x + ")"; break;
@@ -1428,6 +1444,8 @@ class Emitter {
       }
       if (is_transcendental(nd.op)) exact = false;
       std::string v = var();
+      if (is_transcendental(nd.op) || is_tainted(x) || (!y.empty() && is_tainted(y)))
+        tainted.insert(v);
       line("const float " + v + " = " + (P.bf16 ? "tb_rb(" + e + ")" : e) + ";");
       if (!P.bf16) {
         if (nd.op == TB_OP_ADD && (x == flit(0.0f) || y == flit(0.0f))) no_negative_zero.insert(v);
@@ -1574,17 +1592,18 @@ __device__ __forceinline__ void tb_lse_merge(float& m, float& s, float m2, float
   if (m2 > m) { s = s * expf(m - m2) + s2; m = m2; }
   else s = s + s2 * expf(m2 - m);
 }
-// x / y for kernels that carry a tolerance: Newton-Raphson division (one
-// correction of the quotient from the hardware reciprocal estimate, the
-// residual x - y*q taken exactly by an FMA; Markstein's scheme), within about
-// 1 ulp of the correctly rounded quotient.  Zero, infinite and NaN operands
-// take the estimate's quotient, whose special values are already IEEE's.
-__device__ __forceinline__ float tb_div(float x, float y) {
+// 1 / y for kernels that carry a tolerance: the hardware reciprocal estimate
+// with one Newton-Raphson correction (the residual 1 - y*r taken exactly by an
+// FMA), within about 1 ulp of the correctly rounded reciprocal.  Such kernels
+// divide as x * tb_rcp(y) (within about 2 ulp of x / y): a divisor shared by
+// a row's elements then costs one reciprocal per row, not one per element.
+// Zero, infinite and NaN operands take the estimate, whose special values are
+// already IEEE's.
+__device__ __forceinline__ float tb_rcp(float y) {
   float r;
   asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(y));
-  const float q = __fmul_rn(x, r);
-  const float e = __fmaf_rn(-y, q, x);
-  return isfinite(e) && r != 0.0f ? __fmaf_rn(e, r, q) : q;
+  const float e = __fmaf_rn(-y, r, 1.0f);
+  return isfinite(e) ? __fmaf_rn(e, r, r) : r;
 }
 __device__ __forceinline__ float tb_tf32(float x) {
   unsigned r;
@@ -1789,6 +1808,8 @@ static void emit_ew(Program& P, Kernel& K, Emitter& E) {
       vals[m].push_back(x);
     }
   }
+  for (size_t m = 0; m < K.members.size(); ++m)
+    for (const std::string& x : vals[m]) E.note_member_value(x);
   for (size_t m = 0; m < K.members.size(); ++m) {
     if (K.members[m].type == MemberType::PREP) {
       emit_prep_store(E, K.members[m], "lin", vals[m]);
@@ -1885,6 +1906,12 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
   int64_t cap = SMS * 4;
   K.grid = std::max<int64_t>(1, std::min<int64_t>((R + teams - 1) / teams, cap));
   if (has_col || has_all) E.exact = false;
+  // A team's reduction waits only for its own warps (a named barrier per
+  // team), so the teams of a block move through their rows independently.
+  const std::string team_sync =
+      teams > 1 ? "asm volatile(\"bar.sync %0, " + std::to_string(T) +
+                      ";\" :: \"r\"(team + 1) : \"memory\");"
+                : "__syncthreads();";
   E.line("__shared__ float sred[8], sred2[8];");
   if (has_col) E.line("__shared__ float scol[" + lit(L) + "];");
   E.line("const int tid = threadIdx.x, team = tid / " + std::to_string(T) + ", tl = tid % " +
@@ -1955,6 +1982,10 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
           x = E.ref(P.nodes[n].operands[0], idx);
         }
         vals[m].push_back(x);
+        if (mm.type == MemberType::EW || mm.type == MemberType::PREP) {
+          E.note_member_value(x);
+          if (E.is_tainted(x)) E.tainted_members.insert((int)m);
+        }
         std::string ms = std::to_string(m);
         switch (mm.type) {
           case MemberType::ROW_SUM: E.line("ra" + ms + " = __fadd_rn(ra" + ms + ", " + x + ");"); break;
@@ -2043,7 +2074,7 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
                  std::to_string(o) + "); tb_lse_merge(rv" + ms + ", rv" + ts + ", m2, s2); }");
         if (T > 32) {
           E.line("if ((tid & 31) == 0) { sred[tid >> 5] = rv" + ms + "; sred2[tid >> 5] = rv" + ts + "; }");
-          E.line("__syncthreads();");
+          E.line(team_sync);
           int64_t w = T / 32;
           E.line("{ const int w0 = team * " + std::to_string(w) + "; rv" + ms + " = sred[w0]; rv" +
                  ts + " = sred2[w0];");
@@ -2051,7 +2082,7 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
             E.line("  tb_lse_merge(rv" + ms + ", rv" + ts + ", sred[w0 + " + std::to_string(q) +
                    "], sred2[w0 + " + std::to_string(q) + "]);");
           E.line("}");
-          E.line("__syncthreads();");
+          E.line(team_sync);
         }
         E.line("if (act && tl == 0) { " + E.fptr(P.info[mm.node].buf) + "[row] = rv" + ms + "; " +
                E.fptr(P.info[K.members[partner[m]].node].buf) + "[row] = rv" + ts + "; }");
@@ -2065,13 +2096,13 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
                ", " + std::to_string(o) + "));");
       if (T > 32) {
         E.line("if ((tid & 31) == 0) sred[tid >> 5] = rv" + ms + ";");
-        E.line("__syncthreads();");
+        E.line(team_sync);
         int64_t w = T / 32;
         E.line("{ const int w0 = team * " + std::to_string(w) + "; rv" + ms + " = sred[w0];");
         for (int64_t q = 1; q < w; ++q)
           E.line("  rv" + ms + " = " + op + "(rv" + ms + ", sred[w0 + " + std::to_string(q) + "]);");
         E.line("}");
-        E.line("__syncthreads();");
+        E.line(team_sync);
       }
       // f32 accumulation, one rounding (payload/tensor.rs:1085-1089)
       if (P.bf16 && mm.type == MemberType::ROW_SUM) E.line("rv" + ms + " = tb_rb(rv" + ms + ");");
@@ -2667,7 +2698,7 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
       Emitter probe(P, K, (int)P.kernels.size());
       if (K.type == KType::EW) emit_ew(P, K, probe);
       else emit_row(P, K, probe, Lw, finals);
-      carries_tolerance = !probe.exact && !P.bf16;
+      carries_tolerance = !probe.exact && !probe.exact_member_seen && !P.bf16;
       K = saved;
       P.buffers.resize(buffers);
       finals.resize(nfinals);

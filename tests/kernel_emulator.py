@@ -55,6 +55,10 @@ def _host_source(source: str, names) -> str:
             continue
         if 'asm("cvt.rna.tf32.f32' in line:
             line = "  r = emu_tf32_bits(x);"
+        if 'asm volatile("bar.sync' in line:
+            # a team's named barrier: every team of a block reaches its own
+            # the same number of times, so a block barrier stands in for it
+            line = "    __syncthreads();"
         if 'asm("rcp.approx.f32' in line:
             # the hardware reciprocal estimate, restated as the rounded reciprocal
             line = "  r = 1.0f / y;"
