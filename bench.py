@@ -510,8 +510,8 @@ def main():
     opt_cfg = w.optimizer
     opt = None
     if opt_cfg:
-        kind = {"sgd": backend.SGD, "adam": backend.ADAM, "adamw": backend.ADAMW}[opt_cfg["kind"]]
-        opt = backend.Optimizer(plan, dp, kind, zip(w.params, w.grads), opt_cfg["lr"],
+        opt_kind = {"sgd": backend.SGD, "adam": backend.ADAM, "adamw": backend.ADAMW}[opt_cfg["kind"]]
+        opt = backend.Optimizer(plan, dp, opt_kind, zip(w.params, w.grads), opt_cfg["lr"],
                                 opt_cfg.get("beta1", 0.9), opt_cfg.get("beta2", 0.999),
                                 opt_cfg.get("eps", 1e-8), opt_cfg.get("decay", 0.0),
                                 gradient_scale=1.0 / world)
@@ -608,6 +608,40 @@ def main():
     value = samples / (per_step * 1e-3)
     e2e_value = samples / (ms_e2e / args.steps * 1e-3)
 
+    comm_info = None
+    if world > 1:
+        # exposed exchange time: the same step without the gradient all-reduce
+        # (a second plan over the same parameters, no communicator attached),
+        # timed the same way; the difference is what the exchange adds
+        solo = backend.DevicePlan(w.columns)
+        solo_opt = None
+        if opt_cfg:
+            solo_opt = backend.Optimizer(solo, dp, opt_kind, zip(w.params, w.grads), opt_cfg["lr"],
+                                         opt_cfg.get("beta1", 0.9), opt_cfg.get("beta2", 0.999),
+                                         opt_cfg.get("eps", 1e-8), opt_cfg.get("decay", 0.0),
+                                         gradient_scale=1.0 / world)
+        for i in range(3):
+            solo.forward(dp, sym_of[i % nb][0])
+        solo.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        solo_stream = torch.cuda.ExternalStream(solo.stream())
+        s0.record(solo_stream)
+        for i in range(args.steps):
+            solo.forward(dp, sym_of[i % nb][0])
+        s1.record(solo_stream)
+        solo.synchronize()
+        torch.cuda.synchronize()
+        t_solo = torch.tensor([s0.elapsed_time(s1) / args.steps], device="cuda")
+        dist.all_reduce(t_solo, op=dist.ReduceOp.MAX)
+        grad_bytes = sum(int(np.prod(w.columns.nodes[g.index].shape)) * 4 for g in w.grads)
+        comm_info = {"allreduce_bytes_per_step": grad_bytes,
+                     "step_ms_without_exchange": float(t_solo.item()),
+                     "exposed_exchange_ms": per_step - float(t_solo.item()),
+                     "how": "the same step on the same rank without the NCCL all-reduce, "
+                            "max over ranks; exposed = with - without"}
+        del solo_opt, solo
     stats = plan.stats()
     rows = kernel_profile(plan) if rank == 0 and not args.no_kernel_profile else []
     roof = roofline(rows, args.config) if rows else None
@@ -627,7 +661,7 @@ def main():
                         "d2h_bytes_per_step": 4, "wall_ms": wall_e2e},
                 "gpu_launches": stats["kernels"] * args.steps,
                 "roofline": roof, "cpu_baseline": cpu, "clocks": clocks.summary(),
-                "tolerance": tol,
+                "tolerance": tol, "exchange": comm_info,
                 "loss": float(last_loss), "wall_ms_timed": wall,
                 "kernels_per_step": stats["kernels"], "gemms_per_step": stats["gemms"]}
         if args.config in ("gemm", "gemm_skinny") and not args.no_cpu:

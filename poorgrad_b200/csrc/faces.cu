@@ -268,9 +268,17 @@ extern "C" int tbx_gemm_prepared_layout(const float* a_hi, const float* a_lo, in
     b.rows = k;
   }
   cudaStream_t st = 0;
+  // the tests' stream-K scratch, allocated once per process (test hook only)
+  static tb::StreamK sk;
+  if (!sk.workspace) {
+    if (cudaMalloc((void**)&sk.workspace, tb::kStreamKWorkspaceBytes) != cudaSuccess ||
+        cudaMalloc((void**)&sk.flags, tb::kStreamKFlagBytes) != cudaSuccess ||
+        cudaMemset(sk.flags, 0, tb::kStreamKFlagBytes) != cudaSuccess)
+      return TB_RUNTIME;
+  }
   if (engine == 1)
     tb::launch_gemm_simt(a, b, c, batch, m, n, kp, st);
-  else if (!tb::launch_gemm_tcgen05_split(a, b, c, partial, splits, batch, m, n, kp, st))
+  else if (!tb::launch_gemm_tcgen05_split(a, b, c, partial, splits, batch, m, n, kp, st, &sk))
     return TB_DECLINED;
   return cudaDeviceSynchronize() == cudaSuccess ? TB_OK : TB_RUNTIME;
 }
@@ -288,6 +296,7 @@ extern "C" int tbx_tree_sum(const float* g, int shards, int64_t count, float* ou
   return cudaDeviceSynchronize() == cudaSuccess ? TB_OK : TB_RUNTIME;
 }
 extern "C" void tbx_set_gemm_tile_n(int tile) { tb::set_gemm_tile_n(tile); }
+extern "C" void tbx_set_gemm_stream_k(int on) { tb::set_gemm_stream_k(on); }
 extern "C" int tbx_gemm_splits(int64_t batch, int64_t m, int64_t n, int64_t kp) {
   return tb::gemm_splits(batch, m, n, kp);
 }

@@ -35,6 +35,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <algorithm>
+#include <cmath>
 #include <mutex>
 
 #include <cstdlib>
@@ -217,16 +218,84 @@ __device__ __forceinline__ Work decode(int w, int tiles_n, int tiles_m, int spli
   return r;
 }
 
-// Persistent: each CTA walks work items blockIdx.x, +gridDim.x, ...; the
-// stage ring and the two accumulator buffers carry their phases across tiles,
-// so the epilogue of one tile overlaps the main loop of the next.
+// The work of one launch.  Items [0, dp_items) are whole work items (a tile,
+// or one split-K slice of a tile) walked data-parallel: CTA b takes items
+// b, b + grid, ...  The remaining tiles are walked stream-K: their k-blocks
+// form one range of sk_units, cut into `grid` contiguous pieces, one per CTA,
+// so every CTA ends the launch at the same point.  A tile cut between CTAs
+// is summed by the CTA holding its first k-blocks (the owner; that piece is
+// the owner's last), which adds the later pieces in k order from the other
+// CTAs' workspace slots (each of them their CTA's first stream-K piece).
+struct Sched {
+  int tiles_n, tiles_m, splits, split_blocks, k_blocks, m_fast;
+  int dp_items;         // whole items walked data-parallel
+  long long sk_units;   // k-blocks of the stream-K tiles (0: none)
+};
+// One piece of work: a tile's k-blocks [kb0, kb0 + nkb).  kind: 0 = the whole
+// item, 1 = a later piece of a cut tile (to the workspace), 2 = the first
+// piece of a cut tile (its owner).
+struct Seg {
+  Work t;
+  int kb0, nkb, kind;
+  long long tile_u0;    // stream-K unit where the owned tile starts
+};
+struct SegIter {
+  int w;
+  long long u, u_end;
+};
+__device__ __forceinline__ long long sk_start(const Sched& s, int cta, int grid) {
+  return s.sk_units * cta / grid;
+}
+__device__ __forceinline__ SegIter seg_begin(const Sched& s) {
+  SegIter it;
+  it.w = blockIdx.x;
+  it.u = sk_start(s, blockIdx.x, gridDim.x);
+  it.u_end = sk_start(s, blockIdx.x + 1, gridDim.x);
+  return it;
+}
+template <class C>
+__device__ __forceinline__ bool seg_next(const Sched& s, SegIter& it, Seg& g) {
+  if (it.w < s.dp_items) {
+    g.t = decode<C>(it.w, s.tiles_n, s.tiles_m, s.splits, s.m_fast);
+    g.kb0 = g.t.split * s.split_blocks;
+    g.nkb = min(s.k_blocks, g.kb0 + s.split_blocks) - g.kb0;
+    g.kind = 0;
+    g.tile_u0 = 0;
+    it.w += gridDim.x;
+    return true;
+  }
+  if (it.u < it.u_end) {
+    const long long tile = it.u / s.k_blocks;
+    const int lo = (int)(it.u - tile * s.k_blocks);
+    const int hi = (int)min((long long)s.k_blocks, lo + (it.u_end - it.u));
+    g.t = decode<C>(s.dp_items + (int)tile, s.tiles_n, s.tiles_m, 1, s.m_fast);
+    g.kb0 = lo;
+    g.nkb = hi - lo;
+    g.kind = (lo == 0 && hi == s.k_blocks) ? 0 : (lo > 0 ? 1 : 2);
+    g.tile_u0 = tile * s.k_blocks;
+    it.u += hi - lo;
+    return true;
+  }
+  return false;
+}
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Persistent: each CTA walks its pieces of work (Sched); the stage ring and
+// the two accumulator buffers carry their phases across pieces, so the
+// epilogue of one overlaps the main loop of the next.
 template <class C>
 __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
     k_gemm_tcgen05(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
                    const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
-                   float* __restrict__ out, int m, int n, int k_blocks, int split_blocks,
-                   int splits, long long split_stride, int tiles_n, int tiles_m, int work_items,
-                   int m_fast, int a_mn, int b_mn) {
+                   float* __restrict__ out, int m, int n, const Sched sched,
+                   long long split_stride, int a_mn, int b_mn, float* __restrict__ sk_ws,
+                   int* __restrict__ sk_flags) {
   pdl_entry();
   using D = Derived<C>;
   constexpr int BN = C::BN, BK = C::BK, STAGES = C::STAGES, CHUNK = C::CHUNK;
@@ -271,10 +340,12 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       uint32_t g = 0;  // k-blocks issued by this CTA so far
-      for (int w = blockIdx.x; w < work_items && !*abort_flag; w += gridDim.x) {
-        const Work t = decode<C>(w, tiles_n, tiles_m, splits, m_fast);
-        const int kb0 = t.split * split_blocks;
-        const int nkb = min(k_blocks, kb0 + split_blocks) - kb0;
+      SegIter it = seg_begin(sched);
+      Seg sg;
+      while (!*abort_flag && seg_next<C>(sched, it, sg)) {
+        const Work t = sg.t;
+        const int kb0 = sg.kb0;
+        const int nkb = sg.nkb;
         for (int i = 0; i < nkb; ++i, ++g) {
           const int s = g % STAGES;
           const uint32_t round = g / STAGES;
@@ -313,10 +384,10 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
         return mn ? smem_desc_mn(tile + kk * 1024, BK * 128) : smem_desc<C>(tile + kk * 32);
       };
       uint32_t g = 0, gc = 0;  // k-blocks and chunks consumed by this CTA so far
-      for (int w = blockIdx.x; w < work_items && !*abort_flag; w += gridDim.x) {
-        const Work t = decode<C>(w, tiles_n, tiles_m, splits, m_fast);
-        const int kb0 = t.split * split_blocks;
-        const int nkb = min(k_blocks, kb0 + split_blocks) - kb0;
+      SegIter it = seg_begin(sched);
+      Seg sg;
+      while (!*abort_flag && seg_next<C>(sched, it, sg)) {
+        const int nkb = sg.nkb;
         const int chunks = (nkb + CHUNK - 1) / CHUNK;
         for (int c = 0; c < chunks && !*abort_flag; ++c, ++gc) {
           const int b = gc & 1;
@@ -361,10 +432,12 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
     const int c0 = half * EPI_COLS;
     uint32_t gc = 0;
     bool ok = true;
-    for (int w = blockIdx.x; w < work_items && ok; w += gridDim.x) {
-      const Work t = decode<C>(w, tiles_n, tiles_m, splits, m_fast);
-      const int kb0 = t.split * split_blocks;
-      const int nkb = min(k_blocks, kb0 + split_blocks) - kb0;
+    const int ew = warp - 2;  // epilogue warp index
+    SegIter it = seg_begin(sched);
+    Seg sg;
+    while (ok && seg_next<C>(sched, it, sg)) {
+      const Work t = sg.t;
+      const int nkb = sg.nkb;
       const int chunks = (nkb + CHUNK - 1) / CHUNK;
       float total[EPI_COLS];
 #pragma unroll
@@ -390,10 +463,54 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
                      : "memory");
       }
       if (!ok || *abort_flag) break;
+      if (sg.kind == 1) {
+        // a later piece of a cut tile: to this CTA's workspace slot, laid out
+        // [epilogue warp][column][lane] so that each store writes 128
+        // consecutive bytes; then this warp's flag, released at gpu scope.
+        // Each epilogue warp hands over its own rows and columns, so no
+        // barrier wider than a warp is needed.
+        float* slot = sk_ws + (long long)blockIdx.x * (BM * BN) + (long long)ew * EPI_COLS * 32;
+#pragma unroll
+        for (int j = 0; j < EPI_COLS; ++j) __stcg(slot + j * 32 + lane, total[j]);
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) st_release(&sk_flags[blockIdx.x * 8 + ew], 1);
+        continue;
+      }
+      if (sg.kind == 2) {
+        // the owner: add the later pieces in k order, each from the CTA whose
+        // stream-K range starts inside this tile (the same epilogue warp there)
+        const long long tile_u1 = sg.tile_u0 + sched.k_blocks;
+        for (int c = blockIdx.x + 1;
+             c < (int)gridDim.x && sk_start(sched, c, gridDim.x) < tile_u1 && ok; ++c) {
+          if (sk_start(sched, c + 1, gridDim.x) == sk_start(sched, c, gridDim.x)) continue;
+          int* flag = &sk_flags[c * 8 + ew];
+          const unsigned long long start = now_ns();
+          while (ld_acquire(flag) == 0) {
+            if (now_ns() - start > WAIT_NS) {
+              atomicExch(&g_gemm_error, 5);
+              ok = false;
+              break;
+            }
+          }
+          if (!__all_sync(0xffffffffu, ok)) {
+            ok = false;
+            break;
+          }
+          const float* slot = sk_ws + (long long)c * (BM * BN) + (long long)ew * EPI_COLS * 32;
+#pragma unroll
+          for (int j = 0; j < EPI_COLS; ++j)
+            total[j] = __fadd_rn(total[j], __ldcg(slot + j * 32 + lane));
+          __syncwarp();
+          // consumed: the flag starts the next launch at zero
+          if (lane == 0) st_release(flag, 0);
+        }
+        if (!ok) break;
+      }
       // stores: 32-column slabs through this warp's staging tile, so that each
       // store instruction writes one row's 32 consecutive floats
       float* dst = out + (long long)t.split * split_stride + (long long)t.batch * m * n;
-      float(*st)[33] = (float(*)[33])(epi_stage + (warp - 2) * 32 * 33);
+      float(*st)[33] = (float(*)[33])(epi_stage + ew * 32 * 33);
       const int row0 = t.m0 + q * 32;
 #pragma unroll
       for (int g = 0; g < EPI_COLS / 32; ++g) {
@@ -466,6 +583,14 @@ bool make_map(CUtensorMap* map, const float* base, int64_t ld, int64_t rows, int
 }
 
 int g_tile_override = -1;  // TB_GEMM_TILE_N, or a test's forced choice
+int g_stream_k = -1;       // TB_GEMM_STREAM_K=0 turns stream-K off, or a test's choice
+bool stream_k_enabled() {
+  if (g_stream_k < 0) {
+    const char* e = getenv("TB_GEMM_STREAM_K");
+    g_stream_k = e ? atoi(e) : 1;
+  }
+  return g_stream_k != 0;
+}
 
 }  // namespace
 
@@ -518,6 +643,7 @@ int gemm_tile_n(int64_t batch, int64_t m, int64_t n, int64_t kp) {
 }
 
 void set_gemm_tile_n(int tile) { g_tile_override = tile; }
+void set_gemm_stream_k(int on) { g_stream_k = on ? 1 : 0; }
 
 int gemm_splits(int64_t batch, int64_t m, int64_t n, int64_t kp) {
   return splits_for(gemm_tile_n(batch, m, n, kp), batch, m, n, kp);
@@ -556,7 +682,8 @@ bool operand_maps(CUtensorMap* hi, CUtensorMap* lo, const Operand& o, int tile, 
 
 template <class C>
 bool launch_cfg(const Operand& a, const Operand& b, float* c, float* partial, int splits,
-                int64_t batch, int64_t m, int64_t n, int64_t kp, cudaStream_t stream) {
+                int64_t batch, int64_t m, int64_t n, int64_t kp, cudaStream_t stream,
+                const StreamK* sk) {
   using D = Derived<C>;
   if (kp % C::BK != 0) return false;
   CUtensorMap ma, mal, mb, mbl;
@@ -586,9 +713,31 @@ bool launch_cfg(const Operand& a, const Operand& b, float* c, float* partial, in
     if (sms <= 0) sms = 148;
   }
   const int grid = (int)std::min<long long>(items, sms);
+  Sched sched;
+  sched.tiles_n = tiles_n;
+  sched.tiles_m = tiles_m;
+  sched.splits = splits;
+  sched.split_blocks = per;
+  sched.k_blocks = kb;
+  sched.m_fast = m > 0 && n > m ? 1 : 0;
+  sched.dp_items = (int)items;
+  sched.sk_units = 0;
+  // Stream-K for the tiles past the last whole wave but one, when the last
+  // wave would leave SMs idle: whole tiles cost ceil(items / grid) tile
+  // times per CTA, stream-K items / grid plus the hand-over of cut tiles.
+  if (sk && sk->workspace && sk->flags && stream_k_enabled() && splits == 1 && batch == 1 &&
+      items > grid && grid <= kStreamKMaxCtas) {
+    const double waves = (double)items / grid;
+    const long long whole = items / grid;
+    if (std::ceil(waves) - waves > 0.15) {
+      const long long dp_waves = whole >= 2 ? whole - 1 : 0;
+      sched.dp_items = (int)(dp_waves * grid);
+      sched.sk_units = (items - sched.dp_items) * (long long)kb;
+    }
+  }
   launch_pdl(k_gemm_tcgen05<C>, grid, D::THREADS, D::SMEM_BYTES, stream, ma, mal, mb, mbl,
-             target, (int)m, (int)n, kb, per, splits, (long long)(batch * m * n), tiles_n, tiles_m,
-             (int)items, m > 0 && n > m ? 1 : 0, (int)a.mn, (int)b.mn);
+             target, (int)m, (int)n, sched, (long long)(batch * m * n), (int)a.mn, (int)b.mn,
+             sk ? sk->workspace : (float*)nullptr, sk ? sk->flags : (int*)nullptr);
   if (splits > 1) {
     const long long count = batch * m * n;
     int blocks = (int)std::min<long long>((count + 255) / 256, 148 * 8);
@@ -600,7 +749,7 @@ bool launch_cfg(const Operand& a, const Operand& b, float* c, float* partial, in
 
 bool launch_gemm_tcgen05_split(const Operand& a, const Operand& b, float* c, float* partial,
                                int splits, int64_t batch, int64_t m, int64_t n, int64_t kp,
-                               cudaStream_t stream) {
+                               cudaStream_t stream, const StreamK* sk) {
   if (m >= (1LL << 31) || n >= (1LL << 31) || batch > 65535) return false;
   if (((uintptr_t)a.hi | (uintptr_t)a.lo | (uintptr_t)b.hi | (uintptr_t)b.lo) & 15) return false;
   // row strides: 16-byte multiples for the tensor maps; an MN-major row holds
@@ -608,8 +757,8 @@ bool launch_gemm_tcgen05_split(const Operand& a, const Operand& b, float* c, flo
   for (const Operand* o : {&a, &b})
     if (o->ld % 4 != 0 || o->rows < 1 || (o->mn && o->ld % 32 != 0)) return false;
   if (gemm_tile_n(batch, m, n, kp) == 256)
-    return launch_cfg<Cfg<256>>(a, b, c, partial, splits, batch, m, n, kp, stream);
-  return launch_cfg<Cfg<128>>(a, b, c, partial, splits, batch, m, n, kp, stream);
+    return launch_cfg<Cfg<256>>(a, b, c, partial, splits, batch, m, n, kp, stream, sk);
+  return launch_cfg<Cfg<128>>(a, b, c, partial, splits, batch, m, n, kp, stream, sk);
 }
 
 int gemm_error() {

@@ -680,9 +680,10 @@ void launch_gemm_simt(const Operand& a, const Operand& b, float* c, int64_t batc
 }
 
 void launch_gemm(const Operand& a, const Operand& b, float* c, float* partial, int splits,
-                 int64_t batch, int64_t m, int64_t n, int64_t kp, cudaStream_t stream) {
+                 int64_t batch, int64_t m, int64_t n, int64_t kp, cudaStream_t stream,
+                 const StreamK* sk) {
   if (g_engine != 1 &&
-      launch_gemm_tcgen05_split(a, b, c, partial, splits, batch, m, n, kp, stream))
+      launch_gemm_tcgen05_split(a, b, c, partial, splits, batch, m, n, kp, stream, sk))
     return;
   launch_gemm_simt(a, b, c, batch, m, n, kp, stream);
 }

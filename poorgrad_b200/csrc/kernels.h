@@ -54,17 +54,32 @@ inline Operand k_major(const float* hi, const float* lo, int64_t rows, int64_t k
   return o;
 }
 
+// Scratch of the tcgen05 path's stream-K schedule, owned by the caller (one per
+// stream of work: a plan instance): a workspace of kStreamKMaxCtas tiles of
+// 128 x 256 floats and kStreamKMaxCtas * 8 flags, zero before the first launch
+// (every launch leaves them zero).  Without it, tiles are walked whole.
+constexpr int kStreamKMaxCtas = 160;
+struct StreamK {
+  float* workspace = nullptr;
+  int* flags = nullptr;
+};
+constexpr size_t kStreamKWorkspaceBytes = (size_t)kStreamKMaxCtas * 128 * 256 * 4;
+constexpr size_t kStreamKFlagBytes = (size_t)kStreamKMaxCtas * 8 * 4;
+
 // C[b] = (Ahi+Alo)[b] . (Bhi+Blo)[b]^T over prepared operands; the tcgen05 path
-// (split-K into `partial` when splits > 1), else a SIMT path.
+// (split-K into `partial` when splits > 1; stream-K with `sk`), else a SIMT path.
 void launch_gemm(const Operand& a, const Operand& b, float* c, float* partial, int splits,
-                 int64_t batch, int64_t m, int64_t n, int64_t kp, cudaStream_t stream);
+                 int64_t batch, int64_t m, int64_t n, int64_t kp, cudaStream_t stream,
+                 const StreamK* sk = nullptr);
 // The SIMT path alone (tests compare the two).
 void launch_gemm_simt(const Operand& a, const Operand& b, float* c, int64_t batch, int64_t m,
                       int64_t n, int64_t kp, cudaStream_t stream);
 // The tcgen05 path; returns false when the shape or alignment is not served.
 bool launch_gemm_tcgen05_split(const Operand& a, const Operand& b, float* c, float* partial,
                                int splits, int64_t batch, int64_t m, int64_t n, int64_t kp,
-                               cudaStream_t stream);
+                               cudaStream_t stream, const StreamK* sk = nullptr);
+// Turns the stream-K schedule on or off (tests compare the two).
+void set_gemm_stream_k(int on);
 // 2-D tensor map over row-major f32 [rows][width] (width a multiple of 4), no
 // swizzle, boxes of box_cols x box_rows, zero fill outside; false if refused.
 bool encode_rows_f32(CUtensorMap* map, const float* base, int64_t width, int64_t rows,

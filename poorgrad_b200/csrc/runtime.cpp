@@ -311,6 +311,7 @@ struct tb_instance {
   tb_params* bound = nullptr;
   cudaGraphExec_t graph = nullptr;
   bool graph_dirty = true;
+  tb::StreamK stream_k;                // the GEMMs' stream-K scratch (with any GEMM)
   tb_optimizer* optimizer = nullptr;
   tb_comm* comm = nullptr;
   int64_t bucket_bytes = 0;
@@ -325,6 +326,8 @@ struct tb_instance {
     if (graph) cudaGraphExecDestroy(graph);
     for (auto e : events) cudaEventDestroy(e);
     if (arena) cudaFree(arena);
+    if (stream_k.workspace) cudaFree(stream_k.workspace);
+    if (stream_k.flags) cudaFree(stream_k.flags);
     for (void* p : own) cudaFree(p);
     if (stream) cudaStreamDestroy(stream);
     if (comm_stream) cudaStreamDestroy(comm_stream);
@@ -453,7 +456,7 @@ int64_t launch_kernel(tb_instance* plan, size_t k, cudaStream_t stream) {
       b.ld = K.b_ld;
       b.rows = K.b_rows;
       tb::launch_gemm(a, b, fp(plan, K.out), K.partial >= 0 ? fp(plan, K.partial) : nullptr,
-                      (int)K.passes, K.batch, K.m, K.n, K.kp, stream);
+                      (int)K.passes, K.batch, K.m, K.n, K.kp, stream, &plan->stream_k);
       launches += 1;
       break;
     }
@@ -605,6 +608,18 @@ void setup_instance(tb_plan* owner, tb_instance* plan) {
   check(cudaStreamCreateWithFlags(&plan->side_stream, cudaStreamNonBlocking), "cudaStreamCreate");
   plan->buffer_ptr.assign(P.buffers.size(), nullptr);
   if (P.arena_bytes > 0) check(cudaMalloc((void**)&plan->arena, P.arena_bytes), "cudaMalloc(arena)");
+  bool has_gemm = false;
+  for (const tb::Kernel& K : P.kernels) has_gemm = has_gemm || K.type == tb::KType::GEMM;
+  if (has_gemm) {
+    // used only inside one GEMM launch at a time on this instance's stream;
+    // every launch leaves the flags zero again
+    check(cudaMalloc((void**)&plan->stream_k.workspace, tb::kStreamKWorkspaceBytes),
+          "cudaMalloc(stream-K workspace)");
+    check(cudaMalloc((void**)&plan->stream_k.flags, tb::kStreamKFlagBytes),
+          "cudaMalloc(stream-K flags)");
+    check(cudaMemsetAsync(plan->stream_k.flags, 0, tb::kStreamKFlagBytes, plan->stream),
+          "cudaMemset(stream-K flags)");
+  }
   for (size_t b = 0; b < P.buffers.size(); ++b) {
     tb::Buffer& buf = P.buffers[b];
     const tb::Node* node = buf.node >= 0 ? &P.nodes[buf.node] : nullptr;

@@ -102,3 +102,50 @@ def test_mn_major_operands_match_f64(device, batch, m, n, k, splits, a_mn, b_mn,
             assert torch.all(err <= tol), f"engine {engine}: worst {(err / tol).max().item()}"
     finally:
         lib.tbx_set_gemm_tile_n(0)
+
+
+@pytest.mark.parametrize("m,n,k,a_mn,tile", [
+    (16384, 512, 512, 0, 256), (4096, 4096, 512, 0, 256), (20000, 64, 256, 0, 128),
+    (2000, 3000, 100, 1, 256), (1500, 900, 700, 1, 128)])
+def test_stream_k_matches_f64_and_whole_tiles(device, m, n, k, a_mn, tile):
+    # Shapes whose tiles leave the last wave of 148 SMs partly idle: their
+    # tiles are cut into stream-K pieces whose partial sums the owning CTA adds
+    # in k order.  Checked against f64, against whole tiles (stream-K off),
+    # and bitwise against itself on a second launch (the hand-over flags reset).
+    import torch
+    from poorgrad_b200.abi import load_library
+    lib = load_library()
+    f = lib.tbx_gemm_prepared_layout
+    f.restype = C.c_int
+    f.argtypes = ([C.c_void_p, C.c_void_p, C.c_int, C.c_int64] * 2 + [C.c_void_p, C.c_void_p, C.c_int]
+                  + [C.c_int64] * 5 + [C.c_int])
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    a = torch.rand((1, m, k), device="cuda", generator=g) * 2 - 1
+    bt = torch.rand((1, n, k), device="cuda", generator=g) * 2 - 1
+    kp = (k + 31) // 32 * 32
+    if a_mn:
+        a_ld = (m + 31) // 32 * 32
+        ahi, alo = _prep(torch, a.transpose(1, 2).contiguous(), a_ld)
+    else:
+        a_ld = kp
+        ahi, alo = _prep(torch, a, kp)
+    bhi, blo = _prep(torch, bt, kp)
+    ref = torch.bmm(a.double(), bt.double().transpose(1, 2))
+    tol = 8 * EPS * math.sqrt(k) * (1 + ref.abs())
+    lib.tbx_set_gemm_tile_n(tile)
+    outs = {}
+    try:
+        for label, sk in (("stream-k", 1), ("stream-k again", 1), ("whole tiles", 0)):
+            lib.tbx_set_gemm_stream_k(sk)
+            c = torch.full((1, m, n), float("nan"), device="cuda")
+            rc = f(ahi.data_ptr(), alo.data_ptr(), a_mn, a_ld, bhi.data_ptr(), blo.data_ptr(), 0,
+                   kp, c.data_ptr(), 0, 1, 1, m, n, k, kp, 2)
+            assert rc == 0, f"{label} rc {rc}"
+            assert lib.tbx_gemm_error() == 0, label
+            err = (c.double() - ref).abs()
+            assert torch.all(err <= tol), f"{label}: worst {(err / tol).max().item()}"
+            outs[label] = c
+    finally:
+        lib.tbx_set_gemm_stream_k(1)
+        lib.tbx_set_gemm_tile_n(0)
+    assert torch.equal(outs["stream-k"], outs["stream-k again"])
