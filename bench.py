@@ -144,9 +144,25 @@ CONFIGS = {
 }
 
 
-def build_workload(name: str, rank: int, config_only: bool = False):
+def build_workload(name: str, rank: int, config_only: bool = False, overrides=None):
+    """The workload and its config; ``overrides`` (from --batch/--seq/--layers)
+    resize charmlp, mlp and gpt2 for profiling captures, and say so in the
+    config.  The default run uses none."""
     make, cfg = CONFIGS[name]
-    return (None if config_only else make()), dict(cfg)
+    cfg = dict(cfg)
+    o = {k: v for k, v in (overrides or {}).items() if v}
+    if o and name in ("charmlp", "mlp", "gpt2"):
+        from poorgrad_b200 import configs
+        if name == "charmlp":
+            make = lambda: configs.char_mlp(batch=o.get("batch", 16384), seed=4)
+        elif name == "mlp":
+            make = lambda: configs.mlp(batch=o.get("batch", 128))
+        else:
+            make = lambda: configs.gpt2(batch=o.get("batch", 8), seq=o.get("seq", 1024),
+                                        layers=o.get("layers", 12))
+        cfg.update({"global_batch_per_gpu": o.get("batch", cfg.get("global_batch_per_gpu")),
+                    "resized_for_profiling": o})
+    return (None if config_only else make()), cfg
 
 
 def metric_of(name):
@@ -482,6 +498,9 @@ def main():
     ap.add_argument("--impl", default="b200")
     ap.add_argument("--config", default=DEFAULT_CONFIG)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--batch", type=int, default=0, help="per-GPU batch override (profiling)")
+    ap.add_argument("--seq", type=int, default=0, help="gpt2 sequence override (profiling)")
+    ap.add_argument("--layers", type=int, default=0, help="gpt2 layer override (profiling)")
     ap.add_argument("--replay-s", type=float, default=1.5,
                     help="untimed replay before the timed steps (clock sampling)")
     ap.add_argument("--no-kernel-profile", action="store_true",
@@ -503,7 +522,8 @@ def main():
     if code != 0:
         raise SystemExit(f"backend unavailable: {code} {msg}")
 
-    w, cfg = build_workload(args.config, rank)
+    w, cfg = build_workload(args.config, rank, overrides={
+        "batch": args.batch, "seq": args.seq, "layers": args.layers})
     params = w.network.parameters()
     plan = backend.DevicePlan(w.columns)
     dp = backend.DeviceParameters(plan, params)
@@ -603,7 +623,7 @@ def main():
     ms_e2e, wall_e2e, last_loss = timed(True)
     per_step = ms / args.steps
     metric, unit = metric_of(args.config)
-    per_sample = 1024 if args.config == "gpt2" else 1   # tokens per GPT-2 sequence
+    per_sample = (args.seq or 1024) if args.config == "gpt2" else 1   # tokens per GPT-2 sequence
     samples = w.samples * per_sample * world
     value = samples / (per_step * 1e-3)
     e2e_value = samples / (ms_e2e / args.steps * 1e-3)

@@ -253,7 +253,7 @@ __device__ __forceinline__ SegIter seg_begin(const Sched& s) {
   it.u_end = sk_start(s, blockIdx.x + 1, gridDim.x);
   return it;
 }
-template <class C>
+template <class C, bool SK>
 __device__ __forceinline__ bool seg_next(const Sched& s, SegIter& it, Seg& g) {
   if (it.w < s.dp_items) {
     g.t = decode<C>(it.w, s.tiles_n, s.tiles_m, s.splits, s.m_fast);
@@ -264,7 +264,7 @@ __device__ __forceinline__ bool seg_next(const Sched& s, SegIter& it, Seg& g) {
     it.w += gridDim.x;
     return true;
   }
-  if (it.u < it.u_end) {
+  if (SK && it.u < it.u_end) {
     const long long tile = it.u / s.k_blocks;
     const int lo = (int)(it.u - tile * s.k_blocks);
     const int hi = (int)min((long long)s.k_blocks, lo + (it.u_end - it.u));
@@ -289,7 +289,7 @@ __device__ __forceinline__ void st_release(int* p, int v) {
 // Persistent: each CTA walks its pieces of work (Sched); the stage ring and
 // the two accumulator buffers carry their phases across pieces, so the
 // epilogue of one overlaps the main loop of the next.
-template <class C>
+template <class C, bool SK>
 __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
     k_gemm_tcgen05(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
                    const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
@@ -342,7 +342,7 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
       uint32_t g = 0;  // k-blocks issued by this CTA so far
       SegIter it = seg_begin(sched);
       Seg sg;
-      while (!*abort_flag && seg_next<C>(sched, it, sg)) {
+      while (!*abort_flag && seg_next<C, SK>(sched, it, sg)) {
         const Work t = sg.t;
         const int kb0 = sg.kb0;
         const int nkb = sg.nkb;
@@ -386,7 +386,7 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
       uint32_t g = 0, gc = 0;  // k-blocks and chunks consumed by this CTA so far
       SegIter it = seg_begin(sched);
       Seg sg;
-      while (!*abort_flag && seg_next<C>(sched, it, sg)) {
+      while (!*abort_flag && seg_next<C, SK>(sched, it, sg)) {
         const int nkb = sg.nkb;
         const int chunks = (nkb + CHUNK - 1) / CHUNK;
         for (int c = 0; c < chunks && !*abort_flag; ++c, ++gc) {
@@ -435,7 +435,7 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
     const int ew = warp - 2;  // epilogue warp index
     SegIter it = seg_begin(sched);
     Seg sg;
-    while (ok && seg_next<C>(sched, it, sg)) {
+    while (ok && seg_next<C, SK>(sched, it, sg)) {
       const Work t = sg.t;
       const int nkb = sg.nkb;
       const int chunks = (nkb + CHUNK - 1) / CHUNK;
@@ -463,7 +463,7 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
                      : "memory");
       }
       if (!ok || *abort_flag) break;
-      if (sg.kind == 1) {
+      if (SK && sg.kind == 1) {
         // a later piece of a cut tile: to this CTA's workspace slot, laid out
         // [epilogue warp][column][lane] so that each store writes 128
         // consecutive bytes; then this warp's flag, released at gpu scope.
@@ -477,7 +477,7 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
         if (lane == 0) st_release(&sk_flags[blockIdx.x * 8 + ew], 1);
         continue;
       }
-      if (sg.kind == 2) {
+      if (SK && sg.kind == 2) {
         // the owner: add the later pieces in k order, each from the CTA whose
         // stream-K range starts inside this tile (the same epilogue warp there)
         const long long tile_u1 = sg.tile_u0 + sched.k_blocks;
@@ -583,11 +583,16 @@ bool make_map(CUtensorMap* map, const float* base, int64_t ld, int64_t rows, int
 }
 
 int g_tile_override = -1;  // TB_GEMM_TILE_N, or a test's forced choice
-int g_stream_k = -1;       // TB_GEMM_STREAM_K=0 turns stream-K off, or a test's choice
+// Stream-K is off unless TB_GEMM_STREAM_K=1 (or a test turns it on): measured on
+// B200 it made the C4 step's 16384x512x512 products slower (57 against 46 us,
+// two partial-tile epilogues per CTA where whole tiles overlap theirs with the
+// next tile's main loop) and saved about 5% of cycles on 4096^3, which the
+// power cap of a dense GEMM takes back in clock.
+int g_stream_k = -1;
 bool stream_k_enabled() {
   if (g_stream_k < 0) {
     const char* e = getenv("TB_GEMM_STREAM_K");
-    g_stream_k = e ? atoi(e) : 1;
+    g_stream_k = e ? atoi(e) : 0;
   }
   return g_stream_k != 0;
 }
@@ -689,11 +694,13 @@ bool launch_cfg(const Operand& a, const Operand& b, float* c, float* partial, in
   CUtensorMap ma, mal, mb, mbl;
   if (!operand_maps<C>(&ma, &mal, a, BM, batch) || !operand_maps<C>(&mb, &mbl, b, C::BN, batch))
     return false;
-  static bool configured[256] = {};  // the attribute is set per device
+  static bool configured[256] = {};  // the attributes are set per device
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 256) return false;
   if (!configured[dev]) {
-    if (cudaFuncSetAttribute(k_gemm_tcgen05<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(k_gemm_tcgen05<C, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             D::SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(k_gemm_tcgen05<C, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              D::SMEM_BYTES) != cudaSuccess)
       return false;
     configured[dev] = true;
@@ -730,14 +737,19 @@ bool launch_cfg(const Operand& a, const Operand& b, float* c, float* partial, in
     const double waves = (double)items / grid;
     const long long whole = items / grid;
     if (std::ceil(waves) - waves > 0.15) {
-      const long long dp_waves = whole >= 2 ? whole - 1 : 0;
+      const long long dp_waves = whole;
       sched.dp_items = (int)(dp_waves * grid);
       sched.sk_units = (items - sched.dp_items) * (long long)kb;
     }
   }
-  launch_pdl(k_gemm_tcgen05<C>, grid, D::THREADS, D::SMEM_BYTES, stream, ma, mal, mb, mbl,
-             target, (int)m, (int)n, sched, (long long)(batch * m * n), (int)a.mn, (int)b.mn,
-             sk ? sk->workspace : (float*)nullptr, sk ? sk->flags : (int*)nullptr);
+  if (sched.sk_units > 0)
+    launch_pdl(k_gemm_tcgen05<C, true>, grid, D::THREADS, D::SMEM_BYTES, stream, ma, mal, mb, mbl,
+               target, (int)m, (int)n, sched, (long long)(batch * m * n), (int)a.mn, (int)b.mn,
+               sk->workspace, sk->flags);
+  else
+    launch_pdl(k_gemm_tcgen05<C, false>, grid, D::THREADS, D::SMEM_BYTES, stream, ma, mal, mb,
+               mbl, target, (int)m, (int)n, sched, (long long)(batch * m * n), (int)a.mn,
+               (int)b.mn, (float*)nullptr, (int*)nullptr);
   if (splits > 1) {
     const long long count = batch * m * n;
     int blocks = (int)std::min<long long>((count + 255) / 256, 148 * 8);

@@ -108,10 +108,11 @@ def test_mn_major_operands_match_f64(device, batch, m, n, k, splits, a_mn, b_mn,
     (16384, 512, 512, 0, 256), (4096, 4096, 512, 0, 256), (20000, 64, 256, 0, 128),
     (2000, 3000, 100, 1, 256), (1500, 900, 700, 1, 128)])
 def test_stream_k_matches_f64_and_whole_tiles(device, m, n, k, a_mn, tile):
-    # Shapes whose tiles leave the last wave of 148 SMs partly idle: their
-    # tiles are cut into stream-K pieces whose partial sums the owning CTA adds
-    # in k order.  Checked against f64, against whole tiles (stream-K off),
-    # and bitwise against itself on a second launch (the hand-over flags reset).
+    # Shapes whose tiles leave the last wave of 148 SMs partly idle: with the
+    # (opt-in) stream-K schedule their last tiles are cut into pieces whose
+    # partial sums the owning CTA adds in k order.  Checked against f64,
+    # against whole tiles (the default schedule), and bitwise against itself
+    # on a second launch (the hand-over flags reset).
     import torch
     from poorgrad_b200.abi import load_library
     lib = load_library()
@@ -146,6 +147,6 @@ def test_stream_k_matches_f64_and_whole_tiles(device, m, n, k, a_mn, tile):
             assert torch.all(err <= tol), f"{label}: worst {(err / tol).max().item()}"
             outs[label] = c
     finally:
-        lib.tbx_set_gemm_stream_k(1)
+        lib.tbx_set_gemm_stream_k(0)
         lib.tbx_set_gemm_tile_n(0)
     assert torch.equal(outs["stream-k"], outs["stream-k again"])
