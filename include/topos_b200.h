@@ -172,6 +172,14 @@ int tb_plan_gradient_node(const tb_plan* plan, int64_t root, int64_t parameter, 
 int tb_plan_synchronize(tb_plan* plan);
 /* Copies a readable value (row-major, volume elements) to host memory (waits). */
 int tb_plan_read(tb_plan* plan, int64_t node, float* host, int64_t count);
+/* Replaces: `Run::of(value)` (engine/run.rs:139) read without waiting: enqueues the copy of a
+ * readable value to host memory on the plan's stream (tb_plan_stream) and returns, so that a
+ * training loop can launch the next step before it looks at this step's loss.  The values are
+ * in `host` once the stream passes the copy (tb_plan_synchronize, or an event recorded on
+ * tb_plan_stream after this call); `host` should be page-locked, or the copy does not overlap.
+ * A later tb_plan_run overwrites the value on the device, not the copy already enqueued.
+ * bf16 plans answer TB_INVALID (their reads round on the host): use tb_plan_read. */
+int tb_plan_read_async(tb_plan* plan, int64_t node, float* host, int64_t count);
 /* Device address of a readable value's contiguous buffer (valid until the next run). */
 int tb_plan_device_pointer(tb_plan* plan, int64_t node, const float** device);
 /* The CUDA stream (cudaStream_t) the plan runs on. */

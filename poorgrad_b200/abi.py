@@ -190,6 +190,7 @@ def load_library() -> C.CDLL:
         "tb_plan_synchronize": (C.c_int, [P]),
         "tb_plan_gradient_node": (C.c_int, [P, C.c_int64, C.c_int64, C.POINTER(C.c_int64)]),
         "tb_plan_read": (C.c_int, [P, C.c_int64, C.POINTER(C.c_float), C.c_int64]),
+        "tb_plan_read_async": (C.c_int, [P, C.c_int64, C.c_void_p, C.c_int64]),
         "tb_plan_device_pointer": (C.c_int, [P, C.c_int64, C.POINTER(C.c_void_p)]),
         "tb_plan_stream": (P, [P]),
         "tb_run_begin": (C.c_int, [P, P, C.c_int32, C.POINTER(TbFeed), C.POINTER(P)]),

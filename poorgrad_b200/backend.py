@@ -133,6 +133,14 @@ class DevicePlan:
                "tb_plan_read")
         return out
 
+    def read_async(self, symbol, host_pointer: int, count: int):
+        """`Run::of` without waiting: enqueues the copy of a readable value to
+        page-locked host memory at ``host_pointer`` (``count`` floats) on the
+        plan's stream; it is there once the stream passes the copy."""
+        index = symbol.index if hasattr(symbol, "index") else int(symbol)
+        _check(self.lib.tb_plan_read_async(self.handle, index, C.c_void_p(host_pointer), count),
+               "tb_plan_read_async")
+
     def gradient(self, root, parameter) -> np.ndarray:
         """`Run::backward(root)` then `Gradients::of(parameter)` for a plan
         compiled with ``Request(...).backward()``."""

@@ -937,6 +937,20 @@ int tb_plan_read(tb_plan* plan, int64_t node, float* host, int64_t count) {
   });
 }
 
+int tb_plan_read_async(tb_plan* plan, int64_t node, float* host, int64_t count) {
+  return guarded([&]() {
+    tb_instance* inst = plan->main.get();
+    if (inst->prog->bf16)
+      throw Failure(TB_INVALID, "tb_plan_read_async: a bf16 plan's reads round on the host");
+    int b = readable_buffer(*inst->prog, node);
+    if (count * 4 != inst->prog->buffers[b].bytes) throw Failure(TB_INVALID, "read size mismatch");
+    check(cudaMemcpyAsync(host, inst->buffer_ptr[b], count * 4, cudaMemcpyDeviceToHost,
+                          inst->stream),
+          "read");
+    return (int)TB_OK;
+  });
+}
+
 int tb_plan_device_pointer(tb_plan* plan, int64_t node, const float** device) {
   return guarded([&]() {
     int b = readable_buffer(*plan->prog, node);

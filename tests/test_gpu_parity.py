@@ -460,3 +460,23 @@ def test_log_sum_exp_and_log_softmax_extreme_rows(device, row):
     assert_rel(dev[g.index], ref[g.index])
     if abs(row[0]) == 3.0e38:
         assert set(dev[g.index].reshape(-1).tolist()) == {0.0, 1.0}
+
+
+def test_async_read_equals_the_waiting_read(device):
+    # `Run::of` without waiting: the copy is enqueued behind the step, and a
+    # later run does not change the copy already enqueued
+    import torch
+    w = configs.mlp(batch=128)
+    plan = backend.DevicePlan(w.columns)
+    dp = backend.DeviceParameters(plan, w.network.parameters())
+    pinned = [torch.zeros((), dtype=torch.float32).pin_memory() for _ in range(2)]
+    plan.forward(dp, w.feeds(0))
+    plan.read_async(w.loss, pinned[0].data_ptr(), 1)
+    plan.forward(dp, w.feeds(1))
+    plan.read_async(w.loss, pinned[1].data_ptr(), 1)
+    plan.synchronize()
+    second = plan.of(w.loss)
+    plan.forward(dp, w.feeds(0), sync=True)
+    first = plan.of(w.loss)
+    assert pinned[0].numpy().tobytes() == first.tobytes()
+    assert pinned[1].numpy().tobytes() == second.tobytes()
