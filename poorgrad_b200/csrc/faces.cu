@@ -251,7 +251,7 @@ extern "C" int tb_batch_norm_f32(const float* input, const float* scale, const f
 extern "C" void tbx_set_gemm_engine(int engine) { tb::set_gemm_engine(engine); }
 // Operand layouts: a_mn / b_mn select MN-major ([batch][k rows][ld], ld a
 // multiple of 32); K-major operands are [batch][m or n][kp].  engine: 1 = the
-// SIMT kernel, 3 = the narrow-product kernel, otherwise the tcgen05 path.
+// SIMT kernel, otherwise the tcgen05 path.
 extern "C" int tbx_gemm_prepared_layout(const float* a_hi, const float* a_lo, int a_mn,
                                         int64_t a_ld, const float* b_hi, const float* b_lo,
                                         int b_mn, int64_t b_ld, float* c, float* partial,
@@ -279,8 +279,6 @@ extern "C" int tbx_gemm_prepared_layout(const float* a_hi, const float* a_lo, in
   }
   if (engine == 1)
     tb::launch_gemm_simt(a, b, c, batch, m, n, kp, st);
-  else if (engine == 3)
-    tb::launch_gemm_narrow(a, b, c, partial, splits, batch, m, n, kp, st);
   else if (!tb::launch_gemm_tcgen05_split(a, b, c, partial, splits, batch, m, n, kp, st, &sk))
     return TB_DECLINED;
   return cudaDeviceSynchronize() == cudaSuccess ? TB_OK : TB_RUNTIME;

@@ -773,12 +773,6 @@ bool launch_gemm_tcgen05_split(const Operand& a, const Operand& b, float* c, flo
   return launch_cfg<Cfg<128>>(a, b, c, partial, splits, batch, m, n, kp, stream, sk);
 }
 
-void launch_split_sum(const float* partial, float* c, long long count, int splits,
-                      cudaStream_t stream) {
-  const int blocks = (int)std::min<long long>((count + 255) / 256, 148 * 8);
-  launch_pdl(k_split_sum, blocks, 256, 0, stream, partial, c, count, splits);
-}
-
 int gemm_error() {
   int v = 0;
   cudaMemcpyFromSymbol(&v, g_gemm_error, sizeof(int));

@@ -508,101 +508,6 @@ __global__ void __launch_bounds__(256) k_gemm_simt(const float* __restrict__ ahi
   }
 }
 
-// Narrow products (an output at most 32 wide, or a reduction at most 32
-// deep): the tensor-core tile would be mostly padding, or its epilogue would
-// dominate a one-k-block main loop, so a SIMT kernel moves the operands at
-// memory speed instead.  Each block computes a 64 x 32 tile over 32-deep
-// k-chunks staged in shared memory as hi + lo (exactly the original f32
-// values), each thread a 2 x 4 block of outputs with f32 FMA in ascending k;
-// blockIdx.z is (batch, split): a split writes its slice of the ordered
-// split-K partials, summed by k_split_sum as for the tensor-core path.
-constexpr int NARROW_BM = 64, NARROW_BN = 32, NARROW_BK = 32;
-
-__device__ __forceinline__ void narrow_stage(float (*S)[NARROW_BM + 1], int tile_rows,
-                                             const float* __restrict__ h,
-                                             const float* __restrict__ l, int mn, int64_t ld,
-                                             int64_t rows, int64_t r0, int64_t r_end, int64_t k0,
-                                             int64_t k_end) {
-  // S[k][r] for the tile's rows r0 .. r0 + tile_rows and k0 .. k0 + 31
-  const int t = threadIdx.x;
-  if (!mn) {
-    // K-major: 8 threads read one row's 32 contiguous k
-    for (int i = t; i < tile_rows * 8; i += 256) {
-      const int r = i >> 3, kq = (i & 7) * 4;
-      const int64_t gr = r0 + r, gk = k0 + kq;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (gr < r_end && gk < k_end) {
-        const float4 a = *(const float4*)(h + gr * ld + gk);
-        const float4 b = *(const float4*)(l + gr * ld + gk);
-        v = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
-      }
-      S[kq + 0][r] = v.x;
-      S[kq + 1][r] = v.y;
-      S[kq + 2][r] = v.z;
-      S[kq + 3][r] = v.w;
-    }
-  } else {
-    // MN-major: row k holds the tile's rows contiguously
-    for (int i = t; i < NARROW_BK * tile_rows; i += 256) {
-      const int kk = i / tile_rows, r = i % tile_rows;
-      const int64_t gr = r0 + r, gk = k0 + kk;
-      S[kk][r] = (gr < r_end && gk < rows && gk < k_end) ? h[gk * ld + gr] + l[gk * ld + gr] : 0.0f;
-    }
-  }
-}
-
-__global__ void __launch_bounds__(256) k_gemm_narrow(const float* __restrict__ ahi,
-                                                     const float* __restrict__ alo, int a_mn,
-                                                     int64_t a_ld, int64_t a_rows,
-                                                     const float* __restrict__ bhi,
-                                                     const float* __restrict__ blo, int b_mn,
-                                                     int64_t b_ld, int64_t b_rows,
-                                                     float* __restrict__ c, int64_t m, int64_t n,
-                                                     int64_t kp, int splits, int64_t per_k) {
-  pdl_entry();
-  __shared__ float As[NARROW_BK][NARROW_BM + 1];
-  __shared__ float Bs[NARROW_BK][NARROW_BM + 1];
-  const int64_t batch = blockIdx.z / splits, split = blockIdx.z % splits;
-  const int64_t m0 = (int64_t)blockIdx.y * NARROW_BM, n0 = (int64_t)blockIdx.x * NARROW_BN;
-  const int64_t kb = split * per_k, ke = min(kp, kb + per_k);
-  const float* Ah = ahi + batch * a_rows * a_ld;
-  const float* Al = alo + batch * a_rows * a_ld;
-  const float* Bh = bhi + batch * b_rows * b_ld;
-  const float* Bl = blo + batch * b_rows * b_ld;
-  const int tx = threadIdx.x & 7, ty = threadIdx.x >> 3;  // 4 columns, 2 rows each
-  float acc[2][4] = {};
-  for (int64_t k0 = kb; k0 < ke; k0 += NARROW_BK) {
-    narrow_stage(As, NARROW_BM, Ah, Al, a_mn, a_ld, a_rows, m0, m, k0, ke);
-    narrow_stage(Bs, NARROW_BN, Bh, Bl, b_mn, b_ld, b_rows, n0, n, k0, ke);
-    __syncthreads();
-#pragma unroll 8
-    for (int kk = 0; kk < NARROW_BK; ++kk) {
-      const float a0 = As[kk][ty * 2], a1 = As[kk][ty * 2 + 1];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float bv = Bs[kk][tx * 4 + j];
-        acc[0][j] = fmaf(a0, bv, acc[0][j]);
-        acc[1][j] = fmaf(a1, bv, acc[1][j]);
-      }
-    }
-    __syncthreads();
-  }
-  float* C = c + blockIdx.z * m * n;  // (batch, split) slices are m x n apart
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int64_t r = m0 + ty * 2 + i;
-    if (r >= m) continue;
-    const int64_t col = n0 + tx * 4;
-    if (n % 4 == 0 && col + 3 < n) {
-      *(float4*)(C + r * n + col) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (col + j < n) C[r * n + col + j] = acc[i][j];
-    }
-  }
-}
-
 template <bool BF16>
 __global__ void k_adam_scalars(float* s, float beta1, float beta2) {
   pdl_entry();
@@ -774,32 +679,9 @@ void launch_gemm_simt(const Operand& a, const Operand& b, float* c, int64_t batc
              b.ld, b.rows, c, m, n, kp);
 }
 
-bool is_narrow(int64_t n, int64_t kp) { return n <= NARROW_BN || kp <= NARROW_BK; }
-
-void launch_gemm_narrow(const Operand& a, const Operand& b, float* c, float* partial, int splits,
-                        int64_t batch, int64_t m, int64_t n, int64_t kp, cudaStream_t stream) {
-  if (splits < 1 || !partial) splits = 1;
-  // k per split in whole 32-deep chunks
-  const int64_t chunks = (kp + NARROW_BK - 1) / NARROW_BK;
-  const int64_t per = (chunks + splits - 1) / splits * NARROW_BK;
-  splits = (int)((kp + per - 1) / per);
-  float* target = splits > 1 ? partial : c;
-  dim3 grid((unsigned)((n + NARROW_BN - 1) / NARROW_BN), (unsigned)((m + NARROW_BM - 1) / NARROW_BM),
-            (unsigned)(batch * splits));
-  launch_pdl(k_gemm_narrow, grid, 256, 0, stream, a.hi, a.lo, a.mn, a.ld, a.rows, b.hi, b.lo,
-             b.mn, b.ld, b.rows, target, m, n, kp, splits, per);
-  // slices are (batch, split)-major, which is the split-major order
-  // k_split_sum reads when batch == 1 (the only case that splits)
-  if (splits > 1) launch_split_sum(partial, c, batch * m * n, splits, stream);
-}
-
 void launch_gemm(const Operand& a, const Operand& b, float* c, float* partial, int splits,
                  int64_t batch, int64_t m, int64_t n, int64_t kp, cudaStream_t stream,
                  const StreamK* sk) {
-  if (g_engine == 0 && is_narrow(n, kp) && (splits <= 1 || batch == 1)) {
-    launch_gemm_narrow(a, b, c, partial, splits, batch, m, n, kp, stream);
-    return;
-  }
   if (g_engine != 1 &&
       launch_gemm_tcgen05_split(a, b, c, partial, splits, batch, m, n, kp, stream, sk))
     return;

@@ -71,13 +71,6 @@ constexpr size_t kStreamKFlagBytes = (size_t)kStreamKMaxCtas * 8 * 4;
 void launch_gemm(const Operand& a, const Operand& b, float* c, float* partial, int splits,
                  int64_t batch, int64_t m, int64_t n, int64_t kp, cudaStream_t stream,
                  const StreamK* sk = nullptr);
-// out[i] = partial[0][i] + partial[1][i] + ... in split order (split-K sums).
-void launch_split_sum(const float* partial, float* c, long long count, int splits,
-                      cudaStream_t stream);
-// The narrow-product SIMT kernel (n <= 32 or kp <= 32), which the automatic
-// engine picks for such shapes; split-K into `partial` (batch 1) when splits > 1.
-void launch_gemm_narrow(const Operand& a, const Operand& b, float* c, float* partial, int splits,
-                        int64_t batch, int64_t m, int64_t n, int64_t kp, cudaStream_t stream);
 // The SIMT path alone (tests compare the two).
 void launch_gemm_simt(const Operand& a, const Operand& b, float* c, int64_t batch, int64_t m,
                       int64_t n, int64_t kp, cudaStream_t stream);

@@ -150,42 +150,3 @@ def test_stream_k_matches_f64_and_whole_tiles(device, m, n, k, a_mn, tile):
         lib.tbx_set_gemm_stream_k(0)
         lib.tbx_set_gemm_tile_n(0)
     assert torch.equal(outs["stream-k"], outs["stream-k again"])
-
-
-@pytest.mark.parametrize("batch,m,n,k,splits,a_mn,b_mn", [
-    (1, 16384, 27, 512, 1, 0, 1), (1, 16384, 512, 27, 1, 0, 0), (1, 512, 27, 16384, 37, 1, 1),
-    (3, 130, 20, 70, 1, 1, 0), (1, 100, 300, 16, 1, 0, 1), (1, 777, 5, 3000, 5, 1, 1)])
-def test_narrow_product_kernel_matches_f64(device, batch, m, n, k, splits, a_mn, b_mn):
-    # the SIMT kernel the automatic engine picks for outputs at most 32 wide or
-    # reductions at most 32 deep (the char-MLP's 27-symbol head and its
-    # gradients), on both operand layouts, with ordered split-K partials
-    import torch
-    from poorgrad_b200.abi import load_library
-    lib = load_library()
-    f = lib.tbx_gemm_prepared_layout
-    f.restype = C.c_int
-    f.argtypes = ([C.c_void_p, C.c_void_p, C.c_int, C.c_int64] * 2 + [C.c_void_p, C.c_void_p, C.c_int]
-                  + [C.c_int64] * 5 + [C.c_int])
-    g = torch.Generator(device="cuda").manual_seed(11 * batch + m + n + k)
-    a = torch.rand((batch, m, k), device="cuda", generator=g) * 2 - 1
-    bt = torch.rand((batch, n, k), device="cuda", generator=g) * 2 - 1
-    kp = (k + 31) // 32 * 32
-
-    def operand(x, mn):
-        rows = x.shape[1]
-        if not mn:
-            return _prep(torch, x, kp), kp
-        ld = (rows + 31) // 32 * 32
-        return _prep(torch, x.transpose(1, 2).contiguous(), ld), ld
-
-    (ahi, alo), a_ld = operand(a, a_mn)
-    (bhi, blo), b_ld = operand(bt, b_mn)
-    ref = torch.bmm(a.double(), bt.double().transpose(1, 2))
-    tol = (8 if k <= 1024 else 16) * EPS * math.sqrt(k) * (1 + ref.abs())
-    c = torch.full((batch, m, n), float("nan"), device="cuda")
-    part = torch.empty((splits, batch, m, n), device="cuda")
-    rc = f(ahi.data_ptr(), alo.data_ptr(), a_mn, a_ld, bhi.data_ptr(), blo.data_ptr(), b_mn,
-           b_ld, c.data_ptr(), part.data_ptr(), splits, batch, m, n, k, kp, 3)
-    assert rc == 0
-    err = (c.double() - ref).abs()
-    assert torch.all(err <= tol), f"worst {(err / tol).max().item()}"
