@@ -145,6 +145,10 @@ struct Info {
   int owner = -1;          // node whose buffer `buf` is (Layout views)
   int group = -1;          // open/closed group id that computes it
   int alias = -1;          // LogSumExp/LogSoftmax: value of this synthetic node
+  // A readable `0 + y` gradient seed whose value is y's buffer as it stands:
+  // y is accumulated from +0 (a product, a scatter-add, a row, column or full
+  // sum), so it never holds -0 and adding +0 would change no bit.
+  int seed_of = -1;
   int consumers = 0;
   int ops = 0;             // expression size bound for virtual nodes
   std::vector<int> heavy;  // big buffers a virtual expression reads

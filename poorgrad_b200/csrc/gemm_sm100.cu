@@ -522,7 +522,9 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
           float* p = dst + (long long)row0 * n + col;
           const int rows = min(32, m - row0);
 #pragma unroll 8
-          for (int r = 0; r < rows; ++r) p[(long long)r * n] = st[r][lane];
+          // + 0 on the way out: a product never leaves as -0 (a `0 + c`
+          // gradient seed over it is then the product's own buffer)
+          for (int r = 0; r < rows; ++r) p[(long long)r * n] = __fadd_rn(st[r][lane], 0.0f);
         }
         __syncwarp();
       }
@@ -543,7 +545,7 @@ __global__ void k_split_sum(const float* __restrict__ partial, float* __restrict
        i += (long long)gridDim.x * blockDim.x) {
     float acc = partial[i];
     for (int s = 1; s < splits; ++s) acc = __fadd_rn(acc, partial[(long long)s * count + i]);
-    out[i] = acc;
+    out[i] = __fadd_rn(acc, 0.0f);  // never -0, as the unsplit epilogue
   }
 }
 

@@ -534,26 +534,36 @@ __global__ void k_optimizer(const OptEntry* __restrict__ entries, int count, int
   sc.gscale = gscale;
   sc.c1 = kind ? s[2] : 0.0f;
   sc.c2 = kind ? s[3] : 0.0f;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
+  // Four consecutive elements per thread: one search of the entry table per
+  // four elements (a step to the next entry where a tensor ends among them),
+  // and four independent updates in flight.
+  constexpr int PER = 4;
+  for (int64_t base = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * PER; base < total;
+       base += (int64_t)gridDim.x * blockDim.x * PER) {
     int lo = 0, hi = count - 1;
     while (lo < hi) {
       int mid = (lo + hi + 1) >> 1;
-      if (entries[mid].start <= i) lo = mid; else hi = mid - 1;
+      if (entries[mid].start <= base) lo = mid; else hi = mid - 1;
     }
-    const OptEntry& e = entries[lo];
-    const int64_t j = i - e.start;
-    float p = e.p[j];
-    if (kind == 0) {
-      float unused = 0.0f;
-      optimizer_update<BF16>(p, unused, unused, e.g[j], false, sc);
-    } else {
-      float m = e.m[j], v = e.v[j];
-      optimizer_update<BF16>(p, m, v, e.g[j], e.decay != 0, sc);
-      e.m[j] = m;
-      e.v[j] = v;
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int64_t i = base + u;
+      if (i >= total) break;
+      while (lo + 1 < count && entries[lo + 1].start <= i) ++lo;
+      const OptEntry& e = entries[lo];
+      const int64_t j = i - e.start;
+      float p = e.p[j];
+      if (kind == 0) {
+        float unused = 0.0f;
+        optimizer_update<BF16>(p, unused, unused, e.g[j], false, sc);
+      } else {
+        float m = e.m[j], v = e.v[j];
+        optimizer_update<BF16>(p, m, v, e.g[j], e.decay != 0, sc);
+        e.m[j] = m;
+        e.v[j] = v;
+      }
+      e.p[j] = p;
     }
-    e.p[j] = p;
   }
 }
 
@@ -697,7 +707,7 @@ void launch_optimizer(const OptEntry* entries, int count, int64_t total, const f
                       const float* lr, int kind, float beta1, float beta2, float share1,
                       float share2, float eps, float decay, float gscale, bool bf16,
                       cudaStream_t stream) {
-  int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 148 * 8));
+  int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 1023) / 1024, 148 * 8));
   if (bf16)
     launch_pdl(k_optimizer<true>, grid, 256, 0, stream, entries, count, total, scalars, lr, kind,
                beta1, beta2, share1, share2, eps, decay, gscale);

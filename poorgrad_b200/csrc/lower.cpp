@@ -647,8 +647,59 @@ class Lowerer {
         default:
           classify_computed(n, a, b);
       }
+      if (nd.readable && !f.materialized && f.kind != Kind::Sel && fold_seed(n)) continue;
       if (nd.readable && !f.materialized && f.kind != Kind::Sel) materialize(n);
     }
+  }
+
+  // Whether node y's value is accumulated from +0 by its kernel, so that it
+  // never holds -0: a GEMM (its epilogue and split-K sum add +0 on the way
+  // out), a scatter-add (segment sums from zero), and the sums that become
+  // row, column or full reductions of a fused group (their accumulators start
+  // at zero).  The serial REDUCE kernel seeds with the first element: not.
+  bool accumulated_from_zero(int y) const {
+    const Node& nd = P.nodes[y];
+    if (nd.op == TB_OP_MATMUL || nd.op == TB_OP_SCATTER) return true;
+    if (nd.op != TB_OP_SUM && nd.op != TB_OP_SUM_ALONG) return false;
+    const Node& x = P.nodes[nd.operands[0]];
+    if (nd.op == TB_OP_SUM) return x.rank > 0;
+    const int axis = (int)nd.attrs[0];
+    if (axis == x.rank - 1) return true;
+    if (x.rank == 2 && axis == 0) {
+      int64_t T, KC;
+      int vec;
+      row_shape(x.dims(), T, KC, vec);
+      return KC * vec <= 32 && x.shape[1] <= 8192;
+    }
+    return false;
+  }
+
+  // A readable gradient seed `0 + y` (Tape::differentiate's first
+  // contribution, graph/tape.rs:389-393) over such a y that nothing else
+  // reads is y's buffer itself: no copy kernel, and y's buffer is kept as
+  // a readable value.
+  bool fold_seed(int n) {
+    const Node& nd = P.nodes[n];
+    if (P.bf16 || nd.op != TB_OP_ADD) return false;
+    int y = -1;
+    for (int o = 0; o < 2; ++o) {
+      const Info& c = P.info[nd.operands[o]];
+      if (c.kind == Kind::Const && c.c == 0.0f && !std::signbit(c.c)) y = nd.operands[1 - o];
+    }
+    if (y < 0) return false;
+    const Info& fy = P.info[y];
+    if (!fy.materialized || fy.owner != y || P.nodes[y].readable || fy.consumers != 1 ||
+        fy.seed_of >= 0 || !accumulated_from_zero(y) || P.nodes[y].volume() != nd.volume())
+      return false;
+    Info& f = P.info[n];
+    f.kind = Kind::Layout;
+    f.materialized = true;
+    f.buf = fy.buf;
+    f.lay = contiguous(nd);
+    f.owner = y;
+    f.seed_of = y;
+    P.buffers[fy.buf].keep = true;
+    return true;
   }
 
   void classify_computed(int n, int a, int b) {

@@ -365,7 +365,7 @@ int resolve_node(const tb::Program& P, int64_t node) {
 int readable_buffer(const tb::Program& P, int64_t node) {
   int n = resolve_node(P, node);
   const tb::Info& f = P.info[n];
-  if (!P.nodes[n].readable || !f.materialized || f.owner != n)
+  if (!P.nodes[n].readable || !f.materialized || (f.owner != n && f.seed_of < 0))
     throw Failure(TB_INVALID, "node " + std::to_string(node) + " is not a readable value of the plan");
   return f.buf;
 }
@@ -1363,7 +1363,7 @@ int64_t tbx_lower_json(const tb_plan_desc* desc, char* buffer, size_t capacity) 
       // as readable_buffer answers: through the alias of an expanded node
       const int r = resolve_node(*prog, (int64_t)n);
       const tb::Info& f = prog->info[r];
-      if (!prog->nodes[r].readable || !f.materialized || f.owner != r) continue;
+      if (!prog->nodes[r].readable || !f.materialized || (f.owner != r && f.seed_of < 0)) continue;
       o << (first ? "" : ",") << "\"" << n << "\":[" << f.buf << ",";
       json_list(o, prog->nodes[n].dims());
       o << "]";
