@@ -446,12 +446,11 @@ def kernel_profile(plan, reps=20):
     return rows
 
 
-# DRAM read + write bytes per launch of the dominant kernel class, averaged
-# over that class's launches in one ncu capture of the workload
-# (dram__bytes_read.sum + dram__bytes_write.sum), with the profile summary it
-# comes from.
-NCU_TRAFFIC = {"charmlp": {"gemm": (77.29e6, "profiles/charmlp_step_launches.md: the 63 "
-                                    "k_gemm_tcgen05 launches of 7 steps")}}
+# DRAM read + write bytes per launch of the dominant kernel class from one ncu
+# capture of the workload (dram__bytes_read.sum + dram__bytes_write.sum), with
+# the profile summary it comes from.
+NCU_TRAFFIC = {"charmlp": {"gemm": (74.08e6, "profiles/gemm_tcgen05_charmlp_16384x512x512.md: "
+                                    "the step's first product, one launch")}}
 
 
 def traffic(workload, kind):
