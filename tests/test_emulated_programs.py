@@ -5,9 +5,12 @@ gather and scatter) and the data flow between them, checked without a GPU.
 The library kernels are restated in the emulator from their contracts, so
 GEMM results agree within the product's tolerance, not bitwise.
 
-bf16 networks, which the device declines until they have run on a GPU, are
-checked here end to end: their emulated programs equal the bf16 oracle
-bitwise on these cases.  Engine-backward plans (the reverse scan appended by
+bf16 networks are checked here end to end: their emulated programs equal the
+bf16 oracle bitwise on these cases.  That bitwise agreement covers the
+emulator's restatements only (a GEMM rounded once from an f64 hi/lo product,
+column finals summed serially); the device accumulates 3xTF32 in chunks and
+sums finals in strided groups, so device bf16 results are checked within
+tolerance (tests/test_bf16.py), never bitwise.  Engine-backward plans (the reverse scan appended by
 the lowering) follow the oracle's restatement of `Run::backward`."""
 import numpy as np
 import pytest
