@@ -88,3 +88,36 @@ def test_values_past_two_to_the_31_elements_index_in_64_bits(built):
     text = backend.lower_describe(cols, with_source=True)
     assert "typedef long long I;" in text
     backend.nvrtc_check(cols)
+
+
+def test_gradient_seeds_over_products_and_sums_need_no_copy_kernels(charmlp_lines):
+    # Tape::differentiate's `0 + c` seeds (graph/tape.rs:389-393) over a
+    # product, a scatter-add or a fused sum are that value's own buffer: the
+    # step ends with the optimizer inputs written by their producers, not by
+    # copy kernels (the only flat kernels left are the gather, the loss scale
+    # and the tail of the cross-entropy gradient)
+    flat = [l for l in charmlp_lines if re.match(r"\d+: ew ", l)]
+    assert len(flat) <= 3, flat
+
+
+def test_window_patterns_lower_without_materialized_windows(built):
+    # conv -> max-pool: the im2col view chain is read by the operand prep
+    # (the tf32 pair the tensor-core product needs) and the pool's window max
+    # runs inside the kernel that adds the bias and restores NCHW: no window
+    # lanes are stored (engine/pattern/window.rs, reduce_window.rs)
+    import numpy as np
+    from poorgrad_b200 import neural
+    from poorgrad_b200.graph import Dense, Tape
+    from poorgrad_b200.plan import Request
+    t = Tape()
+    rng = np.random.default_rng(0)
+    x = t.input(Dense((8, 4, 16, 16), rng.standard_normal((8, 4, 16, 16)).astype(np.float32)))
+    w = t.parameter(Dense((8, 4, 3, 3), rng.standard_normal((8, 4, 3, 3)).astype(np.float32)))
+    b = t.parameter(Dense((8,), np.zeros(8, np.float32)))
+    p = neural.max_pool(neural.conv2d(x, w, b, stride=1, padding=1), 2, 2)
+    net = t.into_network()
+    lines = [l for l in backend.lower_describe(net.compile(Request([p]))).splitlines()
+             if re.match(r"\d+: ", l)]
+    kinds = [l.split()[1] for l in lines]
+    assert kinds.count("gemm3xtf32") == 1
+    assert kinds.count("prep") == 2 and kinds.count("ew") == 1 and len(lines) == 4, lines
