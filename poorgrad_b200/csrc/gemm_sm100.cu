@@ -298,6 +298,7 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
                    int* __restrict__ sk_flags) {
   pdl_entry();
   using D = Derived<C>;
+  static_assert(4 * C::GROUPS <= 8, "the stream-K flags hold eight epilogue warps per CTA");
   constexpr int BN = C::BN, BK = C::BK, STAGES = C::STAGES, CHUNK = C::CHUNK;
   constexpr int TILE_A = D::TILE_A, TILE_B = D::TILE_B, STAGE_BYTES = D::STAGE_BYTES;
   constexpr int EPI_COLS = D::EPI_COLS;
