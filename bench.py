@@ -503,6 +503,8 @@ def main():
     ap.add_argument("--batch", type=int, default=0, help="per-GPU batch override (profiling)")
     ap.add_argument("--seq", type=int, default=0, help="gpt2 sequence override (profiling)")
     ap.add_argument("--layers", type=int, default=0, help="gpt2 layer override (profiling)")
+    ap.add_argument("--bucket-mb", type=float, default=32.0,
+                    help="gradient all-reduce bucket size (MiB) for N > 1")
     ap.add_argument("--replay-s", type=float, default=1.5,
                     help="untimed replay before the timed steps (clock sampling)")
     ap.add_argument("--no-kernel-profile", action="store_true",
@@ -544,7 +546,7 @@ def main():
             uid.copy_(torch.tensor(list(backend.Comm.unique_id()), dtype=torch.uint8))
         dist.broadcast(uid, 0)
         comm = backend.Comm(rank, world, bytes(uid.cpu().tolist()))
-        comm.attach(plan)
+        comm.attach(plan, bucket_bytes=int(args.bucket_mb * (1 << 20)))
 
     # per-step batches: device-resident (value) and pinned host (e2e)
     nb = max(2, min(8, args.steps))
@@ -672,7 +674,7 @@ def main():
         t_solo = torch.tensor([s0.elapsed_time(s1) / args.steps], device="cuda")
         dist.all_reduce(t_solo, op=dist.ReduceOp.MAX)
         grad_bytes = sum(int(np.prod(w.columns.nodes[g.index].shape)) * 4 for g in w.grads)
-        comm_info = {"allreduce_bytes_per_step": grad_bytes,
+        comm_info = {"allreduce_bytes_per_step": grad_bytes, "bucket_mib": args.bucket_mb,
                      "step_ms_without_exchange": float(t_solo.item()),
                      "exposed_exchange_ms": per_step - float(t_solo.item()),
                      "how": "the same step on the same rank without the NCCL all-reduce, "
