@@ -113,7 +113,6 @@ struct Kernel {
   std::string name, source;
   std::vector<int> params;      // buffer ids, in kernel parameter order
   int64_t grid = 1, block = 256;
-  int blocks_per_sm = 4;        // ROW: the launch bound's resident blocks per SM
   int smem = 0;
   bool exact = true;
   // static kernels

@@ -9,7 +9,6 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
-#include <cstdlib>
 #include <cstring>
 #include <functional>
 #include <map>
@@ -1273,13 +1272,6 @@ class Emitter {
   // correctly rounded) and `0 + x` gradient seeds are dropped (they differ
   // from x only in the sign of a zero).  Exact kernels never set it.
   bool relaxed = false;
-  // Row prefetch: the vector loads of a row's first phase whose address
-  // depends on the row.  A collecting emission lists them (buffer, offset);
-  // the real one then reads them from registers filled one row ahead.
-  bool pf_collect = false;
-  bool in_row_pass = false;
-  std::vector<std::pair<int, std::string>> pf_loads;
-  std::map<std::string, int> pf_index;
   // Values that already carry a tolerance: results of transcendentals, row
   // reductions, and anything computed from them.  A kernel whose every member
   // is such a value (or a reduction) may be emitted relaxed: no exact output
@@ -1366,16 +1358,6 @@ class Emitter {
         off = s_add(off, s_mul(c, lay.stride[d]));
       }
       std::string k = "vec|" + std::to_string(buf) + "|" + off;
-      if (in_row_pass && phase == 0 && off.find("i0") != std::string::npos) {
-        auto it = pf_index.find(k);
-        static const char* pc[4] = {".x", ".y", ".z", ".w"};
-        if (it != pf_index.end()) return "pf" + std::to_string(it->second) + "[kc]" + pc[idx.lane];
-        if (pf_collect) {
-          bool seen = false;
-          for (auto& e : pf_loads) seen = seen || (e.first == buf && e.second == off);
-          if (!seen) pf_loads.push_back({buf, off});
-        }
-      }
       const std::string* hit = find(k);
       std::string v;
       if (hit) {
@@ -1969,20 +1951,10 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
     maxphase = std::max(maxphase, m.phase);
   }
   K.block = 256;
-  // Row prefetch (the real emission, when the collecting one found the
-  // first phase's row loads): a multi-phase kernel whose full passes cover the
-  // row and whose prefetched rows fit in 16 registers loads the next row's
-  // first-phase inputs during the current row's last phase.  The registers
-  // come from a three-blocks-per-SM launch bound: measured on the C4
-  // LayerNorm/tanh backward rows, 37.0 us against 40.7 us.
-  static const bool prefetch_on = !getenv("TB_ROW_PREFETCH") || atoi(getenv("TB_ROW_PREFETCH")) != 0;
-  const bool prefetch = prefetch_on && !E.pf_index.empty() && maxphase >= 1 && vec == 4 &&
-                        L % (T * vec) == 0 && (int64_t)E.pf_index.size() * KC <= 4;
-  if (!prefetch) E.pf_index.clear();
-  K.blocks_per_sm = prefetch ? 3 : 4;
+  // per-block column partials cost blocks * L floats: fewer blocks for wide rows
   // four blocks per SM (the launch bound): for C2's 8192-wide rows, 592 blocks
   // ran the kernel 8% faster than 444 for 5 MB more partials
-  int64_t cap = SMS * K.blocks_per_sm;
+  int64_t cap = SMS * 4;
   K.grid = std::max<int64_t>(1, std::min<int64_t>((R + teams - 1) / teams, cap));
   if (has_col || has_all) E.exact = false;
   // A team's reduction waits only for its own warps (a named barrier per
@@ -2011,47 +1983,18 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
     E.line("float kr" + std::to_string(m) + "[" + std::to_string(KC * vec) + "];");
   }
   hoist_uniform_scalars(P, K, E);
-  std::vector<int64_t> lead(S.begin(), S.end() - 1);
-  // fills the prefetch registers for row `r` (an expression), if it exists
-  auto prefetch_row = [&](const std::string& r) {
-    E.line("{");
-    E.indent += 2;
-    E.line("const I pf_row = " + r + ";");
-    E.line("if (pf_row < " + lit(R) + ") {");
-    E.indent += 2;
-    if (!lead.empty()) E.unravel("pf_row", lead, "i");
-    E.line("#pragma unroll");
-    E.line("for (int kc = 0; kc < " + std::to_string(KC) + "; ++kc) {");
-    E.line("  const I j0 = ((I)kc * " + std::to_string(T) + " + tl) * " + std::to_string(vec) + ";");
-    for (auto& e : E.pf_index) {
-      const auto& ld = E.pf_loads[e.second];
-      E.line("  pf" + std::to_string(e.second) + "[kc] = *(const float4*)(" + E.fptr(ld.first) +
-             " + " + ld.second + ");");
-    }
-    E.line("}");
-    E.indent -= 2;
-    E.line("}");
-    E.indent -= 2;
-    E.line("}");
-  };
-  if (prefetch) {
-    for (auto& e : E.pf_index)
-      E.line("float4 pf" + std::to_string(e.second) + "[" + std::to_string(KC) + "];");
-    prefetch_row("(I)blockIdx.x * " + std::to_string(teams) + " + team");
-  }
   E.line("for (I base = (I)blockIdx.x * " + std::to_string(teams) + "; base < " + lit(R) +
          "; base += (I)gridDim.x * " + std::to_string(teams) + ") {");
   E.indent += 2;
   E.line("const I row = base + team;");
   E.line("const bool act = row < " + lit(R) + ";");
+  std::vector<int64_t> lead(S.begin(), S.end() - 1);
   std::vector<std::string> rc = lead.empty() ? std::vector<std::string>{}
                                              : E.unravel("row", lead, "i");
   if (R % teams == 0) hoist_row_uniform(P, K, E, lead, rc);
   for (int ph = 0; ph <= maxphase; ++ph) {
     E.phase = ph;
     E.line("// phase " + std::to_string(ph));
-    if (prefetch && ph == maxphase)
-      prefetch_row("row + (I)gridDim.x * " + std::to_string(teams));
     for (size_t m = 0; m < K.members.size(); ++m) {
       const Member& mm = K.members[m];
       if (mm.phase != ph) continue;
@@ -2145,9 +2088,7 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
       E.line("for (int kc = 0; kc < " + std::to_string(kc_full) + "; ++kc) {");
       E.indent += 2;
       E.line("const I j0 = ((I)kc * " + std::to_string(T) + " + tl) * " + std::to_string(vec) + ";");
-      E.in_row_pass = true;
       emit_pass();
-      E.in_row_pass = false;
       E.indent -= 2;
       E.line("}");
       E.indent -= 2;
@@ -2160,9 +2101,7 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
       E.line("const I j0 = ((I)kc * " + std::to_string(T) + " + tl) * " + std::to_string(vec) + ";");
       E.line("if (act && j0 < " + lit(L) + ") {");
       E.indent += 2;
-      E.in_row_pass = true;
       emit_pass();
-      E.in_row_pass = false;
       E.indent -= 2;
       E.line("}");
       E.indent -= 2;
@@ -2804,27 +2743,19 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
     // A first, discarded emission learns whether the kernel carries a
     // tolerance; it is then emitted for real, relaxed if it does.
     bool carries_tolerance = false;
-    std::vector<std::pair<int, std::string>> pf_loads;
     if (K.type == KType::EW || K.type == KType::ROW) {
       const Kernel saved = K;
       const size_t buffers = P.buffers.size(), nfinals = finals.size();
       Emitter probe(P, K, (int)P.kernels.size());
-      probe.pf_collect = true;
       if (K.type == KType::EW) emit_ew(P, K, probe);
       else emit_row(P, K, probe, Lw, finals);
       carries_tolerance = !probe.exact && !probe.exact_member_seen && !P.bf16;
-      pf_loads = probe.pf_loads;
       K = saved;
       P.buffers.resize(buffers);
       finals.resize(nfinals);
     }
     Emitter E(P, K, (int)P.kernels.size());
     E.relaxed = carries_tolerance;
-    if (K.type == KType::ROW) {
-      E.pf_loads = pf_loads;
-      for (size_t i = 0; i < pf_loads.size(); ++i)
-        E.pf_index["vec|" + std::to_string(pf_loads[i].first) + "|" + pf_loads[i].second] = (int)i;
-    }
     switch (K.type) {
       case KType::EW: emit_ew(P, K, E); break;
       case KType::ROW: emit_row(P, K, E, Lw, finals); break;
@@ -2862,8 +2793,7 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
     // row kernels run at most four blocks per SM (their grid cap): ask for
     // registers that let all four be resident
     fn << "extern \"C\" __global__ void __launch_bounds__(256"
-       << (K.type == KType::ROW ? ", " + std::to_string(K.blocks_per_sm) : std::string())
-       << ") NAME(const PRM_NAME prm) {\n";
+       << (K.type == KType::ROW ? ", 4" : "") << ") NAME(const PRM_NAME prm) {\n";
     fn << "  typedef " << (E.wide ? "long long" : "int") << " I;\n";
     // launched with programmatic stream serialization: wait for the previous
     // kernels (and their memory) before any access, then let the next launch
