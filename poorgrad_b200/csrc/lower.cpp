@@ -1901,7 +1901,18 @@ static void emit_ew(Program& P, Kernel& K, Emitter& E) {
 // ---- row-space group: phases of elementwise work separated by row reductions
 static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
                      std::vector<Kernel>& finals) {
-  const std::vector<int64_t>& S = K.space;
+  const std::vector<int64_t>& space = K.space;
+  // A one-dimensional space with no row or column reductions (elementwise
+  // members and full sums only) is cut into virtual rows of 128, so that
+  // many blocks share it instead of one team walking all of it; members still
+  // index the flat position row * 128 + j.
+  bool virtual_rows = space.size() == 1 && space[0] >= 4096 && space[0] % 128 == 0;
+  for (auto& m : K.members)
+    if (m.type == MemberType::ROW_SUM || m.type == MemberType::ROW_MAX ||
+        m.type == MemberType::COL_SUM)
+      virtual_rows = false;
+  const std::vector<int64_t> S =
+      virtual_rows ? std::vector<int64_t>{space[0] / 128, 128} : space;
   int64_t L = S.back();
   int64_t R = volume_of(S) / L;
   int64_t T, KC;
@@ -1989,6 +2000,8 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
   E.line("const I row = base + team;");
   E.line("const bool act = row < " + lit(R) + ";");
   std::vector<int64_t> lead(S.begin(), S.end() - 1);
+  if (virtual_rows) lead.clear();  // the row is part of the flat position, not a coordinate
+  const std::string jbase = virtual_rows ? "(row * " + lit(L) + " + j0)" : "j0";
   std::vector<std::string> rc = lead.empty() ? std::vector<std::string>{}
                                              : E.unravel("row", lead, "i");
   if (R % teams == 0) hoist_row_uniform(P, K, E, lead, rc);
@@ -2013,10 +2026,10 @@ static void emit_row(Program& P, Kernel& K, Emitter& E, Lowerer& Lw,
     for (int v = 0; v < vec; ++v) {
       Idx idx;
       idx.c = rc;
-      idx.c.push_back(vec > 1 ? s_add("j0", std::to_string(v)) : "j0");
+      idx.c.push_back(vec > 1 ? s_add(jbase, std::to_string(v)) : jbase);
       if (vec > 1) {
         idx.lane = v;
-        idx.lbase = "j0";
+        idx.lbase = jbase;
       }
       for (size_t m = 0; m < K.members.size(); ++m) {
         const Member& mm = K.members[m];

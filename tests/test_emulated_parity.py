@@ -134,3 +134,18 @@ def test_log_sum_exp_extreme_rows(built, row):
     np.testing.assert_allclose(emu[lse.index], ref[lse.index], rtol=1e-6)
     np.testing.assert_allclose(emu[g.index], ref[g.index], rtol=1e-6, atol=1e-7)
     assert math.isfinite(float(emu[g.index].sum()))
+
+
+def test_long_flat_sums_split_into_virtual_rows(built):
+    # a one-dimensional group with a full sum (the cross-entropy's batch sum)
+    # runs as many 128-wide virtual rows instead of one team over the vector
+    t = Tape()
+    x = t.parameter(tensor((8192,), rnd((8192,), 21, 0.5, 2.0).reshape(-1)))
+    y = t.parameter(tensor((8192,), rnd((8192,), 22).reshape(-1)))
+    z = x.ln() + y
+    loss = (z * y).sum()
+    gx, gy = t.differentiate(loss, [x, y])
+    ref, emu = both(t, [loss, z, gx, gy])
+    np.testing.assert_allclose(emu[loss.index], ref[loss.index], rtol=1e-5)
+    for v in (z, gx, gy):
+        np.testing.assert_allclose(emu[v.index], ref[v.index], rtol=4e-6, atol=1e-7)
