@@ -235,6 +235,10 @@ std::string s_mod(const std::string& a, int64_t k) {
   if (numeric(a, x)) return lit(x % k);
   return "(" + a + "%" + lit(k) + ")";
 }
+// Column sums over at most this many rows run as one serial fold per column
+// (the REDUCE kernel) instead of per-block partials and a final.
+constexpr int64_t kSerialColumnRows = 256;
+
 std::string flit(float f) {
   uint32_t bits;
   memcpy(&bits, &f, 4);
@@ -665,7 +669,7 @@ class Lowerer {
     if (nd.op == TB_OP_SUM) return x.rank > 0;
     const int axis = (int)nd.attrs[0];
     if (axis == x.rank - 1) return true;
-    if (x.rank == 2 && axis == 0) {
+    if (x.rank == 2 && axis == 0 && x.shape[0] > kSerialColumnRows) {
       int64_t T, KC;
       int vec;
       row_shape(x.dims(), T, KC, vec);
@@ -1084,7 +1088,11 @@ class Lowerer {
             group_member(n, max ? MemberType::ROW_MAX : MemberType::ROW_SUM, space);
             break;
           }
-          if (!max && x.rank == 2 && axis == 0) {
+          // A column sum over a short batch (batch-norm statistics over a
+          // mini-batch, a small batch's bias gradients) is one serial fold
+          // per column from the first row: the reference's own order, so
+          // bit-identical, and no partials or final.
+          if (!max && x.rank == 2 && axis == 0 && x.shape[0] > kSerialColumnRows) {
             int64_t T, KC;
             int vec;
             row_shape(space, T, KC, vec);

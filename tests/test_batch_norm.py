@@ -115,3 +115,33 @@ def test_express_with_on_the_device_follows_each_feed(device):
         plan.forward(dp, feeds, sync=True)
         # subtract, sqrt, divide, multiply, add: correctly rounded on both sides
         assert plan.of(out).tobytes() == ref[out.index].tobytes()
+
+
+@pytest.mark.gpu
+def test_training_statistics_on_the_device_are_bitwise_the_recorded_formula(device):
+    # training mode over a mini-batch (batch-norm's BatchNormTraining pattern,
+    # payload/tensor.rs:802-851): the mean and the biased variance are column
+    # folds over at most 256 rows, which the device runs as one serial fold
+    # per feature from the first row -- the reference's order -- so the
+    # statistics and the normalized output equal the oracle bit for bit; the
+    # gradients through them carry the tolerance of their reassociated sums
+    batch, features = 64, 4096
+    t = Tape()
+    rng = np.random.default_rng(3)
+    x = t.parameter(tensor((batch, features), rng.normal(size=(batch, features)).astype(np.float32)))
+    bn = neural.BatchNorm(t, features, scale=rng.uniform(0.5, 1.5, features),
+                          shift=rng.normal(size=features))
+    out, mean, var = bn.express(x)
+    loss = (out * out).sum()
+    grads = t.differentiate(loss, [x] + bn.parameters())
+    net = t.into_network()
+    cols = net.compile(Request([out, mean, var] + grads))
+    ref = oracle.run(cols, net.parameters())
+    plan = backend.DevicePlan(cols)
+    dp = backend.DeviceParameters(plan, net.parameters())
+    plan.forward(dp, sync=True)
+    for v in (mean, var, out):
+        assert plan.of(v).tobytes() == ref[v.index].tobytes()
+    for g in grads:
+        r = ref[g.index]
+        np.testing.assert_allclose(plan.of(g), r, rtol=1e-4, atol=1e-5 * (np.abs(r).max() + 1e-30))
