@@ -696,7 +696,10 @@ def main():
         tol = None if args.no_cpu else tolerance(args.config, w, plan, host_batches[0])
         arena_mb = stats["arena_bytes"] / 2**20
         cfg.update({"workload": args.config, "parallelism": f"dp{world}",
-                    "l2": f"working set > L2: arena {arena_mb:.0f} MiB per step, no flush",
+                    "l2": (f"working set > L2: arena {arena_mb:.0f} MiB per step, no flush"
+                           if arena_mb > 126 else
+                           f"working set {arena_mb:.0f} MiB fits in L2 and is not flushed "
+                           "(a small, latency-bound step)"),
                     "optimizer": opt_cfg.get("kind") if opt_cfg else None})
         line = {"metric": metric, "value": value, "unit": unit,
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
