@@ -319,12 +319,27 @@ struct tb_instance {
   float* gather = nullptr;             // [world][bucket] shard gradients (tree reduction)
   int64_t gather_floats = 0;
   std::vector<cudaEvent_t> events;
+  // Staged feeds: a host feed is copied on its own stream into one of two
+  // staging buffers, overlapping the previous run's kernels; the run then
+  // takes it with a device-to-device copy on its own stream.
+  cudaStream_t copy_stream = nullptr;
+  char* staging[2] = {nullptr, nullptr};
+  int64_t staging_bytes = 0;
+  cudaEvent_t staged[2] = {nullptr, nullptr}, consumed[2] = {nullptr, nullptr};
+  uint64_t runs = 0;
   int64_t launches = 0;
   ~tb_instance() {
     if (stream) cudaStreamSynchronize(stream);
     if (gather) cudaFree(gather);
     if (graph) cudaGraphExecDestroy(graph);
     for (auto e : events) cudaEventDestroy(e);
+    if (copy_stream) cudaStreamSynchronize(copy_stream);
+    for (int k = 0; k < 2; ++k) {
+      if (staging[k]) cudaFree(staging[k]);
+      if (staged[k]) cudaEventDestroy(staged[k]);
+      if (consumed[k]) cudaEventDestroy(consumed[k]);
+    }
+    if (copy_stream) cudaStreamDestroy(copy_stream);
     if (arena) cudaFree(arena);
     if (stream_k.workspace) cudaFree(stream_k.workspace);
     if (stream_k.flags) cudaFree(stream_k.flags);
@@ -607,6 +622,18 @@ void setup_instance(tb_plan* owner, tb_instance* plan) {
   check(cudaStreamCreateWithFlags(&plan->comm_stream, cudaStreamNonBlocking), "cudaStreamCreate");
   check(cudaStreamCreateWithFlags(&plan->side_stream, cudaStreamNonBlocking), "cudaStreamCreate");
   plan->buffer_ptr.assign(P.buffers.size(), nullptr);
+  int64_t input_bytes = 0;
+  for (int b : P.input_buffer)
+    if (b >= 0) input_bytes += (P.buffers[b].bytes + 255) / 256 * 256;
+  if (input_bytes > 0) {
+    check(cudaStreamCreateWithFlags(&plan->copy_stream, cudaStreamNonBlocking), "cudaStreamCreate");
+    for (int k = 0; k < 2; ++k) {
+      check(cudaMalloc((void**)&plan->staging[k], input_bytes), "cudaMalloc(staging)");
+      check(cudaEventCreateWithFlags(&plan->staged[k], cudaEventDisableTiming), "cudaEventCreate");
+      check(cudaEventCreateWithFlags(&plan->consumed[k], cudaEventDisableTiming), "cudaEventCreate");
+    }
+    plan->staging_bytes = input_bytes;
+  }
   if (P.arena_bytes > 0) check(cudaMalloc((void**)&plan->arena, P.arena_bytes), "cudaMalloc(arena)");
   bool has_gemm = false;
   for (const tb::Kernel& K : P.kernels) has_gemm = has_gemm || K.type == tb::KType::GEMM;
@@ -679,6 +706,11 @@ void instantiate(tb_plan* plan) {
 void start_run(tb_instance* plan, tb_params* params, int32_t feed_count, const tb_feed* feeds) {
   tb::Program& P = *plan->prog;
   bind_params(plan, params);
+  // host feeds go through staging slot `k`, free again once the run two
+  // before this one has taken its copy (the `consumed` event)
+  const int k = (int)(plan->runs & 1);
+  bool any_staged = false;
+  int64_t offset = 0;
   for (int32_t f = 0; f < feed_count; ++f) {
     const tb_feed& feed = feeds[f];
     if (feed.slot < 0 || feed.slot >= P.input_slots)
@@ -689,11 +721,41 @@ void start_run(tb_instance* plan, tb_params* params, int32_t feed_count, const t
     const void* src = buf.storage == tb::Storage::InputIndices ? (const void*)feed.indices
                                                                : (const void*)feed.dense;
     if (!src) throw Failure(TB_INVALID, "feed of the wrong payload kind");
-    check(cudaMemcpyAsync(plan->buffer_ptr[b], src, buf.bytes,
-                          feed.on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
-                          plan->stream),
+    if (feed.on_device || !plan->copy_stream ||
+        offset + buf.bytes > plan->staging_bytes) {
+      check(cudaMemcpyAsync(plan->buffer_ptr[b], src, buf.bytes,
+                            feed.on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                            plan->stream),
+            "feed copy");
+      continue;
+    }
+    if (!any_staged) {
+      check(cudaStreamWaitEvent(plan->copy_stream, plan->consumed[k], 0), "wait staging");
+      any_staged = true;
+    }
+    check(cudaMemcpyAsync(plan->staging[k] + offset, src, buf.bytes, cudaMemcpyHostToDevice,
+                          plan->copy_stream),
           "feed copy");
+    offset += (buf.bytes + 255) / 256 * 256;
   }
+  if (any_staged) {
+    check(cudaEventRecord(plan->staged[k], plan->copy_stream), "record staged");
+    check(cudaStreamWaitEvent(plan->stream, plan->staged[k], 0), "wait staged");
+    offset = 0;
+    for (int32_t f = 0; f < feed_count; ++f) {
+      const tb_feed& feed = feeds[f];
+      int b = P.input_buffer[feed.slot];
+      if (b < 0) continue;
+      const tb::Buffer& buf = P.buffers[b];
+      if (feed.on_device || offset + buf.bytes > plan->staging_bytes) continue;
+      check(cudaMemcpyAsync(plan->buffer_ptr[b], plan->staging[k] + offset, buf.bytes,
+                            cudaMemcpyDeviceToDevice, plan->stream),
+            "feed copy");
+      offset += (buf.bytes + 255) / 256 * 256;
+    }
+    check(cudaEventRecord(plan->consumed[k], plan->stream), "record consumed");
+  }
+  plan->runs++;
   run_plan(plan);
 }
 
