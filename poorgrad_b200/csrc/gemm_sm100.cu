@@ -66,6 +66,15 @@ struct Cfg<256> {
   static constexpr uint64_t SWIZZLE = 4, SBO = 512;  // 64-byte swizzle
   static constexpr CUtensorMapSwizzle TMA_SWIZZLE = CU_TENSOR_MAP_SWIZZLE_64B;
 };
+// 128 x 32 for outputs at most 32 wide (a 27-symbol head): a 128-wide tile
+// would be three quarters padding; five 40 KB stages keep more k-blocks in
+// flight for these memory-bound products.
+template <>
+struct Cfg<32> {
+  static constexpr int BN = 32, BK = 32, STAGES = 5, CHUNK = 4, GROUPS = 1;
+  static constexpr uint64_t SWIZZLE = 2, SBO = 1024;  // 128-byte swizzle
+  static constexpr CUtensorMapSwizzle TMA_SWIZZLE = CU_TENSOR_MAP_SWIZZLE_128B;
+};
 template <class C>
 struct Derived {
   static constexpr int TILE_A = BM * C::BK * 4;
@@ -586,6 +595,7 @@ bool make_map(CUtensorMap* map, const float* base, int64_t ld, int64_t rows, int
 }
 
 int g_tile_override = -1;  // TB_GEMM_TILE_N, or a test's forced choice
+int g_narrow_tile = -1;    // TB_GEMM_NARROW_TILE=0 keeps outputs <= 32 wide on 128-wide tiles
 // Stream-K is off unless TB_GEMM_STREAM_K=1 (or a test turns it on): measured on
 // B200 it made the C4 step's 16384x512x512 products slower (57 against 46 us,
 // two partial-tile epilogues per CTA where whole tiles overlap theirs with the
@@ -621,7 +631,7 @@ namespace {
 }  // namespace
 
 static int splits_for(int bn, int64_t batch, int64_t m, int64_t n, int64_t kp) {
-  const int bk = bn == 256 ? Cfg<256>::BK : Cfg<128>::BK;
+  const int bk = bn == 256 ? Cfg<256>::BK : Cfg<128>::BK;  // the 32-wide tile shares the 128-wide tile's BK
   const int64_t tiles = batch * ((m + BM - 1) / BM) * ((n + bn - 1) / bn);
   const int64_t kb = kp / bk;
   if (tiles >= 120 || kb < 16) return 1;
@@ -646,7 +656,13 @@ int gemm_tile_n(int64_t batch, int64_t m, int64_t n, int64_t kp) {
     const char* e = getenv("TB_GEMM_TILE_N");
     g_tile_override = e ? atoi(e) : 0;
   }
-  if (g_tile_override == 128 || g_tile_override == 256) return g_tile_override;
+  if (g_tile_override == 32 || g_tile_override == 128 || g_tile_override == 256)
+    return g_tile_override;
+  if (g_narrow_tile < 0) {
+    const char* e = getenv("TB_GEMM_NARROW_TILE");
+    g_narrow_tile = e ? atoi(e) : 1;
+  }
+  if (n <= 32 && g_narrow_tile) return 32;
   return n <= 64 ? 128 : 256;
 }
 
@@ -771,8 +787,11 @@ bool launch_gemm_tcgen05_split(const Operand& a, const Operand& b, float* c, flo
   // whole 32-float blocks
   for (const Operand* o : {&a, &b})
     if (o->ld % 4 != 0 || o->rows < 1 || (o->mn && o->ld % 32 != 0)) return false;
-  if (gemm_tile_n(batch, m, n, kp) == 256)
+  const int tile = gemm_tile_n(batch, m, n, kp);
+  if (tile == 256)
     return launch_cfg<Cfg<256>>(a, b, c, partial, splits, batch, m, n, kp, stream, sk);
+  if (tile == 32)
+    return launch_cfg<Cfg<32>>(a, b, c, partial, splits, batch, m, n, kp, stream, sk);
   return launch_cfg<Cfg<128>>(a, b, c, partial, splits, batch, m, n, kp, stream, sk);
 }
 

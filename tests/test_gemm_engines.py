@@ -28,7 +28,7 @@ def _prep(torch, x, kp):
 @pytest.mark.parametrize("batch,m,n,k,splits", [
     (1, 128, 128, 32, 1), (1, 256, 384, 96, 1), (2, 130, 70, 40, 1), (1, 1, 5, 7, 1),
     (3, 200, 136, 300, 1), (1, 512, 512, 4096, 4), (1, 128, 256, 1024, 3)])
-@pytest.mark.parametrize("tile", [128, 256])
+@pytest.mark.parametrize("tile", [32, 128, 256])
 def test_tcgen05_matches_f64(device, batch, m, n, k, splits, tile):
     import torch
     from poorgrad_b200.abi import load_library
@@ -61,7 +61,7 @@ def test_tcgen05_matches_f64(device, batch, m, n, k, splits, tile):
     (1, 128, 128, 32, 1), (2, 130, 70, 40, 1), (1, 64, 96, 17, 1), (1, 300, 200, 1000, 3),
     (1, 512, 27, 2048, 4)])
 @pytest.mark.parametrize("a_mn,b_mn", [(0, 1), (1, 0), (1, 1)])
-@pytest.mark.parametrize("tile", [128, 256])
+@pytest.mark.parametrize("tile", [32, 128, 256])
 def test_mn_major_operands_match_f64(device, batch, m, n, k, splits, a_mn, b_mn, tile):
     # an MN-major operand is the value [batch, k, mn] in its own row-major
     # layout, the mn axis padded to a multiple of 32 (how the plan prepares an

@@ -59,7 +59,7 @@ def test_gemm_tile_and_split_rules(built):
     assert lib.tbx_gemm_splits(1, 512, 512, 16384) == 18
     # long-M products need no split
     assert lib.tbx_gemm_splits(1, 16384, 512, 512) == 1
-    # narrow outputs take the 128-wide tile: 4 tiles -> 37 splits
+    # outputs at most 32 wide take the 32-wide tile: 4 tiles -> 37 splits
     assert lib.tbx_gemm_splits(1, 512, 27, 16384) == 37
 
 
