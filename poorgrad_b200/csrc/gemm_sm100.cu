@@ -33,6 +33,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstring>
 #include <cstdio>
 #include <algorithm>
 #include <cmath>
@@ -81,11 +82,13 @@ struct Derived {
   static constexpr int TILE_B = C::BN * C::BK * 4;
   static constexpr int STAGE_BYTES = 2 * TILE_A + 2 * TILE_B;
   static constexpr int THREADS = 64 + 128 * C::GROUPS;
-  // per epilogue warp: a 32 x 33 float tile that turns its lanes' rows into
-  // coalesced row segments
-  static constexpr int EPI_STAGE_BYTES = 32 * 33 * 4;
+  // per epilogue warp: a 32 x 32 float tile in the 128-byte swizzle (16-byte
+  // chunk c of row r at chunk c ^ (r % 8)), 1024-byte aligned, so that a TMA
+  // store can take it whole and the lanes' row writes and column reads are
+  // free of bank conflicts
+  static constexpr int EPI_STAGE_BYTES = 32 * 32 * 4;
   static constexpr int SMEM_BYTES =
-      C::STAGES * STAGE_BYTES + 1024 + 256 + 4 * C::GROUPS * EPI_STAGE_BYTES;
+      C::STAGES * STAGE_BYTES + 1024 + 1024 + 4 * C::GROUPS * EPI_STAGE_BYTES;
   static constexpr int EPI_COLS = C::BN / C::GROUPS;  // 128 columns per epilogue warpgroup
 };
 constexpr unsigned long long WAIT_NS = 4000000000ull;  // 4 s per wait
@@ -201,6 +204,21 @@ __device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t* r) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// TMA store of a 32 x 32 staging tile to (x, y, plane) of the output map.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y,
+                                             int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+          (uint64_t)map),
+      "r"(x), "r"(y), "r"(z), "r"(smem_u32(src))
+      : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Offset (in floats) of element (r, c) of a swizzled 32 x 32 staging tile.
+__device__ __forceinline__ int stage_at(int r, int c) {
+  return r * 32 + ((((c >> 2) ^ (r & 7))) << 2) + (c & 3);
+}
+
 // Work item w of tiles_n x tiles_m x (batch * splits).  The faster-varying
 // tile index is the one whose operand is smaller, so consecutive work items
 // (running concurrently on neighbouring SMs) share the larger operand's tile
@@ -302,6 +320,7 @@ template <class C, bool SK>
 __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
     k_gemm_tcgen05(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
                    const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
+                   const __grid_constant__ CUtensorMap tc, int tma_store,
                    float* __restrict__ out, int m, int n, const Sched sched,
                    long long split_stride, int a_mn, int b_mn, float* __restrict__ sk_ws,
                    int* __restrict__ sk_flags) {
@@ -319,7 +338,7 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
   uint64_t* acc_empty = acc_full + 2;    // [2]: TMEM buffer b drained by the epilogue
   uint32_t* tmem_slot = (uint32_t*)(acc_empty + 2);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
-  float* epi_stage = (float*)(smem + STAGES * STAGE_BYTES + 256);
+  float* epi_stage = (float*)(smem + STAGES * STAGE_BYTES + 1024);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -517,29 +536,50 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
         }
         if (!ok) break;
       }
-      // stores: 32-column slabs through this warp's staging tile, so that each
-      // store instruction writes one row's 32 consecutive floats
+      // stores: 32-column slabs through this warp's staging tile.  Each lane
+      // writes its row (+ 0 on the way: a product never leaves as -0, so a
+      // `0 + c` gradient seed over it is the product's own buffer); then one
+      // TMA store moves the slab, or, where the output's rows are not
+      // 16-byte multiples, each store instruction writes one row's 32
+      // consecutive floats.
       float* dst = out + (long long)t.split * split_stride + (long long)t.batch * m * n;
-      float(*st)[33] = (float(*)[33])(epi_stage + ew * 32 * 33);
+      float* st = epi_stage + ew * 32 * 32;
       const int row0 = t.m0 + q * 32;
+      const int plane = t.split * (int)(split_stride / ((long long)m * n)) + t.batch;
 #pragma unroll
       for (int g = 0; g < EPI_COLS / 32; ++g) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) st[lane][j] = total[g * 32 + j];
+        for (int cc = 0; cc < 8; ++cc)
+          *(float4*)(st + stage_at(lane, cc * 4)) =
+              make_float4(__fadd_rn(total[g * 32 + cc * 4], 0.0f),
+                          __fadd_rn(total[g * 32 + cc * 4 + 1], 0.0f),
+                          __fadd_rn(total[g * 32 + cc * 4 + 2], 0.0f),
+                          __fadd_rn(total[g * 32 + cc * 4 + 3], 0.0f));
+        const int col0 = t.n0 + c0 + g * 32;
+        if (tma_store) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0 && row0 < m && col0 < n) {
+            tma_store_3d(&tc, st, col0, row0, plane);
+            // the slab is read before the next one overwrites it
+            asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+          }
+          __syncwarp();
+          continue;
+        }
         __syncwarp();
-        const int col = t.n0 + c0 + g * 32 + lane;
+        const int col = col0 + lane;
         if (col < n) {
           float* p = dst + (long long)row0 * n + col;
           const int rows = min(32, m - row0);
 #pragma unroll 8
-          // + 0 on the way out: a product never leaves as -0 (a `0 + c`
-          // gradient seed over it is then the product's own buffer)
-          for (int r = 0; r < rows; ++r) p[(long long)r * n] = __fadd_rn(st[r][lane], 0.0f);
+          for (int r = 0; r < rows; ++r) p[(long long)r * n] = st[stage_at(r, lane)];
         }
         __syncwarp();
       }
     }
   }
+  if (warp >= 2 && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 2) {
@@ -595,6 +635,14 @@ bool make_map(CUtensorMap* map, const float* base, int64_t ld, int64_t rows, int
 }
 
 int g_tile_override = -1;  // TB_GEMM_TILE_N, or a test's forced choice
+int g_tma_store = -1;      // TB_GEMM_TMA_STORE=0 keeps the warps' row-segment stores
+bool tma_store_enabled() {
+  if (g_tma_store < 0) {
+    const char* e = getenv("TB_GEMM_TMA_STORE");
+    g_tma_store = e ? atoi(e) : 1;
+  }
+  return g_tma_store != 0;
+}
 int g_narrow_tile = -1;    // TB_GEMM_NARROW_TILE=0 keeps outputs <= 32 wide on 128-wide tiles
 // Stream-K is off unless TB_GEMM_STREAM_K=1 (or a test turns it on): measured on
 // B200 it made the C4 step's 16384x512x512 products slower (57 against 46 us,
@@ -761,14 +809,30 @@ bool launch_cfg(const Operand& a, const Operand& b, float* c, float* partial, in
       sched.sk_units = (items - sched.dp_items) * (long long)kb;
     }
   }
+  // the output as planes [batch * splits][m][n] for TMA stores of 32 x 32
+  // slabs (rows must be 16-byte multiples; otherwise the warps store)
+  CUtensorMap mc;
+  memset(&mc, 0, sizeof mc);
+  int tma_store = 0;
+  if (n % 4 == 0 && ((uintptr_t)target & 15) == 0 && tma_store_enabled()) {
+    EncodeTiled enc = encoder();
+    cuuint64_t dims[3] = {(cuuint64_t)n, (cuuint64_t)m, (cuuint64_t)(batch * splits)};
+    cuuint64_t strides[2] = {(cuuint64_t)(n * 4), (cuuint64_t)(m * n * 4)};
+    cuuint32_t box[3] = {32, 32, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    tma_store = enc && enc(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)target, dims, strides,
+                           box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  }
   if (sched.sk_units > 0)
     launch_pdl(k_gemm_tcgen05<C, true>, grid, D::THREADS, D::SMEM_BYTES, stream, ma, mal, mb, mbl,
-               target, (int)m, (int)n, sched, (long long)(batch * m * n), (int)a.mn, (int)b.mn,
-               sk->workspace, sk->flags);
+               mc, tma_store, target, (int)m, (int)n, sched, (long long)(batch * m * n),
+               (int)a.mn, (int)b.mn, sk->workspace, sk->flags);
   else
     launch_pdl(k_gemm_tcgen05<C, false>, grid, D::THREADS, D::SMEM_BYTES, stream, ma, mal, mb,
-               mbl, target, (int)m, (int)n, sched, (long long)(batch * m * n), (int)a.mn,
-               (int)b.mn, (float*)nullptr, (int*)nullptr);
+               mbl, mc, tma_store, target, (int)m, (int)n, sched, (long long)(batch * m * n),
+               (int)a.mn, (int)b.mn, (float*)nullptr, (int*)nullptr);
   if (splits > 1) {
     const long long count = batch * m * n;
     int blocks = (int)std::min<long long>((count + 255) / 256, 148 * 8);
