@@ -166,6 +166,10 @@ struct Program {
   // storage; every operation rounds its result once, accumulations round once
   bool bf16 = false;
   int gemms = 0;
+  // stored values a generated kernel computed with a tolerance (transcendental
+  // results, reductions and what follows from them): a later kernel that
+  // loads one carries the tolerance too
+  std::set<int> tolerance_nodes;
   // Side-stream kernels (the leading SORTs) run concurrently with the main
   // kernels before side_join, the first main kernel that uses what they wrote;
   // the main stream waits for them there (-1: no side kernels).

@@ -23,6 +23,13 @@
 // (two TMEM buffers, the MMA warp filling one while the epilogue drains the
 // other) bounds the chain and keeps the result as accurate as a serial f32 sum.
 // The kernel is persistent (one CTA per SM walking the tiles).
+// An operand may also arrive raw: its f32 values in the same layout, where the
+// product is bound by memory rather than by the tensor cores.  TMA then loads
+// the f32 tile into the stage's hi slot and two converter warps (after the
+// epilogue's) split it in place -- hi = rna_tf32(x) over x, lo = x - hi
+// into the lo slot, the same pair a prepared operand holds -- before the MMA
+// warp may read the stage: half the operand's bytes cross HBM, and the
+// product is bit for bit the one over the prepared pair.
 // Split-K writes ordered partials that a second kernel sums in split order.
 // No TMA multicast is used anywhere (operands may live on any GPU's arena).
 // Every mbarrier wait is bounded by the global timer: on expiry the kernel
@@ -48,6 +55,7 @@ namespace tb {
 namespace {
 
 constexpr int BM = 128;
+constexpr int CONVERTERS = 64;  // converter threads of a kernel with raw operands
 
 // The two tile shapes.  128 x 128 with 32-float k-blocks (128-byte swizzle,
 // 3 stages, one epilogue warpgroup) and 128 x 256 with 16-float k-blocks
@@ -67,6 +75,14 @@ struct Cfg<256> {
   static constexpr uint64_t SWIZZLE = 4, SBO = 512;  // 64-byte swizzle
   static constexpr CUtensorMapSwizzle TMA_SWIZZLE = CU_TENSOR_MAP_SWIZZLE_64B;
 };
+// 128 x 64 for outputs 33 to 64 wide (attention's per-head products): a
+// 128-wide tile would double their tensor work; four 48 KB stages.
+template <>
+struct Cfg<64> {
+  static constexpr int BN = 64, BK = 32, STAGES = 4, CHUNK = 4, GROUPS = 1;
+  static constexpr uint64_t SWIZZLE = 2, SBO = 1024;  // 128-byte swizzle
+  static constexpr CUtensorMapSwizzle TMA_SWIZZLE = CU_TENSOR_MAP_SWIZZLE_128B;
+};
 // 128 x 32 for outputs at most 32 wide (a 27-symbol head): a 128-wide tile
 // would be three quarters padding; five 40 KB stages keep more k-blocks in
 // flight for these memory-bound products.
@@ -82,6 +98,9 @@ struct Derived {
   static constexpr int TILE_B = C::BN * C::BK * 4;
   static constexpr int STAGE_BYTES = 2 * TILE_A + 2 * TILE_B;
   static constexpr int THREADS = 64 + 128 * C::GROUPS;
+  // with raw f32 operands, two converter warps after the epilogue warps (few
+  // enough that the epilogue keeps its registers)
+  static constexpr int threads(bool raw) { return THREADS + (raw ? CONVERTERS : 0); }
   // per epilogue warp: a 32 x 32 float tile in the 128-byte swizzle (16-byte
   // chunk c of row r at chunk c ^ (r % 8)), 1024-byte aligned, so that a TMA
   // store can take it whole and the lanes' row writes and column reads are
@@ -313,17 +332,49 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
 __device__ __forceinline__ void st_release(int* p, int v) {
   asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// tf32 pair of a raw tile of N4 float4s by the converter threads: hi over the
+// f32 values (rna_tf32, as the prepared operands are rounded), lo = x - hi.
+__device__ __forceinline__ float rna_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+// All of a thread's loads are issued before its first store (in batches of
+// 16 float4s), so one shared-memory latency covers the batch instead of one
+// per element: the stores through `hi` could otherwise alias the next loads.
+template <int N4>
+__device__ __forceinline__ void split_tile(float4* __restrict__ hi, float4* __restrict__ lo,
+                                           int ct) {
+  constexpr int PER = N4 / CONVERTERS;  // float4s per thread
+  constexpr int BATCH = PER < 16 ? PER : 16;
+  static_assert(N4 % CONVERTERS == 0 && PER % BATCH == 0, "tile splits evenly");
+#pragma unroll
+  for (int b0 = 0; b0 < PER; b0 += BATCH) {
+    float4 v[BATCH];
+#pragma unroll
+    for (int j = 0; j < BATCH; ++j) v[j] = hi[ct + (b0 + j) * CONVERTERS];
+#pragma unroll
+    for (int j = 0; j < BATCH; ++j) {
+      const float4 h =
+          make_float4(rna_tf32(v[j].x), rna_tf32(v[j].y), rna_tf32(v[j].z), rna_tf32(v[j].w));
+      hi[ct + (b0 + j) * CONVERTERS] = h;
+      lo[ct + (b0 + j) * CONVERTERS] =
+          make_float4(__fsub_rn(v[j].x, h.x), __fsub_rn(v[j].y, h.y), __fsub_rn(v[j].z, h.z),
+                      __fsub_rn(v[j].w, h.w));
+    }
+  }
+}
 // Persistent: each CTA walks its pieces of work (Sched); the stage ring and
 // the two accumulator buffers carry their phases across pieces, so the
 // epilogue of one overlaps the main loop of the next.
-template <class C, bool SK>
-__global__ void __launch_bounds__(Derived<C>::THREADS, 1)
+template <class C, bool SK, bool RAW>
+__global__ void __launch_bounds__(Derived<C>::threads(RAW), 1)
     k_gemm_tcgen05(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
                    const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
                    const __grid_constant__ CUtensorMap tc, int tma_store,
                    float* __restrict__ out, int m, int n, const Sched sched,
-                   long long split_stride, int a_mn, int b_mn, float* __restrict__ sk_ws,
-                   int* __restrict__ sk_flags) {
+                   long long split_stride, int a_mn, int b_mn, int raw,
+                   float* __restrict__ sk_ws, int* __restrict__ sk_flags) {
   pdl_entry();
   using D = Derived<C>;
   static_assert(4 * C::GROUPS <= 8, "the stream-K flags hold eight epilogue warps per CTA");
@@ -334,7 +385,8 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* full = (uint64_t*)(smem + STAGES * STAGE_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* acc_full = empty + STAGES;   // [2]: chunk partial ready in TMEM buffer b
+  uint64_t* conv = empty + STAGES;       // [STAGES]: raw tiles of the stage split (RAW)
+  uint64_t* acc_full = conv + STAGES;    // [2]: chunk partial ready in TMEM buffer b
   uint64_t* acc_empty = acc_full + 2;    // [2]: TMEM buffer b drained by the epilogue
   uint32_t* tmem_slot = (uint32_t*)(acc_empty + 2);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
@@ -346,6 +398,7 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&conv[s], CONVERTERS);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -384,22 +437,24 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
           }
           if (*abort_flag) break;
           uint8_t* base = smem + s * STAGE_BYTES;
-          mbar_expect_tx(&full[s], STAGE_BYTES);
+          // a raw operand's one f32 tile lands in its hi slot
+          const bool ra = RAW && (raw & 1), rb = RAW && (raw & 2);
+          mbar_expect_tx(&full[s], STAGE_BYTES - (ra ? TILE_A : 0) - (rb ? TILE_B : 0));
           const int kx = (kb0 + i) * BK;
           if (!a_mn) {
             tma_load_3d(base, &ta_hi, kx, t.m0, t.batch, &full[s]);
-            tma_load_3d(base + TILE_A, &ta_lo, kx, t.m0, t.batch, &full[s]);
+            if (!ra) tma_load_3d(base + TILE_A, &ta_lo, kx, t.m0, t.batch, &full[s]);
           } else {  // one box: BM/32 MN blocks of BK rows
             tma_load_4d(base, &ta_hi, 0, kx, t.m0 / 32, t.batch, &full[s]);
-            tma_load_4d(base + TILE_A, &ta_lo, 0, kx, t.m0 / 32, t.batch, &full[s]);
+            if (!ra) tma_load_4d(base + TILE_A, &ta_lo, 0, kx, t.m0 / 32, t.batch, &full[s]);
           }
           uint8_t* bb = base + 2 * TILE_A;
           if (!b_mn) {
             tma_load_3d(bb, &tb_hi, kx, t.n0, t.batch, &full[s]);
-            tma_load_3d(bb + TILE_B, &tb_lo, kx, t.n0, t.batch, &full[s]);
+            if (!rb) tma_load_3d(bb + TILE_B, &tb_lo, kx, t.n0, t.batch, &full[s]);
           } else {
             tma_load_4d(bb, &tb_hi, 0, kx, t.n0 / 32, t.batch, &full[s]);
-            tma_load_4d(bb + TILE_B, &tb_lo, 0, kx, t.n0 / 32, t.batch, &full[s]);
+            if (!rb) tma_load_4d(bb + TILE_B, &tb_lo, 0, kx, t.n0 / 32, t.batch, &full[s]);
           }
         }
       }
@@ -430,7 +485,8 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
           for (int i = c * CHUNK; i < i_end; ++i, ++g) {
             const int s = g % STAGES;
             const uint32_t round = g / STAGES;
-            if (!mbar_wait(&full[s], round & 1, 2)) {
+            // with raw operands the stage is ready once the converters split it
+            if (!mbar_wait(RAW ? &conv[s] : &full[s], round & 1, 2)) {
               *abort_flag = 1;
               break;
             }
@@ -451,6 +507,33 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
           }
           umma_commit(&acc_full[b]);
         }
+      }
+    }
+  } else if (RAW && warp >= 2 + 4 * C::GROUPS) {
+    // converters: each stage's raw tiles become tf32 pairs in place, 16 bytes
+    // per thread per step over the tile as stored (the split is elementwise,
+    // so the swizzle does not matter); the writes are made visible to the
+    // tensor cores' async proxy before the stage is released to the MMA warp
+    const int ct = threadIdx.x - 32 * (2 + 4 * C::GROUPS);
+    uint32_t g = 0;
+    SegIter it = seg_begin(sched);
+    Seg sg;
+    while (!*abort_flag && seg_next<C, SK>(sched, it, sg)) {
+      for (int i = 0; i < sg.nkb; ++i, ++g) {
+        const int s = g % STAGES;
+        const uint32_t round = g / STAGES;
+        if (!mbar_wait(&full[s], round & 1, 6)) {
+          *abort_flag = 1;
+          break;
+        }
+        uint8_t* base = smem + s * STAGE_BYTES;
+        if (raw & 1) split_tile<TILE_A / 16>((float4*)base, (float4*)(base + TILE_A), ct);
+        if (raw & 2)
+          split_tile<TILE_B / 16>((float4*)(base + 2 * TILE_A),
+                                  (float4*)(base + 2 * TILE_A + TILE_B), ct);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&conv[s]))
+                     : "memory");
       }
     }
   } else {
@@ -643,7 +726,7 @@ bool tma_store_enabled() {
   }
   return g_tma_store != 0;
 }
-int g_narrow_tile = -1;    // TB_GEMM_NARROW_TILE=0 keeps outputs <= 32 wide on 128-wide tiles
+int g_narrow_tile = -1;    // TB_GEMM_NARROW_TILE=0 keeps outputs <= 64 wide on 128-wide tiles
 // Stream-K is off unless TB_GEMM_STREAM_K=1 (or a test turns it on): measured on
 // B200 it made the C4 step's 16384x512x512 products slower (57 against 46 us,
 // two partial-tile epilogues per CTA where whole tiles overlap theirs with the
@@ -679,7 +762,7 @@ namespace {
 }  // namespace
 
 static int splits_for(int bn, int64_t batch, int64_t m, int64_t n, int64_t kp) {
-  const int bk = bn == 256 ? Cfg<256>::BK : Cfg<128>::BK;  // the 32-wide tile shares the 128-wide tile's BK
+  const int bk = bn == 256 ? Cfg<256>::BK : Cfg<128>::BK;  // the 32- and 64-wide tiles share the 128-wide tile's BK
   const int64_t tiles = batch * ((m + BM - 1) / BM) * ((n + bn - 1) / bn);
   const int64_t kb = kp / bk;
   if (tiles >= 120 || kb < 16) return 1;
@@ -704,14 +787,16 @@ int gemm_tile_n(int64_t batch, int64_t m, int64_t n, int64_t kp) {
     const char* e = getenv("TB_GEMM_TILE_N");
     g_tile_override = e ? atoi(e) : 0;
   }
-  if (g_tile_override == 32 || g_tile_override == 128 || g_tile_override == 256)
+  if (g_tile_override == 32 || g_tile_override == 64 || g_tile_override == 128 ||
+      g_tile_override == 256)
     return g_tile_override;
   if (g_narrow_tile < 0) {
     const char* e = getenv("TB_GEMM_NARROW_TILE");
     g_narrow_tile = e ? atoi(e) : 1;
   }
   if (n <= 32 && g_narrow_tile) return 32;
-  return n <= 64 ? 128 : 256;
+  if (n <= 64) return g_narrow_tile ? 64 : 128;
+  return 256;
 }
 
 void set_gemm_tile_n(int tile) { g_tile_override = tile; }
@@ -743,13 +828,33 @@ bool make_map_mn(CUtensorMap* map, const float* base, int64_t ld, int64_t rows, 
 // Tensor maps of one operand's hi and lo buffers: K-major boxes are BK floats
 // by the tile's rows (the config's swizzle), MN-major boxes the tile's MN
 // blocks of 32 floats by BK rows (128-byte swizzle of 32-byte atoms).
+// A raw operand (no lo buffer) has one map, over its f32 values; `lo` then
+// repeats it and is never loaded.
 template <class C>
 bool operand_maps(CUtensorMap* hi, CUtensorMap* lo, const Operand& o, int tile, int64_t batch) {
-  if (o.mn)
-    return make_map_mn(hi, o.hi, o.ld, o.rows, batch, tile, C::BK) &&
-           make_map_mn(lo, o.lo, o.ld, o.rows, batch, tile, C::BK);
-  return make_map(hi, o.hi, o.ld, o.rows, batch, C::BK, tile, C::TMA_SWIZZLE) &&
-         make_map(lo, o.lo, o.ld, o.rows, batch, C::BK, tile, C::TMA_SWIZZLE);
+  if (o.mn) {
+    if (!make_map_mn(hi, o.hi, o.ld, o.rows, batch, tile, C::BK)) return false;
+    if (!o.lo) return (*lo = *hi, true);
+    return make_map_mn(lo, o.lo, o.ld, o.rows, batch, tile, C::BK);
+  }
+  if (!make_map(hi, o.hi, o.ld, o.rows, batch, C::BK, tile, C::TMA_SWIZZLE)) return false;
+  if (!o.lo) return (*lo = *hi, true);
+  return make_map(lo, o.lo, o.ld, o.rows, batch, C::BK, tile, C::TMA_SWIZZLE);
+}
+
+template <class C, bool RAW>
+bool configure(int dev) {
+  using D = Derived<C>;
+  static bool configured[256] = {};  // the attributes are set per device
+  if (configured[dev]) return true;
+  if (cudaFuncSetAttribute(k_gemm_tcgen05<C, false, RAW>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           D::SMEM_BYTES) != cudaSuccess ||
+      cudaFuncSetAttribute(k_gemm_tcgen05<C, true, RAW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           D::SMEM_BYTES) != cudaSuccess)
+    return false;
+  configured[dev] = true;
+  return true;
 }
 
 template <class C>
@@ -761,16 +866,13 @@ bool launch_cfg(const Operand& a, const Operand& b, float* c, float* partial, in
   CUtensorMap ma, mal, mb, mbl;
   if (!operand_maps<C>(&ma, &mal, a, BM, batch) || !operand_maps<C>(&mb, &mbl, b, C::BN, batch))
     return false;
-  static bool configured[256] = {};  // the attributes are set per device
+  const int raw = (a.lo ? 0 : 1) | (b.lo ? 0 : 2);
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 256) return false;
-  if (!configured[dev]) {
-    if (cudaFuncSetAttribute(k_gemm_tcgen05<C, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             D::SMEM_BYTES) != cudaSuccess ||
-        cudaFuncSetAttribute(k_gemm_tcgen05<C, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             D::SMEM_BYTES) != cudaSuccess)
-      return false;
-    configured[dev] = true;
+  if constexpr (C::GROUPS == 1) {
+    if (!(raw ? configure<C, true>(dev) : configure<C, false>(dev))) return false;
+  } else {
+    if (raw || !configure<C, false>(dev)) return false;
   }
   const int kb = (int)(kp / C::BK);
   if (splits < 1 || !partial) splits = 1;
@@ -825,14 +927,29 @@ bool launch_cfg(const Operand& a, const Operand& b, float* c, float* partial, in
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
   }
-  if (sched.sk_units > 0)
-    launch_pdl(k_gemm_tcgen05<C, true>, grid, D::THREADS, D::SMEM_BYTES, stream, ma, mal, mb, mbl,
-               mc, tma_store, target, (int)m, (int)n, sched, (long long)(batch * m * n),
-               (int)a.mn, (int)b.mn, sk->workspace, sk->flags);
+  const long long plane = batch * m * n;
+  float* ws = sched.sk_units > 0 ? sk->workspace : nullptr;
+  int* flags = sched.sk_units > 0 ? sk->flags : nullptr;
+  if constexpr (C::GROUPS == 1) {
+    if (sched.sk_units > 0 && raw)
+      launch_pdl(k_gemm_tcgen05<C, true, true>, grid, D::threads(true), D::SMEM_BYTES, stream, ma,
+                 mal, mb, mbl, mc, tma_store, target, (int)m, (int)n, sched, plane, (int)a.mn,
+                 (int)b.mn, raw, ws, flags);
+    else if (raw)
+      launch_pdl(k_gemm_tcgen05<C, false, true>, grid, D::threads(true), D::SMEM_BYTES, stream,
+                 ma, mal, mb, mbl, mc, tma_store, target, (int)m, (int)n, sched, plane,
+                 (int)a.mn, (int)b.mn, raw, ws, flags);
+  }
+  if (raw) {
+    // launched above (the one-warpgroup tiles only)
+  } else if (sched.sk_units > 0)
+    launch_pdl(k_gemm_tcgen05<C, true, false>, grid, D::threads(false), D::SMEM_BYTES, stream, ma,
+               mal, mb, mbl, mc, tma_store, target, (int)m, (int)n, sched, plane, (int)a.mn,
+               (int)b.mn, raw, ws, flags);
   else
-    launch_pdl(k_gemm_tcgen05<C, false>, grid, D::THREADS, D::SMEM_BYTES, stream, ma, mal, mb,
-               mbl, mc, tma_store, target, (int)m, (int)n, sched, (long long)(batch * m * n),
-               (int)a.mn, (int)b.mn, (float*)nullptr, (int*)nullptr);
+    launch_pdl(k_gemm_tcgen05<C, false, false>, grid, D::threads(false), D::SMEM_BYTES, stream,
+               ma, mal, mb, mbl, mc, tma_store, target, (int)m, (int)n, sched, plane, (int)a.mn,
+               (int)b.mn, raw, ws, flags);
   if (splits > 1) {
     const long long count = batch * m * n;
     int blocks = (int)std::min<long long>((count + 255) / 256, 148 * 8);
@@ -851,11 +968,16 @@ bool launch_gemm_tcgen05_split(const Operand& a, const Operand& b, float* c, flo
   // whole 32-float blocks
   for (const Operand* o : {&a, &b})
     if (o->ld % 4 != 0 || o->rows < 1 || (o->mn && o->ld % 32 != 0)) return false;
-  const int tile = gemm_tile_n(batch, m, n, kp);
+  int tile = gemm_tile_n(batch, m, n, kp);
+  // the 256-wide tile's two epilogue warpgroups leave no registers for the
+  // converters: raw operands take the 128-wide tile
+  if (tile == 256 && (!a.lo || !b.lo)) tile = 128;
   if (tile == 256)
     return launch_cfg<Cfg<256>>(a, b, c, partial, splits, batch, m, n, kp, stream, sk);
   if (tile == 32)
     return launch_cfg<Cfg<32>>(a, b, c, partial, splits, batch, m, n, kp, stream, sk);
+  if (tile == 64)
+    return launch_cfg<Cfg<64>>(a, b, c, partial, splits, batch, m, n, kp, stream, sk);
   return launch_cfg<Cfg<128>>(a, b, c, partial, splits, batch, m, n, kp, stream, sk);
 }
 

@@ -425,20 +425,23 @@ __global__ void __launch_bounds__(32) k_segment_sum_tma(const __grid_constant__ 
 }
 
 // Four consecutive reduction indices k..k+3 of operand row r, as hi + lo
-// (exactly the original f32 values); zero outside the operand.
+// (exactly the original f32 values), or the values themselves for a raw
+// operand (no lo); zero outside the operand.
 __device__ __forceinline__ float4 simt_quad(const float* __restrict__ h,
                                             const float* __restrict__ l, int mn, int64_t ld,
                                             int64_t rows, int64_t r, int64_t r_end, int64_t k) {
   float4 q = make_float4(0, 0, 0, 0);
   if (r >= r_end) return q;
   if (!mn) {
-    const float4 a = *(const float4*)(h + r * ld + k), b = *(const float4*)(l + r * ld + k);
+    const float4 a = *(const float4*)(h + r * ld + k);
+    if (!l) return a;
+    const float4 b = *(const float4*)(l + r * ld + k);
     return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
   }
   float v[4];
 #pragma unroll
   for (int u = 0; u < 4; ++u)
-    v[u] = k + u < rows ? h[(k + u) * ld + r] + l[(k + u) * ld + r] : 0.0f;
+    v[u] = k + u < rows ? h[(k + u) * ld + r] + (l ? l[(k + u) * ld + r] : 0.0f) : 0.0f;
   return make_float4(v[0], v[1], v[2], v[3]);
 }
 
@@ -458,9 +461,9 @@ __global__ void __launch_bounds__(256) k_gemm_simt(const float* __restrict__ ahi
   const int64_t b = blockIdx.z;
   const int64_t m0 = (int64_t)blockIdx.y * 64, n0 = (int64_t)blockIdx.x * 64;
   const float* Ah = ahi + b * a_rows * a_ld;
-  const float* Al = alo + b * a_rows * a_ld;
+  const float* Al = alo ? alo + b * a_rows * a_ld : nullptr;
   const float* Bh = bhi + b * b_rows * b_ld;
-  const float* Bl = blo + b * b_rows * b_ld;
+  const float* Bl = blo ? blo + b * b_rows * b_ld : nullptr;
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   float acc[4][4] = {};
   const int lr = threadIdx.x >> 2;       // 0..63 row within tile

@@ -38,9 +38,12 @@ void launch_segment_sum(const float* perm, const int* rstart, const int* rend, f
 // the reduction index contiguous (ld = kp, zero-padded).  MN-major: a row per
 // reduction index (rows = K, no padding needed), the output index contiguous
 // (ld >= M or N, a multiple of 32).  A is M x K, B is given as N x K.
+// A raw operand has no lo: `hi` holds the f32 values themselves, in the same
+// layout (K-major rows then hold all kp reduction indices, ld >= kp), and the
+// GEMM splits them into the pair on the way in.
 struct Operand {
   const float* hi = nullptr;
-  const float* lo = nullptr;
+  const float* lo = nullptr;  // nullptr: raw f32 operand
   int mn = 0;        // 0: K-major, 1: MN-major
   int64_t ld = 0;    // floats between consecutive rows
   int64_t rows = 0;  // rows per batch entry
@@ -86,7 +89,7 @@ bool encode_rows_f32(CUtensorMap* map, const float* base, int64_t width, int64_t
                      int box_cols, int box_rows);
 // Error code recorded by a segment-sum kernel whose bounded wait expired (0 = none).
 int segment_error();
-// Tile width (128 or 256) the tcgen05 path uses for a shape; a test may force one.
+// Tile width (32, 64, 128 or 256) the tcgen05 path uses for a shape; a test may force one.
 int gemm_tile_n(int64_t batch, int64_t m, int64_t n, int64_t kp);
 void set_gemm_tile_n(int tile);
 // Split-K factor the tcgen05 path uses for a shape (1 = no split).

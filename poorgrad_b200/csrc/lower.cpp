@@ -1041,7 +1041,8 @@ class Lowerer {
             for (int o = 0; o < 2; ++o) {
               bool flip = false;
               const int base = strip_transposes(nd.operands[o], flip);
-              if (!prepared.count(base) && fusable_prep(base)) prepare(base, batch);
+              if (!prepared.count(base) && !raw_base.count(base) && fusable_prep(base))
+                prepare(base, batch);
             }
           }
           // the GEMM reads only tf32 pairs; what a pair is made from is read by
@@ -1185,6 +1186,13 @@ class Lowerer {
     r.rows = b.shape[b.rank - 2];
     r.cols = b.shape[b.rank - 1];
     r.ld = (r.cols + 31) / 32 * 32;
+    if (raw_base.count(base)) {
+      // the GEMM reads the stored f32 values (no lo) and splits them itself
+      r.hi = P.info[base].buf;
+      readers[base].insert(-1);
+      prepared[base] = r;
+      return r;
+    }
     r.hi = new_buffer(Storage::Arena, batch * r.rows * r.ld * 4, -1);
     r.lo = new_buffer(Storage::Arena, batch * r.rows * r.ld * 4, -1);
     if (fusable_prep(base)) {
@@ -1252,10 +1260,77 @@ class Lowerer {
     P.gemms++;
   }
 
+  // ---- raw GEMM operands
+  // A value every product reads as a memory-bound operand -- the product's
+  // other output extent is at most 64, so each element meets at most 64
+  // others (and, read as B, the product is at most 128 wide) -- is stored
+  // once in f32 and split into its tf32 pair inside the GEMM: half the bytes
+  // of a prepared pair are written and read.  The value
+  // must be a dense [batch][rows][cols] buffer with cols a multiple of 32 (no
+  // padding, 16-byte rows); an expression that is not yet stored is
+  // materialized for it.  Products wide enough to be bound by the tensor cores
+  // keep prepared pairs.  A bf16 network keeps them too: its prep kernels
+  // round what they load to bf16 (a GEMM's f32 result included), which a raw
+  // operand read by the GEMM itself would skip.
+  std::set<int> raw_base;
+  static constexpr int64_t kRawOperandReuse = 64;
+
+  bool dense_view(int n) const {
+    const Info& f = P.info[n];
+    const Node& nd = P.nodes[n];
+    if (f.kind == Kind::Expr && !f.materialized) return true;  // materialized below
+    if (!(f.kind == Kind::Layout || (f.kind == Kind::Expr && f.materialized)) || f.buf < 0)
+      return false;
+    if (f.lay.offset != 0 || f.lay.rank != nd.rank) return false;
+    int64_t s = 1;
+    for (int i = nd.rank - 1; i >= 0; --i) {
+      if (nd.shape[i] != 1 && f.lay.stride[i] != s) return false;
+      s *= nd.shape[i];
+    }
+    return P.buffers[f.buf].bytes >= nd.volume() * 4;
+  }
+
+  void choose_raw_operands() {
+    if (P.bf16) return;
+    if (const char* e = getenv("TB_RAW_OPERANDS"))
+      if (atoi(e) == 0) return;
+    std::map<int, bool> ok;
+    for (int n : P.order) {
+      const Node& nd = P.nodes[n];
+      const Info& f = P.info[n];
+      if (nd.op != TB_OP_MATMUL || !f.materialized || f.owner != n) continue;
+      const Node& A = P.nodes[nd.operands[0]];
+      const Node& B = P.nodes[nd.operands[1]];
+      const int split = A.rank - 2;
+      int64_t batch = 1;
+      for (int i = 0; i < split; ++i) batch *= A.shape[i];
+      const int64_t M = A.shape[split], N = B.shape[split + 1];
+      for (int o = 0; o < 2; ++o) {
+        bool flip = false;
+        const int base = strip_transposes(nd.operands[o], flip);
+        const Node& b = P.nodes[base];
+        // a raw B must not need the 256-wide tile, which has no room for the
+        // converters (the product would fall back to narrower tiles)
+        bool fit = (o == 0 ? N : M) <= kRawOperandReuse && (o == 0 || N <= 128) && b.rank >= 2 &&
+                   b.shape[b.rank - 1] % 32 == 0 && b.volume() == batch * b.shape[b.rank - 2] *
+                   b.shape[b.rank - 1] && dense_view(base);
+        auto it = ok.find(base);
+        ok[base] = (it == ok.end() ? true : it->second) && fit;
+      }
+    }
+    for (auto& [base, fit] : ok) {
+      if (!fit) continue;
+      const Info& f = P.info[base];
+      if (f.kind == Kind::Expr && !f.materialized) materialize(base);
+      raw_base.insert(base);
+    }
+  }
+
   void run(const tb_plan_desc* d) {
     load(d);
     count_consumers();
     classify();
+    choose_raw_operands();
     group_all();
   }
 };
@@ -1424,8 +1499,12 @@ class Emitter {
       return v;
     }
     if (f.materialized || f.kind == Kind::Layout) {
-      std::string v = load(f.buf, f.lay, idx);
-      return rounded(v);
+      std::string v = rounded(load(f.buf, f.lay, idx));
+      // a stored value that an earlier kernel computed with a tolerance
+      // carries it into this kernel too
+      if (P.tolerance_nodes.count(n) || (f.owner >= 0 && P.tolerance_nodes.count(f.owner)))
+        tainted.insert(v);
+      return v;
     }
     std::string v = def(n, idx);
     memo.back()[k] = v;
@@ -2726,14 +2805,17 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
     Kernel K = kernels[i];
     std::vector<Kernel> finals;
     if (K.type == KType::GEMM) {
-      K.reads = {K.a_hi, K.a_lo, K.b_hi, K.b_lo};
+      K.reads.clear();
+      for (int b : {K.a_hi, K.a_lo, K.b_hi, K.b_lo})
+        if (b >= 0) K.reads.push_back(b);
       K.writes = {K.out};
       if (K.partial >= 0) K.writes.push_back(K.partial);
       K.exact = false;
       K.describe = "gemm3xtf32 batch=" + std::to_string(K.batch) + " m=" + std::to_string(K.m) +
                    " n=" + std::to_string(K.n) + " k=" + std::to_string(K.k) +
                    " splits=" + std::to_string(K.passes) + " a=" + (K.a_mn ? "mn" : "k") +
-                   " b=" + (K.b_mn ? "mn" : "k");
+                   (K.a_lo < 0 ? ":raw" : "") + " b=" + (K.b_mn ? "mn" : "k") +
+                   (K.b_lo < 0 ? ":raw" : "");
       P.kernels.push_back(K);
       continue;
     }
@@ -2777,6 +2859,15 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
     }
     Emitter E(P, K, (int)P.kernels.size());
     E.relaxed = carries_tolerance;
+    // after the emission: which of the kernel's stored values carry a tolerance
+    auto note_tolerance = [&](const Emitter& done) {
+      for (size_t m = 0; m < K.members.size(); ++m) {
+        const Member& mm = K.members[m];
+        const bool reduction = mm.type == MemberType::ROW_SUM || mm.type == MemberType::ROW_MAX ||
+                               mm.type == MemberType::COL_SUM || mm.type == MemberType::ALL_SUM;
+        if (reduction || done.tainted_members.count((int)m)) P.tolerance_nodes.insert(mm.node);
+      }
+    };
     switch (K.type) {
       case KType::EW: emit_ew(P, K, E); break;
       case KType::ROW: emit_row(P, K, E, Lw, finals); break;
@@ -2808,6 +2899,7 @@ std::unique_ptr<Program> lower(const tb_plan_desc* desc) {
       default: fail("codegen: unexpected kernel type");
     }
     K.exact = E.exact;
+    if (K.type == KType::EW || K.type == KType::ROW) note_tolerance(E);
     E.wide = needs_wide(P, K);
     std::ostringstream fn;
     fn << "struct PRM_NAME { void* p[" << std::max<size_t>(1, K.params.size()) << "]; };\n";

@@ -461,12 +461,12 @@ int64_t launch_kernel(tb_instance* plan, size_t k, cudaStream_t stream) {
     case tb::KType::GEMM: {
       tb::Operand a, b;
       a.hi = fp(plan, K.a_hi);
-      a.lo = fp(plan, K.a_lo);
+      a.lo = K.a_lo >= 0 ? fp(plan, K.a_lo) : nullptr;  // none: raw f32 operand
       a.mn = K.a_mn;
       a.ld = K.a_ld;
       a.rows = K.a_rows;
       b.hi = fp(plan, K.b_hi);
-      b.lo = fp(plan, K.b_lo);
+      b.lo = K.b_lo >= 0 ? fp(plan, K.b_lo) : nullptr;
       b.mn = K.b_mn;
       b.ld = K.b_ld;
       b.rows = K.b_rows;

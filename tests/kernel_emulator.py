@@ -104,8 +104,20 @@ def _round_bf16(x):
     return oracle.round_bf16(x)
 
 
+def _tf32_pair(x):
+    """hi = x rounded to tf32 (nearest, ties away from zero), lo = x - hi: the
+    pair a GEMM splits a raw f32 operand into."""
+    bits = x.view(np.uint32)
+    hi = ((bits + np.uint32(0x1000)) & np.uint32(0xFFFFE000)).view(np.float32)
+    hi = np.where(np.isfinite(x), hi, x).astype(np.float32)
+    return hi, (x - hi).astype(np.float32)
+
+
 def _operand(hi, lo, mn, ld, rows, batch, outer, inner):
-    """The operand matrices [batch, outer, inner] from a prepared pair."""
+    """The operand matrices [batch, outer, inner] from a prepared pair, or
+    from raw f32 values (``lo`` None) split the way the GEMM splits them."""
+    if lo is None:
+        hi, lo = _tf32_pair(np.ascontiguousarray(hi[: batch * rows * ld]))
     h = hi[: batch * rows * ld].reshape(batch, rows, ld).astype(np.float64)
     l_ = lo[: batch * rows * ld].reshape(batch, rows, ld).astype(np.float64)
     if mn:  # stored [inner][outer]
@@ -170,10 +182,11 @@ def run_program(columns, parameters, feeds=None, gradients=False):
                                                  C.c_uint(K["block"]))
         elif t == "gemm":
             batch, m, n, k = K["batch"], K["m"], K["n"], K["k"]
-            ah, al = _operand(f32(K["a_hi"]), f32(K["a_lo"]), K["a_mn"], K["a_ld"],
+            lo_of = lambda b: f32(b) if b >= 0 else None
+            ah, al = _operand(f32(K["a_hi"]), lo_of(K["a_lo"]), K["a_mn"], K["a_ld"],
                               K["a_rows"], batch, m, k)
             # B is [k, n]: MN-major B stores it row-major, K-major B stores [n][k]
-            bh, bl = _operand(f32(K["b_hi"]), f32(K["b_lo"]), not K["b_mn"], K["b_ld"],
+            bh, bl = _operand(f32(K["b_hi"]), lo_of(K["b_lo"]), not K["b_mn"], K["b_ld"],
                               K["b_rows"], batch, k, n)
             c = ah @ bh + ah @ bl + al @ bh
             f32(K["out"])[: batch * m * n] = c.astype(np.float32).reshape(-1)

@@ -42,7 +42,9 @@ def compare(cols, params, feeds=None, tol=3e-5, bitwise=False):
 @pytest.mark.parametrize("name,kw", [
     ("mlp", dict(batch=16)), ("charmlp", dict(batch=32)), ("fused", dict(rows=32, cols=64)),
     ("gpt2", dict(batch=1, seq=8, layers=1, d=16, heads=2, vocab=11, mlp=32)),
-    ("gpt2", dict(batch=2, seq=16, layers=2, d=32, heads=4, vocab=50, mlp=64))])
+    ("gpt2", dict(batch=2, seq=16, layers=2, d=32, heads=4, vocab=50, mlp=64)),
+    # 64-wide heads and sequence: every attention product reads raw f32 operands
+    ("gpt2", dict(batch=1, seq=64, layers=1, d=128, heads=2, vocab=50, mlp=256))])
 def test_config_programs_follow_the_oracle(built, name, kw):
     w = configs.BUILDERS[name](**kw)
     compare(w.columns, w.network.parameters(), w.feeds(0) if w.feeds else None)

@@ -28,7 +28,7 @@ def _prep(torch, x, kp):
 @pytest.mark.parametrize("batch,m,n,k,splits", [
     (1, 128, 128, 32, 1), (1, 256, 384, 96, 1), (2, 130, 70, 40, 1), (1, 1, 5, 7, 1),
     (3, 200, 136, 300, 1), (1, 512, 512, 4096, 4), (1, 128, 256, 1024, 3)])
-@pytest.mark.parametrize("tile", [32, 128, 256])
+@pytest.mark.parametrize("tile", [32, 64, 128, 256])
 def test_tcgen05_matches_f64(device, batch, m, n, k, splits, tile):
     import torch
     from poorgrad_b200.abi import load_library
@@ -61,7 +61,7 @@ def test_tcgen05_matches_f64(device, batch, m, n, k, splits, tile):
     (1, 128, 128, 32, 1), (2, 130, 70, 40, 1), (1, 64, 96, 17, 1), (1, 300, 200, 1000, 3),
     (1, 512, 27, 2048, 4)])
 @pytest.mark.parametrize("a_mn,b_mn", [(0, 1), (1, 0), (1, 1)])
-@pytest.mark.parametrize("tile", [32, 128, 256])
+@pytest.mark.parametrize("tile", [32, 64, 128, 256])
 def test_mn_major_operands_match_f64(device, batch, m, n, k, splits, a_mn, b_mn, tile):
     # an MN-major operand is the value [batch, k, mn] in its own row-major
     # layout, the mn axis padded to a multiple of 32 (how the plan prepares an
@@ -150,3 +150,62 @@ def test_stream_k_matches_f64_and_whole_tiles(device, m, n, k, a_mn, tile):
         lib.tbx_set_gemm_stream_k(0)
         lib.tbx_set_gemm_tile_n(0)
     assert torch.equal(outs["stream-k"], outs["stream-k again"])
+
+
+@pytest.mark.parametrize("batch,m,n,k,splits", [
+    (1, 128, 27, 64, 1), (2, 130, 70, 40, 1), (1, 300, 64, 1000, 3), (1, 512, 27, 2048, 4),
+    (3, 64, 200, 96, 1)])
+@pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("raw", [1, 2, 3])
+@pytest.mark.parametrize("tile", [32, 64, 128, 256])
+def test_raw_operands_equal_prepared_pairs(device, batch, m, n, k, splits, a_mn, b_mn, raw, tile):
+    # A raw operand is the f32 values in the prepared layout (no lo buffer):
+    # the GEMM splits each tile into its tf32 pair in shared memory.  The
+    # pair is the one the plan's prep writes, so the product is bitwise the
+    # product over prepared pairs, for either layout, any tile (the 256-wide
+    # request runs on the 128-wide tile), split-K, and the SIMT engine.
+    import torch
+    from poorgrad_b200.abi import load_library
+    lib = load_library()
+    f = lib.tbx_gemm_prepared_layout
+    f.restype = C.c_int
+    f.argtypes = ([C.c_void_p, C.c_void_p, C.c_int, C.c_int64] * 2 + [C.c_void_p, C.c_void_p, C.c_int]
+                  + [C.c_int64] * 5 + [C.c_int])
+    g = torch.Generator(device="cuda").manual_seed(11 * batch + m + n + k + raw)
+    a = torch.randn((batch, m, k), device="cuda", generator=g)
+    bt = torch.randn((batch, n, k), device="cuda", generator=g)
+    kp = (k + 31) // 32 * 32
+
+    def operand(x, mn):
+        rows = x.shape[1]
+        src = x.transpose(1, 2).contiguous() if mn else x
+        ld = (rows + 31) // 32 * 32 if mn else kp
+        hi, lo = _prep(torch, src, ld)
+        padded = torch.zeros_like(hi)
+        padded[:, :, :src.shape[2]] = src
+        return hi, lo, padded.contiguous(), ld
+
+    ahi, alo, araw, a_ld = operand(a, a_mn)
+    bhi, blo, braw, b_ld = operand(bt, b_mn)
+    ref = torch.bmm(a.double(), bt.double().transpose(1, 2))
+    tol = 16 * EPS * math.sqrt(k) * (1 + ref.abs())
+    lib.tbx_set_gemm_tile_n(tile)
+    try:
+        for engine in (2, 1):
+            outs = []
+            for use_raw in (0, raw):
+                pa = (araw.data_ptr(), None) if use_raw & 1 else (ahi.data_ptr(), alo.data_ptr())
+                pb = (braw.data_ptr(), None) if use_raw & 2 else (bhi.data_ptr(), blo.data_ptr())
+                c = torch.full((batch, m, n), float("nan"), device="cuda")
+                part = torch.empty((splits, batch, m, n), device="cuda")
+                rc = f(pa[0], pa[1], a_mn, a_ld, pb[0], pb[1], b_mn, b_ld, c.data_ptr(),
+                       part.data_ptr(), splits, batch, m, n, k, kp, engine)
+                assert rc == 0, f"engine {engine} raw {use_raw} rc {rc}"
+                assert lib.tbx_gemm_error() == 0
+                outs.append(c)
+            err = (outs[1].double() - ref).abs()
+            assert torch.all(err <= tol), f"engine {engine}: worst {(err / tol).max().item()}"
+            if engine == 2:
+                assert torch.equal(outs[0], outs[1]), "raw operands changed the product's bits"
+    finally:
+        lib.tbx_set_gemm_tile_n(0)

@@ -290,6 +290,14 @@ def test_c5_gpt2_tiny(device):
     _config_parity(w, w.feeds(0), rtol=1e-3, atol=1e-4)
 
 
+def test_c5_gpt2_with_raw_attention_operands(device):
+    # 64-wide heads over 64 positions: every attention product reads its
+    # operands as raw f32 values and splits them inside the GEMM
+    w = configs.gpt2(batch=1, seq=64, layers=1, d=128, heads=2, vocab=50, mlp=256)
+    assert ":raw" in backend.lower_describe(w.columns)
+    _config_parity(w, w.feeds(0), rtol=1e-3, atol=1e-4)
+
+
 def test_sgd_step_matches_the_reference_rule(device):
     w = configs.mlp(batch=128)
     feeds = w.feeds(0)

@@ -32,11 +32,31 @@ def test_weight_gradients_read_the_forward_preps_transposed(charmlp_lines):
 
 def test_activation_preps_ride_in_their_producing_row_kernels(charmlp_lines):
     # the LayerNorm forward (tanh output) and backward (dX) row kernels write
-    # the tf32 pair of the GEMM operand they compute
+    # the tf32 pair of the GEMM operand they compute -- all but the second
+    # hidden layer's output, which only the 27-wide head products read
     rows = [l for l in charmlp_lines if ": row " in l and "space=[16384,512]" in l]
-    assert sum("prep" in l for l in rows) == 4
+    assert sum("prep" in l for l in rows) == 3
     standalone = [l for l in charmlp_lines if ": prep " in l and "[1,16384,512]" in l]
     assert not standalone
+
+
+def test_operands_of_memory_bound_products_stay_f32(charmlp_lines):
+    # the head's logits (n=27) and its weight gradient (m=512, n=27) read the
+    # second hidden layer's output as raw f32 values, split into the tf32
+    # pair inside the GEMM: no pair of it is written
+    gemms = [l for l in charmlp_lines if "gemm3xtf32" in l]
+    raw = [l for l in gemms if ":raw" in l]
+    assert len(raw) == 2
+    assert any("m=16384 n=27 k=512" in l and "a=k:raw" in l for l in raw)
+    assert any("m=512 n=27 k=16384" in l and "a=mn:raw" in l for l in raw)
+    # products wide enough for the tensor cores keep prepared pairs
+    assert not any(":raw" in l for l in gemms if " n=512 " in l)
+
+
+def test_raw_operands_can_be_turned_off(built, monkeypatch):
+    monkeypatch.setenv("TB_RAW_OPERANDS", "0")
+    w = configs.char_mlp()
+    assert ":raw" not in backend.lower_describe(w.columns)
 
 
 def test_narrow_column_finals_share_a_launch(charmlp_lines):
@@ -121,3 +141,16 @@ def test_window_patterns_lower_without_materialized_windows(built):
     kinds = [l.split()[1] for l in lines]
     assert kinds.count("gemm3xtf32") == 1
     assert kinds.count("prep") == 2 and kinds.count("ew") == 1 and len(lines) == 4, lines
+
+
+def test_attention_probabilities_stay_f32_for_their_narrow_products(built):
+    # the probabilities [heads, T, T] feed P.V and dV = P^T.dO, both 64 wide
+    # (the head width): raw f32 operands.  The score gradient dS also feeds
+    # dK^T = Q^T.dS as B, a 1024-wide product on the 256-wide tile, so it
+    # keeps its prepared pair.
+    w = configs.gpt2(batch=1, seq=1024, layers=1, vocab=64)
+    lines = [l for l in backend.lower_describe(w.columns).splitlines() if "batch=12 " in l]
+    assert any("m=1024 n=64 k=1024" in l and "a=k:raw" in l for l in lines)
+    assert any("m=1024 n=64 k=1024" in l and "a=mn:raw" in l for l in lines)
+    assert any("m=1024 n=64 k=1024" in l and "a=k b=mn" in l for l in lines)  # dQ = dS.K
+    assert not any(":raw" in l for l in lines if "m=64 n=1024" in l or "n=1024 k=64" in l)
