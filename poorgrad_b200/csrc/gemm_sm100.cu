@@ -23,13 +23,13 @@
 // (two TMEM buffers, the MMA warp filling one while the epilogue drains the
 // other) bounds the chain and keeps the result as accurate as a serial f32 sum.
 // The kernel is persistent (one CTA per SM walking the tiles).
-// An operand may also arrive raw: its f32 values in the same layout, where the
-// product is bound by memory rather than by the tensor cores.  TMA then loads
-// the f32 tile into the stage's hi slot and two converter warps (after the
-// epilogue's) split it in place -- hi = rna_tf32(x) over x, lo = x - hi
-// into the lo slot, the same pair a prepared operand holds -- before the MMA
-// warp may read the stage: half the operand's bytes cross HBM, and the
-// product is bit for bit the one over the prepared pair.
+// A may also arrive raw: its f32 values in the same layout, where the product
+// is bound by memory rather than by the tensor cores.  A stage then holds the
+// f32 A tile and B's pair, so more k-blocks fit in flight; the epilogue warps,
+// each lane one row of the tile, split the row into hi = rna_tf32(x) and
+// lo = x - hi -- the pair a prepared operand holds -- and store both into one
+// of four tensor-memory A buffers, from which the MMA reads A.  Half of A's
+// bytes cross HBM, and the product is bit for bit the one over the pair.
 // Split-K writes ordered partials that a second kernel sums in split order.
 // No TMA multicast is used anywhere (operands may live on any GPU's arena).
 // Every mbarrier wait is bounded by the global timer: on expiry the kernel
@@ -55,7 +55,6 @@ namespace tb {
 namespace {
 
 constexpr int BM = 128;
-constexpr int CONVERTERS = 64;  // converter threads of a kernel with raw operands
 
 // The two tile shapes.  128 x 128 with 32-float k-blocks (128-byte swizzle,
 // 3 stages, one epilogue warpgroup) and 128 x 256 with 16-float k-blocks
@@ -98,9 +97,14 @@ struct Derived {
   static constexpr int TILE_B = C::BN * C::BK * 4;
   static constexpr int STAGE_BYTES = 2 * TILE_A + 2 * TILE_B;
   static constexpr int THREADS = 64 + 128 * C::GROUPS;
-  // with raw f32 operands, two converter warps after the epilogue warps (few
-  // enough that the epilogue keeps its registers)
-  static constexpr int threads(bool raw) { return THREADS + (raw ? CONVERTERS : 0); }
+  // raw A: a stage is the f32 A tile and B's pair; the bytes of the paired
+  // layout's stages hold RAW_STAGES of them.  A's pairs live in A_BUFS
+  // tensor-memory buffers of 64 columns (hi, then lo) after the accumulators.
+  static constexpr int RAW_STAGE_BYTES = TILE_A + 2 * TILE_B;
+  static constexpr int RAW_STAGES_FIT = C::STAGES * STAGE_BYTES / RAW_STAGE_BYTES;
+  static constexpr int RAW_STAGES = RAW_STAGES_FIT > 8 ? 8 : RAW_STAGES_FIT;
+  static constexpr int A_BUFS = 4;
+  static constexpr int MAX_STAGES = RAW_STAGES > C::STAGES ? RAW_STAGES : C::STAGES;
   // per epilogue warp: a 32 x 32 float tile in the 128-byte swizzle (16-byte
   // chunk c of row r at chunk c ^ (r % 8)), 1024-byte aligned, so that a TMA
   // store can take it whole and the lanes' row writes and column reads are
@@ -332,43 +336,34 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
 __device__ __forceinline__ void st_release(int* p, int v) {
   asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-// tf32 pair of a raw tile of N4 float4s by the converter threads: hi over the
-// f32 values (rna_tf32, as the prepared operands are rounded), lo = x - hi.
+// hi = rna_tf32(x): the rounding the prepared operands use.
 __device__ __forceinline__ float rna_tf32(float x) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return __uint_as_float(r);
 }
-// All of a thread's loads are issued before its first store (in batches of
-// 16 float4s), so one shared-memory latency covers the batch instead of one
-// per element: the stores through `hi` could otherwise alias the next loads.
-template <int N4>
-__device__ __forceinline__ void split_tile(float4* __restrict__ hi, float4* __restrict__ lo,
-                                           int ct) {
-  constexpr int PER = N4 / CONVERTERS;  // float4s per thread
-  constexpr int BATCH = PER < 16 ? PER : 16;
-  static_assert(N4 % CONVERTERS == 0 && PER % BATCH == 0, "tile splits evenly");
-#pragma unroll
-  for (int b0 = 0; b0 < PER; b0 += BATCH) {
-    float4 v[BATCH];
-#pragma unroll
-    for (int j = 0; j < BATCH; ++j) v[j] = hi[ct + (b0 + j) * CONVERTERS];
-#pragma unroll
-    for (int j = 0; j < BATCH; ++j) {
-      const float4 h =
-          make_float4(rna_tf32(v[j].x), rna_tf32(v[j].y), rna_tf32(v[j].z), rna_tf32(v[j].w));
-      hi[ct + (b0 + j) * CONVERTERS] = h;
-      lo[ct + (b0 + j) * CONVERTERS] =
-          make_float4(__fsub_rn(v[j].x, h.x), __fsub_rn(v[j].y, h.y), __fsub_rn(v[j].z, h.z),
-                      __fsub_rn(v[j].w, h.w));
-    }
-  }
+// A in tensor memory (tf32, K along the columns), B from shared memory.
+__device__ __forceinline__ void umma_tf32_ta(uint32_t tmem, uint32_t a_tmem, uint64_t b,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void tmem_st16(uint32_t addr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16};" ::"r"(addr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
 }
 // Persistent: each CTA walks its pieces of work (Sched); the stage ring and
 // the two accumulator buffers carry their phases across pieces, so the
 // epilogue of one overlaps the main loop of the next.
 template <class C, bool SK, bool RAW>
-__global__ void __launch_bounds__(Derived<C>::threads(RAW), 1)
+__global__ void __launch_bounds__(Derived<C>::THREADS, 1)
     k_gemm_tcgen05(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
                    const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
                    const __grid_constant__ CUtensorMap tc, int tma_store,
@@ -378,19 +373,30 @@ __global__ void __launch_bounds__(Derived<C>::threads(RAW), 1)
   pdl_entry();
   using D = Derived<C>;
   static_assert(4 * C::GROUPS <= 8, "the stream-K flags hold eight epilogue warps per CTA");
-  constexpr int BN = C::BN, BK = C::BK, STAGES = C::STAGES, CHUNK = C::CHUNK;
-  constexpr int TILE_A = D::TILE_A, TILE_B = D::TILE_B, STAGE_BYTES = D::STAGE_BYTES;
+  static_assert(!RAW || C::GROUPS == 1, "raw A needs the one-warpgroup epilogue");
+  constexpr int BN = C::BN, BK = C::BK, CHUNK = C::CHUNK;
+  constexpr int TILE_A = D::TILE_A, TILE_B = D::TILE_B;
+  // stages: [A hi | A lo | B hi | B lo], or with raw A [A f32 | B hi | B lo]
+  constexpr int STAGES = RAW ? D::RAW_STAGES : C::STAGES;
+  constexpr int STAGE_BYTES = RAW ? D::RAW_STAGE_BYTES : D::STAGE_BYTES;
+  constexpr int B_OFF = RAW ? TILE_A : 2 * TILE_A;
+  constexpr int A_BUFS = D::A_BUFS;
+  constexpr uint32_t A_COL0 = 2 * BN;  // tensor-memory column of A buffer 0 (RAW)
+  constexpr uint32_t TMEM_COLS = RAW ? 512 : 2 * BN;
+  static_assert(!RAW || A_COL0 + 64 * A_BUFS <= TMEM_COLS, "A buffers fit in tensor memory");
   constexpr int EPI_COLS = D::EPI_COLS;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t* full = (uint64_t*)(smem + STAGES * STAGE_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* conv = empty + STAGES;       // [STAGES]: raw tiles of the stage split (RAW)
-  uint64_t* acc_full = conv + STAGES;    // [2]: chunk partial ready in TMEM buffer b
-  uint64_t* acc_empty = acc_full + 2;    // [2]: TMEM buffer b drained by the epilogue
+  // barriers and flags after the paired layout's stages (the raw layout's fit inside)
+  uint64_t* full = (uint64_t*)(smem + C::STAGES * D::STAGE_BYTES);
+  uint64_t* empty = full + D::MAX_STAGES;
+  uint64_t* a_full = empty + D::MAX_STAGES;  // [A_BUFS]: A's pair stored in tensor memory (RAW)
+  uint64_t* a_empty = a_full + A_BUFS;       // [A_BUFS]: its products done (RAW)
+  uint64_t* acc_full = a_empty + A_BUFS;     // [2]: chunk partial ready in TMEM buffer b
+  uint64_t* acc_empty = acc_full + 2;        // [2]: TMEM buffer b drained by the epilogue
   uint32_t* tmem_slot = (uint32_t*)(acc_empty + 2);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
-  float* epi_stage = (float*)(smem + STAGES * STAGE_BYTES + 1024);
+  float* epi_stage = (float*)(smem + C::STAGES * D::STAGE_BYTES + 1024);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -398,7 +404,10 @@ __global__ void __launch_bounds__(Derived<C>::threads(RAW), 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&conv[s], CONVERTERS);
+    }
+    for (int q = 0; q < A_BUFS; ++q) {
+      mbar_init(&a_full[q], 128);
+      mbar_init(&a_empty[q], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -411,7 +420,7 @@ __global__ void __launch_bounds__(Derived<C>::threads(RAW), 1)
   if (warp == 2) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
-                 "r"(2 * BN));
+                 "r"(TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -437,31 +446,31 @@ __global__ void __launch_bounds__(Derived<C>::threads(RAW), 1)
           }
           if (*abort_flag) break;
           uint8_t* base = smem + s * STAGE_BYTES;
-          // a raw operand's one f32 tile lands in its hi slot
-          const bool ra = RAW && (raw & 1), rb = RAW && (raw & 2);
-          mbar_expect_tx(&full[s], STAGE_BYTES - (ra ? TILE_A : 0) - (rb ? TILE_B : 0));
+          mbar_expect_tx(&full[s], STAGE_BYTES);
           const int kx = (kb0 + i) * BK;
+          // raw A: the f32 tile alone (its map is over the values)
           if (!a_mn) {
             tma_load_3d(base, &ta_hi, kx, t.m0, t.batch, &full[s]);
-            if (!ra) tma_load_3d(base + TILE_A, &ta_lo, kx, t.m0, t.batch, &full[s]);
+            if (!RAW) tma_load_3d(base + TILE_A, &ta_lo, kx, t.m0, t.batch, &full[s]);
           } else {  // one box: BM/32 MN blocks of BK rows
             tma_load_4d(base, &ta_hi, 0, kx, t.m0 / 32, t.batch, &full[s]);
-            if (!ra) tma_load_4d(base + TILE_A, &ta_lo, 0, kx, t.m0 / 32, t.batch, &full[s]);
+            if (!RAW) tma_load_4d(base + TILE_A, &ta_lo, 0, kx, t.m0 / 32, t.batch, &full[s]);
           }
-          uint8_t* bb = base + 2 * TILE_A;
+          uint8_t* bb = base + B_OFF;
           if (!b_mn) {
             tma_load_3d(bb, &tb_hi, kx, t.n0, t.batch, &full[s]);
-            if (!rb) tma_load_3d(bb + TILE_B, &tb_lo, kx, t.n0, t.batch, &full[s]);
+            tma_load_3d(bb + TILE_B, &tb_lo, kx, t.n0, t.batch, &full[s]);
           } else {
             tma_load_4d(bb, &tb_hi, 0, kx, t.n0 / 32, t.batch, &full[s]);
-            if (!rb) tma_load_4d(bb + TILE_B, &tb_lo, 0, kx, t.n0 / 32, t.batch, &full[s]);
+            tma_load_4d(bb + TILE_B, &tb_lo, 0, kx, t.n0 / 32, t.batch, &full[s]);
           }
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = instr_desc(BM, BN, a_mn, b_mn);
+      // A in tensor memory is K-major whatever its layout in HBM
+      const uint32_t idesc = instr_desc(BM, BN, RAW ? 0 : a_mn, b_mn);
       // operand descriptor of k-step kk: K-major steps 32 bytes along the
       // swizzled row, MN-major steps one 1024-byte atom (8 rows of 128 bytes)
       auto desc_of = [&](uint32_t tile, int mn, int kk) -> uint64_t {
@@ -485,55 +494,41 @@ __global__ void __launch_bounds__(Derived<C>::threads(RAW), 1)
           for (int i = c * CHUNK; i < i_end; ++i, ++g) {
             const int s = g % STAGES;
             const uint32_t round = g / STAGES;
-            // with raw operands the stage is ready once the converters split it
-            if (!mbar_wait(RAW ? &conv[s] : &full[s], round & 1, 2)) {
+            if (!mbar_wait(&full[s], round & 1, 2)) {
+              *abort_flag = 1;
+              break;
+            }
+            // raw A: its pair in tensor-memory buffer g % A_BUFS
+            const int qa = (int)(g % A_BUFS);
+            if (RAW && !mbar_wait(&a_full[qa], (g / A_BUFS) & 1, 7)) {
               *abort_flag = 1;
               break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
             const uint32_t a_hi = base, a_lo = base + TILE_A;
-            const uint32_t b_hi = base + 2 * TILE_A, b_lo = b_hi + TILE_B;
+            const uint32_t b_hi = base + B_OFF, b_lo = b_hi + TILE_B;
+            const uint32_t ta = tmem + A_COL0 + 64 * qa;  // hi columns, then lo
 #pragma unroll
             for (int kk = 0; kk < BK / 8; ++kk) {
               const uint32_t first = (i > c * CHUNK || kk > 0) ? 1u : 0u;
-              const uint64_t dah = desc_of(a_hi, a_mn, kk), dal = desc_of(a_lo, a_mn, kk);
               const uint64_t dbh = desc_of(b_hi, b_mn, kk), dbl = desc_of(b_lo, b_mn, kk);
-              umma_tf32(acc, dal, dbh, idesc, first);
-              umma_tf32(acc, dah, dbl, idesc, 1u);
-              umma_tf32(acc, dah, dbh, idesc, 1u);
+              if constexpr (RAW) {
+                umma_tf32_ta(acc, ta + 32 + kk * 8, dbh, idesc, first);
+                umma_tf32_ta(acc, ta + kk * 8, dbl, idesc, 1u);
+                umma_tf32_ta(acc, ta + kk * 8, dbh, idesc, 1u);
+              } else {
+                const uint64_t dah = desc_of(a_hi, a_mn, kk), dal = desc_of(a_lo, a_mn, kk);
+                umma_tf32(acc, dal, dbh, idesc, first);
+                umma_tf32(acc, dah, dbl, idesc, 1u);
+                umma_tf32(acc, dah, dbh, idesc, 1u);
+              }
             }
             umma_commit(&empty[s]);
+            if (RAW) umma_commit(&a_empty[qa]);
           }
           umma_commit(&acc_full[b]);
         }
-      }
-    }
-  } else if (RAW && warp >= 2 + 4 * C::GROUPS) {
-    // converters: each stage's raw tiles become tf32 pairs in place, 16 bytes
-    // per thread per step over the tile as stored (the split is elementwise,
-    // so the swizzle does not matter); the writes are made visible to the
-    // tensor cores' async proxy before the stage is released to the MMA warp
-    const int ct = threadIdx.x - 32 * (2 + 4 * C::GROUPS);
-    uint32_t g = 0;
-    SegIter it = seg_begin(sched);
-    Seg sg;
-    while (!*abort_flag && seg_next<C, SK>(sched, it, sg)) {
-      for (int i = 0; i < sg.nkb; ++i, ++g) {
-        const int s = g % STAGES;
-        const uint32_t round = g / STAGES;
-        if (!mbar_wait(&full[s], round & 1, 6)) {
-          *abort_flag = 1;
-          break;
-        }
-        uint8_t* base = smem + s * STAGE_BYTES;
-        if (raw & 1) split_tile<TILE_A / 16>((float4*)base, (float4*)(base + TILE_A), ct);
-        if (raw & 2)
-          split_tile<TILE_B / 16>((float4*)(base + 2 * TILE_A),
-                                  (float4*)(base + 2 * TILE_A + TILE_B), ct);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&conv[s]))
-                     : "memory");
       }
     }
   } else {
@@ -545,6 +540,75 @@ __global__ void __launch_bounds__(Derived<C>::threads(RAW), 1)
     uint32_t gc = 0;
     bool ok = true;
     const int ew = warp - 2;  // epilogue warp index
+    // Raw A: these warps also split A, each lane its row of the tile, into
+    // tensor memory.  The conversions run ahead of the drains: before chunk
+    // c is drained, every k-block through A_BUFS - 1 past its end is split,
+    // so the MMA warp has work while the chunk drains, the next piece's
+    // first k-blocks included.  (Splitting k-block g waits for the products
+    // of g - A_BUFS, which lie in chunk c or before: no wait goes around.)
+    SegIter cit = seg_begin(sched);
+    Seg csg;
+    bool chave = RAW && seg_next<C, SK>(sched, cit, csg);
+    int ci = 0;        // k-blocks of csg split
+    uint32_t cg = 0;   // k-blocks split by this CTA
+    uint32_t g0 = 0;   // this CTA's k-blocks before the current piece
+    auto convert_until = [&](uint32_t target) {
+      if constexpr (RAW) {
+        static_assert(BK == 32, "a k-block is 32 tensor-memory columns");
+        const int r = q * 32 + lane;  // this lane's row of the A tile
+        while (ok && chave && cg < target) {
+          if (ci >= csg.nkb) {
+            ci = 0;
+            chave = seg_next<C, SK>(sched, cit, csg);
+            continue;
+          }
+          const int s = (int)(cg % STAGES), qa = (int)(cg % A_BUFS);
+          if (!mbar_wait(&full[s], (cg / STAGES) & 1, 6) ||
+              !mbar_wait(&a_empty[qa], ((cg / A_BUFS) & 1) ^ 1, 8)) {
+            ok = false;
+            *abort_flag = 1;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const float* at = (const float*)(smem + s * STAGE_BYTES);
+          const uint32_t col = tmem + lane_base + A_COL0 + 64 * qa;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float x[16];
+            if (!a_mn) {
+              // K-major tile: 128-byte rows, 16-byte chunk j at j ^ (r % 8)
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float4 v = *(const float4*)(at + stage_at(r, (h * 4 + j) * 4));
+                x[4 * j] = v.x;
+                x[4 * j + 1] = v.y;
+                x[4 * j + 2] = v.z;
+                x[4 * j + 3] = v.w;
+              }
+            } else {
+              // MN-major tile, unswizzled: [row block][k][32 rows]
+#pragma unroll
+              for (int j = 0; j < 16; ++j) x[j] = at[((r >> 5) * BK + h * 16 + j) * 32 + (r & 31)];
+            }
+            uint32_t hi[16], lo[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float hv = rna_tf32(x[j]);
+              hi[j] = __float_as_uint(hv);
+              lo[j] = __float_as_uint(__fsub_rn(x[j], hv));
+            }
+            tmem_st16(col + h * 16, hi);
+            tmem_st16(col + 32 + h * 16, lo);
+          }
+          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+          asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&a_full[qa]))
+                       : "memory");
+          ++ci;
+          ++cg;
+        }
+      }
+    };
     SegIter it = seg_begin(sched);
     Seg sg;
     while (ok && seg_next<C, SK>(sched, it, sg)) {
@@ -556,6 +620,8 @@ __global__ void __launch_bounds__(Derived<C>::threads(RAW), 1)
       for (int j = 0; j < EPI_COLS; ++j) total[j] = 0.0f;
       for (int c = 0; c < chunks; ++c, ++gc) {
         const int b = gc & 1;
+        convert_until(g0 + (uint32_t)min(nkb, (c + 1) * CHUNK) + (A_BUFS - 1));
+        if (!ok) break;
         if (!mbar_wait(&acc_full[b], (gc >> 1) & 1, 3)) {
           ok = false;
           break;
@@ -574,6 +640,7 @@ __global__ void __launch_bounds__(Derived<C>::threads(RAW), 1)
         asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&acc_empty[b]))
                      : "memory");
       }
+      g0 += nkb;
       if (!ok || *abort_flag) break;
       if (SK && sg.kind == 1) {
         // a later piece of a cut tile: to this CTA's workspace slot, laid out
@@ -667,7 +734,8 @@ __global__ void __launch_bounds__(Derived<C>::threads(RAW), 1)
   __syncthreads();
   if (warp == 2) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(TMEM_COLS));
   }
 }
 
@@ -810,9 +878,11 @@ namespace {
 // Tensor map over an MN-major buffer [batch][rows][ld] seen as 32-float MN
 // blocks: dimensions (32 floats, rows, ld / 32 blocks 128 bytes apart, batch),
 // so one box of (32, bk, tile / 32) lands block after block -- the operand
-// tile the MMA reads.  Every address stays inside its row of ld floats.
+// tile the MMA reads.  Every address stays inside its row of ld floats.  A
+// raw A tile, which the epilogue warps read rather than the MMA, is unswizzled.
 bool make_map_mn(CUtensorMap* map, const float* base, int64_t ld, int64_t rows, int64_t batch,
-                 int tile, int bk) {
+                 int tile, int bk,
+                 CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B) {
   EncodeTiled enc = encoder();
   if (!enc) return false;
   cuuint64_t dims[4] = {32, (cuuint64_t)rows, (cuuint64_t)(ld / 32), (cuuint64_t)batch};
@@ -820,8 +890,7 @@ bool make_map_mn(CUtensorMap* map, const float* base, int64_t ld, int64_t rows, 
   cuuint32_t box[4] = {32, (cuuint32_t)bk, (cuuint32_t)(tile / 32), 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void*)base, dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -833,8 +902,12 @@ bool make_map_mn(CUtensorMap* map, const float* base, int64_t ld, int64_t rows, 
 template <class C>
 bool operand_maps(CUtensorMap* hi, CUtensorMap* lo, const Operand& o, int tile, int64_t batch) {
   if (o.mn) {
+    if (!o.lo) {
+      if (!make_map_mn(hi, o.hi, o.ld, o.rows, batch, tile, C::BK, CU_TENSOR_MAP_SWIZZLE_NONE))
+        return false;
+      return (*lo = *hi, true);
+    }
     if (!make_map_mn(hi, o.hi, o.ld, o.rows, batch, tile, C::BK)) return false;
-    if (!o.lo) return (*lo = *hi, true);
     return make_map_mn(lo, o.lo, o.ld, o.rows, batch, tile, C::BK);
   }
   if (!make_map(hi, o.hi, o.ld, o.rows, batch, C::BK, tile, C::TMA_SWIZZLE)) return false;
@@ -866,7 +939,9 @@ bool launch_cfg(const Operand& a, const Operand& b, float* c, float* partial, in
   CUtensorMap ma, mal, mb, mbl;
   if (!operand_maps<C>(&ma, &mal, a, BM, batch) || !operand_maps<C>(&mb, &mbl, b, C::BN, batch))
     return false;
-  const int raw = (a.lo ? 0 : 1) | (b.lo ? 0 : 2);
+  // raw A is split into tensor memory; a raw B is not served here
+  if (!b.lo) return false;
+  const int raw = a.lo ? 0 : 1;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 256) return false;
   if constexpr (C::GROUPS == 1) {
@@ -932,22 +1007,22 @@ bool launch_cfg(const Operand& a, const Operand& b, float* c, float* partial, in
   int* flags = sched.sk_units > 0 ? sk->flags : nullptr;
   if constexpr (C::GROUPS == 1) {
     if (sched.sk_units > 0 && raw)
-      launch_pdl(k_gemm_tcgen05<C, true, true>, grid, D::threads(true), D::SMEM_BYTES, stream, ma,
+      launch_pdl(k_gemm_tcgen05<C, true, true>, grid, D::THREADS, D::SMEM_BYTES, stream, ma,
                  mal, mb, mbl, mc, tma_store, target, (int)m, (int)n, sched, plane, (int)a.mn,
                  (int)b.mn, raw, ws, flags);
     else if (raw)
-      launch_pdl(k_gemm_tcgen05<C, false, true>, grid, D::threads(true), D::SMEM_BYTES, stream,
+      launch_pdl(k_gemm_tcgen05<C, false, true>, grid, D::THREADS, D::SMEM_BYTES, stream,
                  ma, mal, mb, mbl, mc, tma_store, target, (int)m, (int)n, sched, plane,
                  (int)a.mn, (int)b.mn, raw, ws, flags);
   }
   if (raw) {
     // launched above (the one-warpgroup tiles only)
   } else if (sched.sk_units > 0)
-    launch_pdl(k_gemm_tcgen05<C, true, false>, grid, D::threads(false), D::SMEM_BYTES, stream, ma,
+    launch_pdl(k_gemm_tcgen05<C, true, false>, grid, D::THREADS, D::SMEM_BYTES, stream, ma,
                mal, mb, mbl, mc, tma_store, target, (int)m, (int)n, sched, plane, (int)a.mn,
                (int)b.mn, raw, ws, flags);
   else
-    launch_pdl(k_gemm_tcgen05<C, false, false>, grid, D::threads(false), D::SMEM_BYTES, stream,
+    launch_pdl(k_gemm_tcgen05<C, false, false>, grid, D::THREADS, D::SMEM_BYTES, stream,
                ma, mal, mb, mbl, mc, tma_store, target, (int)m, (int)n, sched, plane, (int)a.mn,
                (int)b.mn, raw, ws, flags);
   if (splits > 1) {
@@ -971,7 +1046,7 @@ bool launch_gemm_tcgen05_split(const Operand& a, const Operand& b, float* c, flo
   int tile = gemm_tile_n(batch, m, n, kp);
   // the 256-wide tile's two epilogue warpgroups leave no registers for the
   // converters: raw operands take the 128-wide tile
-  if (tile == 256 && (!a.lo || !b.lo)) tile = 128;
+  if (tile == 256 && !a.lo) tile = 128;
   if (tile == 256)
     return launch_cfg<Cfg<256>>(a, b, c, partial, splits, batch, m, n, kp, stream, sk);
   if (tile == 32)

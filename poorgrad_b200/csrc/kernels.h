@@ -40,7 +40,8 @@ void launch_segment_sum(const float* perm, const int* rstart, const int* rend, f
 // (ld >= M or N, a multiple of 32).  A is M x K, B is given as N x K.
 // A raw operand has no lo: `hi` holds the f32 values themselves, in the same
 // layout (K-major rows then hold all kp reduction indices, ld >= kp), and the
-// GEMM splits them into the pair on the way in.
+// GEMM splits them into the pair on the way in.  The tcgen05 path takes a raw
+// A only (it declines a raw B); the SIMT path takes either.
 struct Operand {
   const float* hi = nullptr;
   const float* lo = nullptr;  // nullptr: raw f32 operand

@@ -1261,11 +1261,10 @@ class Lowerer {
   }
 
   // ---- raw GEMM operands
-  // A value every product reads as a memory-bound operand -- the product's
-  // other output extent is at most 64, so each element meets at most 64
-  // others (and, read as B, the product is at most 128 wide) -- is stored
-  // once in f32 and split into its tf32 pair inside the GEMM: half the bytes
-  // of a prepared pair are written and read.  The value
+  // A value every product reads as its A operand and as a memory-bound one --
+  // the product is at most 64 wide, so each element meets at most 64 others
+  // -- is stored once in f32 and split into its tf32 pair inside the GEMM:
+  // half the bytes of a prepared pair are written and read.  The value
   // must be a dense [batch][rows][cols] buffer with cols a multiple of 32 (no
   // padding, 16-byte rows); an expression that is not yet stored is
   // materialized for it.  Products wide enough to be bound by the tensor cores
@@ -1304,14 +1303,12 @@ class Lowerer {
       const int split = A.rank - 2;
       int64_t batch = 1;
       for (int i = 0; i < split; ++i) batch *= A.shape[i];
-      const int64_t M = A.shape[split], N = B.shape[split + 1];
+      const int64_t N = B.shape[split + 1];
       for (int o = 0; o < 2; ++o) {
         bool flip = false;
         const int base = strip_transposes(nd.operands[o], flip);
         const Node& b = P.nodes[base];
-        // a raw B must not need the 256-wide tile, which has no room for the
-        // converters (the product would fall back to narrower tiles)
-        bool fit = (o == 0 ? N : M) <= kRawOperandReuse && (o == 0 || N <= 128) && b.rank >= 2 &&
+        bool fit = o == 0 && N <= kRawOperandReuse && b.rank >= 2 &&
                    b.shape[b.rank - 1] % 32 == 0 && b.volume() == batch * b.shape[b.rank - 2] *
                    b.shape[b.rank - 1] && dense_view(base);
         auto it = ok.find(base);
