@@ -381,8 +381,15 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
   constexpr int STAGE_BYTES = RAW ? D::RAW_STAGE_BYTES : D::STAGE_BYTES;
   constexpr int B_OFF = RAW ? TILE_A : 2 * TILE_A;
   constexpr int A_BUFS = D::A_BUFS;
-  constexpr uint32_t A_COL0 = 2 * BN;  // tensor-memory column of A buffer 0 (RAW)
-  constexpr uint32_t TMEM_COLS = RAW ? 512 : 2 * BN;
+  // Narrow tiles read B's hi and lo tiles, adjacent in the stage, as one
+  // 2N-wide operand: A_hi.[B_hi | B_lo] into columns [0, 2N) and A_lo.B_hi
+  // added into [N, 2N) -- two tensor-core instructions per k-step instead of
+  // three.  A narrow product costs about as much per instruction as a wide
+  // one, so this is a third fewer cycles; the epilogue adds the halves.
+  constexpr bool JOINT_B = BN <= 64;
+  constexpr uint32_t ACC_W = JOINT_B ? 2 * BN : BN;  // columns of one accumulator buffer
+  constexpr uint32_t A_COL0 = 2 * ACC_W;  // tensor-memory column of A buffer 0 (RAW)
+  constexpr uint32_t TMEM_COLS = RAW ? 512 : 2 * ACC_W;
   static_assert(!RAW || A_COL0 + 64 * A_BUFS <= TMEM_COLS, "A buffers fit in tensor memory");
   constexpr int EPI_COLS = D::EPI_COLS;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -471,6 +478,7 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
     if (lane == 0) {
       // A in tensor memory is K-major whatever its layout in HBM
       const uint32_t idesc = instr_desc(BM, BN, RAW ? 0 : a_mn, b_mn);
+      const uint32_t idesc2 = instr_desc(BM, 2 * BN, RAW ? 0 : a_mn, b_mn);  // JOINT_B
       // operand descriptor of k-step kk: K-major steps 32 bytes along the
       // swizzled row, MN-major steps one 1024-byte atom (8 rows of 128 bytes)
       auto desc_of = [&](uint32_t tile, int mn, int kk) -> uint64_t {
@@ -489,7 +497,7 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
             break;
           }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t acc = tmem + b * BN;
+          const uint32_t acc = tmem + b * ACC_W;
           const int i_end = min(nkb, (c + 1) * CHUNK);
           for (int i = c * CHUNK; i < i_end; ++i, ++g) {
             const int s = g % STAGES;
@@ -513,7 +521,14 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
             for (int kk = 0; kk < BK / 8; ++kk) {
               const uint32_t first = (i > c * CHUNK || kk > 0) ? 1u : 0u;
               const uint64_t dbh = desc_of(b_hi, b_mn, kk), dbl = desc_of(b_lo, b_mn, kk);
-              if constexpr (RAW) {
+              if constexpr (JOINT_B && RAW) {
+                umma_tf32_ta(acc, ta + kk * 8, dbh, idesc2, first);
+                umma_tf32_ta(acc + BN, ta + 32 + kk * 8, dbh, idesc, 1u);
+              } else if constexpr (JOINT_B) {
+                const uint64_t dah = desc_of(a_hi, a_mn, kk), dal = desc_of(a_lo, a_mn, kk);
+                umma_tf32(acc, dah, dbh, idesc2, first);
+                umma_tf32(acc + BN, dal, dbh, idesc, 1u);
+              } else if constexpr (RAW) {
                 umma_tf32_ta(acc, ta + 32 + kk * 8, dbh, idesc, first);
                 umma_tf32_ta(acc, ta + kk * 8, dbl, idesc, 1u);
                 umma_tf32_ta(acc, ta + kk * 8, dbh, idesc, 1u);
@@ -630,7 +645,15 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
 #pragma unroll
         for (int gq = 0; gq < EPI_COLS / 16; ++gq) {
           uint32_t r[16];
-          tmem_ld16(tmem + lane_base + b * BN + c0 + gq * 16, r);
+          tmem_ld16(tmem + lane_base + b * ACC_W + c0 + gq * 16, r);
+          if constexpr (JOINT_B) {
+            // the chunk's partial: Ahi.Bhi + (Ahi.Blo + Alo.Bhi)
+            uint32_t x[16];
+            tmem_ld16(tmem + lane_base + b * ACC_W + BN + c0 + gq * 16, x);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              r[j] = __float_as_uint(__fadd_rn(__uint_as_float(r[j]), __uint_as_float(x[j])));
+          }
 #pragma unroll
           for (int j = 0; j < 16; ++j)
             total[gq * 16 + j] = c == 0 ? __uint_as_float(r[j])
