@@ -368,7 +368,7 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
                    const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
                    const __grid_constant__ CUtensorMap tc, int tma_store,
                    float* __restrict__ out, int m, int n, const Sched sched,
-                   long long split_stride, int a_mn, int b_mn, int raw,
+                   long long split_stride, int a_mn, int b_mn,
                    float* __restrict__ sk_ws, int* __restrict__ sk_flags) {
   pdl_entry();
   using D = Derived<C>;
@@ -1032,22 +1032,22 @@ bool launch_cfg(const Operand& a, const Operand& b, float* c, float* partial, in
     if (sched.sk_units > 0 && raw)
       launch_pdl(k_gemm_tcgen05<C, true, true>, grid, D::THREADS, D::SMEM_BYTES, stream, ma,
                  mal, mb, mbl, mc, tma_store, target, (int)m, (int)n, sched, plane, (int)a.mn,
-                 (int)b.mn, raw, ws, flags);
+                 (int)b.mn, ws, flags);
     else if (raw)
       launch_pdl(k_gemm_tcgen05<C, false, true>, grid, D::THREADS, D::SMEM_BYTES, stream,
                  ma, mal, mb, mbl, mc, tma_store, target, (int)m, (int)n, sched, plane,
-                 (int)a.mn, (int)b.mn, raw, ws, flags);
+                 (int)a.mn, (int)b.mn, ws, flags);
   }
   if (raw) {
     // launched above (the one-warpgroup tiles only)
   } else if (sched.sk_units > 0)
     launch_pdl(k_gemm_tcgen05<C, true, false>, grid, D::THREADS, D::SMEM_BYTES, stream, ma,
                mal, mb, mbl, mc, tma_store, target, (int)m, (int)n, sched, plane, (int)a.mn,
-               (int)b.mn, raw, ws, flags);
+               (int)b.mn, ws, flags);
   else
     launch_pdl(k_gemm_tcgen05<C, false, false>, grid, D::THREADS, D::SMEM_BYTES, stream,
                ma, mal, mb, mbl, mc, tma_store, target, (int)m, (int)n, sched, plane, (int)a.mn,
-               (int)b.mn, raw, ws, flags);
+               (int)b.mn, ws, flags);
   if (splits > 1) {
     const long long count = batch * m * n;
     int blocks = (int)std::min<long long>((count + 255) / 256, 148 * 8);

@@ -154,3 +154,6 @@ def test_attention_probabilities_stay_f32_for_their_narrow_products(built):
     assert any("m=1024 n=64 k=1024" in l and "a=mn:raw" in l for l in lines)
     assert any("m=1024 n=64 k=1024" in l and "a=k b=mn" in l for l in lines)  # dQ = dS.K
     assert not any(":raw" in l for l in lines if "m=64 n=1024" in l or "n=1024 k=64" in l)
+    # a raw operand is always A: the tensor-core path splits A only
+    every = backend.lower_describe(w.columns)
+    assert not re.search(r"b=(k|mn):raw", every)
