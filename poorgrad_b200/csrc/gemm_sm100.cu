@@ -336,12 +336,6 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
 __device__ __forceinline__ void st_release(int* p, int v) {
   asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-// hi = rna_tf32(x): the rounding the prepared operands use.
-__device__ __forceinline__ float rna_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
-}
 // A in tensor memory (tf32, K along the columns), B from shared memory.
 __device__ __forceinline__ void umma_tf32_ta(uint32_t tmem, uint32_t a_tmem, uint64_t b,
                                              uint32_t idesc, uint32_t accumulate) {
@@ -571,6 +565,17 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
       if constexpr (RAW) {
         static_assert(BK == 32, "a k-block is 32 tensor-memory columns");
         const int r = q * 32 + lane;  // this lane's row of the A tile
+        // The stores of one k-block complete while the next is loaded and
+        // split: its buffer is released (a_full) only after that, so a store's
+        // latency is paid once per call, not once per k-block.
+        int pending = -1;  // A buffer whose stores are in flight
+        auto release = [&]() {
+          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+          asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&a_full[pending]))
+                       : "memory");
+          pending = -1;
+        };
         while (ok && chave && cg < target) {
           if (ci >= csg.nkb) {
             ci = 0;
@@ -586,42 +591,46 @@ __global__ void __launch_bounds__(Derived<C>::THREADS, 1)
           }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const float* at = (const float*)(smem + s * STAGE_BYTES);
-          const uint32_t col = tmem + lane_base + A_COL0 + 64 * qa;
+          float x[32];
+          if (!a_mn) {
+            // K-major tile: 128-byte rows, 16-byte chunk j at j ^ (r % 8)
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            float x[16];
-            if (!a_mn) {
-              // K-major tile: 128-byte rows, 16-byte chunk j at j ^ (r % 8)
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const float4 v = *(const float4*)(at + stage_at(r, (h * 4 + j) * 4));
-                x[4 * j] = v.x;
-                x[4 * j + 1] = v.y;
-                x[4 * j + 2] = v.z;
-                x[4 * j + 3] = v.w;
-              }
-            } else {
-              // MN-major tile, unswizzled: [row block][k][32 rows]
-#pragma unroll
-              for (int j = 0; j < 16; ++j) x[j] = at[((r >> 5) * BK + h * 16 + j) * 32 + (r & 31)];
+            for (int j = 0; j < 8; ++j) {
+              const float4 v = *(const float4*)(at + stage_at(r, 4 * j));
+              x[4 * j] = v.x;
+              x[4 * j + 1] = v.y;
+              x[4 * j + 2] = v.z;
+              x[4 * j + 3] = v.w;
             }
-            uint32_t hi[16], lo[16];
+          } else {
+            // MN-major tile, unswizzled: [row block][k][32 rows]
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const float hv = rna_tf32(x[j]);
-              hi[j] = __float_as_uint(hv);
-              lo[j] = __float_as_uint(__fsub_rn(x[j], hv));
-            }
-            tmem_st16(col + h * 16, hi);
-            tmem_st16(col + 32 + h * 16, lo);
+            for (int j = 0; j < 32; ++j) x[j] = at[((r >> 5) * BK + j) * 32 + (r & 31)];
           }
-          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-          asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&a_full[qa]))
-                       : "memory");
+          uint32_t hi[32], lo[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            // rna_tf32 (the prepared operands' rounding) in integer
+            // arithmetic: half a tf32 unit added to the magnitude and the 13
+            // low bits cleared -- nearest, ties away from zero, a carry into
+            // the exponent rounding up; infinities and NaNs kept
+            const uint32_t u = __float_as_uint(x[j]);
+            const uint32_t h =
+                (u & 0x7f800000u) == 0x7f800000u ? u : ((u + 0x1000u) & 0xffffe000u);
+            hi[j] = h;
+            lo[j] = __float_as_uint(__fsub_rn(x[j], __uint_as_float(h)));
+          }
+          if (pending >= 0) release();
+          const uint32_t col = tmem + lane_base + A_COL0 + 64 * qa;
+          tmem_st16(col, hi);
+          tmem_st16(col + 16, hi + 16);
+          tmem_st16(col + 32, lo);
+          tmem_st16(col + 48, lo + 16);
+          pending = qa;
           ++ci;
           ++cg;
         }
+        if (pending >= 0) release();
       }
     };
     SegIter it = seg_begin(sched);
