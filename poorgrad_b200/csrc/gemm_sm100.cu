@@ -10,14 +10,17 @@
 //               box of BK-float rows; an MN-major tile is one box of 32-wide
 //               MN blocks (BK rows of 128 bytes each, 32-byte swizzle atoms);
 //   warp 1      MMA issuer: one elected thread issues tcgen05.mma kind::tf32
-//               (M=128, N=BN, K=8), three products per k-step, and commits each
-//               stage back to the producer;
+//               (M=128, N=BN, K=8), three products per k-step (two on the
+//               32- and 64-wide tiles, which read B's hi and lo tiles as one
+//               2N-wide operand), and commits each stage back to the producer;
 //   warps 2..   epilogue (one warpgroup per 128 columns of the tile): every
 //               CHUNK k-blocks the tensor-memory partial is read (tcgen05.ld,
 //               each warp its TMEM lane quarter) and added in IEEE f32 to
-//               register accumulators; the finished tile goes out through a
-//               per-warp 32 x 33 staging tile, one 128-byte row segment per
-//               store instruction; warp 2 owns the TMEM allocation.
+//               register accumulators; the finished tile goes out through
+//               per-warp 32 x 32 staging slabs in the 128-byte swizzle, one TMA
+//               store each (or one 128-byte row segment per store instruction
+//               where the output rows are not 16-byte multiples); warp 2 owns
+//               the TMEM allocation.
 // The tensor cores accumulate with truncating adders, so an accumulation chain
 // of k terms drifts like k ulps; draining the accumulator every CHUNK k-blocks
 // (two TMEM buffers, the MMA warp filling one while the epilogue drains the
