@@ -147,3 +147,24 @@ def test_composite_engine_backward_program_follows_the_oracle(built):
         np.testing.assert_allclose(out[v.index], ref[v.index], rtol=1e-5, atol=1e-6)
     for p, r in zip((a, b, s), oracle.backward(cols, params, loss, [a, b, s])):
         np.testing.assert_allclose(out[grads[(loss.index, p.index)]], r, rtol=1e-5, atol=1e-6)
+
+
+def test_raw_operand_programs_follow_the_oracle(built):
+    # a narrow MLP head whose activations reach both its products as raw f32
+    # A operands (the logits, K-major, and the weight gradient, MN-major)
+    import re
+    from poorgrad_b200 import backend
+    from poorgrad_b200.graph import Dense
+    rng = np.random.default_rng(5)
+    t = Tape()
+    x = t.input(Dense((256, 96), rng.standard_normal((256, 96)).astype(np.float32)))
+    w1 = t.parameter(Dense((96, 64), rng.standard_normal((96, 64)).astype(np.float32) * 0.1))
+    w2 = t.parameter(Dense((64, 24), rng.standard_normal((64, 24)).astype(np.float32) * 0.1))
+    h = x.matmul(w1).tanh()
+    loss = (h.matmul(w2) * h.matmul(w2)).sum()
+    grads = t.differentiate(loss, [w1, w2])
+    net = t.into_network()
+    cols = net.compile(Request([loss] + grads))
+    text = backend.lower_describe(cols)
+    assert re.search(r"a=k:raw", text) and re.search(r"a=mn:raw", text)
+    compare(cols, net.parameters())

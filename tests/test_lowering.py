@@ -157,3 +157,58 @@ def test_attention_probabilities_stay_f32_for_their_narrow_products(built):
     # a raw operand is always A: the tensor-core path splits A only
     every = backend.lower_describe(w.columns)
     assert not re.search(r"b=(k|mn):raw", every)
+
+
+def _product_lines(build):
+    from poorgrad_b200.graph import Tape
+    from poorgrad_b200.plan import Request
+    t = Tape()
+    roots = build(t)
+    cols = t.into_network().compile(Request(roots))
+    return [l for l in backend.lower_describe(cols).splitlines() if "gemm3xtf32" in l]
+
+
+def test_which_operands_stay_raw(built):
+    # raw: the A operand of products at most 64 wide, stored densely with
+    # rows of a multiple of 32 floats -- an input as it is, a computed value
+    # once in f32; everything else keeps its prepared pair
+    import numpy as np
+    from poorgrad_b200.graph import Dense, filled
+    rng = np.random.default_rng(1)
+
+    def dense(shape):
+        return Dense(shape, rng.standard_normal(shape).astype(np.float32))
+
+    # an input feeding a 48-wide product: raw, no prep for it
+    lines = _product_lines(lambda t: [t.input(dense((256, 64))).matmul(t.parameter(dense((64, 48))))])
+    assert len(lines) == 1 and "a=k:raw" in lines[0]
+    # the same input also feeding a 256-wide product: pairs for both
+    def two(t):
+        x = t.input(dense((256, 64)))
+        return [x.matmul(t.parameter(dense((64, 48)))), x.matmul(t.parameter(dense((64, 256))))]
+    assert not any(":raw" in l for l in _product_lines(two))
+    # rows that are not a multiple of 32 floats: a pair (it would need padding)
+    lines = _product_lines(lambda t: [t.input(dense((256, 40))).matmul(t.parameter(dense((40, 48))))])
+    assert not any(":raw" in l for l in lines)
+    # a computed value read by a narrow product: raw, stored by its fusion group
+    lines = _product_lines(
+        lambda t: [(t.input(dense((256, 64))).tanh()).matmul(t.parameter(dense((64, 16))))])
+    assert len(lines) == 1 and "a=k:raw" in lines[0]
+    # a value read transposed as A (a weight gradient's shape): raw, MN-major
+    lines = _product_lines(
+        lambda t: [t.input(dense((512, 64))).transpose().matmul(t.input(dense((512, 32))))])
+    assert len(lines) == 1 and "a=mn:raw" in lines[0] and "b=mn" in lines[0]
+    # the B side of a narrow product (its own M is large) is never raw
+    assert "b=mn:raw" not in lines[0] and "b=k:raw" not in lines[0]
+
+
+def test_bf16_networks_keep_prepared_pairs(built):
+    import numpy as np
+    from poorgrad_b200.graph import BF16, Dense, Tape
+    from poorgrad_b200.plan import Request
+    rng = np.random.default_rng(2)
+    t = Tape(BF16)
+    x = t.input(Dense((256, 64), rng.standard_normal((256, 64)).astype(np.float32)))
+    y = x.matmul(t.parameter(Dense((64, 16), rng.standard_normal((64, 16)).astype(np.float32))))
+    cols = t.into_network().compile(Request([y]))
+    assert ":raw" not in backend.lower_describe(cols)
