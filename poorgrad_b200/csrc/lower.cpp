@@ -247,6 +247,28 @@ std::string flit(float f) {
   return buf;
 }
 
+// The constant a flit() literal spells, if `s` is one.
+static bool literal_value(const std::string& s, float& out) {
+  unsigned bits = 0;
+  int used = 0;
+  if (sscanf(s.c_str(), "__int_as_float(0x%8x)%n", &bits, &used) != 1 || used != (int)s.size())
+    return false;
+  memcpy(&out, &bits, 4);
+  return true;
+}
+// 1/c when c is a power of two, whose reciprocal is exact (a normal c's
+// reciprocal is at least 2^-127, a representable subnormal): x / c and
+// x * (1/c) are then the same real number, rounded once -- bit for bit the
+// same result, NaN, infinity and signed zero included.
+static bool exact_reciprocal(float c, float& r) {
+  uint32_t bits;
+  memcpy(&bits, &c, 4);
+  const uint32_t e = (bits >> 23) & 0xff;
+  if ((bits & 0x7fffff) != 0 || e == 0 || e == 0xff) return false;
+  r = 1.0f / c;
+  return true;
+}
+
 struct Idx {
   std::vector<std::string> c;
   int lane = -1;          // c.back() == lbase + lane
@@ -1563,10 +1585,15 @@ class Emitter {
         case TB_OP_ADD: e = "__fadd_rn(" + x + ", " + y + ")"; break;
         case TB_OP_SUB: e = "__fsub_rn(" + x + ", " + y + ")"; break;
         case TB_OP_MUL: e = "__fmul_rn(" + x + ", " + y + ")"; break;
-        case TB_OP_DIV:
-          e = relaxed && !P.bf16 ? "__fmul_rn(" + x + ", tb_rcp(" + y + "))"
-                                 : "__fdiv_rn(" + x + ", " + y + ")";
+        case TB_OP_DIV: {
+          float c = 0.0f, r = 0.0f;
+          if (literal_value(y, c) && exact_reciprocal(c, r))
+            e = "__fmul_rn(" + x + ", " + flit(r) + ")";  // a power-of-two divisor
+          else
+            e = relaxed && !P.bf16 ? "__fmul_rn(" + x + ", tb_rcp(" + y + "))"
+                                   : "__fdiv_rn(" + x + ", " + y + ")";
           break;
+        }
         case TB_OP_NEG: e = "(-" + x + ")"; break;
         case TB_OP_TANH: e = "tanhf(" + x + ")"; break;
         case TB_OP_EXP: e = "expf(" + x + ")"; break;

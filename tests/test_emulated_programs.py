@@ -168,3 +168,25 @@ def test_raw_operand_programs_follow_the_oracle(built):
     text = backend.lower_describe(cols)
     assert re.search(r"a=k:raw", text) and re.search(r"a=mn:raw", text)
     compare(cols, net.parameters())
+
+
+def test_power_of_two_divisors_divide_bitwise(built):
+    # x / 2^k is emitted as x * 2^-k (an exact reciprocal: the same real
+    # number rounded once), so exact kernels stay bit-identical to the
+    # reference's division -- subnormal results, infinities, NaNs and signed
+    # zeros included; a divisor that is not a power of two keeps the division
+    import re
+    from poorgrad_b200 import backend
+    from poorgrad_b200.graph import Dense, filled
+    vals = np.array([1.0, -3.0, 7e-39, -1e-45, 3.4e38, -0.0, 0.0, np.inf, -np.inf, np.nan,
+                     1.17549435e-38, 0.1, 12345.678, -2.5e-40, 6.0, 1e30], np.float32)
+    x_payload = Dense((4, 4), vals.reshape(4, 4))
+    t = Tape()
+    x = t.parameter(x_payload)
+    outs = [x / x.literal(filled((4, 4), c)) for c in (4.0, 0.5, 2.0 ** -100, 2.0 ** 100, 3.0)]
+    net = t.into_network()
+    cols = net.compile(Request(outs))
+    src = backend.lower_describe(cols, with_source=True)
+    divisions = re.findall(r"__fdiv_rn\([^,]*, ([^)]*\))\)", src)
+    assert divisions and set(divisions) == {"__int_as_float(0x40400000)"}  # only the one by 3
+    compare(cols, net.parameters(), bitwise=True)
