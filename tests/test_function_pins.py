@@ -116,3 +116,42 @@ def test_powf_routes_the_power_and_exponential_rules(built):
         assert dev[v.index].tobytes() == ref[v.index].tobytes()
     d = dev[ge.index].reshape(-1)
     assert math.isclose(float(d[0]), g1[0], rel_tol=4e-6) and math.isnan(float(d[1]))
+
+
+def test_scatter_accumulates_repeated_rows_and_gathers_back(built):
+    # scatter_tests.rs: rows [1,2],[3,4],[5,6] scattered by [0, 2, 0] into 3
+    # rows give [6,8],[0,0],[3,4]; the backward gathers the seed by the same
+    # selection, each source row reading its own target row back
+    from poorgrad_b200.graph import selection
+    t = Tape()
+    g = t.parameter(tensor([3, 2], [1, 2, 3, 4, 5, 6]))
+    sel = t.leaf(selection([0, 2, 0], 3))
+    y = g.scatter(sel, 3)
+    seed = t.leaf(tensor([3, 2], [1, 2, 3, 4, 5, 6]))
+    (gg,) = t.differentiate((y * seed).sum(), [g])
+    ref, dev = both(t, [y, gg])
+    assert values(ref, y) == [6.0, 8.0, 0.0, 0.0, 3.0, 4.0]
+    assert values(ref, gg) == [1.0, 2.0, 5.0, 6.0, 1.0, 2.0]
+    for v in (y, gg):
+        assert dev[v.index].tobytes() == ref[v.index].tobytes()
+
+
+def test_fold_sums_overlapping_windows_and_unfolds_back(built):
+    # fold_tests.rs: an eight-element axis unfolded by size 3, step 2 (three
+    # windows) folds back with the overlaps summed; the backward unfolds the
+    # seed by the same parameters
+    t = Tape()
+    x = t.parameter(tensor([8], list(range(1, 9))))
+    w = x.unfold(0, 3, 2, 1)
+    y = w.fold(0, 3, 2, 1, 8)
+    seed = t.leaf(tensor([8], [0.5 * v for v in range(8)]))
+    (gx,) = t.differentiate((y * seed).sum(), [x])
+    ref, dev = both(t, [w, y, gx])
+    # windows [1,2,3], [3,4,5], [5,6,7]; element 8 is in none
+    assert values(ref, w) == [1, 2, 3, 3, 4, 5, 5, 6, 7]
+    assert values(ref, y) == [1, 2, 6, 4, 10, 6, 7, 0]
+    # d/dx = unfold(seed) folded back onto x: the seed times each element's
+    # window count
+    assert values(ref, gx) == [0.0, 0.5, 2.0, 1.5, 4.0, 2.5, 3.0, 0.0]
+    for v in (w, y, gx):
+        assert dev[v.index].tobytes() == ref[v.index].tobytes()
