@@ -155,3 +155,22 @@ def test_fold_sums_overlapping_windows_and_unfolds_back(built):
     assert values(ref, gx) == [0.0, 0.5, 2.0, 1.5, 4.0, 2.5, 3.0, 0.0]
     for v in (w, y, gx):
         assert dev[v.index].tobytes() == ref[v.index].tobytes()
+
+
+def test_literals_mix_into_expressions(built):
+    # graph/tests/value_tests.rs (payload_literals_mix_into_expressions): at
+    # x = 3, y = 2x + 1 = 7 with dy/dx = 2, and z = 6 / x = 2 with
+    # dz/dx = -6 / x^2 = -2/3; every literal is its own leaf
+    t = Tape()
+    x = t.parameter(tensor([], [3.0]))
+    before = len(t)
+    y = t.leaf(filled([], 2.0)) * x + t.leaf(filled([], 1.0))
+    z = t.leaf(filled([], 6.0)) / x
+    assert len(t) - before == 6  # 2, the product, 1, the sum, 6, the quotient
+    gy, = t.differentiate(y, [x])
+    gz, = t.differentiate(z, [x])
+    ref, dev = both(t, [y, z, gy, gz])
+    assert values(ref, y) == [7.0] and values(ref, z) == [2.0] and values(ref, gy) == [2.0]
+    assert values(ref, gz) == [float(np.float32(-(np.float32(2.0) / np.float32(3.0))))]
+    for v in (y, z, gy, gz):
+        assert dev[v.index].tobytes() == ref[v.index].tobytes()
