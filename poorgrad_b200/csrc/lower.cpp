@@ -1589,6 +1589,8 @@ class Emitter {
           float c = 0.0f, r = 0.0f;
           if (literal_value(y, c) && exact_reciprocal(c, r))
             e = "__fmul_rn(" + x + ", " + flit(r) + ")";  // a power-of-two divisor
+          else if (x == flit(1.0f) && relaxed && !P.bf16)
+            e = "tb_rcp(" + y + ")";  // 1 * r is r
           else
             e = relaxed && !P.bf16 ? "__fmul_rn(" + x + ", tb_rcp(" + y + "))"
                                    : "__fdiv_rn(" + x + ", " + y + ")";
